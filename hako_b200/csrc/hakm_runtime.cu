@@ -1,0 +1,887 @@
+// hakm_runtime.cu — device context and C ABI of libhakm_cuda.
+//
+// hakmc_create binds the same tensors hakm_ctx_new binds (src/model.c:17-76)
+// from an MLF2 image in host memory, uploads them once in a kernel-friendly
+// device layout (same bytes, re-ordered), sizes the fp32 KV cache
+// [seq][layer][max_seq][kv_dim] like the reference's, and captures one decode
+// step as a CUDA graph. A step is: embedding, then per layer
+//   qkv  (rmsnorm+q8 prologue; Q4_K q/k rows with bias+RoPE+K append; Q6_K v
+//         rows with bias+V append)
+//   attn (GQA decode attention)
+//   wo   (q8 prologue; Q4_K + residual)
+//   ffn  (rmsnorm+q8 prologue; Q4_K gate/up interleaved + SwiGLU)
+//   down (fp32; Q6_K + residual)
+// then lm_head (rmsnorm; Q6_K logits + argmax + step finalisation).
+#include "../../include/hakm_cuda.h"
+#include "hakm_internal.h"
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+using namespace hakm;
+
+// ------------------------------------------------------------ errors
+
+static thread_local std::string g_err;
+
+static void set_err(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+}
+
+#define CK(call)                                                                    \
+  do {                                                                              \
+    cudaError_t e_ = (call);                                                        \
+    if (e_ != cudaSuccess) {                                                        \
+      set_err("%s:%d %s: %s", __FILE__, __LINE__, #call, cudaGetErrorString(e_)); \
+      return HAKMC_ECUDA;                                                           \
+    }                                                                               \
+  } while (0)
+
+extern "C" const char* hakmc_last_error(void) { return g_err.c_str(); }
+extern "C" int hakmc_version(void) { return 100; }
+
+// ------------------------------------------------------------ MLF2 parsing
+
+// MLF2 v2 (include/mlf2.h:55-87 of mithraeums/hako): 128-byte header,
+// 104-byte directory entries, tensor data relative to data_off.
+namespace {
+
+struct MTensor {
+  std::string name;
+  uint32_t type = 0, n_dims = 0;
+  uint64_t dims[4] = {0, 0, 0, 0};
+  const uint8_t* data = nullptr;
+  uint64_t nbytes = 0;
+};
+
+struct MImage {
+  uint32_t n_layers, d_model, n_heads, n_kv, head_dim, ffn, ctx, vocab, flags;
+  float theta, eps;
+  std::map<std::string, MTensor> t;
+};
+
+template <class T>
+T rd(const uint8_t* p) {
+  T v;
+  memcpy(&v, p, sizeof v);
+  return v;
+}
+
+int parse_mlf2(const uint8_t* img, size_t size, MImage& m) {
+  if (!img || size < 128) { set_err("MLF2 image too small"); return HAKMC_EFORMAT; }
+  if (memcmp(img, "MLF2", 4) != 0) { set_err("bad magic (not MLF2)"); return HAKMC_EFORMAT; }
+  if (rd<uint32_t>(img + 4) != 2) { set_err("unsupported MLF2 version %u", rd<uint32_t>(img + 4)); return HAKMC_EFORMAT; }
+  m.n_layers = rd<uint32_t>(img + 12); m.d_model = rd<uint32_t>(img + 16);
+  m.n_heads = rd<uint32_t>(img + 20); m.n_kv = rd<uint32_t>(img + 24);
+  m.head_dim = rd<uint32_t>(img + 28); m.ffn = rd<uint32_t>(img + 32);
+  m.ctx = rd<uint32_t>(img + 36); m.vocab = rd<uint32_t>(img + 40);
+  m.theta = rd<float>(img + 44); m.eps = rd<float>(img + 48);
+  m.flags = rd<uint32_t>(img + 52);
+  const uint32_t nt = rd<uint32_t>(img + 56);
+  const uint64_t toff = rd<uint64_t>(img + 60), doff = rd<uint64_t>(img + 76);
+  if (toff + (uint64_t)nt * 104 > size || doff > size) { set_err("corrupt offsets"); return HAKMC_EFORMAT; }
+  for (uint32_t i = 0; i < nt; i++) {
+    const uint8_t* e = img + toff + (size_t)i * 104;
+    MTensor t;
+    t.name.assign((const char*)e, strnlen((const char*)e, 48));
+    t.type = rd<uint32_t>(e + 48);
+    t.n_dims = rd<uint32_t>(e + 52);
+    for (int d = 0; d < 4; d++) t.dims[d] = rd<uint64_t>(e + 56 + 8 * d);
+    const uint64_t rel = rd<uint64_t>(e + 88);
+    t.nbytes = rd<uint64_t>(e + 96);
+    if (doff + rel + t.nbytes > size) { set_err("tensor %s past end of image", t.name.c_str()); return HAKMC_EFORMAT; }
+    t.data = img + doff + rel;
+    m.t[t.name] = t;
+  }
+  return 0;
+}
+
+size_t row_bytes(uint32_t type, int n_in) {
+  if (type == W_Q4K) return (size_t)(n_in / QK) * Q4K_BYTES;
+  if (type == W_Q6K) return (size_t)(n_in / QK) * Q6K_BYTES;
+  if (type == 0) return (size_t)n_in * 4;
+  return 0;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ context
+
+struct DevMat {         // one weight matrix on the device
+  int type = 0, rows = 0, cols = 0;
+  uint8_t* w = nullptr;       // Q4_K rows or Q6_K bodies
+  uint16_t* wd = nullptr;     // Q6_K d plane
+};
+
+struct DevLayer {
+  float *attn_norm, *ffn_norm, *bqk, *bv;
+  DevMat wqk, wv, wo, wgu, down;
+};
+
+struct hakmc_ctx {
+  int device = 0, num_sms = 148;
+  int L, D, H, KVH, hd, KV, F, V, max_seq, max_batch;
+  float theta, eps;
+  bool tied = false, pdl = true;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_ms = 0.f;
+  std::vector<void*> allocs;
+  std::vector<DevLayer> layers;
+  DevMat tok_embd, lm_head;
+  float* out_norm = nullptr;
+  // KV cache [seq][layer][max_seq][KV]
+  float *k_cache = nullptr, *v_cache = nullptr;
+  // activations (sequence 0 for the single-sequence graph)
+  float *xb, *q, *k, *v, *att, *hbuf, *logits, *rope_cs, *attn_part;
+  int *token_dev, *pos_dev, *step_dev, *token_log, *prompt_dev;
+  int prompt_cap = 0;
+  unsigned long long* argmax_key;
+  unsigned int *done_counter, *attn_counters;
+  int token_log_cap = 0;
+  int* h_pinned = nullptr;    // pinned staging: [0] token in, [1] argmax out
+  float* logits_pinned = nullptr;
+  int pos = 0;                // host mirror of *pos_dev
+  int run_layers = 0;
+  std::map<int, cudaGraphExec_t> graphs;  // keyed by attention split count
+};
+
+static int dalloc(hakmc_ctx* c, void** p, size_t n) {
+  cudaError_t e = cudaMalloc(p, n ? n : 16);
+  if (e != cudaSuccess) {
+    set_err("cudaMalloc(%zu): %s", n, cudaGetErrorString(e));
+    return HAKMC_ENOMEM;
+  }
+  c->allocs.push_back(*p);
+  return 0;
+}
+
+// Upload rows of a Q4_K / Q6_K matrix. `order[i]` is the source row of device
+// row i (identity when empty). Q6_K rows are split into 208-byte bodies and
+// an fp16 d plane (hakmc_q6k_pack layout).
+static int upload_mat(hakmc_ctx* c, DevMat& dm, const MTensor& t, int exp_cols, int exp_rows,
+                      const std::vector<int>& order, const MTensor* t2 = nullptr) {
+  if (t.type != W_Q4K && t.type != W_Q6K) {
+    set_err("tensor %s: type %u unsupported on the device (Q4_K/Q6_K only)", t.name.c_str(), t.type);
+    return HAKMC_EFORMAT;
+  }
+  if ((int)t.dims[0] != exp_cols || (int)t.dims[1] != exp_rows || exp_cols % QK) {
+    set_err("tensor %s: dims [%llu,%llu], expected [%d,%d]", t.name.c_str(),
+            (unsigned long long)t.dims[0], (unsigned long long)t.dims[1], exp_cols, exp_rows);
+    return HAKMC_EFORMAT;
+  }
+  const size_t rb = row_bytes(t.type, exp_cols);
+  if (t.nbytes < rb * exp_rows) { set_err("tensor %s: short data", t.name.c_str()); return HAKMC_EFORMAT; }
+  int rows = exp_rows;
+  if (t2) {  // interleave t (even device rows) with t2 (odd device rows)
+    if (t2->type != t.type || t2->dims[0] != t.dims[0] || t2->dims[1] != t.dims[1]) {
+      set_err("tensors %s/%s must share type and shape", t.name.c_str(), t2->name.c_str());
+      return HAKMC_EFORMAT;
+    }
+    rows = 2 * exp_rows;
+  }
+  dm.type = (int)t.type;
+  dm.rows = rows;
+  dm.cols = exp_cols;
+  const int nb = exp_cols / QK;
+  auto src_row = [&](int i) -> const uint8_t* {
+    if (t2) return ((i & 1) ? t2->data : t.data) + (size_t)(i >> 1) * rb;
+    const int s = order.empty() ? i : order[i];
+    return t.data + (size_t)s * rb;
+  };
+  std::vector<uint8_t> host((size_t)rows * rb);
+  if (t.type == W_Q4K) {
+    for (int i = 0; i < rows; i++) memcpy(host.data() + (size_t)i * rb, src_row(i), rb);
+    int e = dalloc(c, (void**)&dm.w, host.size());
+    if (e) return e;
+    CK(cudaMemcpy(dm.w, host.data(), host.size(), cudaMemcpyHostToDevice));
+  } else {
+    const size_t body = (size_t)rows * nb * Q6K_BODY;
+    for (int i = 0; i < rows; i++) {
+      const uint8_t* s = src_row(i);
+      for (int b = 0; b < nb; b++) {
+        memcpy(host.data() + ((size_t)i * nb + b) * Q6K_BODY, s + (size_t)b * Q6K_BYTES, Q6K_BODY);
+        memcpy(host.data() + body + ((size_t)i * nb + b) * 2, s + (size_t)b * Q6K_BYTES + Q6K_BODY, 2);
+      }
+    }
+    int e = dalloc(c, (void**)&dm.w, host.size());
+    if (e) return e;
+    dm.wd = reinterpret_cast<uint16_t*>(dm.w + body);
+    CK(cudaMemcpy(dm.w, host.data(), host.size(), cudaMemcpyHostToDevice));
+  }
+  return 0;
+}
+
+static int upload_f32(hakmc_ctx* c, float** dst, const MTensor* t, int n, const std::vector<int>& order) {
+  if (!t) { *dst = nullptr; return 0; }
+  if (t->type != 0 || (int)t->dims[0] != n || t->nbytes < (size_t)n * 4) {
+    set_err("tensor %s: expected %d f32", t->name.c_str(), n);
+    return HAKMC_EFORMAT;
+  }
+  std::vector<float> h(n);
+  const float* s = reinterpret_cast<const float*>(t->data);
+  for (int i = 0; i < n; i++) h[i] = s[order.empty() ? i : order[i]];
+  int e = dalloc(c, (void**)dst, (size_t)n * 4);
+  if (e) return e;
+  CK(cudaMemcpy(*dst, h.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+  return 0;
+}
+
+// Device row 2p+t of head h holds source row h*hd + p + t*hd/2, so the two
+// halves of every NeoX rotation pair (src/nn.c:36-41) meet in one chunk.
+static std::vector<int> rope_pair_order(int n_heads, int hd) {
+  std::vector<int> o((size_t)n_heads * hd);
+  for (int h = 0; h < n_heads; h++)
+    for (int p = 0; p < hd / 2; p++) {
+      o[h * hd + 2 * p] = h * hd + p;
+      o[h * hd + 2 * p + 1] = h * hd + p + hd / 2;
+    }
+  return o;
+}
+
+static Seg make_seg(const DevMat& m, int epi, float* out) {
+  Seg s = {};
+  s.w = m.w;
+  s.wd = m.wd;
+  s.type = m.type;
+  s.n_rows = m.rows;
+  s.epi = epi;
+  s.out = out;
+  return s;
+}
+
+static void finish_params(PhaseParams& p) {
+  int cb = 0;
+  p.need_q8 = 0;
+  for (int i = 0; i < p.n_seg; i++) {
+    p.seg[i].chunk_begin = cb;
+    cb += (p.seg[i].n_rows + ROWS_PER_CHUNK - 1) / ROWS_PER_CHUNK;
+    if (p.seg[i].type == W_Q4K) p.need_q8 = 1;
+  }
+  p.total_chunks = cb;
+}
+
+static cudaError_t run_phase(hakmc_ctx* c, PhaseParams& p) {
+  finish_params(p);
+  return launch_phase(p, phase_grid(p, c->num_sms), c->stream, c->pdl);
+}
+
+// Enqueue one decode step for sequence 0 on c->stream.
+static cudaError_t enqueue_step(hakmc_ctx* c, int n_split) {
+  cudaError_t e = launch_embed_q6k(c->xb, c->tok_embd.w, c->tok_embd.wd, c->token_dev, c->D, nullptr,
+                                   c->stream, c->pdl);
+  if (e != cudaSuccess) return e;
+  const size_t lstride = (size_t)c->max_seq * c->KV;
+  for (int l = 0; l < c->run_layers; l++) {
+    DevLayer& y = c->layers[l];
+    float* kc = c->k_cache + (size_t)l * lstride;
+    float* vc = c->v_cache + (size_t)l * lstride;
+    {  // qkv
+      PhaseParams p = {};
+      p.n_in = c->D; p.act = ACT_RMS; p.x = c->xb; p.norm_w = y.attn_norm; p.eps = c->eps;
+      p.n_seg = 2;
+      p.seg[0] = make_seg(y.wqk, EPI_ROPE_QK, c->q);
+      p.seg[0].out2 = c->k; p.seg[0].cache = kc; p.seg[0].split = c->D; p.seg[0].bias = y.bqk;
+      p.seg[1] = make_seg(y.wv, EPI_V_CACHE, c->v);
+      p.seg[1].cache = vc; p.seg[1].bias = y.bv;
+      p.rope_cs = c->rope_cs; p.pos_dev = c->pos_dev; p.head_dim = c->hd; p.kv_dim = c->KV;
+      if ((e = run_phase(c, p)) != cudaSuccess) return e;
+    }
+    {  // attention
+      AttnParams a = {};
+      a.q = c->q; a.k_cache = kc; a.v_cache = vc; a.out = c->att; a.pos_dev = c->pos_dev;
+      a.n_heads = c->H; a.n_kv = c->KVH; a.head_dim = c->hd; a.scale = 1.0f / sqrtf((float)c->hd);
+      a.n_split = n_split; a.part = c->attn_part; a.counters = c->attn_counters;
+      if ((e = launch_attention(a, c->stream, c->pdl)) != cudaSuccess) return e;
+    }
+    {  // wo + residual
+      PhaseParams p = {};
+      p.n_in = c->D; p.act = ACT_F32; p.x = c->att;
+      p.n_seg = 1;
+      p.seg[0] = make_seg(y.wo, EPI_RESID, c->xb);
+      if ((e = run_phase(c, p)) != cudaSuccess) return e;
+    }
+    {  // gate/up + SwiGLU
+      PhaseParams p = {};
+      p.n_in = c->D; p.act = ACT_RMS; p.x = c->xb; p.norm_w = y.ffn_norm; p.eps = c->eps;
+      p.n_seg = 1;
+      p.seg[0] = make_seg(y.wgu, EPI_SWIGLU, c->hbuf);
+      if ((e = run_phase(c, p)) != cudaSuccess) return e;
+    }
+    {  // down + residual
+      PhaseParams p = {};
+      p.n_in = c->F; p.act = ACT_F32; p.x = c->hbuf;
+      p.n_seg = 1;
+      p.seg[0] = make_seg(y.down, EPI_RESID, c->xb);
+      if ((e = run_phase(c, p)) != cudaSuccess) return e;
+    }
+  }
+  {  // final norm + lm_head + argmax + finalise
+    PhaseParams p = {};
+    p.n_in = c->D; p.act = ACT_RMS; p.x = c->xb; p.norm_w = c->out_norm; p.eps = c->eps;
+    p.n_seg = 1;
+    p.seg[0] = make_seg(c->lm_head, EPI_ARGMAX, c->logits);
+    p.argmax_key = c->argmax_key; p.done_counter = c->done_counter;
+    p.next_token = c->token_dev; p.token_log = c->token_log; p.step_dev = c->step_dev;
+    p.token_log_cap = c->token_log_cap;
+    p.pos_inc = c->pos_dev;
+    if ((e = run_phase(c, p)) != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+static int n_split_for(const hakmc_ctx* c, int pos) { return pos / ATTN_CHUNK + 1; }
+
+static int get_graph(hakmc_ctx* c, int n_split, cudaGraphExec_t* out) {
+  auto it = c->graphs.find(n_split);
+  if (it != c->graphs.end()) { *out = it->second; return 0; }
+  cudaGraph_t g = nullptr;
+  CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  cudaError_t e = enqueue_step(c, n_split);
+  cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+  if (e != cudaSuccess || e2 != cudaSuccess) {
+    set_err("graph capture failed: %s / %s", cudaGetErrorString(e), cudaGetErrorString(e2));
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    return HAKMC_ECUDA;
+  }
+  cudaGraphExec_t ge = nullptr;
+  e = cudaGraphInstantiate(&ge, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) { set_err("graph instantiate: %s", cudaGetErrorString(e)); return HAKMC_ECUDA; }
+  c->graphs[n_split] = ge;
+  *out = ge;
+  return 0;
+}
+
+static void drop_graphs(hakmc_ctx* c) {
+  for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+  c->graphs.clear();
+}
+
+// One step at the host-mirrored position (token already in token_dev).
+static int launch_one(hakmc_ctx* c) {
+  if (c->pos >= c->max_seq) { set_err("position %d beyond max_seq %d", c->pos, c->max_seq); return HAKMC_ERANGE; }
+  cudaGraphExec_t g;
+  int r = get_graph(c, n_split_for(c, c->pos), &g);
+  if (r) return r;
+  CK(cudaGraphLaunch(g, c->stream));
+  c->pos++;
+  return 0;
+}
+
+extern "C" void hakmc_destroy(hakmc_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  drop_graphs(c);
+  for (void* p : c->allocs) cudaFree(p);
+  if (c->h_pinned) cudaFreeHost(c->h_pinned);
+  if (c->logits_pinned) cudaFreeHost(c->logits_pinned);
+  if (c->ev0) cudaEventDestroy(c->ev0);
+  if (c->ev1) cudaEventDestroy(c->ev1);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  delete c;
+}
+
+static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
+  MImage m;
+  int r = parse_mlf2(img, size, m);
+  if (r) return r;
+  c->L = (int)m.n_layers; c->D = (int)m.d_model; c->H = (int)m.n_heads; c->KVH = (int)m.n_kv;
+  c->hd = (int)m.head_dim; c->KV = c->KVH * c->hd; c->F = (int)m.ffn; c->V = (int)m.vocab;
+  c->theta = m.theta; c->eps = m.eps; c->tied = (m.flags & 2u) != 0;
+  c->run_layers = c->L;
+  if (c->D % QK || c->F % QK || c->H % c->KVH || c->H * c->hd != c->D || (c->hd != 64 && c->hd != 128) ||
+      c->H / c->KVH > 8 || c->KV % 4) {
+    set_err("unsupported shape: d %d heads %d/%d hd %d ffn %d", c->D, c->H, c->KVH, c->hd, c->F);
+    return HAKMC_EINVAL;
+  }
+  auto need = [&](const std::string& n) -> const MTensor* {
+    auto it = m.t.find(n);
+    if (it == m.t.end()) { set_err("missing tensor %s", n.c_str()); return nullptr; }
+    return &it->second;
+  };
+  auto opt = [&](const std::string& n) -> const MTensor* {
+    auto it = m.t.find(n);
+    return it == m.t.end() ? nullptr : &it->second;
+  };
+  CK(cudaSetDevice(c->device));
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, c->device));
+  c->num_sms = prop.multiProcessorCount;
+  CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  CK(cudaEventCreate(&c->ev0));
+  CK(cudaEventCreate(&c->ev1));
+  const char* pe = getenv("HAKMC_PDL");
+  c->pdl = !(pe && pe[0] == '0');
+
+  const MTensor *te = need("token_embd.weight"), *on = need("output_norm.weight");
+  if (!te || !on) return HAKMC_EFORMAT;
+  const MTensor* ow = c->tied ? te : need("output.weight");
+  if (!ow) return HAKMC_EFORMAT;
+  std::vector<int> none;
+  if (te->type != W_Q6K) { set_err("token_embd: only Q6_K embeddings are supported"); return HAKMC_EFORMAT; }
+  if ((r = upload_mat(c, c->tok_embd, *te, c->D, c->V, none))) return r;
+  if (c->tied) c->lm_head = c->tok_embd;
+  else if ((r = upload_mat(c, c->lm_head, *ow, c->D, c->V, none))) return r;
+  if ((r = upload_f32(c, &c->out_norm, on, c->D, none))) return r;
+
+  const std::vector<int> qo = rope_pair_order(c->H, c->hd), ko = rope_pair_order(c->KVH, c->hd);
+  std::vector<int> qko(qo);
+  for (int i : ko) qko.push_back(c->D + i);
+  c->layers.resize(c->L);
+  char nm[96];
+  for (int l = 0; l < c->L; l++) {
+    DevLayer& y = c->layers[l];
+    auto T = [&](const char* s) { snprintf(nm, sizeof nm, "blk.%d.%s", l, s); return std::string(nm); };
+    const MTensor *an = need(T("attn_norm.weight")), *fn = need(T("ffn_norm.weight")),
+                  *wq = need(T("attn_q.weight")), *wk = need(T("attn_k.weight")),
+                  *wv = need(T("attn_v.weight")), *wo = need(T("attn_output.weight")),
+                  *wg = need(T("ffn_gate.weight")), *wu = need(T("ffn_up.weight")),
+                  *wd = need(T("ffn_down.weight"));
+    if (!an || !fn || !wq || !wk || !wv || !wo || !wg || !wu || !wd) return HAKMC_EFORMAT;
+    const MTensor *bq = opt(T("attn_q.bias")), *bk = opt(T("attn_k.bias")), *bv = opt(T("attn_v.bias"));
+    if ((r = upload_f32(c, &y.attn_norm, an, c->D, none))) return r;
+    if ((r = upload_f32(c, &y.ffn_norm, fn, c->D, none))) return r;
+    // q and k rows share one Q4_K/Q6_K segment: concatenate, then pair-order
+    if (wq->type != wk->type) { set_err("attn_q/attn_k types differ"); return HAKMC_EFORMAT; }
+    {
+      MTensor cat = *wq;
+      const size_t rb = row_bytes(wq->type, c->D);
+      std::vector<uint8_t> buf(rb * (size_t)(c->D + c->KV));
+      if (wq->nbytes < rb * c->D || wk->nbytes < rb * c->KV || (int)wk->dims[1] != c->KV ||
+          (int)wk->dims[0] != c->D) {
+        set_err("attn_q/attn_k shape mismatch");
+        return HAKMC_EFORMAT;
+      }
+      memcpy(buf.data(), wq->data, rb * c->D);
+      memcpy(buf.data() + rb * c->D, wk->data, rb * c->KV);
+      cat.data = buf.data(); cat.nbytes = buf.size(); cat.dims[1] = (uint64_t)(c->D + c->KV);
+      if ((r = upload_mat(c, y.wqk, cat, c->D, c->D + c->KV, qko))) return r;
+    }
+    if (bq && bk) {
+      std::vector<float> b((size_t)(c->D + c->KV));
+      if (bq->type || bk->type || (int)bq->dims[0] != c->D || (int)bk->dims[0] != c->KV) {
+        set_err("q/k bias shape"); return HAKMC_EFORMAT;
+      }
+      for (int i = 0; i < c->D + c->KV; i++)
+        b[i] = qko[i] < c->D ? reinterpret_cast<const float*>(bq->data)[qko[i]]
+                             : reinterpret_cast<const float*>(bk->data)[qko[i] - c->D];
+      if ((r = dalloc(c, (void**)&y.bqk, b.size() * 4))) return r;
+      CK(cudaMemcpy(y.bqk, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
+    } else if (bq || bk) {
+      set_err("layer %d: only one of attn_q/attn_k bias present", l);
+      return HAKMC_EFORMAT;
+    } else {
+      y.bqk = nullptr;
+    }
+    if ((r = upload_mat(c, y.wv, *wv, c->D, c->KV, none))) return r;
+    if ((r = upload_f32(c, &y.bv, bv, c->KV, none))) return r;
+    if ((r = upload_mat(c, y.wo, *wo, c->D, c->D, none))) return r;
+    if ((r = upload_mat(c, y.wgu, *wg, c->D, c->F, none, wu))) return r;
+    if ((r = upload_mat(c, y.down, *wd, c->F, c->D, none))) return r;
+  }
+
+  // KV cache and activations
+  const size_t kv = (size_t)c->max_batch * c->L * c->max_seq * c->KV;
+  if ((r = dalloc(c, (void**)&c->k_cache, kv * 4))) return r;
+  if ((r = dalloc(c, (void**)&c->v_cache, kv * 4))) return r;
+  CK(cudaMemset(c->k_cache, 0, kv * 4));
+  CK(cudaMemset(c->v_cache, 0, kv * 4));
+  const int B = c->max_batch;
+  if ((r = dalloc(c, (void**)&c->xb, (size_t)B * c->D * 4))) return r;
+  if ((r = dalloc(c, (void**)&c->q, (size_t)B * c->D * 4))) return r;
+  if ((r = dalloc(c, (void**)&c->k, (size_t)B * c->KV * 4))) return r;
+  if ((r = dalloc(c, (void**)&c->v, (size_t)B * c->KV * 4))) return r;
+  if ((r = dalloc(c, (void**)&c->att, (size_t)B * c->D * 4))) return r;
+  if ((r = dalloc(c, (void**)&c->hbuf, (size_t)B * c->F * 4))) return r;
+  if ((r = dalloc(c, (void**)&c->logits, (size_t)B * c->V * 4))) return r;
+  const int max_split = (c->max_seq + ATTN_CHUNK - 1) / ATTN_CHUNK;
+  if ((r = dalloc(c, (void**)&c->attn_part,
+                  attention_scratch_floats(c->KVH, max_split, c->H / c->KVH, c->hd) * 4 * B)))
+    return r;
+  if ((r = dalloc(c, (void**)&c->attn_counters, 64 * 4 * B))) return r;
+  CK(cudaMemset(c->attn_counters, 0, 64 * 4 * B));
+  if ((r = dalloc(c, (void**)&c->token_dev, 16 * B))) return r;
+  if ((r = dalloc(c, (void**)&c->pos_dev, 16 * B))) return r;
+  if ((r = dalloc(c, (void**)&c->step_dev, 16))) return r;
+  c->token_log_cap = c->max_seq + 8;
+  if ((r = dalloc(c, (void**)&c->token_log, (size_t)c->token_log_cap * 4))) return r;
+  if ((r = dalloc(c, (void**)&c->argmax_key, 8 * B))) return r;
+  if ((r = dalloc(c, (void**)&c->done_counter, 4 * B))) return r;
+  CK(cudaMemset(c->token_dev, 0, 16 * B));
+  CK(cudaMemset(c->pos_dev, 0, 16 * B));
+  CK(cudaMemset(c->step_dev, 0, 16));
+  CK(cudaMemset(c->argmax_key, 0, 8 * B));
+  CK(cudaMemset(c->done_counter, 0, 4 * B));
+
+  // RoPE table with the reference's formula and the host libm
+  // (src/nn.c:35-37): freq = powf(theta, -(2i/hd)), angle = pos * freq.
+  {
+    const int half = c->hd / 2;
+    std::vector<float> cs((size_t)c->max_seq * half * 2);
+    for (int p = 0; p < c->max_seq; p++)
+      for (int i = 0; i < half; i++) {
+        const float freq = powf(c->theta, -((float)(2 * i) / (float)c->hd));
+        const float ang = (float)p * freq;
+        cs[((size_t)p * half + i) * 2] = cosf(ang);
+        cs[((size_t)p * half + i) * 2 + 1] = sinf(ang);
+      }
+    if ((r = dalloc(c, (void**)&c->rope_cs, cs.size() * 4))) return r;
+    CK(cudaMemcpy(c->rope_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  }
+  CK(cudaMallocHost((void**)&c->h_pinned, 64));
+  CK(cudaMallocHost((void**)&c->logits_pinned, (size_t)c->V * 4));
+  CK(cudaDeviceSynchronize());
+  return 0;
+}
+
+extern "C" hakmc_ctx* hakmc_create(const void* image, size_t size, int max_seq, int max_batch, int device) {
+  if (max_seq <= 0 || max_batch <= 0) { set_err("max_seq and max_batch must be positive"); return nullptr; }
+  hakmc_ctx* c = new hakmc_ctx();
+  c->device = device;
+  c->max_seq = max_seq;
+  c->max_batch = max_batch;
+  if (create_impl(c, (const uint8_t*)image, size) != 0) {
+    std::string keep = g_err;
+    hakmc_destroy(c);
+    g_err = keep;
+    return nullptr;
+  }
+  return c;
+}
+
+extern "C" void hakmc_reset(hakmc_ctx* c) {
+  if (!c) return;
+  hakmc_set_pos(c, 0);
+}
+
+extern "C" int hakmc_pos(const hakmc_ctx* c) { return c ? c->pos : -1; }
+extern "C" int hakmc_vocab(const hakmc_ctx* c) { return c ? c->V : -1; }
+extern "C" int hakmc_dim(const hakmc_ctx* c) { return c ? c->D : -1; }
+extern "C" int hakmc_n_layers(const hakmc_ctx* c) { return c ? c->L : -1; }
+extern "C" float hakmc_last_device_ms(const hakmc_ctx* c) { return c ? c->last_ms : -1.f; }
+
+extern "C" int hakmc_set_pos(hakmc_ctx* c, int pos) {
+  if (!c || pos < 0 || pos > c->max_seq) { set_err("bad position"); return HAKMC_EINVAL; }
+  CK(cudaSetDevice(c->device));
+  c->h_pinned[2] = pos;
+  CK(cudaMemcpyAsync(c->pos_dev, &c->h_pinned[2], 4, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  c->pos = pos;
+  return 0;
+}
+
+extern "C" int hakmc_set_layers(hakmc_ctx* c, int n) {
+  if (!c) return HAKMC_EINVAL;
+  const int nl = (n < 0 || n > c->L) ? c->L : n;
+  if (nl != c->run_layers) {
+    CK(cudaSetDevice(c->device));
+    CK(cudaStreamSynchronize(c->stream));
+    drop_graphs(c);
+    c->run_layers = nl;
+  }
+  return 0;
+}
+
+extern "C" int hakmc_forward(hakmc_ctx* c, int token, float* logits, int* argmax) {
+  if (!c) return HAKMC_EINVAL;
+  if (token < 0 || token >= c->V) { set_err("token %d out of range", token); return HAKMC_EINVAL; }
+  CK(cudaSetDevice(c->device));
+  c->h_pinned[0] = token;
+  CK(cudaEventRecord(c->ev0, c->stream));
+  CK(cudaMemcpyAsync(c->token_dev, &c->h_pinned[0], 4, cudaMemcpyHostToDevice, c->stream));
+  int r = launch_one(c);
+  if (r) return r;
+  CK(cudaMemcpyAsync(&c->h_pinned[1], c->token_dev, 4, cudaMemcpyDeviceToHost, c->stream));
+  if (logits) CK(cudaMemcpyAsync(c->logits_pinned, c->logits, (size_t)c->V * 4, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaEventRecord(c->ev1, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  CK(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
+  if (argmax) *argmax = c->h_pinned[1];
+  if (logits) memcpy(logits, c->logits_pinned, (size_t)c->V * 4);
+  return 0;
+}
+
+extern "C" int hakmc_generate(hakmc_ctx* c, const int* prompt, int n_prompt, int n_gen, int* out) {
+  if (!c || !prompt || n_prompt <= 0 || n_gen < 0 || (n_gen > 0 && !out)) return HAKMC_EINVAL;
+  if (c->pos + n_prompt + n_gen - 1 > c->max_seq) { set_err("sequence exceeds max_seq"); return HAKMC_ERANGE; }
+  if (c->pos + n_prompt + n_gen > c->token_log_cap) { set_err("token log too small"); return HAKMC_ERANGE; }
+  for (int i = 0; i < n_prompt; i++)
+    if (prompt[i] < 0 || prompt[i] >= c->V) { set_err("prompt token out of range"); return HAKMC_EINVAL; }
+  CK(cudaSetDevice(c->device));
+  if (n_prompt > c->prompt_cap) {
+    void* p = nullptr;
+    int r = dalloc(c, &p, (size_t)n_prompt * 4);
+    if (r) return r;
+    c->prompt_dev = (int*)p;
+    c->prompt_cap = n_prompt;
+  }
+  std::vector<int> pp(prompt, prompt + n_prompt);
+  CK(cudaMemcpyAsync(c->prompt_dev, pp.data(), (size_t)n_prompt * 4, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaMemsetAsync(c->step_dev, 0, 4, c->stream));
+  CK(cudaEventRecord(c->ev0, c->stream));
+  for (int i = 0; i < n_prompt; i++) {
+    CK(cudaMemcpyAsync(c->token_dev, c->prompt_dev + i, 4, cudaMemcpyDeviceToDevice, c->stream));
+    int r = launch_one(c);
+    if (r) return r;
+  }
+  for (int g = 1; g < n_gen; g++) {
+    int r = launch_one(c);
+    if (r) return r;
+  }
+  CK(cudaEventRecord(c->ev1, c->stream));
+  if (n_gen > 0)
+    CK(cudaMemcpyAsync(out, c->token_log + (n_prompt - 1), (size_t)n_gen * 4, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  CK(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
+  return 0;
+}
+
+extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* pos, int n_seq,
+                                   float* logits, int* argmax) {
+  (void)tokens; (void)pos; (void)logits; (void)argmax;
+  if (!c || n_seq <= 0 || n_seq > c->max_batch) { set_err("bad batch"); return HAKMC_EINVAL; }
+  set_err("batched decode is not built yet");
+  return HAKMC_EINVAL;
+}
+
+extern "C" int hakmc_hidden(hakmc_ctx* c, int seq, float* out) {
+  if (!c || !out || seq < 0 || seq >= c->max_batch) return HAKMC_EINVAL;
+  CK(cudaSetDevice(c->device));
+  CK(cudaMemcpyAsync(out, c->xb + (size_t)seq * c->D, (size_t)c->D * 4, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  return 0;
+}
+
+extern "C" int hakmc_fill_kv(hakmc_ctx* c, int seq, const float* k, const float* v, int n_pos) {
+  if (!c || !k || !v || seq < 0 || seq >= c->max_batch || n_pos < 0 || n_pos > c->max_seq) {
+    set_err("bad fill_kv arguments");
+    return HAKMC_EINVAL;
+  }
+  CK(cudaSetDevice(c->device));
+  const size_t row = (size_t)n_pos * c->KV * 4;
+  for (int l = 0; l < c->L; l++) {
+    const size_t off = (((size_t)seq * c->L + l) * c->max_seq) * c->KV;
+    CK(cudaMemcpy(c->k_cache + off, k + (size_t)l * n_pos * c->KV, row, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->v_cache + off, v + (size_t)l * n_pos * c->KV, row, cudaMemcpyHostToDevice));
+  }
+  if (seq == 0) return hakmc_set_pos(c, n_pos);
+  return 0;
+}
+
+// ------------------------------------------------------------ kernel-level API
+
+namespace {
+// Small per-device scratch the kernel-level entry points share: a position
+// word, attention partials and tickets, a RoPE row and argmax words. Grown on
+// demand; one per device for the life of the process.
+struct DevScratch {
+  int* pos = nullptr;
+  unsigned* counters = nullptr;
+  float* part = nullptr;
+  size_t part_floats = 0;
+  float* rope = nullptr;
+  size_t rope_floats = 0;
+  unsigned long long* key = nullptr;
+  unsigned* done = nullptr;
+  int* tok = nullptr;
+};
+std::mutex g_scr_mu;
+std::map<int, DevScratch> g_scr;
+
+int scratch(DevScratch** out, size_t part_floats, size_t rope_floats) {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_scr_mu);
+  DevScratch& s = g_scr[dev];
+  if (!s.pos) {
+    CK(cudaMalloc(&s.pos, 64));
+    CK(cudaMalloc(&s.counters, 64 * 4));
+    CK(cudaMemset(s.counters, 0, 64 * 4));
+    CK(cudaMalloc(&s.key, 64));
+    CK(cudaMemset(s.key, 0, 64));
+    CK(cudaMalloc(&s.done, 64));
+    CK(cudaMemset(s.done, 0, 64));
+    CK(cudaMalloc(&s.tok, 64));
+  }
+  if (part_floats > s.part_floats) {
+    CK(cudaDeviceSynchronize());
+    if (s.part) cudaFree(s.part);
+    CK(cudaMalloc(&s.part, part_floats * 4));
+    s.part_floats = part_floats;
+  }
+  if (rope_floats > s.rope_floats) {
+    CK(cudaDeviceSynchronize());
+    if (s.rope) cudaFree(s.rope);
+    CK(cudaMalloc(&s.rope, rope_floats * 4));
+    s.rope_floats = rope_floats;
+  }
+  *out = &s;
+  return 0;
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+}  // namespace
+
+#define CKL(expr)                                                                           \
+  do {                                                                                      \
+    cudaError_t e_ = (expr);                                                                \
+    if (e_ != cudaSuccess) { set_err("%s: %s", #expr, cudaGetErrorString(e_)); return HAKMC_ECUDA; } \
+  } while (0)
+
+extern "C" int hakmc_quantize_q8_32(const float* x, int n, int8_t* xq, float* xs, void* stream) {
+  if (!x || !xq || !xs || n <= 0 || n % 32) { set_err("quantize: n must be a positive multiple of 32"); return HAKMC_EINVAL; }
+  CKL(launch_quantize_q8(x, n, xq, xs, (cudaStream_t)stream));
+  return 0;
+}
+
+static int gemv_common(float* out, const void* w, int type, const float* x, const int8_t* xq, const float* xs,
+                       const float* bias, int n_out, int n_in, int act, void* stream) {
+  if (!out || !w || n_out <= 0 || n_in <= 0 || n_in % QK) { set_err("gemv: n_in must be a positive multiple of 256"); return HAKMC_EINVAL; }
+  if (!aligned16(w) || (x && !aligned16(x)) || (xq && !aligned16(xq))) { set_err("gemv: buffers must be 16-byte aligned"); return HAKMC_EINVAL; }
+  PhaseParams p = {};
+  p.n_in = n_in; p.act = act; p.x = x; p.xq = xq; p.xs = xs;
+  p.n_seg = 1;
+  Seg s = {};
+  s.w = (const uint8_t*)w;
+  s.type = type;
+  s.n_rows = n_out;
+  s.epi = EPI_STORE;
+  s.out = out;
+  s.bias = bias;
+  if (type == W_Q6K) s.wd = reinterpret_cast<const uint16_t*>((const uint8_t*)w + (size_t)n_out * (n_in / QK) * Q6K_BODY);
+  p.seg[0] = s;
+  finish_params(p);
+  if (phase_smem_bytes(p) > 110 * 1024) { set_err("gemv: n_in too large"); return HAKMC_EINVAL; }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  CKL(launch_phase(p, phase_grid(p, sms), (cudaStream_t)stream, false));
+  return 0;
+}
+
+extern "C" int hakmc_gemv_q4k_q8(float* out, const void* w, const int8_t* xq, const float* xs, const float* bias,
+                                 int n_out, int n_in, void* stream) {
+  if (!xq || !xs) return HAKMC_EINVAL;
+  return gemv_common(out, w, W_Q4K, nullptr, xq, xs, bias, n_out, n_in, ACT_Q8, stream);
+}
+
+extern "C" int hakmc_gemv_q4k(float* out, const void* w, const float* x, const float* bias, int n_out, int n_in,
+                              void* stream) {
+  if (!x) return HAKMC_EINVAL;
+  return gemv_common(out, w, W_Q4K, x, nullptr, nullptr, bias, n_out, n_in, ACT_F32, stream);
+}
+
+extern "C" int hakmc_q4k_subsums(int32_t* iqx, int32_t* ix, const void* w, const int8_t* xq, int n_out, int n_in,
+                                 void* stream) {
+  if (!iqx || !ix || !w || !xq || n_out <= 0 || n_in <= 0 || n_in % QK) return HAKMC_EINVAL;
+  CKL(launch_q4k_subsums(iqx, ix, (const uint8_t*)w, xq, n_out, n_in, (cudaStream_t)stream));
+  return 0;
+}
+
+extern "C" size_t hakmc_q6k_packed_bytes(int n_rows, int n_in) {
+  return (size_t)n_rows * (n_in / QK) * Q6K_BYTES;
+}
+
+extern "C" int hakmc_q6k_pack(void* dst, const void* src, int n_rows, int n_in, void* stream) {
+  if (!dst || !src || n_rows <= 0 || n_in <= 0 || n_in % QK) return HAKMC_EINVAL;
+  CKL(launch_q6k_pack((uint8_t*)dst, (const uint8_t*)src, n_rows, n_in, (cudaStream_t)stream));
+  return 0;
+}
+
+extern "C" int hakmc_gemv_q6k(float* out, const void* w, const float* x, const float* bias, int n_out, int n_in,
+                              void* stream) {
+  if (!x) return HAKMC_EINVAL;
+  return gemv_common(out, w, W_Q6K, x, nullptr, nullptr, bias, n_out, n_in, ACT_F32, stream);
+}
+
+extern "C" int hakmc_lmhead_argmax(float* logits, int* argmax, const void* w, const float* x, const float* norm_w,
+                                   float eps, int n_vocab, int n_in, void* stream) {
+  if (!argmax || !w || !x || n_vocab <= 0 || n_in % QK || !aligned16(w) || !aligned16(x)) return HAKMC_EINVAL;
+  DevScratch* s;
+  int r = scratch(&s, 0, 0);
+  if (r) return r;
+  PhaseParams p = {};
+  p.n_in = n_in; p.act = norm_w ? ACT_RMS : ACT_F32; p.x = x; p.norm_w = norm_w; p.eps = eps;
+  p.n_seg = 1;
+  Seg sg = {};
+  sg.w = (const uint8_t*)w;
+  sg.wd = reinterpret_cast<const uint16_t*>((const uint8_t*)w + (size_t)n_vocab * (n_in / QK) * Q6K_BODY);
+  sg.type = W_Q6K; sg.n_rows = n_vocab; sg.epi = EPI_ARGMAX; sg.out = logits;
+  p.seg[0] = sg;
+  p.argmax_key = s->key; p.done_counter = s->done; p.next_token = argmax;
+  finish_params(p);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  CKL(launch_phase(p, phase_grid(p, sms), (cudaStream_t)stream, false));
+  return 0;
+}
+
+extern "C" int hakmc_dequant(float* out, const void* w, int type, int n_rows, int n_in, void* stream) {
+  if (!out || !w || n_rows <= 0 || n_in % QK || (type != W_Q4K && type != W_Q6K)) return HAKMC_EINVAL;
+  CKL(launch_dequant(out, (const uint8_t*)w, type, n_rows, n_in, (cudaStream_t)stream));
+  return 0;
+}
+
+extern "C" int hakmc_rmsnorm(float* y, const float* x, const float* w, int n, float eps, void* stream) {
+  if (!y || !x || !w || n <= 0) return HAKMC_EINVAL;
+  CKL(launch_rmsnorm(y, x, w, n, eps, (cudaStream_t)stream));
+  return 0;
+}
+
+extern "C" int hakmc_attention(float* out, const float* q, const float* kc, const float* vc, int pos, int n_heads,
+                               int n_kv, int head_dim, void* stream) {
+  if (!out || !q || !kc || !vc || pos < 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > 8 ||
+      (head_dim != 64 && head_dim != 128) || n_kv > 64) {
+    set_err("attention: unsupported arguments");
+    return HAKMC_EINVAL;
+  }
+  const int n_split = pos / ATTN_CHUNK + 1;
+  DevScratch* s;
+  int r = scratch(&s, attention_scratch_floats(n_kv, n_split, n_heads / n_kv, head_dim), 0);
+  if (r) return r;
+  cudaStream_t st = (cudaStream_t)stream;
+  CKL(cudaMemcpyAsync(s->pos, &pos, 4, cudaMemcpyHostToDevice, st));
+  AttnParams a = {};
+  a.q = q; a.k_cache = kc; a.v_cache = vc; a.out = out; a.pos_dev = s->pos;
+  a.n_heads = n_heads; a.n_kv = n_kv; a.head_dim = head_dim; a.scale = 1.0f / sqrtf((float)head_dim);
+  a.n_split = n_split; a.part = s->part; a.counters = s->counters;
+  CKL(launch_attention(a, st, false));
+  CKL(cudaStreamSynchronize(st));
+  return 0;
+}
+
+extern "C" int hakmc_rope_neox(float* x, int n_heads, int head_dim, int pos, float theta, void* stream) {
+  if (!x || n_heads <= 0 || head_dim <= 0 || head_dim % 2 || pos < 0) return HAKMC_EINVAL;
+  const int half = head_dim / 2;
+  DevScratch* s;
+  int r = scratch(&s, 0, (size_t)half * 2);
+  if (r) return r;
+  std::vector<float> cs((size_t)half * 2);
+  for (int i = 0; i < half; i++) {
+    const float freq = powf(theta, -((float)(2 * i) / (float)head_dim));
+    const float ang = (float)pos * freq;
+    cs[2 * i] = cosf(ang);
+    cs[2 * i + 1] = sinf(ang);
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  CKL(cudaMemcpyAsync(s->rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, st));
+  CKL(launch_rope(x, s->rope, nullptr, n_heads, head_dim, st));
+  CKL(cudaStreamSynchronize(st));
+  return 0;
+}

@@ -1,0 +1,170 @@
+/*
+ * hakm_cuda.h — C ABI of libhakm_cuda, the B200 (sm_100a) decode path for the
+ * hako engine (mithraeums/hako).
+ *
+ * Plain pointers, sizes and ints only. Every entry point names the reference
+ * interface it replaces (path:line inside mithraeums/hako). Errors follow the
+ * reference's convention of a negative return (or NULL) plus a message; the
+ * message is available from hakmc_last_error() instead of stderr.
+ *
+ * Device pointers are marked [dev]; host pointers [host]. `stream` is a
+ * cudaStream_t passed as void* (NULL = the legacy default stream).
+ */
+#pragma once
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HAKMC_OK          0
+#define HAKMC_EINVAL    (-22)   /* bad argument / shape                     */
+#define HAKMC_ENOMEM    (-12)   /* device allocation failed                 */
+#define HAKMC_EFORMAT   (-74)   /* malformed MLF2 image / missing tensor    */
+#define HAKMC_ECUDA     (-5)    /* CUDA runtime or kernel launch error      */
+#define HAKMC_ERANGE    (-34)   /* position beyond the KV-cache capacity    */
+#define HAKMC_ETIMEOUT  (-62)   /* a bounded device-side wait gave up       */
+#define HAKMC_ENCCL     (-71)   /* NCCL error                               */
+
+typedef struct hakmc_ctx hakmc_ctx;
+
+/* Last error message of the calling thread ("" if none). */
+const char *hakmc_last_error(void);
+/* ABI version: 100*major + minor. */
+int hakmc_version(void);
+
+/* ==================================================================
+ * Model context — replaces the decode engine of src/model.h:29-37.
+ * ================================================================== */
+
+/* Build a device context from an MLF2 image already in host memory (for
+ * example the read-only mmap that mlf2_open makes: hakm_model.map and
+ * .map_size, src/loader.h:6-13). Replaces hakm_ctx_new (src/model.c:17-76):
+ * binds the same tensors by name, uploads them once to `device`, and sizes
+ * the KV cache for max_seq positions of max_batch sequences.
+ * Returns NULL on failure (see hakmc_last_error). */
+hakmc_ctx *hakmc_create(const void *mlf2_image, size_t image_size,
+                        int max_seq, int max_batch, int device);
+/* Replaces hakm_ctx_free (src/model.c:78-86). */
+void hakmc_destroy(hakmc_ctx *c);
+/* Replaces hakm_reset (src/model.c:88): every sequence back to position 0. */
+void hakmc_reset(hakmc_ctx *c);
+int  hakmc_pos(const hakmc_ctx *c);          /* hakm_ctx.pos (model.h:20)     */
+int  hakmc_set_pos(hakmc_ctx *c, int pos);   /* rewind within filled cache    */
+int  hakmc_vocab(const hakmc_ctx *c);        /* hakm_ctx.vocab (model.h:17)   */
+int  hakmc_dim(const hakmc_ctx *c);          /* hakm_ctx.d_model              */
+int  hakmc_n_layers(const hakmc_ctx *c);
+
+/* One decode step at the current position. Replaces hakm_forward
+ * (src/model.c:93-165). [host] logits (vocab floats, may be NULL) receives
+ * the logits the reference returns; [host] argmax (may be NULL) receives the
+ * greedy token of sample_token at temperature 0 (src/sample.c:28-32: first
+ * maximum wins). Advances the position by one. 0 or a negative code. */
+int hakmc_forward(hakmc_ctx *c, int token, float *logits, int *argmax);
+
+/* Greedy decode loop of the CLI and the embed API (cli/main.c:56-75,
+ * src/hakm_api.c:148-166) kept on the device: feeds n_prompt [host] ids one
+ * position at a time (as hakm_forward does), then emits n_gen greedy ids
+ * into [host] out_tokens. No host round trip between tokens. */
+int hakmc_generate(hakmc_ctx *c, const int *prompt, int n_prompt, int n_gen,
+                   int *out_tokens);
+
+/* Batched decode: one step for n_seq independent sequences (n_seq <=
+ * max_batch), sequence i at position pos[i] with input tokens[i] ([host]).
+ * The reference decodes one sequence at a time; each row of this call equals
+ * hakm_forward on a context holding that sequence's cache. argmax [host] gets
+ * n_seq ids; logits [host] (may be NULL) n_seq*vocab floats. */
+int hakmc_forward_batch(hakmc_ctx *c, const int *tokens, const int *pos,
+                        int n_seq, float *logits, int *argmax);
+
+/* Test hooks. Run only the first n layers of each forward (the residual
+ * stream is then what the reference holds in hakm_ctx.xb after that many
+ * layers, src/model.c:102-157); n < 0 restores all layers. */
+int hakmc_set_layers(hakmc_ctx *c, int n_layers);
+/* Copy the residual stream of sequence `seq` after the last forward into
+ * [host] out (d_model floats). */
+int hakmc_hidden(hakmc_ctx *c, int seq, float *out);
+/* Fill the KV cache of sequence `seq` for positions [0, n_pos) of every
+ * layer from [host] k and v ([n_layers][n_pos][n_kv_heads*head_dim] fp32),
+ * and set that sequence's position to n_pos. Mirrors pre-filling
+ * hakm_ctx.k_cache / v_cache / pos (src/model.h:20-21). */
+int hakmc_fill_kv(hakmc_ctx *c, int seq, const float *k, const float *v, int n_pos);
+
+/* Time of the last hakmc_forward / hakmc_generate / hakmc_forward_batch
+ * call's device work in milliseconds (CUDA events on the context stream). */
+float hakmc_last_device_ms(const hakmc_ctx *c);
+
+/* ==================================================================
+ * Kernel-level entry points (device buffers). For unit parity tests and
+ * callers that keep their own weights. Return 0 or a negative code; they
+ * launch on `stream` and do not synchronize.
+ * ================================================================== */
+
+/* Replaces quantize_row_q8_32 (src/quant.c:127-144), bit-exact with the
+ * reference as built (-ffast-math: xs = amax * fl(1/127)). [dev] x[n] fp32 ->
+ * xq[n] int8, xs[n/32] fp32. n % 32 == 0. */
+int hakmc_quantize_q8_32(const float *x, int n, int8_t *xq, float *xs, void *stream);
+
+/* Q4_K matmul with int8 activations: out[r] = q4k_vec_dot(w row r, xq, xs)
+ * (+ bias[r]) for r < n_out. Replaces the Q4_K branch of matmul / mm_worker
+ * (src/nn.c:76-82, src/quant.c:150-232). [dev] w: n_out rows of n_in/256
+ * verbatim 144-byte block_q4_K (src/quant.h:12-17). bias may be NULL.
+ * n_in % 256 == 0. */
+int hakmc_gemv_q4k_q8(float *out, const void *w, const int8_t *xq, const float *xs,
+                      const float *bias, int n_out, int n_in, void *stream);
+
+/* The whole Q4_K matmul of src/nn.c:179-210: quantizes the fp32 [dev] x once
+ * (quantize_row_q8_32), then the int8 row dots. Same layout rules. */
+int hakmc_gemv_q4k(float *out, const void *w, const float *x, const float *bias,
+                   int n_out, int n_in, void *stream);
+
+/* Exact per-32 sub-block integer sums of q4k_vec_dot (src/quant.c:163-267):
+ * iqx[r*(n_in/32)+j] = sum(q*xq), ix[..] = sum(xq) for row r, sub-block j. */
+int hakmc_q4k_subsums(int32_t *iqx, int32_t *ix, const void *w, const int8_t *xq,
+                      int n_out, int n_in, void *stream);
+
+/* Re-lay n_rows rows of verbatim 210-byte block_q6_K (src/quant.h:19-24)
+ * into this library's device layout (same byte count): per row the
+ * 208-byte {ql, qh, scales} parts of each block, then one plane of fp16 d.
+ * [dev] src and dst must not overlap. */
+int hakmc_q6k_pack(void *dst, const void *src, int n_rows, int n_in, void *stream);
+size_t hakmc_q6k_packed_bytes(int n_rows, int n_in);
+
+/* Q6_K matmul with fp32 activations (the generic dequant-and-dot path the
+ * reference takes for Q6_K, src/nn.c:84-95, src/quant.c:94-123). [dev] w in
+ * the packed layout of hakmc_q6k_pack. bias may be NULL. */
+int hakmc_gemv_q6k(float *out, const void *w_packed, const float *x, const float *bias,
+                   int n_out, int n_in, void *stream);
+
+/* lm_head + greedy pick fused: logits (may be NULL) = W . rmsnorm(x) and
+ * argmax[0] = first index of the maximum (src/model.c:160-161 then
+ * src/sample.c:28-32). [dev] norm_w may be NULL for no norm. */
+int hakmc_lmhead_argmax(float *logits, int *argmax, const void *w_packed,
+                        const float *x, const float *norm_w, float eps,
+                        int n_vocab, int n_in, void *stream);
+
+/* Dequantize n_rows rows (verbatim Q4_K or Q6_K blocks, `type` 12 or 14 as
+ * in include/mlf2.h:44-49) to fp32 (src/quant.c:68-123, 234-248). */
+int hakmc_dequant(float *out, const void *w, int type, int n_rows, int n_in, void *stream);
+
+/* y = x / rms(x) * w (src/nn.c:13-18), one vector of n. */
+int hakmc_rmsnorm(float *y, const float *x, const float *w, int n, float eps, void *stream);
+
+/* GQA decode attention for one layer and one sequence over an fp32 cache in
+ * the reference layout [max_seq][n_kv*hd] (src/model.c:124-142, softmax
+ * src/nn.c:20-27): out[h] = softmax(q_h . K[0..pos] / sqrt(hd)) V[0..pos]
+ * for h < n_heads, kv head h / (n_heads/n_kv). [dev] all buffers.
+ * Split over positions in chunks of 256 with an in-kernel combine, using a
+ * scratch area the library allocates once per device. */
+int hakmc_attention(float *out, const float *q, const float *k_cache, const float *v_cache,
+                    int pos, int n_heads, int n_kv, int head_dim, void *stream);
+
+/* NeoX RoPE in place on n_heads heads of head_dim at position pos
+ * (src/nn.c:32-42), angles from a table built on the host with the
+ * reference's formula. */
+int hakmc_rope_neox(float *x, int n_heads, int head_dim, int pos, float theta, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
