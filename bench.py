@@ -1,0 +1,298 @@
+#!/usr/bin/env python3
+"""bench.py — batch-1 greedy decode throughput of the hako decode path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--model 3b|7b]
+
+Workload (config 0 of the benchmark spec): random-init Qwen2 3B-shaped model
+in MLF2 (Q4_K + Q6_K, seed 0), 16 seeded prompt ids, then greedy decode. One
+step = one decoded token at batch 1. The prompt and W warm-up tokens run
+untimed; exactly K decode steps are timed with CUDA events, bracketed by a
+barrier and a device synchronize. Weights (2.03 GB) exceed the 126 MB L2, so
+every step streams them from HBM.
+
+- value: K / device time of the device-resident decode loop (hakmc_decode).
+- e2e: the same K steps through the reference-facing per-token call
+  (hakmc_forward: host token in, host argmax out, synchronous), wall clock.
+- roofline: the FFN gate/up GEMV phase (the largest launch of the step),
+  timed live with CUDA events on the context stream over launches rotating
+  through the layers.
+- cpu_baseline: the reference engine's own compiled decode (oracle/_ref) on
+  this host's cores, on a bounded sample of the same workload.
+
+N > 1 (torchrun): one independent replica per GPU (no collective on this
+path yet); value = all ranks' tokens / the slowest rank's time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PROMPT_LEN = 16
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d, "measured"
+    except OSError:
+        return PEAKS_FALLBACK, "fallback"
+
+
+def prompt_ids(model: str):
+    if model == "7b":
+        return np.random.default_rng(3).integers(0, 151643, 32).tolist()
+    return np.random.default_rng(0).integers(0, 151643, PROMPT_LEN).tolist()
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100", "-i", str(self.idx)],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.out = ""
+        if self.p:
+            self.p.terminate()
+            try:
+                self.out, _ = self.p.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+                self.out = ""
+
+    def summary(self):
+        rows = [r.split(",") for r in self.out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows]
+        mx = float(rows[0][2])
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
+        loaded = [s for s in sm if s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300))
+        pg = dist
+    return world, rank, local, pg
+
+
+def reduce_max(pg, v: float, device):
+    if pg is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(pg, device):
+    import torch
+    torch.cuda.synchronize(device)
+    if pg is not None:
+        pg.barrier()
+        torch.cuda.synchronize(device)
+
+
+def cpu_reference_decode(path: str, model: str, n_decode: int, max_seq: int):
+    """The reference's own hakm_forward (oracle/_ref) on all host cores:
+    prompt untimed, then n_decode timed greedy steps. Returns tok/s, cores."""
+    cores = min(os.cpu_count() or 1, 16)  # the reference pool caps at 16 (src/nn.c:61)
+    os.environ["HAKM_THREADS"] = str(cores)
+    from oracle.oracle import RefModel
+    m = RefModel(path, max_seq)
+    am = 0
+    for t in prompt_ids(model):
+        _, am = m.forward(t, want_logits=False)
+    t0 = time.perf_counter()
+    for _ in range(n_decode):
+        _, am = m.forward(am, want_logits=False)
+    dt = time.perf_counter() - t0
+    m.close()
+    return n_decode / dt, cores
+
+
+def run_reference_arm(args):
+    world, rank, local, pg = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0, None
+    if rank != 0:
+        return 0
+    from hako_b200 import synth
+    cfg = synth.PRESETS[args.model]
+    path = synth.cached_model(cfg)
+    max_seq = len(prompt_ids(args.model)) + args.warmup + args.steps + 8
+    cores = min(os.cpu_count() or 1, 16)
+    os.environ["HAKM_THREADS"] = str(cores)
+    from oracle.oracle import RefModel
+    m = RefModel(path, max_seq)
+    am = 0
+    for t in prompt_ids(args.model):
+        _, am = m.forward(t, want_logits=False)
+    for _ in range(args.warmup):
+        _, am = m.forward(am, want_logits=False)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _, am = m.forward(am, want_logits=False)
+    dt = time.perf_counter() - t0
+    m.close()
+    v = args.steps / dt
+    line = {"impl": "reference", "metric": "decode tok/s (batch 1)", "value": v, "unit": "tok/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8/fp32",
+            "data": "synthetic (seeded random-init weights, seeded prompt ids)",
+            "config": config_block(args, world),
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
+                             "sample": f"{args.steps} greedy decode steps after a {len(prompt_ids(args.model))}-id prompt"},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_block(args, world):
+    from hako_b200 import synth
+    cfg = synth.PRESETS[args.model]
+    return {"workload": f"config {'0' if args.model == '3b' else '3'}: Qwen2 {args.model.upper()}-shaped "
+                        f"Q4_K_M greedy decode, batch 1",
+            "model": f"qwen2-{args.model}-synthetic", "layers": cfg.n_layers, "d_model": cfg.d_model,
+            "heads": f"{cfg.n_heads}/{cfg.n_kv_heads}", "ffn": cfg.ffn_dim, "vocab": cfg.vocab,
+            "prompt_len": len(prompt_ids(args.model)), "global_batch": world, "seq_len": None,
+            "parallelism": "replicas" if world > 1 else "single",
+            "l2": "weights stream from HBM every step (2.03 GB > 126 MB L2)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="3b", choices=["3b", "7b"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference_arm(args)
+
+    import torch
+    world, rank, local, pg = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    from hako_b200 import HakmCtx, lib, synth
+    cfg = synth.PRESETS[args.model]
+    path = synth.cached_model(cfg)
+    prompt = prompt_ids(args.model)
+    max_seq = len(prompt) + 2 * (args.warmup + args.steps) + 16
+    ctx = HakmCtx(path, max_seq=max_seq, device=local)
+
+    # prompt + warm-up (untimed)
+    for t in prompt:
+        ctx.forward(t, want_logits=False)
+    toks = np.zeros(args.warmup, np.int32)
+    import ctypes as C
+    lib.hakmc_decode(ctx._h, args.warmup, C.c_void_p(toks.ctypes.data))
+
+    # timed: K device-resident decode steps
+    pos0 = ctx.pos
+    barrier(pg, device)
+    with ClockSampler(local) as clk:
+        barrier(pg, device)
+        t0 = time.perf_counter()
+        out = np.zeros(args.steps, np.int32)
+        rc = lib.hakmc_decode(ctx._h, args.steps, C.c_void_p(out.ctypes.data))
+        barrier(pg, device)
+        wall = time.perf_counter() - t0
+    if rc != 0:
+        raise RuntimeError(f"hakmc_decode failed: {rc}")
+    dev_ms = float(ctx.last_device_ms)
+    max_ms = reduce_max(pg, dev_ms, device)
+    value = world * args.steps / (max_ms / 1e3)
+
+    # e2e: the same number of steps through the per-token host call
+    ctx.set_pos(pos0)
+    am = int(out[0])
+    barrier(pg, device)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _, am = ctx.forward(am, want_logits=False)
+    e2e_s = reduce_max(pg, time.perf_counter() - t0, device)
+    e2e = world * args.steps / e2e_s
+
+    # roofline: FFN gate/up phase (largest launch), live CUDA-event timing
+    pk, pk_kind = peaks()
+    ffn_ms = C.c_float(0)
+    lib.hakmc_time_phase(ctx._h, 3, 4 * cfg.n_layers, C.byref(ffn_ms))
+    ffn_bytes = 2 * cfg.ffn_dim * (cfg.d_model // 256) * 144 + cfg.d_model * 8 + cfg.ffn_dim * 4
+    achieved = ffn_bytes / (ffn_ms.value / 1e3) / 1e9
+    # token-level: all weights + KV read per step
+    pos_mid = pos0 + args.steps // 2
+    tok_bytes = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(pos_mid)
+    tok_gbs = tok_bytes * (args.steps / (dev_ms / 1e3)) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get(f"ffn_gate_up_{args.model}")
+
+    line = {"metric": "decode tok/s (batch 1)", "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int8 x int4/int6 dot, fp32 accumulate", "data": "synthetic (seeded random-init weights, seeded prompt ids)",
+            "config": config_block(args, world),
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+            "gpu_launches": (2 + 5 * cfg.n_layers) * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "phase_kernel (ffn gate/up, Q4_K)", "achieved": achieved,
+                         "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                         "peak_source": pk_kind, "traffic": traffic, "bytes_per_launch": ffn_bytes,
+                         "launch_ms": ffn_ms.value},
+            "token_roofline": {"bytes_per_token": tok_bytes, "achieved": tok_gbs, "peak": pk["hbm_gbs"],
+                               "unit": "GB/s", "frac": tok_gbs / pk["hbm_gbs"],
+                               "roofline_tok_s": pk["hbm_gbs"] * 1e9 / tok_bytes},
+            "clocks": clk.summary(), "wall_s": wall}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores = cpu_reference_decode(path, args.model, 6, max_seq)
+        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
+                                "sample": f"6 greedy decode steps after the {len(prompt)}-id prompt "
+                                          "(reference hakm_forward, oracle/_ref)"}
+    ctx.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

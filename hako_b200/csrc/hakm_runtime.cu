@@ -278,18 +278,18 @@ static cudaError_t run_phase(hakmc_ctx* c, PhaseParams& p) {
   return launch_phase(p, phase_grid(p, c->num_sms), c->stream, c->pdl);
 }
 
-// Enqueue one decode step for sequence 0 on c->stream.
-static cudaError_t enqueue_step(hakmc_ctx* c, int n_split) {
-  cudaError_t e = launch_embed_q6k(c->xb, c->tok_embd.w, c->tok_embd.wd, c->token_dev, c->D, nullptr,
-                                   c->stream, c->pdl);
-  if (e != cudaSuccess) return e;
+enum { PH_QKV = 0, PH_ATTN = 1, PH_WO = 2, PH_FFN = 3, PH_DOWN = 4, PH_LMHEAD = 5 };
+
+// Enqueue one phase of layer l (l ignored for PH_LMHEAD). `timing` strips the
+// step-finalisation side effects so a phase can be relaunched on its own.
+static cudaError_t enqueue_phase(hakmc_ctx* c, int l, int ph, int n_split, bool timing) {
   const size_t lstride = (size_t)c->max_seq * c->KV;
-  for (int l = 0; l < c->run_layers; l++) {
-    DevLayer& y = c->layers[l];
-    float* kc = c->k_cache + (size_t)l * lstride;
-    float* vc = c->v_cache + (size_t)l * lstride;
-    {  // qkv
-      PhaseParams p = {};
+  DevLayer& y = c->layers[l < c->L ? l : 0];
+  float* kc = c->k_cache + (size_t)l * lstride;
+  float* vc = c->v_cache + (size_t)l * lstride;
+  PhaseParams p = {};
+  switch (ph) {
+    case PH_QKV:
       p.n_in = c->D; p.act = ACT_RMS; p.x = c->xb; p.norm_w = y.attn_norm; p.eps = c->eps;
       p.n_seg = 2;
       p.seg[0] = make_seg(y.wqk, EPI_ROPE_QK, c->q);
@@ -297,49 +297,53 @@ static cudaError_t enqueue_step(hakmc_ctx* c, int n_split) {
       p.seg[1] = make_seg(y.wv, EPI_V_CACHE, c->v);
       p.seg[1].cache = vc; p.seg[1].bias = y.bv;
       p.rope_cs = c->rope_cs; p.pos_dev = c->pos_dev; p.head_dim = c->hd; p.kv_dim = c->KV;
-      if ((e = run_phase(c, p)) != cudaSuccess) return e;
-    }
-    {  // attention
+      return run_phase(c, p);
+    case PH_ATTN: {
       AttnParams a = {};
       a.q = c->q; a.k_cache = kc; a.v_cache = vc; a.out = c->att; a.pos_dev = c->pos_dev;
       a.n_heads = c->H; a.n_kv = c->KVH; a.head_dim = c->hd; a.scale = 1.0f / sqrtf((float)c->hd);
       a.n_split = n_split; a.part = c->attn_part; a.counters = c->attn_counters;
-      if ((e = launch_attention(a, c->stream, c->pdl)) != cudaSuccess) return e;
+      return launch_attention(a, c->stream, c->pdl);
     }
-    {  // wo + residual
-      PhaseParams p = {};
+    case PH_WO:
       p.n_in = c->D; p.act = ACT_F32; p.x = c->att;
       p.n_seg = 1;
       p.seg[0] = make_seg(y.wo, EPI_RESID, c->xb);
-      if ((e = run_phase(c, p)) != cudaSuccess) return e;
-    }
-    {  // gate/up + SwiGLU
-      PhaseParams p = {};
+      return run_phase(c, p);
+    case PH_FFN:
       p.n_in = c->D; p.act = ACT_RMS; p.x = c->xb; p.norm_w = y.ffn_norm; p.eps = c->eps;
       p.n_seg = 1;
       p.seg[0] = make_seg(y.wgu, EPI_SWIGLU, c->hbuf);
-      if ((e = run_phase(c, p)) != cudaSuccess) return e;
-    }
-    {  // down + residual
-      PhaseParams p = {};
+      return run_phase(c, p);
+    case PH_DOWN:
       p.n_in = c->F; p.act = ACT_F32; p.x = c->hbuf;
       p.n_seg = 1;
       p.seg[0] = make_seg(y.down, EPI_RESID, c->xb);
-      if ((e = run_phase(c, p)) != cudaSuccess) return e;
-    }
+      return run_phase(c, p);
+    default:  // final norm + lm_head + argmax + step finalisation
+      p.n_in = c->D; p.act = ACT_RMS; p.x = c->xb; p.norm_w = c->out_norm; p.eps = c->eps;
+      p.n_seg = 1;
+      p.seg[0] = make_seg(c->lm_head, EPI_ARGMAX, c->logits);
+      p.argmax_key = c->argmax_key;
+      if (!timing) {
+        p.done_counter = c->done_counter;
+        p.next_token = c->token_dev; p.token_log = c->token_log; p.step_dev = c->step_dev;
+        p.token_log_cap = c->token_log_cap;
+        p.pos_inc = c->pos_dev;
+      }
+      return run_phase(c, p);
   }
-  {  // final norm + lm_head + argmax + finalise
-    PhaseParams p = {};
-    p.n_in = c->D; p.act = ACT_RMS; p.x = c->xb; p.norm_w = c->out_norm; p.eps = c->eps;
-    p.n_seg = 1;
-    p.seg[0] = make_seg(c->lm_head, EPI_ARGMAX, c->logits);
-    p.argmax_key = c->argmax_key; p.done_counter = c->done_counter;
-    p.next_token = c->token_dev; p.token_log = c->token_log; p.step_dev = c->step_dev;
-    p.token_log_cap = c->token_log_cap;
-    p.pos_inc = c->pos_dev;
-    if ((e = run_phase(c, p)) != cudaSuccess) return e;
-  }
-  return cudaSuccess;
+}
+
+// Enqueue one decode step for sequence 0 on c->stream.
+static cudaError_t enqueue_step(hakmc_ctx* c, int n_split) {
+  cudaError_t e = launch_embed_q6k(c->xb, c->tok_embd.w, c->tok_embd.wd, c->token_dev, c->D, nullptr,
+                                   c->stream, c->pdl);
+  if (e != cudaSuccess) return e;
+  for (int l = 0; l < c->run_layers; l++)
+    for (int ph = PH_QKV; ph <= PH_DOWN; ph++)
+      if ((e = enqueue_phase(c, l, ph, n_split, false)) != cudaSuccess) return e;
+  return enqueue_phase(c, 0, PH_LMHEAD, n_split, false);
 }
 
 static int n_split_for(const hakmc_ctx* c, int pos) { return pos / ATTN_CHUNK + 1; }
@@ -648,6 +652,43 @@ extern "C" int hakmc_generate(hakmc_ctx* c, const int* prompt, int n_prompt, int
     CK(cudaMemcpyAsync(out, c->token_log + (n_prompt - 1), (size_t)n_gen * 4, cudaMemcpyDeviceToHost, c->stream));
   CK(cudaStreamSynchronize(c->stream));
   CK(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
+  return 0;
+}
+
+extern "C" int hakmc_decode(hakmc_ctx* c, int n_steps, int* out) {
+  if (!c || n_steps < 0) return HAKMC_EINVAL;
+  if (c->pos + n_steps > c->max_seq) { set_err("sequence exceeds max_seq"); return HAKMC_ERANGE; }
+  if (n_steps > c->token_log_cap) { set_err("token log too small"); return HAKMC_ERANGE; }
+  CK(cudaSetDevice(c->device));
+  // token_log[i] records the argmax of step i, i.e. the input of step i+1; the
+  // first input is the argmax already waiting in token_dev
+  CK(cudaMemsetAsync(c->step_dev, 0, 4, c->stream));
+  if (out && n_steps > 0) CK(cudaMemcpyAsync(out, c->token_dev, 4, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaEventRecord(c->ev0, c->stream));
+  for (int i = 0; i < n_steps; i++) {
+    int r = launch_one(c);
+    if (r) return r;
+  }
+  CK(cudaEventRecord(c->ev1, c->stream));
+  if (out && n_steps > 1)
+    CK(cudaMemcpyAsync(out + 1, c->token_log, (size_t)(n_steps - 1) * 4, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  CK(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
+  return 0;
+}
+
+extern "C" int hakmc_time_phase(hakmc_ctx* c, int phase, int iters, float* avg_ms) {
+  if (!c || phase < 0 || phase > PH_LMHEAD || iters <= 0 || !avg_ms) return HAKMC_EINVAL;
+  CK(cudaSetDevice(c->device));
+  const int ns = n_split_for(c, c->pos < c->max_seq ? c->pos : c->max_seq - 1);
+  for (int i = 0; i < 3; i++) CK(enqueue_phase(c, i % c->L, phase, ns, true));  // warm-up
+  CK(cudaEventRecord(c->ev0, c->stream));
+  for (int i = 0; i < iters; i++) CK(enqueue_phase(c, i % c->L, phase, ns, true));
+  CK(cudaEventRecord(c->ev1, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  float ms = 0.f;
+  CK(cudaEventElapsedTime(&ms, c->ev0, c->ev1));
+  *avg_ms = ms / iters;
   return 0;
 }
 

@@ -70,6 +70,13 @@ int hakmc_forward(hakmc_ctx *c, int token, float *logits, int *argmax);
 int hakmc_generate(hakmc_ctx *c, const int *prompt, int n_prompt, int n_gen,
                    int *out_tokens);
 
+/* Continue the greedy stream of the current sequence for n_steps positions
+ * without returning to the host between steps (the decode half of
+ * cli/main.c:63-75): each step's input is the previous step's argmax. The
+ * first input is the argmax of the last hakmc_forward / hakmc_generate step.
+ * [host] out_tokens (may be NULL) receives the n_steps inputs consumed. */
+int hakmc_decode(hakmc_ctx *c, int n_steps, int *out_tokens);
+
 /* Batched decode: one step for n_seq independent sequences (n_seq <=
  * max_batch), sequence i at position pos[i] with input tokens[i] ([host]).
  * The reference decodes one sequence at a time; each row of this call equals
@@ -90,6 +97,13 @@ int hakmc_hidden(hakmc_ctx *c, int seq, float *out);
  * and set that sequence's position to n_pos. Mirrors pre-filling
  * hakm_ctx.k_cache / v_cache / pos (src/model.h:20-21). */
 int hakmc_fill_kv(hakmc_ctx *c, int seq, const float *k, const float *v, int n_pos);
+
+/* Average device time in ms of one launch of decode-step phase `phase`
+ * (0 qkv, 1 attention, 2 attn-output, 3 ffn gate/up, 4 ffn down, 5 lm_head),
+ * over `iters` launches rotating through the layers so each launch streams
+ * its weights from HBM, timed with CUDA events on the context stream.
+ * No counterpart in the reference (measurement hook). */
+int hakmc_time_phase(hakmc_ctx *c, int phase, int iters, float *avg_ms);
 
 /* Time of the last hakmc_forward / hakmc_generate / hakmc_forward_batch
  * call's device work in milliseconds (CUDA events on the context stream). */

@@ -166,6 +166,8 @@ class Reference:
             "refd_forward": (_i, [_vp, _i, _vp, _vp]),
             "refd_greedy": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
             "refd_matmul_raw": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
+            "refd_read_kv": (_i, [_vp, _vp, _vp, _i]),
+            "refd_set_pos": (None, [_vp, _i]),
             "quantize_row_q8_32": (None, [_vp, _i, _vp, _vp]),
             "q4k_vec_dot": (_f, [_vp, _i, _vp, _vp]),
             "dequant_q4_K": (None, [_vp, _vp, _i]),
@@ -247,6 +249,15 @@ class RefModel:
 
     def hidden(self):
         return np.ctypeslib.as_array(self.r.L.refd_hidden(self.h), (self.dim,)).copy()
+
+    def read_kv(self, n_layers: int, kv_dim: int, n_pos: int):
+        k = np.empty((n_layers, n_pos, kv_dim), np.float32)
+        v = np.empty_like(k)
+        assert self.r.L.refd_read_kv(self.h, _p(k), _p(v), n_pos) == 0
+        return k, v
+
+    def set_pos(self, pos: int):
+        self.r.L.refd_set_pos(self.h, pos)
 
     def set_layers(self, n):
         self.r.L.refd_set_layers(self.h, n)

@@ -90,3 +90,21 @@ int refd_matmul_raw(float *out, const float *x, int type, const void *w,
 	matmul(out, x, &m, &t, bias, n_out, n_in);
 	return 0;
 }
+
+/* Copy the KV cache of the first n_pos positions of every layer out of
+ * hakm_ctx.k_cache / v_cache ([layer][max_seq][kv_dim], src/model.c:72-73)
+ * into k / v laid out [layer][n_pos][kv_dim]. */
+int refd_read_kv(void *cv, float *k, float *v, int n_pos) {
+	hakm_ctx *c = (hakm_ctx *)cv;
+	if (n_pos > c->max_seq) return -1;
+	size_t row = (size_t)c->kv_dim * n_pos;
+	for (int l = 0; l < c->n_layers; l++) {
+		memcpy(k + (size_t)l * row, c->k_cache + (size_t)l * c->max_seq * c->kv_dim, row * sizeof(float));
+		memcpy(v + (size_t)l * row, c->v_cache + (size_t)l * c->max_seq * c->kv_dim, row * sizeof(float));
+	}
+	return 0;
+}
+
+/* Set the decode position (hakm_ctx.pos, src/model.h:20) over a cache the
+ * caller filled. */
+void refd_set_pos(void *cv, int pos) { ((hakm_ctx *)cv)->pos = pos; }

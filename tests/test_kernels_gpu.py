@@ -1,0 +1,254 @@
+"""Kernel-level parity through the C ABI on the GPU.
+
+Bars: bit-exact for the int8 activation quantizer, the Q4_K integer sub-block
+sums, dequantization and the embedding row; rel-L2 <= 1e-5 for fp32 matmul
+outputs given identical inputs (the quantizer is then bit-exact, so only the
+fp32 summation order differs); the greedy pick must return the first index of
+the maximum."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from conftest import golden_npz, rel_l2
+from hako_b200 import check, lib, synth
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+
+
+def P(t):
+    return C.c_void_p(t.data_ptr())
+
+
+_KEEP = []
+
+
+@pytest.fixture(autouse=True)
+def _keep_alive():
+    """Device copies made inline (P(dev(...))) must outlive the launch: the
+    caching allocator would otherwise hand their memory to the next copy."""
+    yield
+    sync()
+    _KEEP.clear()
+
+
+def dev(a, cuda):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    _KEEP.append(t)
+    return t
+
+
+def sync():
+    import torch
+    torch.cuda.synchronize()
+
+
+def empty(shape, dtype, cuda):
+    import torch
+    return torch.empty(shape, dtype=dtype, device=cuda)
+
+
+def test_quantize_golden_bit_exact(cuda):
+    import torch
+    g = golden_npz("q8.npz")
+    for i in range(len([k for k in g.files if k.startswith("xq")])):
+        x = g[f"x{i}"]
+        xq = empty(x.size, torch.int8, cuda)
+        xs = empty(x.size // 32, torch.float32, cuda)
+        check(lib.hakmc_quantize_q8_32(P(dev(x, cuda)), x.size, P(xq), P(xs), None))
+        sync()
+        assert np.array_equal(xq.cpu().numpy(), g[f"xq{i}"]), i
+        assert np.array_equal(xs.cpu().numpy().view(np.uint32), g[f"xs{i}"].view(np.uint32)), i
+
+
+def test_quantize_random_bit_exact(cuda, reference):
+    import torch
+    rng = np.random.default_rng(5)
+    for n in (32, 2048, 11008, 18944):
+        x = (rng.standard_normal(n) * rng.uniform(1e-4, 1e3)).astype(np.float32)
+        xq = empty(n, torch.int8, cuda)
+        xs = empty(n // 32, torch.float32, cuda)
+        check(lib.hakmc_quantize_q8_32(P(dev(x, cuda)), n, P(xq), P(xs), None))
+        sync()
+        rq, rs = reference.quantize_q8_32(x)
+        assert np.array_equal(xq.cpu().numpy(), rq) and np.array_equal(xs.cpu().numpy(), rs)
+
+
+def test_q4k_integer_sums_pinned(cuda):
+    import torch
+    g = golden_npz("q4k.npz")
+    for t in range(g["pin_blocks"].shape[0]):
+        iqx = empty(8, torch.int32, cuda)
+        ix = empty(8, torch.int32, cuda)
+        check(lib.hakmc_q4k_subsums(P(iqx), P(ix), P(dev(g["pin_blocks"][t], cuda)),
+                                    P(dev(g["pin_xq"][t], cuda)), 1, 256, None))
+        sync()
+        assert np.array_equal(iqx.cpu().numpy(), g["pin_iqx"][t])
+        assert np.array_equal(ix.cpu().numpy(), g["pin_ix"][t])
+
+
+@pytest.mark.parametrize("rows,k", [(256, 2048), (2048, 2048), (11008, 2048), (2048, 11008),
+                                    (3584, 3584), (512, 3584), (18944, 3584), (3584, 18944)])
+def test_q4k_subsums_bit_exact(cuda, oracle, rows, k):
+    import torch
+    w = synth.random_q4k(rows, k, rows + k)
+    x = synth.normal(k, k)
+    xq, xs = oracle.quantize_q8_32(x)
+    sub = min(rows, 64)
+    iqx = empty(sub * k // 32, torch.int32, cuda)
+    ix = torch.empty_like(iqx)
+    check(lib.hakmc_q4k_subsums(P(iqx), P(ix), P(dev(w, cuda)), P(dev(xq, cuda)), sub, k, None))
+    sync()
+    oi, ox = oracle.q4k_subsums(w, sub, k, xq)
+    assert np.array_equal(iqx.cpu().numpy(), oi) and np.array_equal(ix.cpu().numpy(), ox)
+
+
+@pytest.mark.parametrize("rows,k", [(256, 2048), (2048, 2048), (11008, 2048), (2048, 11008),
+                                    (512, 3584), (18944, 3584), (3584, 18944), (4, 256), (3, 512)])
+def test_gemv_q4k_matches_reference(cuda, reference, rows, k):
+    import torch
+    w = synth.random_q4k(rows, k, 3 * rows + k)
+    x = synth.normal(k, k + 1)
+    out = empty(rows, torch.float32, cuda)
+    check(lib.hakmc_gemv_q4k(P(out), P(dev(w, cuda)), P(dev(x, cuda)), None, rows, k, None))
+    sync()
+    assert rel_l2(out.cpu().numpy(), reference.matmul(w, 12, x, rows, k)) < TOL
+    # pre-quantized activation entry point, with bias
+    xq, xs = reference.quantize_q8_32(x)
+    b = synth.normal(rows, 77)
+    check(lib.hakmc_gemv_q4k_q8(P(out), P(dev(w, cuda)), P(dev(xq, cuda)), P(dev(xs, cuda)),
+                                P(dev(b, cuda)), rows, k, None))
+    sync()
+    assert rel_l2(out.cpu().numpy(), reference.matmul(w, 12, x, rows, k, bias=b)) < TOL
+
+
+def test_gemv_q4k_golden_dots(cuda):
+    import torch
+    g = golden_npz("q4k.npz")
+    out = empty(8, torch.float32, cuda)
+    check(lib.hakmc_gemv_q4k_q8(P(out), P(dev(g["w"], cuda)), P(dev(g["xq"], cuda)), P(dev(g["xs"], cuda)),
+                                None, 8, 2048, None))
+    sync()
+    assert rel_l2(out.cpu().numpy(), g["dots"]) < TOL
+
+
+@pytest.mark.parametrize("rows,k", [(256, 2048), (2048, 2048), (2048, 11008), (512, 3584),
+                                    (3584, 18944), (151936, 2048), (5, 256)])
+def test_gemv_q6k_matches_reference(cuda, reference, rows, k):
+    import torch
+    w = synth.random_q6k(rows, k, 5 * rows + k)
+    x = synth.normal(k, k + 2)
+    wd = dev(w, cuda)
+    packed = torch.empty_like(wd)
+    check(lib.hakmc_q6k_pack(P(packed), P(wd), rows, k, None))
+    out = empty(rows, torch.float32, cuda)
+    b = synth.normal(rows, 78)
+    check(lib.hakmc_gemv_q6k(P(out), P(packed), P(dev(x, cuda)), P(dev(b, cuda)), rows, k, None))
+    sync()
+    assert rel_l2(out.cpu().numpy(), reference.matmul(w, 14, x, rows, k, bias=b)) < TOL
+
+
+def test_dequant_bit_exact(cuda):
+    import torch
+    g = golden_npz("dequant.npz")
+    for key, t, ref in (("w4", 12, "d4"), ("w6", 14, "d6")):
+        out = empty(4096, torch.float32, cuda)
+        check(lib.hakmc_dequant(P(out), P(dev(g[key], cuda)), t, 4, 1024, None))
+        sync()
+        assert np.array_equal(out.cpu().numpy(), g[ref])
+
+
+@pytest.mark.parametrize("vocab,k", [(151936, 2048), (152064, 3584), (1000, 256)])
+def test_lmhead_argmax(cuda, reference, vocab, k):
+    import torch
+    w = synth.random_q6k(vocab, k, vocab)
+    x = synth.normal(k, 3)
+    nw = (1 + 0.1 * synth.normal(k, 4)).astype(np.float32)
+    wd = dev(w, cuda)
+    packed = torch.empty_like(wd)
+    check(lib.hakmc_q6k_pack(P(packed), P(wd), vocab, k, None))
+    lg = empty(vocab, torch.float32, cuda)
+    am = torch.zeros(1, dtype=torch.int32, device=cuda)
+    check(lib.hakmc_lmhead_argmax(P(lg), P(am), P(packed), P(dev(x, cuda)), P(dev(nw, cuda)), 1e-6,
+                                  vocab, k, None))
+    sync()
+    ref = reference.matmul(w, 14, reference.rmsnorm(x, nw, 1e-6), vocab, k)
+    assert rel_l2(lg.cpu().numpy(), ref) < TOL
+    assert int(am.item()) == int(np.argmax(lg.cpu().numpy()))
+
+
+def test_lmhead_argmax_ties_pick_first(cuda):
+    """Duplicate rows give equal logits: the lowest index wins, as with the
+    reference's strict '>' scan (src/sample.c:30)."""
+    import torch
+    k, vocab = 256, 4096
+    w = synth.random_q6k(vocab, k, 9)
+    row = w[:210].copy()
+    for r in (17, 1000, 4000):  # three copies of the same row
+        w[r * 210:(r + 1) * 210] = row
+    # make that row the clear maximum: large positive d, positive scales
+    x = np.ones(k, np.float32)
+    for r in (0, 17, 1000, 4000):
+        w[r * 210 + 192:r * 210 + 208] = 31
+        w[r * 210:r * 210 + 192] = 0xFF  # q = 63 -> +31
+        w[r * 210 + 208:r * 210 + 210] = np.frombuffer(np.uint16(0x3C00).tobytes(), np.uint8)
+    wd = dev(w, cuda)
+    packed = torch.empty_like(wd)
+    check(lib.hakmc_q6k_pack(P(packed), P(wd), vocab, k, None))
+    am = torch.zeros(1, dtype=torch.int32, device=cuda)
+    check(lib.hakmc_lmhead_argmax(None, P(am), P(packed), P(dev(x, cuda)), None, 1e-6, vocab, k, None))
+    sync()
+    assert int(am.item()) == 0
+
+
+def test_rmsnorm(cuda):
+    import torch
+    g = golden_npz("ops.npz")
+    y = empty(2048, torch.float32, cuda)
+    check(lib.hakmc_rmsnorm(P(y), P(dev(g["x"], cuda)), P(dev(g["w"], cuda)), 2048, 1e-6, None))
+    sync()
+    assert rel_l2(y.cpu().numpy(), g["rms"]) < 1e-6
+
+
+@pytest.mark.parametrize("pos", [0, 1, 17, 511, 4095])
+def test_rope(cuda, pos):
+    g = golden_npz("ops.npz")
+    q = dev(g["q"], cuda)
+    check(lib.hakmc_rope_neox(P(q), 16, 128, pos, 1e6, None))
+    sync()
+    assert np.abs(q.cpu().numpy() - g[f"rope{pos}"]).max() < 2e-6 + 1e-7 * pos
+
+
+def attention_ref(q, kc, vc, pos, H, KVH, hd):
+    """src/model.c:124-142 in float64."""
+    out = np.zeros(H * hd)
+    KV = KVH * hd
+    for h in range(H):
+        kh = h // (H // KVH)
+        qh = q[h * hd:(h + 1) * hd].astype(np.float64)
+        K = kc[:pos + 1].reshape(pos + 1, KV)[:, kh * hd:(kh + 1) * hd].astype(np.float64)
+        V = vc[:pos + 1].reshape(pos + 1, KV)[:, kh * hd:(kh + 1) * hd].astype(np.float64)
+        s = K @ qh / np.sqrt(hd)
+        p = np.exp(s - s.max())
+        p /= p.sum()
+        out[h * hd:(h + 1) * hd] = p @ V
+    return out
+
+
+@pytest.mark.parametrize("H,KVH,hd,pos", [(16, 2, 128, 0), (16, 2, 128, 63), (16, 2, 128, 255),
+                                          (16, 2, 128, 256), (28, 4, 128, 1000), (28, 4, 128, 4095),
+                                          (4, 2, 64, 300)])
+def test_attention(cuda, H, KVH, hd, pos):
+    import torch
+    rng = np.random.default_rng(pos + H)
+    max_seq = 4096
+    q = rng.standard_normal(H * hd).astype(np.float32)
+    kc = rng.standard_normal((max_seq, KVH * hd)).astype(np.float32)
+    vc = rng.standard_normal((max_seq, KVH * hd)).astype(np.float32)
+    out = empty(H * hd, torch.float32, cuda)
+    check(lib.hakmc_attention(P(out), P(dev(q, cuda)), P(dev(kc, cuda)), P(dev(vc, cuda)), pos, H, KVH, hd, None))
+    sync()
+    assert rel_l2(out.cpu().numpy(), attention_ref(q, kc, vc, pos, H, KVH, hd)) < TOL
