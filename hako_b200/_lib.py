@@ -33,6 +33,7 @@ SIGNATURES = {
     "hakmc_set_layers": (_i, [_vp, _i]),
     "hakmc_hidden": (_i, [_vp, _i, _vp]),
     "hakmc_fill_kv": (_i, [_vp, _i, _vp, _vp, _i]),
+    "hakmc_debug_read": (_i, [_vp, _i, _vp]),
     "hakmc_last_device_ms": (_f, [_vp]),
     "hakmc_quantize_q8_32": (_i, [_vp, _i, _vp, _vp, _vp]),
     "hakmc_gemv_q4k_q8": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp]),

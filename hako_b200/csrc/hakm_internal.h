@@ -10,11 +10,36 @@ namespace hakm {
 constexpr int QK = 256;            // k-quant super-block (src/quant.h:9)
 constexpr int Q4K_BYTES = 144;     // block_q4_K (src/quant.h:12-17)
 constexpr int Q6K_BYTES = 210;     // block_q6_K (src/quant.h:19-24)
-constexpr int Q6K_BODY = 208;      // packed device layout: {ql, qh, scales} per block
-constexpr int ROWS_PER_CHUNK = 4;  // rows a warp reduces together
+constexpr int Q6K_BODY = 208;      // {ql, qh, scales} part of a block_q6_K
 constexpr int MAX_SEGS = 3;
 
 enum WType { W_Q4K = 12, W_Q6K = 14 };
+
+// Device layouts. A row is cut into chunks of 8 super-blocks (2048 columns):
+//  Q4_K: verbatim 144-byte blocks, so a chunk is 1152 contiguous bytes.
+//  Q6_K: a chunk holds the 208-byte bodies of its (up to) 8 blocks, then their
+//        8 fp16 d values: 1680 bytes = 8 * 210, the verbatim byte count; a
+//        short last chunk is padded to 16 bytes. Every chunk starts 16-byte
+//        aligned, so a stage of chunks is one bulk copy per row.
+constexpr int CHUNK_BLOCKS = 8;
+constexpr int Q4K_CHUNK = CHUNK_BLOCKS * Q4K_BYTES;  // 1152
+constexpr int Q6K_CHUNK = CHUNK_BLOCKS * Q6K_BYTES;  // 1680
+
+__host__ __device__ inline int n_chunks(int nb) { return (nb + CHUNK_BLOCKS - 1) / CHUNK_BLOCKS; }
+__host__ __device__ inline int q6_chunk_blocks(int nb, int c) {
+  const int m = nb - CHUNK_BLOCKS * c;
+  return m < CHUNK_BLOCKS ? m : CHUNK_BLOCKS;
+}
+__host__ __device__ inline int chunk_bytes(int type, int nb, int c) {
+  const int m = q6_chunk_blocks(nb, c);
+  return type == W_Q4K ? m * Q4K_BYTES : ((m * Q6K_BYTES + 15) & ~15);
+}
+__host__ __device__ inline size_t dev_row_bytes(int type, int nb) {
+  if (type == W_Q4K) return (size_t)nb * Q4K_BYTES;
+  const int full = nb / CHUNK_BLOCKS, rem = nb % CHUNK_BLOCKS;
+  return (size_t)full * Q6K_CHUNK + (rem ? (size_t)((rem * Q6K_BYTES + 15) & ~15) : 0);
+}
+
 
 // How the GEMV prologue builds the activation it keeps in shared memory.
 enum ActMode {
@@ -35,8 +60,7 @@ enum Epi {
 
 // One block of output rows that share a weight type and an epilogue.
 struct Seg {
-  const uint8_t* w;      // Q4_K: verbatim rows; Q6_K: packed bodies
-  const uint16_t* wd;    // Q6_K: fp16 d plane [n_rows][nb]
+  const uint8_t* w;      // rows in the device layout above
   const float* bias;     // device row order, may be null
   float* out;            // primary output
   float* out2;           // EPI_ROPE_QK: k output (rows >= split)
@@ -45,7 +69,6 @@ struct Seg {
   int n_rows;
   int epi;
   int split;             // EPI_ROPE_QK: first k row (= q rows)
-  int chunk_begin;       // first global chunk id of this segment
 };
 
 struct PhaseParams {
@@ -59,7 +82,8 @@ struct PhaseParams {
   int need_q8;           // some segment is Q4_K (quantize in the prologue)
   int n_seg;
   Seg seg[MAX_SEGS];
-  int total_chunks;
+  // filled by launch_phase: ring geometry and per-CTA partial-sum slots
+  int n_stages, stage_bytes, part_floats;
   // position-dependent epilogues
   const float* rope_cs;  // [max_seq][head_dim/2] (cos, sin) pairs
   const int* pos_dev;    // current position (device)
@@ -74,12 +98,15 @@ struct PhaseParams {
   int token_log_cap;     // entries in token_log; steps beyond it are not logged
   int* step_dev;         // step counter for token_log (may be null)
   int* pos_inc;          // position to increment (may be null)
+  int* err_flag;         // set non-zero when a bounded wait gives up (may be null)
 };
 
-// ---- launchers (hakm_kernels.cu) ----
-size_t phase_smem_bytes(const PhaseParams& p);
-cudaError_t launch_phase(const PhaseParams& p, int grid, cudaStream_t s, bool pdl);
-int phase_grid(const PhaseParams& p, int num_sms);
+// ---- streaming GEMV phases (hakm_stream.cu) ----
+cudaError_t launch_phase(const PhaseParams& p, int num_sms, cudaStream_t s, bool pdl);
+size_t phase_smem_bytes(const PhaseParams& p, int grid);
+constexpr int PHASE_SMEM_MAX = 220 * 1024;
+
+// ---- small kernels (hakm_kernels.cu) ----
 
 cudaError_t launch_quantize_q8(const float* x, int n, int8_t* xq, float* xs, cudaStream_t s);
 cudaError_t launch_q4k_subsums(int32_t* iqx, int32_t* ix, const uint8_t* w, const int8_t* xq,
@@ -87,8 +114,8 @@ cudaError_t launch_q4k_subsums(int32_t* iqx, int32_t* ix, const uint8_t* w, cons
 cudaError_t launch_q6k_pack(uint8_t* dst, const uint8_t* src, int n_rows, int n_in, cudaStream_t s);
 cudaError_t launch_dequant(float* out, const uint8_t* w, int type, int n_rows, int n_in, cudaStream_t s);
 cudaError_t launch_rmsnorm(float* y, const float* x, const float* w, int n, float eps, cudaStream_t s);
-cudaError_t launch_embed_q6k(float* xb, const uint8_t* wb, const uint16_t* wd, const int* token,
-                             int n_in, unsigned long long* argmax_key, cudaStream_t s, bool pdl);
+cudaError_t launch_embed_q6k(float* xb, const uint8_t* w, const int* token, int n_in, cudaStream_t s,
+                             bool pdl);
 cudaError_t launch_rope(float* x, const float* rope_cs, const int* pos_dev, int n_heads, int head_dim,
                         cudaStream_t s);
 

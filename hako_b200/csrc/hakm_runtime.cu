@@ -119,10 +119,9 @@ size_t row_bytes(uint32_t type, int n_in) {
 
 // ------------------------------------------------------------ context
 
-struct DevMat {         // one weight matrix on the device
+struct DevMat {         // one weight matrix on the device (layout: hakm_internal.h)
   int type = 0, rows = 0, cols = 0;
-  uint8_t* w = nullptr;       // Q4_K rows or Q6_K bodies
-  uint16_t* wd = nullptr;     // Q6_K d plane
+  uint8_t* w = nullptr;
 };
 
 struct DevLayer {
@@ -150,6 +149,7 @@ struct hakmc_ctx {
   int prompt_cap = 0;
   unsigned long long* argmax_key;
   unsigned int *done_counter, *attn_counters;
+  int* err_flag = nullptr;    // set by a kernel whose bounded wait gave up
   int token_log_cap = 0;
   int* h_pinned = nullptr;    // pinned staging: [0] token in, [1] argmax out
   float* logits_pinned = nullptr;
@@ -201,26 +201,26 @@ static int upload_mat(hakmc_ctx* c, DevMat& dm, const MTensor& t, int exp_cols, 
     const int s = order.empty() ? i : order[i];
     return t.data + (size_t)s * rb;
   };
-  std::vector<uint8_t> host((size_t)rows * rb);
+  const size_t drb = dev_row_bytes((int)t.type, nb);
+  std::vector<uint8_t> host((size_t)rows * drb, 0);
   if (t.type == W_Q4K) {
-    for (int i = 0; i < rows; i++) memcpy(host.data() + (size_t)i * rb, src_row(i), rb);
-    int e = dalloc(c, (void**)&dm.w, host.size());
-    if (e) return e;
-    CK(cudaMemcpy(dm.w, host.data(), host.size(), cudaMemcpyHostToDevice));
+    for (int i = 0; i < rows; i++) memcpy(host.data() + (size_t)i * drb, src_row(i), rb);
   } else {
-    const size_t body = (size_t)rows * nb * Q6K_BODY;
+    // chunks of 8 blocks: the 208-byte bodies, then the 8 fp16 d values
     for (int i = 0; i < rows; i++) {
       const uint8_t* s = src_row(i);
+      uint8_t* d = host.data() + (size_t)i * drb;
       for (int b = 0; b < nb; b++) {
-        memcpy(host.data() + ((size_t)i * nb + b) * Q6K_BODY, s + (size_t)b * Q6K_BYTES, Q6K_BODY);
-        memcpy(host.data() + body + ((size_t)i * nb + b) * 2, s + (size_t)b * Q6K_BYTES + Q6K_BODY, 2);
+        const int c = b / CHUNK_BLOCKS, j = b % CHUNK_BLOCKS, m = q6_chunk_blocks(nb, c);
+        uint8_t* chunk = d + (size_t)c * Q6K_CHUNK;
+        memcpy(chunk + j * Q6K_BODY, s + (size_t)b * Q6K_BYTES, Q6K_BODY);
+        memcpy(chunk + m * Q6K_BODY + 2 * j, s + (size_t)b * Q6K_BYTES + Q6K_BODY, 2);
       }
     }
-    int e = dalloc(c, (void**)&dm.w, host.size());
-    if (e) return e;
-    dm.wd = reinterpret_cast<uint16_t*>(dm.w + body);
-    CK(cudaMemcpy(dm.w, host.data(), host.size(), cudaMemcpyHostToDevice));
   }
+  int e = dalloc(c, (void**)&dm.w, host.size());
+  if (e) return e;
+  CK(cudaMemcpy(dm.w, host.data(), host.size(), cudaMemcpyHostToDevice));
   return 0;
 }
 
@@ -254,7 +254,6 @@ static std::vector<int> rope_pair_order(int n_heads, int hd) {
 static Seg make_seg(const DevMat& m, int epi, float* out) {
   Seg s = {};
   s.w = m.w;
-  s.wd = m.wd;
   s.type = m.type;
   s.n_rows = m.rows;
   s.epi = epi;
@@ -263,19 +262,15 @@ static Seg make_seg(const DevMat& m, int epi, float* out) {
 }
 
 static void finish_params(PhaseParams& p) {
-  int cb = 0;
   p.need_q8 = 0;
-  for (int i = 0; i < p.n_seg; i++) {
-    p.seg[i].chunk_begin = cb;
-    cb += (p.seg[i].n_rows + ROWS_PER_CHUNK - 1) / ROWS_PER_CHUNK;
+  for (int i = 0; i < p.n_seg; i++)
     if (p.seg[i].type == W_Q4K) p.need_q8 = 1;
-  }
-  p.total_chunks = cb;
 }
 
 static cudaError_t run_phase(hakmc_ctx* c, PhaseParams& p) {
   finish_params(p);
-  return launch_phase(p, phase_grid(p, c->num_sms), c->stream, c->pdl);
+  p.err_flag = c->err_flag;
+  return launch_phase(p, c->num_sms, c->stream, c->pdl);
 }
 
 enum { PH_QKV = 0, PH_ATTN = 1, PH_WO = 2, PH_FFN = 3, PH_DOWN = 4, PH_LMHEAD = 5 };
@@ -337,8 +332,7 @@ static cudaError_t enqueue_phase(hakmc_ctx* c, int l, int ph, int n_split, bool 
 
 // Enqueue one decode step for sequence 0 on c->stream.
 static cudaError_t enqueue_step(hakmc_ctx* c, int n_split) {
-  cudaError_t e = launch_embed_q6k(c->xb, c->tok_embd.w, c->tok_embd.wd, c->token_dev, c->D, nullptr,
-                                   c->stream, c->pdl);
+  cudaError_t e = launch_embed_q6k(c->xb, c->tok_embd.w, c->token_dev, c->D, c->stream, c->pdl);
   if (e != cudaSuccess) return e;
   for (int l = 0; l < c->run_layers; l++)
     for (int ph = PH_QKV; ph <= PH_DOWN; ph++)
@@ -526,6 +520,8 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
   if ((r = dalloc(c, (void**)&c->token_log, (size_t)c->token_log_cap * 4))) return r;
   if ((r = dalloc(c, (void**)&c->argmax_key, 8 * B))) return r;
   if ((r = dalloc(c, (void**)&c->done_counter, 4 * B))) return r;
+  if ((r = dalloc(c, (void**)&c->err_flag, 16))) return r;
+  CK(cudaMemset(c->err_flag, 0, 16));
   CK(cudaMemset(c->token_dev, 0, 16 * B));
   CK(cudaMemset(c->pos_dev, 0, 16 * B));
   CK(cudaMemset(c->step_dev, 0, 16));
@@ -708,6 +704,17 @@ extern "C" int hakmc_hidden(hakmc_ctx* c, int seq, float* out) {
   return 0;
 }
 
+extern "C" int hakmc_debug_read(hakmc_ctx* c, int which, float* out) {
+  if (!c || !out) return HAKMC_EINVAL;
+  const float* src[7] = {c->xb, c->q, c->k, c->v, c->att, c->hbuf, c->logits};
+  const int n[7] = {c->D, c->D, c->KV, c->KV, c->D, c->F, c->V};
+  if (which < 0 || which > 6) return HAKMC_EINVAL;
+  CK(cudaSetDevice(c->device));
+  CK(cudaMemcpyAsync(out, src[which], (size_t)n[which] * 4, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  return 0;
+}
+
 extern "C" int hakmc_fill_kv(hakmc_ctx* c, int seq, const float* k, const float* v, int n_pos) {
   if (!c || !k || !v || seq < 0 || seq >= c->max_batch || n_pos < 0 || n_pos > c->max_seq) {
     set_err("bad fill_kv arguments");
@@ -804,14 +811,13 @@ static int gemv_common(float* out, const void* w, int type, const float* x, cons
   s.epi = EPI_STORE;
   s.out = out;
   s.bias = bias;
-  if (type == W_Q6K) s.wd = reinterpret_cast<const uint16_t*>((const uint8_t*)w + (size_t)n_out * (n_in / QK) * Q6K_BODY);
   p.seg[0] = s;
   finish_params(p);
-  if (phase_smem_bytes(p) > 110 * 1024) { set_err("gemv: n_in too large"); return HAKMC_EINVAL; }
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  CKL(launch_phase(p, phase_grid(p, sms), (cudaStream_t)stream, false));
+  if (phase_smem_bytes(p, sms) > (size_t)PHASE_SMEM_MAX) { set_err("gemv: n_in too large"); return HAKMC_EINVAL; }
+  CKL(launch_phase(p, sms, (cudaStream_t)stream, false));
   return 0;
 }
 
@@ -835,7 +841,7 @@ extern "C" int hakmc_q4k_subsums(int32_t* iqx, int32_t* ix, const void* w, const
 }
 
 extern "C" size_t hakmc_q6k_packed_bytes(int n_rows, int n_in) {
-  return (size_t)n_rows * (n_in / QK) * Q6K_BYTES;
+  return (size_t)n_rows * dev_row_bytes(W_Q6K, n_in / QK);
 }
 
 extern "C" int hakmc_q6k_pack(void* dst, const void* src, int n_rows, int n_in, void* stream) {
@@ -861,7 +867,6 @@ extern "C" int hakmc_lmhead_argmax(float* logits, int* argmax, const void* w, co
   p.n_seg = 1;
   Seg sg = {};
   sg.w = (const uint8_t*)w;
-  sg.wd = reinterpret_cast<const uint16_t*>((const uint8_t*)w + (size_t)n_vocab * (n_in / QK) * Q6K_BODY);
   sg.type = W_Q6K; sg.n_rows = n_vocab; sg.epi = EPI_ARGMAX; sg.out = logits;
   p.seg[0] = sg;
   p.argmax_key = s->key; p.done_counter = s->done; p.next_token = argmax;
@@ -869,7 +874,7 @@ extern "C" int hakmc_lmhead_argmax(float* logits, int* argmax, const void* w, co
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  CKL(launch_phase(p, phase_grid(p, sms), (cudaStream_t)stream, false));
+  CKL(launch_phase(p, sms, (cudaStream_t)stream, false));
   return 0;
 }
 

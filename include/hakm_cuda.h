@@ -92,6 +92,13 @@ int hakmc_set_layers(hakmc_ctx *c, int n_layers);
 /* Copy the residual stream of sequence `seq` after the last forward into
  * [host] out (d_model floats). */
 int hakmc_hidden(hakmc_ctx *c, int seq, float *out);
+/* Copy a device activation of sequence 0 after the last forward into [host]
+ * out: which = 0 residual stream (d_model), 1 q after RoPE (d_model), 2 k
+ * after RoPE (kv_dim), 3 v (kv_dim), 4 attention output (d_model), 5 SwiGLU
+ * output (ffn_dim), 6 logits (vocab). Test hook; the buffers hold the values
+ * of the last layer that ran (hakm_ctx scratch, src/model.h:24). */
+int hakmc_debug_read(hakmc_ctx *c, int which, float *out);
+
 /* Fill the KV cache of sequence `seq` for positions [0, n_pos) of every
  * layer from [host] k and v ([n_layers][n_pos][n_kv_heads*head_dim] fp32),
  * and set that sequence's position to n_pos. Mirrors pre-filling

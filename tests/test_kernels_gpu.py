@@ -51,6 +51,16 @@ def empty(shape, dtype, cuda):
     return torch.empty(shape, dtype=dtype, device=cuda)
 
 
+def packed_q6k(w, rows, k, cuda):
+    """Upload verbatim Q6_K rows and re-lay them with hakmc_q6k_pack."""
+    import torch
+    src = dev(w, cuda)
+    dst = torch.empty(lib.hakmc_q6k_packed_bytes(rows, k), dtype=torch.uint8, device=cuda)
+    _KEEP.append(dst)
+    check(lib.hakmc_q6k_pack(P(dst), P(src), rows, k, None))
+    return dst
+
+
 def test_quantize_golden_bit_exact(cuda):
     import torch
     g = golden_npz("q8.npz")
@@ -141,9 +151,7 @@ def test_gemv_q6k_matches_reference(cuda, reference, rows, k):
     import torch
     w = synth.random_q6k(rows, k, 5 * rows + k)
     x = synth.normal(k, k + 2)
-    wd = dev(w, cuda)
-    packed = torch.empty_like(wd)
-    check(lib.hakmc_q6k_pack(P(packed), P(wd), rows, k, None))
+    packed = packed_q6k(w, rows, k, cuda)
     out = empty(rows, torch.float32, cuda)
     b = synth.normal(rows, 78)
     check(lib.hakmc_gemv_q6k(P(out), P(packed), P(dev(x, cuda)), P(dev(b, cuda)), rows, k, None))
@@ -167,9 +175,7 @@ def test_lmhead_argmax(cuda, reference, vocab, k):
     w = synth.random_q6k(vocab, k, vocab)
     x = synth.normal(k, 3)
     nw = (1 + 0.1 * synth.normal(k, 4)).astype(np.float32)
-    wd = dev(w, cuda)
-    packed = torch.empty_like(wd)
-    check(lib.hakmc_q6k_pack(P(packed), P(wd), vocab, k, None))
+    packed = packed_q6k(w, vocab, k, cuda)
     lg = empty(vocab, torch.float32, cuda)
     am = torch.zeros(1, dtype=torch.int32, device=cuda)
     check(lib.hakmc_lmhead_argmax(P(lg), P(am), P(packed), P(dev(x, cuda)), P(dev(nw, cuda)), 1e-6,
@@ -195,9 +201,7 @@ def test_lmhead_argmax_ties_pick_first(cuda):
         w[r * 210 + 192:r * 210 + 208] = 31
         w[r * 210:r * 210 + 192] = 0xFF  # q = 63 -> +31
         w[r * 210 + 208:r * 210 + 210] = np.frombuffer(np.uint16(0x3C00).tobytes(), np.uint8)
-    wd = dev(w, cuda)
-    packed = torch.empty_like(wd)
-    check(lib.hakmc_q6k_pack(P(packed), P(wd), vocab, k, None))
+    packed = packed_q6k(w, vocab, k, cuda)
     am = torch.zeros(1, dtype=torch.int32, device=cuda)
     check(lib.hakmc_lmhead_argmax(None, P(am), P(packed), P(dev(x, cuda)), None, 1e-6, vocab, k, None))
     sync()
