@@ -30,6 +30,7 @@ SIGNATURES = {
     "hakmc_forward_batch": (_i, [_vp, _vp, _vp, _i, _vp, _vp]),
     "hakmc_decode": (_i, [_vp, _i, _vp]),
     "hakmc_time_phase": (_i, [_vp, _i, _i, _vp]),
+    "hakmc_trace_phase": (_i, [_vp, _i, _i, _vp, _i]),
     "hakmc_set_layers": (_i, [_vp, _i]),
     "hakmc_hidden": (_i, [_vp, _i, _vp]),
     "hakmc_fill_kv": (_i, [_vp, _i, _vp, _vp, _i]),

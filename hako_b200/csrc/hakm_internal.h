@@ -99,6 +99,7 @@ struct PhaseParams {
   int* step_dev;         // step counter for token_log (may be null)
   int* pos_inc;          // position to increment (may be null)
   int* err_flag;         // set non-zero when a bounded wait gives up (may be null)
+  unsigned long long* trace;  // per-CTA %globaltimer stamps (measurement hook, may be null)
 };
 
 // ---- streaming GEMV phases (hakm_stream.cu) ----
@@ -131,7 +132,7 @@ struct AttnParams {
   float* part;           // scratch [n_kv][n_split][G][2 + hd]
   unsigned int* counters;  // [n_kv], self-resetting
 };
-constexpr int ATTN_CHUNK = 256;
+constexpr int ATTN_CHUNK = 64;   // positions per attention CTA
 cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl);
 size_t attention_scratch_floats(int n_kv, int n_split, int group, int head_dim);
 

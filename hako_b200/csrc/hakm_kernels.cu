@@ -191,22 +191,24 @@ cudaError_t launch_rope(float* x, const float* rope_cs, const int* pos_dev, int 
 
 // GQA decode attention (src/model.c:124-142, softmax src/nn.c:20-27). One CTA
 // per (kv head, chunk of ATTN_CHUNK positions) serves the G query heads that
-// share the kv head, so K and V stream once. Scores: one thread per position
-// (its K row as 128-bit loads, q broadcast from smem). Softmax per head. Out:
-// each warp sums a stride of positions for all G heads, then a cross-warp
-// reduction. Chunks combine flash-decode style (max / sum rescale); the last
-// CTA of a kv head (atomic ticket) merges them, so one launch suffices.
+// share the kv head. The chunk's K and V rows are staged in shared memory
+// with every load in flight at once (rows padded by 4 floats so float4 reads
+// down a column of positions are bank-conflict free); scores, softmax and the
+// weighted V sum then run out of shared memory. Chunks combine flash-decode
+// style (max / sum rescale); the last CTA of a kv head (atomic ticket) merges
+// them, so one launch suffices at any context length.
 template <int HD>
 __global__ void __launch_bounds__(256) attention_kernel(const AttnParams a) {
   extern __shared__ __align__(16) float sm[];
-  constexpr int MAXG = 8;
+  constexpr int MAXG = 8, KP = HD + 4;
   const int G = a.n_heads / a.n_kv;
   const int kvh = blockIdx.x, split = blockIdx.y;
   const int kv_dim = a.n_kv * HD;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-  float* qs = sm;                       // [G][HD]
-  float* sc = qs + MAXG * HD;           // [G][ATTN_CHUNK]
-  float* red = sc + MAXG * ATTN_CHUNK;  // [nw][G][HD]
+  float* qs = sm;                     // [G][HD]
+  float* ks = qs + MAXG * HD;         // [ATTN_CHUNK][KP]
+  float* vs = ks + ATTN_CHUNK * KP;   // [ATTN_CHUNK][HD]
+  float* sc = vs + ATTN_CHUNK * HD;   // [G][ATTN_CHUNK]
   __shared__ float stat_m[MAXG], stat_l[MAXG];
   __shared__ bool last;
 
@@ -214,34 +216,40 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttnParams a) {
   pdl_wait();
   const int pos = *a.pos_dev;
   const int s0 = split * ATTN_CHUNK;
-  const int s1 = min(s0 + ATTN_CHUNK, pos + 1);
-  const int ns = s1 - s0;  // may be <= 0 for chunks past pos
+  const int ns = min(ATTN_CHUNK, pos + 1 - s0);  // may be <= 0 for chunks past pos
 
-  for (int i = tid; i < G * HD; i += blockDim.x) qs[i] = a.q[(kvh * G) * HD + i];
+  // stage q, K and V (all loads issued before any use)
+  constexpr int R4 = HD / 4;
+  const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)kvh * G * HD);
+  for (int i = tid; i < G * R4; i += blockDim.x) reinterpret_cast<float4*>(qs)[i] = q4[i];
+  if (ns > 0) {
+    const float* kb = a.k_cache + (size_t)s0 * kv_dim + kvh * HD;
+    const float* vb = a.v_cache + (size_t)s0 * kv_dim + kvh * HD;
+    for (int i = tid; i < ns * R4; i += blockDim.x) {
+      const int r = i / R4, c4 = i % R4;
+      const float4 kv = *reinterpret_cast<const float4*>(kb + (size_t)r * kv_dim + 4 * c4);
+      const float4 vv = *reinterpret_cast<const float4*>(vb + (size_t)r * kv_dim + 4 * c4);
+      *reinterpret_cast<float4*>(ks + r * KP + 4 * c4) = kv;
+      *reinterpret_cast<float4*>(vs + r * HD + 4 * c4) = vv;
+    }
+  }
   __syncthreads();
 
-  if (tid < ns) {
-    const float4* kr = reinterpret_cast<const float4*>(a.k_cache + (size_t)(s0 + tid) * kv_dim + kvh * HD);
-    float dot[MAXG];
+  // scores: one (head, position) pair per thread iteration, positions fastest
+  for (int i = tid; i < G * ATTN_CHUNK; i += blockDim.x) {
+    const int g = i / ATTN_CHUNK, r = i % ATTN_CHUNK;
+    if (r < ns) {
+      const float4* kr = reinterpret_cast<const float4*>(ks + r * KP);
+      const float4* qr = reinterpret_cast<const float4*>(qs + g * HD);
+      float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-    for (int g = 0; g < MAXG; g++) dot[g] = 0.f;
-#pragma unroll 4
-    for (int d4 = 0; d4 < HD / 4; d4++) {
-      const float4 kv = kr[d4];
-#pragma unroll
-      for (int g = 0; g < MAXG; g++) {
-        if (g < G) {
-          const float4 qv = reinterpret_cast<const float4*>(qs + g * HD)[d4];
-          dot[g] = fmaf(qv.x, kv.x, dot[g]);
-          dot[g] = fmaf(qv.y, kv.y, dot[g]);
-          dot[g] = fmaf(qv.z, kv.z, dot[g]);
-          dot[g] = fmaf(qv.w, kv.w, dot[g]);
-        }
+      for (int c4 = 0; c4 < R4; c4 += 2) {
+        const float4 k0 = kr[c4], k1 = kr[c4 + 1], x0 = qr[c4], x1 = qr[c4 + 1];
+        d0 = fmaf(x0.x, k0.x, d0); d0 = fmaf(x0.y, k0.y, d0); d0 = fmaf(x0.z, k0.z, d0); d0 = fmaf(x0.w, k0.w, d0);
+        d1 = fmaf(x1.x, k1.x, d1); d1 = fmaf(x1.y, k1.y, d1); d1 = fmaf(x1.z, k1.z, d1); d1 = fmaf(x1.w, k1.w, d1);
       }
+      sc[g * ATTN_CHUNK + r] = (d0 + d1) * a.scale;
     }
-#pragma unroll
-    for (int g = 0; g < MAXG; g++)
-      if (g < G) sc[g * ATTN_CHUNK + tid] = dot[g] * a.scale;
   }
   __syncthreads();
 
@@ -261,50 +269,26 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttnParams a) {
   }
   __syncthreads();
 
-  // weighted V: lane owns HD/32 consecutive dims
-  constexpr int DPL = HD / 32;
-  float acc[MAXG][DPL];
-#pragma unroll
-  for (int g = 0; g < MAXG; g++)
-#pragma unroll
-    for (int j = 0; j < DPL; j++) acc[g][j] = 0.f;
-  for (int i = warp; i < ns; i += nw) {
-    const float* vr = a.v_cache + (size_t)(s0 + i) * kv_dim + kvh * HD + lane * DPL;
-    float v[DPL];
-    if constexpr (DPL == 4) {
-      const float4 t = *reinterpret_cast<const float4*>(vr);
-      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[DPL - 1] = t.w;
-    } else {
-#pragma unroll
-      for (int j = 0; j < DPL; j++) v[j] = vr[j];
-    }
-#pragma unroll
-    for (int g = 0; g < MAXG; g++) {
-      if (g < G) {
-        const float e = sc[g * ATTN_CHUNK + i];
-#pragma unroll
-        for (int j = 0; j < DPL; j++) acc[g][j] = fmaf(e, v[j], acc[g][j]);
-      }
-    }
-  }
-#pragma unroll
-  for (int g = 0; g < MAXG; g++)
-    if (g < G)
-#pragma unroll
-      for (int j = 0; j < DPL; j++) red[(warp * MAXG + g) * HD + lane * DPL + j] = acc[g][j];
-  __syncthreads();
-
+  // weighted V: one (head, 4 dims) pair per thread iteration
   const bool single = (a.n_split == 1);
-  for (int i = tid; i < G * HD; i += blockDim.x) {
-    const int g = i / HD, d = i % HD;
-    float s = 0.f;
-    for (int w = 0; w < nw; w++) s += red[(w * MAXG + g) * HD + d];
+  for (int i = tid; i < G * R4; i += blockDim.x) {
+    const int g = i / R4, c4 = i % R4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < ns; r++) {
+      const float e = sc[g * ATTN_CHUNK + r];
+      const float4 v = *reinterpret_cast<const float4*>(vs + r * HD + 4 * c4);
+      acc.x = fmaf(e, v.x, acc.x); acc.y = fmaf(e, v.y, acc.y);
+      acc.z = fmaf(e, v.z, acc.z); acc.w = fmaf(e, v.w, acc.w);
+    }
     if (single) {
-      a.out[(kvh * G + g) * HD + d] = s / stat_l[g];
+      const float inv = 1.0f / stat_l[g];
+      float4 o;
+      o.x = acc.x * inv; o.y = acc.y * inv; o.z = acc.z * inv; o.w = acc.w * inv;
+      *reinterpret_cast<float4*>(a.out + (size_t)(kvh * G + g) * HD + 4 * c4) = o;
     } else {
       float* pp = a.part + ((size_t)(kvh * a.n_split + split) * G + g) * (HD + 2);
-      pp[2 + d] = s;
-      if (d == 0) { pp[0] = ns > 0 ? stat_m[g] : -CUDART_INF_F; pp[1] = ns > 0 ? stat_l[g] : 0.f; }
+      pp[2 + 4 * c4] = acc.x; pp[3 + 4 * c4] = acc.y; pp[4 + 4 * c4] = acc.z; pp[5 + 4 * c4] = acc.w;
+      if (c4 == 0) { pp[0] = ns > 0 ? stat_m[g] : -CUDART_INF_F; pp[1] = ns > 0 ? stat_l[g] : 0.f; }
     }
   }
   if (!single) {
@@ -324,16 +308,16 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttnParams a) {
           const volatile float* pp = a.part + ((size_t)(kvh * a.n_split + sp) * G + g) * (HD + 2);
           m = fmaxf(m, pp[0]);
         }
-        float l = 0.f, s = 0.f;
+        float l = 0.f, acc = 0.f;
         for (int sp = 0; sp < a.n_split; sp++) {
           const volatile float* pp = a.part + ((size_t)(kvh * a.n_split + sp) * G + g) * (HD + 2);
           if (pp[1] > 0.f) {
             const float f = expf(pp[0] - m);
             l += pp[1] * f;
-            s += pp[2 + d] * f;
+            acc += pp[2 + d] * f;
           }
         }
-        a.out[(kvh * G + g) * HD + d] = s / l;
+        a.out[(kvh * G + g) * HD + d] = acc / l;
       }
       if (tid == 0) a.counters[kvh] = 0u;
     }
@@ -344,11 +328,18 @@ size_t attention_scratch_floats(int n_kv, int n_split, int group, int head_dim) 
   return (size_t)n_kv * n_split * group * (head_dim + 2);
 }
 
-cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl) {
+template <int HD>
+static cudaError_t launch_attn(const AttnParams& a, cudaStream_t s, bool pdl) {
   constexpr int MAXG = 8;
-  if (a.n_heads % a.n_kv || a.n_heads / a.n_kv > MAXG) return cudaErrorInvalidValue;
-  const int hd = a.head_dim;
-  const size_t smem = (size_t)(MAXG * hd + MAXG * ATTN_CHUNK + 8 * MAXG * hd) * sizeof(float);
+  const size_t smem = (size_t)(MAXG * HD + ATTN_CHUNK * (HD + 4) + ATTN_CHUNK * HD + MAXG * ATTN_CHUNK) * 4;
+  static unsigned done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 32 && !(done & (1u << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    done |= 1u << dev;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.n_kv, a.n_split);
   cfg.blockDim = dim3(256);
@@ -359,22 +350,13 @@ cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (hd == 128) {
-    static bool done = false;
-    if (!done) {
-      cudaFuncSetAttribute(attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      done = true;
-    }
-    return cudaLaunchKernelEx(&cfg, attention_kernel<128>, a);
-  }
-  if (hd == 64) {
-    static bool done = false;
-    if (!done) {
-      cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      done = true;
-    }
-    return cudaLaunchKernelEx(&cfg, attention_kernel<64>, a);
-  }
+  return cudaLaunchKernelEx(&cfg, attention_kernel<HD>, a);
+}
+
+cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl) {
+  if (a.n_heads % a.n_kv || a.n_heads / a.n_kv > 8) return cudaErrorInvalidValue;
+  if (a.head_dim == 128) return launch_attn<128>(a, s, pdl);
+  if (a.head_dim == 64) return launch_attn<64>(a, s, pdl);
   return cudaErrorInvalidValue;
 }
 

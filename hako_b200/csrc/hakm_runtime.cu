@@ -267,9 +267,12 @@ static void finish_params(PhaseParams& p) {
     if (p.seg[i].type == W_Q4K) p.need_q8 = 1;
 }
 
+static unsigned long long* g_trace = nullptr;  // set only inside hakmc_trace_phase
+
 static cudaError_t run_phase(hakmc_ctx* c, PhaseParams& p) {
   finish_params(p);
   p.err_flag = c->err_flag;
+  p.trace = g_trace;
   return launch_phase(p, c->num_sms, c->stream, c->pdl);
 }
 
@@ -340,7 +343,15 @@ static cudaError_t enqueue_step(hakmc_ctx* c, int n_split) {
   return enqueue_phase(c, 0, PH_LMHEAD, n_split, false);
 }
 
-static int n_split_for(const hakmc_ctx* c, int pos) { return pos / ATTN_CHUNK + 1; }
+// Attention chunk count used for position `pos`, rounded up to a power of two
+// so a handful of captured graphs cover every position (chunks past pos run
+// empty and contribute nothing to the combine).
+static int n_split_for(const hakmc_ctx* c, int pos) {
+  const int need = pos / ATTN_CHUNK + 1, cap = (c->max_seq + ATTN_CHUNK - 1) / ATTN_CHUNK;
+  int k = 1;
+  while (k < need) k <<= 1;
+  return k < cap ? k : cap;
+}
 
 static int get_graph(hakmc_ctx* c, int n_split, cudaGraphExec_t* out) {
   auto it = c->graphs.find(n_split);
@@ -361,6 +372,17 @@ static int get_graph(hakmc_ctx* c, int n_split, cudaGraphExec_t* out) {
   if (e != cudaSuccess) { set_err("graph instantiate: %s", cudaGetErrorString(e)); return HAKMC_ECUDA; }
   c->graphs[n_split] = ge;
   *out = ge;
+  return 0;
+}
+
+// Capture (once) every step graph positions [p0, p1) will use, so no capture
+// happens between timed launches.
+static int ensure_graphs(hakmc_ctx* c, int p0, int p1) {
+  for (int p = p0; p < p1 && p < c->max_seq; p++) {
+    cudaGraphExec_t g;
+    const int r = get_graph(c, n_split_for(c, p), &g);
+    if (r) return r;
+  }
   return 0;
 }
 
@@ -630,6 +652,10 @@ extern "C" int hakmc_generate(hakmc_ctx* c, const int* prompt, int n_prompt, int
     c->prompt_dev = (int*)p;
     c->prompt_cap = n_prompt;
   }
+  {
+    const int r = ensure_graphs(c, c->pos, c->pos + n_prompt + n_gen);
+    if (r) return r;
+  }
   std::vector<int> pp(prompt, prompt + n_prompt);
   CK(cudaMemcpyAsync(c->prompt_dev, pp.data(), (size_t)n_prompt * 4, cudaMemcpyHostToDevice, c->stream));
   CK(cudaMemsetAsync(c->step_dev, 0, 4, c->stream));
@@ -656,6 +682,10 @@ extern "C" int hakmc_decode(hakmc_ctx* c, int n_steps, int* out) {
   if (c->pos + n_steps > c->max_seq) { set_err("sequence exceeds max_seq"); return HAKMC_ERANGE; }
   if (n_steps > c->token_log_cap) { set_err("token log too small"); return HAKMC_ERANGE; }
   CK(cudaSetDevice(c->device));
+  {
+    const int r = ensure_graphs(c, c->pos, c->pos + n_steps);
+    if (r) return r;
+  }
   // token_log[i] records the argmax of step i, i.e. the input of step i+1; the
   // first input is the argmax already waiting in token_dev
   CK(cudaMemsetAsync(c->step_dev, 0, 4, c->stream));
@@ -686,6 +716,25 @@ extern "C" int hakmc_time_phase(hakmc_ctx* c, int phase, int iters, float* avg_m
   CK(cudaEventElapsedTime(&ms, c->ev0, c->ev1));
   *avg_ms = ms / iters;
   return 0;
+}
+
+extern "C" int hakmc_trace_phase(hakmc_ctx* c, int phase, int layer, unsigned long long* stamps, int max_ctas) {
+  if (!c || phase < 0 || phase > PH_LMHEAD || phase == PH_ATTN || !stamps || layer < 0 || layer >= c->L)
+    return HAKMC_EINVAL;
+  CK(cudaSetDevice(c->device));
+  const size_t n = (size_t)max_ctas * 8;
+  unsigned long long* d = nullptr;
+  CK(cudaMalloc(&d, n * 8));
+  CK(cudaMemset(d, 0, n * 8));
+  const int ns = n_split_for(c, c->pos < c->max_seq ? c->pos : c->max_seq - 1);
+  g_trace = d;
+  cudaError_t e = enqueue_phase(c, layer, phase, ns, true);
+  g_trace = nullptr;
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(stamps, d, n * 8, cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (e != cudaSuccess) { set_err("trace: %s", cudaGetErrorString(e)); return HAKMC_ECUDA; }
+  return max_ctas < c->num_sms ? max_ctas : c->num_sms;
 }
 
 extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* pos, int n_seq,

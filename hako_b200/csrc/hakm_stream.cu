@@ -30,14 +30,16 @@
 
 namespace hakm {
 
-constexpr int CONSUMER_WARPS = 16;
+constexpr int CONSUMER_WARPS = 12;
 constexpr int THREADS = 32 * (CONSUMER_WARPS + 1);
 constexpr int TILE_ROWS = 16;
 constexpr int UNITS = TILE_ROWS / 4;  // 4-row units per stage
 constexpr int GROUPS = CONSUMER_WARPS / UNITS;  // consumer groups, one stage each
-constexpr int MAX_STAGES = 8;
+constexpr int MAX_STAGES = 12;
+constexpr int SMEM_HEADER = 256;  // full[MAX_STAGES] and empty[MAX_STAGES] mbarriers
 constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clock
 constexpr int BAR_CONSUMERS = 1;
+constexpr int RMS_SLOTS = 2;  // 8-element slots per consumer thread in the rmsnorm prologue
 constexpr int PHASE_BUDGET = 220 * 1024;
 
 // ------------------------------------------------------------------ PTX
@@ -77,6 +79,19 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
                "l"(src), "r"(bytes), "r"(bar)
                : "memory");
 }
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// trace slots per CTA: 0 start, 1 prologue done, 2 first stage ready,
+// 3 last unit done, 4 epilogue done, 5 producer done issuing
+constexpr int TRACE_SLOTS = 8;
+#define TRACE(i)                                                               \
+  do {                                                                         \
+    if (p.trace) p.trace[(size_t)blockIdx.x * TRACE_SLOTS + (i)] = gtime();   \
+  } while (0)
+
 __device__ __forceinline__ void consumers_sync() {
   asm volatile("bar.sync %0, %1;" ::"n"(BAR_CONSUMERS), "n"(CONSUMER_WARPS * 32) : "memory");
 }
@@ -118,12 +133,47 @@ __device__ float consumers_sum(float v, float* red) {
   return warp_sum(t);
 }
 
+// 8-element slot s of the activation: fp32 values to xf, and for Q4_K rows the
+// per-32 int8 codes. The 4 slots of a 32-block are 4 adjacent lanes, so the
+// block max and code sum take two shuffles (quantize_row_q8_32 as built:
+// xs = amax * fl(1/127), q = rint(x * (127/amax)), src/quant.c:127-144).
+__device__ __forceinline__ void store_slot(const PhaseParams& p, int s, bool live, const float v[8], float* xf,
+                                           int8_t* xq, float* xs, int* xsum) {
+  if (live) {
+    reinterpret_cast<float4*>(xf)[2 * s] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(xf)[2 * s + 1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  if (!p.need_q8) return;
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  const float sc = amax * (1.0f / 127.0f);
+  const float inv = q8_inv(amax, sc);
+  int q[8], sum = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) { q[i] = q8_round(v[i] * inv); sum += q[i]; }
+  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  if (live) {
+    uint2 pk;
+    pk.x = (uint32_t)(q[0] & 255) | ((uint32_t)(q[1] & 255) << 8) | ((uint32_t)(q[2] & 255) << 16) |
+           ((uint32_t)(q[3] & 255) << 24);
+    pk.y = (uint32_t)(q[4] & 255) | ((uint32_t)(q[5] & 255) << 8) | ((uint32_t)(q[6] & 255) << 16) |
+           ((uint32_t)(q[7] & 255) << 24);
+    reinterpret_cast<uint2*>(xq)[s] = pk;
+    if ((s & 3) == 0) { xs[s >> 2] = sc; xsum[s >> 2] = sum; }
+  }
+}
+
 // Activation in shared memory: fp32 x (rmsnorm'ed for ACT_RMS) and, for Q4_K
 // segments, its per-32 int8 quantization with the per-block sums of xq.
-// Quantization runs 4 threads per 32-element block (8 elements each, two
-// shuffles for the block max and sum), in one pass with the normalisation.
-__device__ void build_activation(const PhaseParams& p, float* xf, int8_t* xq, float* xs, int* xsum, float* red) {
-  const int K = p.n_in, nsb = K >> 5;
+// ACT_RMS (K <= 8 * consumer threads): one slot per thread, the norm weights
+// already in registers (loaded before the dependency wait), one reduction.
+__device__ void build_activation(const PhaseParams& p, const float wpre[RMS_SLOTS][8], float* xf, int8_t* xq, float* xs,
+                                 int* xsum, float* red) {
+  const int K = p.n_in, nsb = K >> 5, nslot = K >> 3;
   const int t = threadIdx.x - 32, nt = CONSUMER_WARPS * 32;
   const int lane = t & 31, w = t >> 5;
   if (p.act == ACT_Q8) {
@@ -140,64 +190,47 @@ __device__ void build_activation(const PhaseParams& p, float* xf, int8_t* xq, fl
     return;
   }
   const float4* x4 = reinterpret_cast<const float4*>(p.x);
-  float4* xf4 = reinterpret_cast<float4*>(xf);
-  float scale = 1.0f;
   if (p.act == ACT_RMS) {
+    float v[RMS_SLOTS][8];
     float ss = 0.f;
-    for (int i = t; i < K / 4; i += nt) {
-      const float4 v = x4[i];
-      xf4[i] = v;
-      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+#pragma unroll
+    for (int j = 0; j < RMS_SLOTS; j++) {
+      const int s = t + j * nt;
+      if (s < nslot) {
+        const float4 a = x4[2 * s], b = x4[2 * s + 1];
+        v[j][0] = a.x; v[j][1] = a.y; v[j][2] = a.z; v[j][3] = a.w;
+        v[j][4] = b.x; v[j][5] = b.y; v[j][6] = b.z; v[j][7] = b.w;
+#pragma unroll
+        for (int i = 0; i < 8; i++) ss += v[j][i] * v[j][i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[j][i] = 0.f;
+      }
     }
     const float tot = consumers_sum(ss, red);
     // src/nn.c:16-17: scale = 1/sqrtf(ss/n + eps); y = x * scale * w
-    scale = 1.0f / sqrtf(tot / (float)K + p.eps);
-  }
-  const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
-  // 8-element slots; slot s covers elements [8s, 8s+8) of block s/4
-  for (int s0 = 0; s0 < K / 8; s0 += nt) {
-    const int s = s0 + t;
-    const bool live = s < K / 8;
-    float v[8];
-    if (live) {
-      float4 a, b;
-      if (p.act == ACT_RMS) {
-        a = xf4[2 * s]; b = xf4[2 * s + 1];
-        const float4 ga = w4[2 * s], gb = w4[2 * s + 1];
-        a.x = a.x * scale * ga.x; a.y = a.y * scale * ga.y; a.z = a.z * scale * ga.z; a.w = a.w * scale * ga.w;
-        b.x = b.x * scale * gb.x; b.y = b.y * scale * gb.y; b.z = b.z * scale * gb.z; b.w = b.w * scale * gb.w;
-      } else {
-        a = x4[2 * s]; b = x4[2 * s + 1];
-      }
-      xf4[2 * s] = a; xf4[2 * s + 1] = b;
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-    } else {
+    const float scale = 1.0f / sqrtf(tot / (float)K + p.eps);
 #pragma unroll
-      for (int i = 0; i < 8; i++) v[i] = 0.f;
+    for (int j = 0; j < RMS_SLOTS; j++) {
+      const int s = t + j * nt;
+      if (j * nt >= nslot) break;  // uniform: no live slot for any thread
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[j][i] = v[j][i] * scale * wpre[j][i];
+      store_slot(p, s, s < nslot, v[j], xf, xq, xs, xsum);
     }
-    if (p.need_q8) {
-      // the 4 slots of a block are 4 adjacent lanes (K/8 and nt are multiples of 4)
-      float amax = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-      const float sc = amax * (1.0f / 127.0f);
-      const float inv = q8_inv(amax, sc);
-      int q[8], sum = 0;
-#pragma unroll
-      for (int i = 0; i < 8; i++) { q[i] = q8_round(v[i] * inv); sum += q[i]; }
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+  } else {
+    for (int s0 = 0; s0 < nslot; s0 += nt) {
+      const int s = s0 + t;
+      const bool live = s < nslot;
+      float v[8];
       if (live) {
-        uint2 pk;
-        pk.x = (uint32_t)(q[0] & 255) | ((uint32_t)(q[1] & 255) << 8) | ((uint32_t)(q[2] & 255) << 16) |
-               ((uint32_t)(q[3] & 255) << 24);
-        pk.y = (uint32_t)(q[4] & 255) | ((uint32_t)(q[5] & 255) << 8) | ((uint32_t)(q[6] & 255) << 16) |
-               ((uint32_t)(q[7] & 255) << 24);
-        reinterpret_cast<uint2*>(xq)[s] = pk;
-        if ((s & 3) == 0) { xs[s >> 2] = sc; xsum[s >> 2] = sum; }
+        const float4 a = x4[2 * s], b = x4[2 * s + 1];
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = 0.f;
       }
+      store_slot(p, s, live, v, xf, xq, xs, xsum);
     }
   }
   consumers_sync();
@@ -214,19 +247,34 @@ __device__ __forceinline__ float i22_to_float(int v) {
 // Q4_K: lane (bl = lane/4, g = lane%4) owns qs bytes [32g, 32g+32) of block bl
 // of the chunk: low nibbles are sub-block 2g, high nibbles sub-block 2g+1
 // (src/quant.c:239-259). Per sub-block: xs * (d*s*sum(q*xq) - dmin*m*sum(xq)).
-__device__ __forceinline__ void q4k_unit(const uint8_t* st, int nrows, int m, int c, const int8_t* xq,
-                                         const float* xs, const int* xsum, float acc[4]) {
+// The lane's activation slice of one chunk (64 int8 codes, two scales, two
+// code sums) fits in registers; short rows keep it for the whole kernel.
+struct Q4X {
+  int a[8], b[8];
+  float xsa, xsb;
+  int sma, smb;
+};
+
+__device__ __forceinline__ Q4X q4x_load(const int8_t* xq, const float* xs, const int* xsum, int c, int nb) {
+  const int lane = threadIdx.x & 31, bl = lane >> 2, g = lane & 3;
+  Q4X X;
+  const int b = min(CHUNK_BLOCKS * c + bl, nb - 1);  // lanes past the row end load a valid block, unused
+  const int4* xa = reinterpret_cast<const int4*>(xq + 256 * b + 64 * g);
+  const int4 xa0 = xa[0], xa1 = xa[1], xb0 = xa[2], xb1 = xa[3];
+  X.a[0] = xa0.x; X.a[1] = xa0.y; X.a[2] = xa0.z; X.a[3] = xa0.w;
+  X.a[4] = xa1.x; X.a[5] = xa1.y; X.a[6] = xa1.z; X.a[7] = xa1.w;
+  X.b[0] = xb0.x; X.b[1] = xb0.y; X.b[2] = xb0.z; X.b[3] = xb0.w;
+  X.b[4] = xb1.x; X.b[5] = xb1.y; X.b[6] = xb1.z; X.b[7] = xb1.w;
+  X.xsa = xs[8 * b + 2 * g]; X.xsb = xs[8 * b + 2 * g + 1];
+  X.sma = xsum[8 * b + 2 * g]; X.smb = xsum[8 * b + 2 * g + 1];
+  return X;
+}
+
+__device__ __forceinline__ void q4k_unit(const uint8_t* st, int nrows, int m, const Q4X& X, float acc[4]) {
   const int lane = threadIdx.x & 31, bl = lane >> 2, g = lane & 3;
 #pragma unroll
   for (int r = 0; r < 4; r++) acc[r] = 0.f;
   if (bl >= m) return;
-  const int b = CHUNK_BLOCKS * c + bl, ja = 2 * g, jb = 2 * g + 1;
-  const int4* xa = reinterpret_cast<const int4*>(xq + 256 * b + 64 * g);
-  const int4 xa0 = xa[0], xa1 = xa[1], xb0 = xa[2], xb1 = xa[3];
-  const int xw_a[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
-  const int xw_b[8] = {xb0.x, xb0.y, xb0.z, xb0.w, xb1.x, xb1.y, xb1.z, xb1.w};
-  const float xsa = xs[8 * b + ja], xsb = xs[8 * b + jb];
-  const int sma = xsum[8 * b + ja], smb = xsum[8 * b + jb];
   const int shf = 8 * (g & 1);  // byte of j&3 inside the scale words, (2g)&3 = 2(g&1)
 #pragma unroll
   for (int r = 0; r < 4; r++) {
@@ -239,8 +287,8 @@ __device__ __forceinline__ void q4k_unit(const uint8_t* st, int nrows, int m, in
       int ia = 0, ib = 0;
 #pragma unroll
       for (int i = 0; i < 8; i++) {
-        ia = __dp4a((int)(qw[i] & 0x0F0F0F0Fu), xw_a[i], ia);
-        ib = __dp4a((int)((qw[i] >> 4) & 0x0F0F0F0Fu), xw_b[i], ib);
+        ia = __dp4a((int)(qw[i] & 0x0F0F0F0Fu), X.a[i], ia);
+        ib = __dp4a((int)((qw[i] >> 4) & 0x0F0F0F0Fu), X.b[i], ib);
       }
       const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
       // get_scale_min_k4 (src/quant.c:57-66) for j = 2g and 2g+1: scales[0..3]
@@ -258,8 +306,8 @@ __device__ __forceinline__ void q4k_unit(const uint8_t* st, int nrows, int m, in
       }
       // xs * (d*(s*iqx) - dmin*(m*ix)): the integer products are exact
       // (|s*iqx| <= 63*32*15*127 < 2^22) and become floats by exponent bias
-      acc[r] += xsa * (d * i22_to_float(sa * ia) - dmin * i22_to_float(ma * sma));
-      acc[r] += xsb * (d * i22_to_float(sb * ib) - dmin * i22_to_float(mb * smb));
+      acc[r] += X.xsa * (d * i22_to_float(sa * ia) - dmin * i22_to_float(ma * X.sma));
+      acc[r] += X.xsb * (d * i22_to_float(sb * ib) - dmin * i22_to_float(mb * X.smb));
     }
   }
 }
@@ -269,8 +317,27 @@ __device__ __forceinline__ void q4k_unit(const uint8_t* st, int nrows, int m, in
 // 128n + 16k + i (scale group 8n + k), high nibbles 128n + 64 + 16k + i (group
 // 8n + 4 + k); their two high bits sit in qh[32n + 16(k&1) + i] at bits 0/2
 // and 4/6 — the element map of dequant_q6_K (src/quant.c:94-123).
-__device__ __forceinline__ void q6k_unit(const uint8_t* st, int nrows, int m, int c, const float* xf,
-                                         float acc[4]) {
+struct Q6X {
+  float lo[2][16], hi[2][16];
+};
+
+__device__ __forceinline__ void q6x_load(const float* xf, int c, int nb, Q6X& X) {
+  const int lane = threadIdx.x & 31, bq = lane >> 3, n = (lane >> 2) & 1, k = lane & 3;
+#pragma unroll
+  for (int pass = 0; pass < 2; pass++) {
+    const int b = min(CHUNK_BLOCKS * c + 4 * pass + bq, nb - 1);
+    const float4* xl4 = reinterpret_cast<const float4*>(xf + 256 * b + 128 * n + 16 * k);
+    const float4* xh4 = reinterpret_cast<const float4*>(xf + 256 * b + 128 * n + 64 + 16 * k);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const float4 a = xl4[i], e = xh4[i];
+      X.lo[pass][4 * i] = a.x; X.lo[pass][4 * i + 1] = a.y; X.lo[pass][4 * i + 2] = a.z; X.lo[pass][4 * i + 3] = a.w;
+      X.hi[pass][4 * i] = e.x; X.hi[pass][4 * i + 1] = e.y; X.hi[pass][4 * i + 2] = e.z; X.hi[pass][4 * i + 3] = e.w;
+    }
+  }
+}
+
+__device__ __forceinline__ void q6k_unit(const uint8_t* st, int nrows, int m, const Q6X& X, float acc[4]) {
   const int lane = threadIdx.x & 31, bq = lane >> 3, n = (lane >> 2) & 1, k = lane & 3;
   const int sh_lo = (k < 2) ? 0 : 2, sh_hi = (k < 2) ? 4 : 6;
 #pragma unroll
@@ -279,16 +346,6 @@ __device__ __forceinline__ void q6k_unit(const uint8_t* st, int nrows, int m, in
   for (int pass = 0; pass < 2; pass++) {
     const int bl = 4 * pass + bq;
     if (bl >= m) continue;
-    const int b = CHUNK_BLOCKS * c + bl;
-    const float4* xl4 = reinterpret_cast<const float4*>(xf + 256 * b + 128 * n + 16 * k);
-    const float4* xh4 = reinterpret_cast<const float4*>(xf + 256 * b + 128 * n + 64 + 16 * k);
-    float xl[16], xh[16];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const float4 a = xl4[i], e = xh4[i];
-      xl[4 * i] = a.x; xl[4 * i + 1] = a.y; xl[4 * i + 2] = a.z; xl[4 * i + 3] = a.w;
-      xh[4 * i] = e.x; xh[4 * i + 1] = e.y; xh[4 * i + 2] = e.z; xh[4 * i + 3] = e.w;
-    }
 #pragma unroll
     for (int r = 0; r < 4; r++) {
       if (r < nrows) {
@@ -307,8 +364,8 @@ __device__ __forceinline__ void q6k_unit(const uint8_t* st, int nrows, int m, in
           const uint32_t hi = ((lw[i] >> 4) & 0x0F0F0F0Fu) | (((hw[i] >> sh_hi) & 0x03030303u) << 4);
 #pragma unroll
           for (int t = 0; t < 4; t++) {
-            slo = fmaf(q6_val(lo, t), xl[4 * i + t], slo);
-            shi = fmaf(q6_val(hi, t), xh[4 * i + t], shi);
+            slo = fmaf(q6_val(lo, t), X.lo[pass][4 * i + t], slo);
+            shi = fmaf(q6_val(hi, t), X.hi[pass][4 * i + t], shi);
           }
         }
         // scales: sc[8n + k] is byte k of word 0 of this half, sc[8n + 4 + k] byte k of word 1
@@ -413,13 +470,17 @@ __device__ void epilogue(const PhaseParams& p, const SegRange* sr, const float* 
 
 // ------------------------------------------------------------------ kernel
 
-template <int KINDS>
+// KINDS: bit 0 = Q4_K segments, bit 1 = Q6_K segments. CACHE: the lane's
+// activation slices stay in registers for the whole kernel (rows of at most
+// two chunks for Q4_K, one chunk for Q6_K); otherwise they are re-read from
+// shared memory per 4-row unit.
+template <int KINDS, bool CACHE>
 __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constant__ PhaseParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAX_STAGES;
   const int S_ = p.n_stages, SB = p.stage_bytes;
-  uint8_t* ring = smem + 128;
+  uint8_t* ring = smem + SMEM_HEADER;
   const int K = p.n_in, nb = K / QK, nsb = K / 32;
   float* xf = reinterpret_cast<float*>(ring + (size_t)S_ * SB);
   int8_t* xq = reinterpret_cast<int8_t*>(xf + K);
@@ -430,6 +491,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
 
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) TRACE(0);
   if (threadIdx.x == 0) {
     for (int i = 0; i < S_; i++) {
       mbar_init(smem_addr(&full[i]), 1);
@@ -472,6 +534,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
         }
       }
     }
+    if (lane == 0) TRACE(5);
     // drain: every copy this CTA issued must land before the CTA exits
     if (lane == 0) {
       for (int j = (i > S_ ? i - S_ : 0); j < i; j++)
@@ -479,9 +542,37 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
     }
   } else {
     // ---------------- consumers ----------------
+    // norm weights do not depend on the previous kernel: fetch them first
+    float wpre[RMS_SLOTS][8];
+#pragma unroll
+    for (int j = 0; j < RMS_SLOTS; j++) {
+      const int s = threadIdx.x - 32 + j * CONSUMER_WARPS * 32;
+      if (p.act == ACT_RMS && s < p.n_in / 8) {
+        const float4* w4 = reinterpret_cast<const float4*>(p.norm_w);
+        const float4 a = w4[2 * s], b = w4[2 * s + 1];
+        wpre[j][0] = a.x; wpre[j][1] = a.y; wpre[j][2] = a.z; wpre[j][3] = a.w;
+        wpre[j][4] = b.x; wpre[j][5] = b.y; wpre[j][6] = b.z; wpre[j][7] = b.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) wpre[j][i] = 0.f;
+      }
+    }
     pdl_wait();
-    build_activation(p, xf, xq, xs, xsum, red);
+    build_activation(p, wpre, xf, xq, xs, xsum, red);
+    if (threadIdx.x == 32) TRACE(1);
     const int cw = warp - 1, mine = cw >> 2, unit = cw & 3;
+    bool first = true;
+    // short rows: the lane's activation slice stays in registers for the kernel
+    const int nch_all = n_chunks(nb);
+    constexpr bool c4 = CACHE && (KINDS & 1);
+    constexpr bool c6 = CACHE && KINDS == 2;
+    Q4X x4c0, x4c1;
+    Q6X x6c;
+    if constexpr (c4) {
+      x4c0 = q4x_load(xq, xs, xsum, 0, nb);
+      x4c1 = nch_all > 1 ? q4x_load(xq, xs, xsum, 1, nb) : x4c0;
+    }
+    if constexpr (c6) q6x_load(xf, 0, nb, x6c);
     int i = 0;
     for (int s = 0; s < p.n_seg && !failed; s++) {
       const int type = (KINDS == 1) ? W_Q4K : (KINDS == 2) ? W_Q6K : p.seg[s].type;
@@ -491,15 +582,30 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
           if (i % GROUPS != mine) continue;
           const int slot = i % S_;
           if (!mbar_wait(smem_addr(&full[slot]), (i / S_) & 1)) { failed = true; break; }
+          if (first && threadIdx.x == 32) TRACE(2);
+          first = false;
           const int t0 = 4 * unit, nru = min(4, nr - t0);
           if (nru > 0) {
             const uint8_t* st = ring + (size_t)slot * SB;
             const int m = q6_chunk_blocks(nb, c);
             float acc[4];
+#pragma unroll
+            for (int r = 0; r < 4; r++) acc[r] = 0.f;
             if (type == W_Q4K) {
-              if constexpr (KINDS & 1) q4k_unit(st + t0 * Q4K_CHUNK, nru, m, c, xq, xs, xsum, acc);
+              if constexpr (KINDS & 1) {
+                if constexpr (c4) q4k_unit(st + t0 * Q4K_CHUNK, nru, m, c == 0 ? x4c0 : x4c1, acc);
+                else q4k_unit(st + t0 * Q4K_CHUNK, nru, m, q4x_load(xq, xs, xsum, c, nb), acc);
+              }
             } else {
-              if constexpr (KINDS & 2) q6k_unit(st + t0 * Q6K_CHUNK, nru, m, c, xf, acc);
+              if constexpr (KINDS & 2) {
+                if constexpr (c6) {
+                  q6k_unit(st + t0 * Q6K_CHUNK, nru, m, x6c, acc);
+                } else {
+                  Q6X X;
+                  q6x_load(xf, c, nb, X);
+                  q6k_unit(st + t0 * Q6K_CHUNK, nru, m, X, acc);
+                }
+              }
             }
             const float tot = reduce4(acc);
             if ((lane & 7) == 0 && (lane >> 3) < nru)
@@ -511,7 +617,9 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       }
     }
     consumers_sync();
+    if (threadIdx.x == 32) TRACE(3);
     if (!failed) epilogue(p, sr, part, red);
+    if (threadIdx.x == 32) TRACE(4);
   }
 
   if (failed && p.err_flag) atomicExch(p.err_flag, 1);
@@ -566,13 +674,13 @@ static size_t plan(PhaseParams& q, int grid) {
   }
   q.stage_bytes = TILE_ROWS * stride;
   q.part_floats = (part + 3) & ~3;
-  const size_t fixed = 128 + (size_t)K * 4 + K + (size_t)(K / 32) * 8 + (size_t)q.part_floats * 4 + 64 * 4;
+  const size_t fixed = SMEM_HEADER + (size_t)K * 4 + K + (size_t)(K / 32) * 8 + (size_t)q.part_floats * 4 + 64 * 4;
   // Stage i lives in slot i % S and is consumed by group i % GROUPS. S must
   // be a multiple of GROUPS: then every slot belongs to one group, which waits
   // on that slot's phases strictly in order — a parity wait can never see a
   // phase two behind and alias.
   const long avail = (long)PHASE_BUDGET - (long)fixed;
-  const int k = avail >= 2L * GROUPS * q.stage_bytes ? 2 : 1;
+  const int k = avail >= 3L * GROUPS * q.stage_bytes ? 3 : (avail >= 2L * GROUPS * q.stage_bytes ? 2 : 1);
   q.n_stages = k * GROUPS;
   return fixed + (size_t)q.n_stages * q.stage_bytes;
 }
@@ -582,13 +690,13 @@ size_t phase_smem_bytes(const PhaseParams& p, int grid) {
   return plan(q, grid);
 }
 
-template <int KINDS>
+template <int KINDS, bool CACHE>
 static cudaError_t launch_k(const PhaseParams& p, int grid, size_t smem, cudaStream_t s, bool pdl) {
   static unsigned done = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 32 && !(done & (1u << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(stream_kernel<KINDS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(stream_kernel<KINDS, CACHE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          PHASE_SMEM_MAX);
     if (e != cudaSuccess) return e;
     done |= 1u << dev;
@@ -603,18 +711,19 @@ static cudaError_t launch_k(const PhaseParams& p, int grid, size_t smem, cudaStr
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, stream_kernel<KINDS>, p);
+  return cudaLaunchKernelEx(&cfg, stream_kernel<KINDS, CACHE>, p);
 }
 
 cudaError_t launch_phase(const PhaseParams& p0, int num_sms, cudaStream_t s, bool pdl) {
   PhaseParams p = p0;
+  if (p.act == ACT_RMS && p.n_in > 8 * RMS_SLOTS * CONSUMER_WARPS * 32) return cudaErrorInvalidValue;
   const int grid = phase_grid_size(p, num_sms);
   const size_t smem = plan(p, grid);
   if (smem > (size_t)PHASE_SMEM_MAX || p.n_stages > MAX_STAGES) return cudaErrorInvalidValue;
-  const int kinds = phase_kinds(p);
-  if (kinds == 1) return launch_k<1>(p, grid, smem, s, pdl);
-  if (kinds == 2) return launch_k<2>(p, grid, smem, s, pdl);
-  return launch_k<3>(p, grid, smem, s, pdl);
+  const int kinds = phase_kinds(p), nch = n_chunks(p.n_in / QK);
+  if (kinds == 1) return nch <= 2 ? launch_k<1, true>(p, grid, smem, s, pdl) : launch_k<1, false>(p, grid, smem, s, pdl);
+  if (kinds == 2) return nch == 1 ? launch_k<2, true>(p, grid, smem, s, pdl) : launch_k<2, false>(p, grid, smem, s, pdl);
+  return nch <= 2 ? launch_k<3, true>(p, grid, smem, s, pdl) : launch_k<3, false>(p, grid, smem, s, pdl);
 }
 
 }  // namespace hakm

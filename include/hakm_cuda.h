@@ -112,6 +112,13 @@ int hakmc_fill_kv(hakmc_ctx *c, int seq, const float *k, const float *v, int n_p
  * No counterpart in the reference (measurement hook). */
 int hakmc_time_phase(hakmc_ctx *c, int phase, int iters, float *avg_ms);
 
+/* Measurement hook: run one launch of phase `phase` of layer `layer` (see
+ * hakmc_time_phase) with per-CTA %globaltimer stamps written to [host]
+ * stamps (n_ctas * 8 u64: start, prologue done, first stage ready, last unit
+ * done, epilogue done, producer done). Returns the CTA count or a negative
+ * code. No counterpart in the reference. */
+int hakmc_trace_phase(hakmc_ctx *c, int phase, int layer, unsigned long long *stamps, int max_ctas);
+
 /* Time of the last hakmc_forward / hakmc_generate / hakmc_forward_batch
  * call's device work in milliseconds (CUDA events on the context stream). */
 float hakmc_last_device_ms(const hakmc_ctx *c);
