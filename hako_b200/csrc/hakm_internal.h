@@ -79,7 +79,8 @@ struct PhaseParams {
   float eps;
   const int8_t* xq;      // ACT_Q8 input
   const float* xs;
-  int need_q8;           // some segment is Q4_K (quantize in the prologue)
+  int need_q8;           // some segment is Q4_K (int8 activation in the prologue)
+  int need_q6;           // some segment is Q6_K (fixed-point limbs in the prologue)
   int n_seg;
   Seg seg[MAX_SEGS];
   // filled by launch_phase: ring geometry and per-CTA partial-sum slots

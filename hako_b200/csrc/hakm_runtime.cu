@@ -263,8 +263,11 @@ static Seg make_seg(const DevMat& m, int epi, float* out) {
 
 static void finish_params(PhaseParams& p) {
   p.need_q8 = 0;
-  for (int i = 0; i < p.n_seg; i++)
+  p.need_q6 = 0;
+  for (int i = 0; i < p.n_seg; i++) {
     if (p.seg[i].type == W_Q4K) p.need_q8 = 1;
+    if (p.seg[i].type == W_Q6K) p.need_q6 = 1;
+  }
 }
 
 static unsigned long long* g_trace = nullptr;  // set only inside hakmc_trace_phase

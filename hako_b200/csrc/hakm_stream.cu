@@ -32,15 +32,17 @@ namespace hakm {
 
 constexpr int CONSUMER_WARPS = 12;
 constexpr int THREADS = 32 * (CONSUMER_WARPS + 1);
-constexpr int TILE_ROWS = 16;
-constexpr int UNITS = TILE_ROWS / 4;  // 4-row units per stage
-constexpr int GROUPS = CONSUMER_WARPS / UNITS;  // consumer groups, one stage each
+constexpr int TILE_ROWS = 16;         // most rows a stage holds
+constexpr int STAGE_TARGET = 40 * 1024;  // bytes a stage aims for
+constexpr int PHASE_BUDGET = 220 * 1024;  // dynamic shared memory a phase CTA may use
+// Consumer groups: stage i is consumed by group i % groups. Short rows (one
+// or two chunks) use 3 groups of 4 warps, so three stages are in work at
+// once; long rows use one group of all 12 warps on 8-row stages.
 constexpr int MAX_STAGES = 12;
 constexpr int SMEM_HEADER = 256;  // full[MAX_STAGES] and empty[MAX_STAGES] mbarriers
 constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clock
 constexpr int BAR_CONSUMERS = 1;
 constexpr int RMS_SLOTS = 2;  // 8-element slots per consumer thread in the rmsnorm prologue
-constexpr int PHASE_BUDGET = 220 * 1024;
 
 // ------------------------------------------------------------------ PTX
 
@@ -98,6 +100,39 @@ __device__ __forceinline__ void consumers_sync() {
 
 // ------------------------------------------------------------------ schedule
 
+// Limb planes of the Q6_K activation: 64 bytes of padding after every 128
+// elements (see struct Act).
+__host__ __device__ inline size_t limb_plane_bytes(int K) { return (size_t)K + (size_t)K / 2; }
+__device__ __forceinline__ int limb_pos(int e) { return e + 64 * (e >> 7); }
+
+// Shared-memory bytes of the activation for an n_in of K.
+__host__ __device__ inline size_t act_bytes(int K, bool q8, bool q6) {
+  size_t b = 0;
+  if (q8) b += (size_t)K + (size_t)(K / 32) * 8;
+  if (q6) b += 3 * limb_plane_bytes(K) + (size_t)(K / 16) * 8;
+  return b;
+}
+
+// Rows per stage for a segment: whole rows, as many (power of two, <= 16) as
+// fit STAGE_TARGET. A segment's rows are contiguous, so a stage is ONE bulk
+// copy: per-copy cost in the copy engine made 16 row-sized copies per stage
+// the bottleneck.
+__host__ __device__ inline int phase_groups(int nb) { return n_chunks(nb) >= 3 ? 1 : 3; }
+__host__ __device__ inline int stage_rows(int type, int nb) {
+  const size_t rb = dev_row_bytes(type, nb);
+  // long rows: up to twice the target, but two stages must fit beside the
+  // activation (fp32 + int8 copies, scales) in the shared-memory budget
+  const size_t act = act_bytes(nb * QK, true, true) + 8192;
+  size_t target = STAGE_TARGET;
+  if (phase_groups(nb) == 1) {
+    const size_t two = ((size_t)PHASE_BUDGET - act) / 2;
+    target = two < 2 * (size_t)STAGE_TARGET ? two : 2 * (size_t)STAGE_TARGET;
+  }
+  int r = TILE_ROWS;
+  while (r > 1 && (size_t)r * rb > target) r >>= 1;
+  return r;
+}
+
 struct SegRange {
   int row0, row1, nch, part_base;
 };
@@ -133,58 +168,117 @@ __device__ float consumers_sum(float v, float* red) {
   return warp_sum(t);
 }
 
-// 8-element slot s of the activation: fp32 values to xf, and for Q4_K rows the
-// per-32 int8 codes. The 4 slots of a 32-block are 4 adjacent lanes, so the
-// block max and code sum take two shuffles (quantize_row_q8_32 as built:
-// xs = amax * fl(1/127), q = rint(x * (127/amax)), src/quant.c:127-144).
-__device__ __forceinline__ void store_slot(const PhaseParams& p, int s, bool live, const float v[8], float* xf,
-                                           int8_t* xq, float* xs, int* xsum) {
-  if (live) {
-    reinterpret_cast<float4*>(xf)[2 * s] = make_float4(v[0], v[1], v[2], v[3]);
-    reinterpret_cast<float4*>(xf)[2 * s + 1] = make_float4(v[4], v[5], v[6], v[7]);
+// The activation in shared memory, in the two forms the row types consume:
+//  q8    (Q4_K rows): per-32 int8 codes xq, scales xs and code sums xsum —
+//        quantize_row_q8_32 as the reference builds it (src/quant.c:127-144).
+//  limbs (Q6_K rows): each 16-element group as exact 23-bit fixed point
+//        relative to its largest element, X = rint(x * 2^(22-E)), split into
+//        bytes X = X2*2^16 + X1*2^8 + X0 (X0, X1 unsigned, X2 signed) so the
+//        fp32-activation dot of the generic path (src/nn.c:84-95) becomes
+//        three int8 dot products; lp[g] = (32 * sum(X), 2^(E-22)). Planes
+//        put 64 bytes of padding after every 128 elements, which makes the
+//        lanes' 16-byte reads bank-conflict free.
+struct Act {
+  int8_t* xq;
+  float* xs;
+  int* xsum;
+  uint8_t* l0;
+  uint8_t* l1;
+  uint8_t* l2;
+  float2* lp;
+};
+
+
+__device__ __forceinline__ Act carve_act(uint8_t* base, int K, bool q8, bool q6) {
+  Act a = {};
+  uint8_t* p = base;
+  if (q6) {
+    a.lp = reinterpret_cast<float2*>(p);
+    p += (size_t)(K / 16) * 8;
+    a.l0 = p; p += limb_plane_bytes(K);
+    a.l1 = p; p += limb_plane_bytes(K);
+    a.l2 = p; p += limb_plane_bytes(K);
   }
-  if (!p.need_q8) return;
-  float amax = 0.f;
+  if (q8) {
+    a.xs = reinterpret_cast<float*>(p);
+    p += (size_t)(K / 32) * 4;
+    a.xsum = reinterpret_cast<int*>(p);
+    p += (size_t)(K / 32) * 4;
+    a.xq = reinterpret_cast<int8_t*>(p);
+  }
+  return a;
+}
+
+// 8-element slot s (elements [8s, 8s+8)). For q8 the 4 slots of a 32-block
+// are 4 adjacent lanes, for limbs the 2 slots of a 16-group 2 adjacent lanes,
+// so block and group reductions are one or two shuffles.
+__device__ __forceinline__ void store_slot(const PhaseParams& p, int s, bool live, const float v[8], const Act& A) {
+  float amax8 = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-  const float sc = amax * (1.0f / 127.0f);
-  const float inv = q8_inv(amax, sc);
-  int q[8], sum = 0;
+  for (int i = 0; i < 8; i++) amax8 = fmaxf(amax8, fabsf(v[i]));
+  if (p.need_q6) {
+    const float amax = fmaxf(amax8, __shfl_xor_sync(0xffffffffu, amax8, 1));
+    const uint32_t e = (__float_as_uint(amax) >> 23) & 0xFF;
+    const bool ok = e >= 22 && e < 255;  // groups below 2^-105 contribute nothing
+    const float f = ok ? __uint_as_float((275u - e) << 23) : 0.f;       // 2^(22-E)
+    const float invf = ok ? __uint_as_float((e - 21u) << 23) : 0.f;     // 2^(E-22)
+    uint32_t w0[2] = {0, 0}, w1[2] = {0, 0}, w2[2] = {0, 0};
+    int xsum16 = 0;
 #pragma unroll
-  for (int i = 0; i < 8; i++) { q[i] = q8_round(v[i] * inv); sum += q[i]; }
-  sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-  sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-  if (live) {
-    uint2 pk;
-    pk.x = (uint32_t)(q[0] & 255) | ((uint32_t)(q[1] & 255) << 8) | ((uint32_t)(q[2] & 255) << 16) |
-           ((uint32_t)(q[3] & 255) << 24);
-    pk.y = (uint32_t)(q[4] & 255) | ((uint32_t)(q[5] & 255) << 8) | ((uint32_t)(q[6] & 255) << 16) |
-           ((uint32_t)(q[7] & 255) << 24);
-    reinterpret_cast<uint2*>(xq)[s] = pk;
-    if ((s & 3) == 0) { xs[s >> 2] = sc; xsum[s >> 2] = sum; }
+    for (int i = 0; i < 8; i++) {
+      const int X = __float2int_rn(v[i] * f);  // exact scaling, |X| <= 2^22
+      xsum16 += X;
+      w0[i >> 2] |= (uint32_t)(X & 255) << (8 * (i & 3));
+      w1[i >> 2] |= (uint32_t)((X >> 8) & 255) << (8 * (i & 3));
+      w2[i >> 2] |= (uint32_t)((X >> 16) & 255) << (8 * (i & 3));
+    }
+    xsum16 += __shfl_xor_sync(0xffffffffu, xsum16, 1);
+    if (live) {
+      const int pos = limb_pos(8 * s);
+      *reinterpret_cast<uint2*>(A.l0 + pos) = make_uint2(w0[0], w0[1]);
+      *reinterpret_cast<uint2*>(A.l1 + pos) = make_uint2(w1[0], w1[1]);
+      *reinterpret_cast<uint2*>(A.l2 + pos) = make_uint2(w2[0], w2[1]);
+      if ((s & 1) == 0) A.lp[s >> 1] = make_float2(32.0f * (float)xsum16, invf);
+    }
+  }
+  if (p.need_q8) {
+    float amax = fmaxf(amax8, __shfl_xor_sync(0xffffffffu, amax8, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float sc = amax * (1.0f / 127.0f);
+    const float inv = q8_inv(amax, sc);
+    int q[8], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) { q[i] = q8_round(v[i] * inv); sum += q[i]; }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (live) {
+      uint2 pk;
+      pk.x = (uint32_t)(q[0] & 255) | ((uint32_t)(q[1] & 255) << 8) | ((uint32_t)(q[2] & 255) << 16) |
+             ((uint32_t)(q[3] & 255) << 24);
+      pk.y = (uint32_t)(q[4] & 255) | ((uint32_t)(q[5] & 255) << 8) | ((uint32_t)(q[6] & 255) << 16) |
+             ((uint32_t)(q[7] & 255) << 24);
+      reinterpret_cast<uint2*>(A.xq)[s] = pk;
+      if ((s & 3) == 0) { A.xs[s >> 2] = sc; A.xsum[s >> 2] = sum; }
+    }
   }
 }
 
-// Activation in shared memory: fp32 x (rmsnorm'ed for ACT_RMS) and, for Q4_K
-// segments, its per-32 int8 quantization with the per-block sums of xq.
-// ACT_RMS (K <= 8 * consumer threads): one slot per thread, the norm weights
-// already in registers (loaded before the dependency wait), one reduction.
-__device__ void build_activation(const PhaseParams& p, const float wpre[RMS_SLOTS][8], float* xf, int8_t* xq, float* xs,
-                                 int* xsum, float* red) {
+// Activation build. ACT_RMS (K <= 8 * RMS_SLOTS * consumer threads): the
+// norm weights are already in registers (loaded before the dependency wait)
+// and one block reduction gives the rms scale.
+__device__ void build_activation(const PhaseParams& p, const float wpre[RMS_SLOTS][8], const Act& A, float* red) {
   const int K = p.n_in, nsb = K >> 5, nslot = K >> 3;
   const int t = threadIdx.x - 32, nt = CONSUMER_WARPS * 32;
   const int lane = t & 31, w = t >> 5;
   if (p.act == ACT_Q8) {
     const int4* src = reinterpret_cast<const int4*>(p.xq);
-    int4* dst = reinterpret_cast<int4*>(xq);
+    int4* dst = reinterpret_cast<int4*>(A.xq);
     for (int i = t; i < K / 16; i += nt) dst[i] = src[i];
-    for (int i = t; i < nsb; i += nt) xs[i] = p.xs[i];
+    for (int i = t; i < nsb; i += nt) A.xs[i] = p.xs[i];
     consumers_sync();
     for (int b = w; b < nsb; b += CONSUMER_WARPS) {
-      const int s = warp_isum((int)xq[32 * b + lane]);
-      if (lane == 0) xsum[b] = s;
+      const int s = warp_isum((int)A.xq[32 * b + lane]);
+      if (lane == 0) A.xsum[b] = s;
     }
     consumers_sync();
     return;
@@ -216,7 +310,7 @@ __device__ void build_activation(const PhaseParams& p, const float wpre[RMS_SLOT
       if (j * nt >= nslot) break;  // uniform: no live slot for any thread
 #pragma unroll
       for (int i = 0; i < 8; i++) v[j][i] = v[j][i] * scale * wpre[j][i];
-      store_slot(p, s, s < nslot, v[j], xf, xq, xs, xsum);
+      store_slot(p, s, s < nslot, v[j], A);
     }
   } else {
     for (int s0 = 0; s0 < nslot; s0 += nt) {
@@ -230,7 +324,7 @@ __device__ void build_activation(const PhaseParams& p, const float wpre[RMS_SLOT
 #pragma unroll
         for (int i = 0; i < 8; i++) v[i] = 0.f;
       }
-      store_slot(p, s, live, v, xf, xq, xs, xsum);
+      store_slot(p, s, live, v, A);
     }
   }
   consumers_sync();
@@ -270,45 +364,46 @@ __device__ __forceinline__ Q4X q4x_load(const int8_t* xq, const float* xs, const
   return X;
 }
 
-__device__ __forceinline__ void q4k_unit(const uint8_t* st, int nrows, int m, const Q4X& X, float acc[4]) {
+__device__ __forceinline__ void q4k_unit(const uint8_t* st, int rstride, int nrows, int m, const Q4X& X,
+                                         float acc[4]) {
   const int lane = threadIdx.x & 31, bl = lane >> 2, g = lane & 3;
 #pragma unroll
   for (int r = 0; r < 4; r++) acc[r] = 0.f;
   if (bl >= m) return;
-  const int shf = 8 * (g & 1);  // byte of j&3 inside the scale words, (2g)&3 = 2(g&1)
+  // all four rows' loads first (rows past nrows re-read row 0, result unused)
+  uint4 hd[4], q0[4], q1[4];
 #pragma unroll
   for (int r = 0; r < 4; r++) {
-    if (r < nrows) {
-      const uint8_t* blk = st + r * Q4K_CHUNK + bl * Q4K_BYTES;
-      const uint4 hd = *reinterpret_cast<const uint4*>(blk);
-      const uint4 q0 = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g);
-      const uint4 q1 = *reinterpret_cast<const uint4*>(blk + 32 + 32 * g);
-      const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-      int ia = 0, ib = 0;
+    const uint8_t* blk = st + (r < nrows ? r : 0) * rstride + bl * Q4K_BYTES;
+    hd[r] = *reinterpret_cast<const uint4*>(blk);
+    q0[r] = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g);
+    q1[r] = *reinterpret_cast<const uint4*>(blk + 32 + 32 * g);
+  }
+  const int shf = 16 * (g & 1);  // scale bytes of j = 2g, 2g+1 within their words
+  const bool low = g < 2;        // j < 4: plain 6-bit fields (src/quant.c:59-61)
 #pragma unroll
-      for (int i = 0; i < 8; i++) {
-        ia = __dp4a((int)(qw[i] & 0x0F0F0F0Fu), X.a[i], ia);
-        ib = __dp4a((int)((qw[i] >> 4) & 0x0F0F0F0Fu), X.b[i], ib);
-      }
-      const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
-      // get_scale_min_k4 (src/quant.c:57-66) for j = 2g and 2g+1: scales[0..3]
-      // in hd.y, [4..7] in hd.z, [8..11] in hd.w; j < 4 iff g < 2
-      int sa, ma, sb, mb;
-      {
-        const uint32_t Y = hd.y >> (2 * shf), Z = hd.z >> (2 * shf), W = hd.w >> (2 * shf);
-        const uint32_t Y1 = Y >> 8, Z1 = Z >> 8, W1 = W >> 8;
-        if (g < 2) {
-          sa = Y & 63; ma = Z & 63; sb = Y1 & 63; mb = Z1 & 63;
-        } else {
-          sa = (W & 15) | ((Y >> 2) & 0x30); ma = ((W >> 4) & 15) | ((Z >> 2) & 0x30);
-          sb = (W1 & 15) | ((Y1 >> 2) & 0x30); mb = ((W1 >> 4) & 15) | ((Z1 >> 2) & 0x30);
-        }
-      }
-      // xs * (d*(s*iqx) - dmin*(m*ix)): the integer products are exact
-      // (|s*iqx| <= 63*32*15*127 < 2^22) and become floats by exponent bias
-      acc[r] += X.xsa * (d * i22_to_float(sa * ia) - dmin * i22_to_float(ma * X.sma));
-      acc[r] += X.xsb * (d * i22_to_float(sb * ib) - dmin * i22_to_float(mb * X.smb));
+  for (int r = 0; r < 4; r++) {
+    const uint32_t qw[8] = {q0[r].x, q0[r].y, q0[r].z, q0[r].w, q1[r].x, q1[r].y, q1[r].z, q1[r].w};
+    int ia = 0, ib = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      ia = __dp4a((int)(qw[i] & 0x0F0F0F0Fu), X.a[i], ia);
+      ib = __dp4a((int)((qw[i] >> 4) & 0x0F0F0F0Fu), X.b[i], ib);
     }
+    const float d = half_bits_to_float(hd[r].x), dmin = half_bits_to_float(hd[r].x >> 16);
+    // get_scale_min_k4 (src/quant.c:57-66) for j = 2g, 2g+1, branch-free:
+    // scales[0..3] in hd.y, [4..7] in hd.z, [8..11] in hd.w
+    const uint32_t Y = hd[r].y >> shf, Z = hd[r].z >> shf, W = hd[r].w >> shf;
+    const uint32_t Y1 = Y >> 8, Z1 = Z >> 8, W1 = W >> 8;
+    const int sa = low ? (Y & 63) : ((W & 15) | ((Y >> 2) & 0x30));
+    const int ma = low ? (Z & 63) : (((W >> 4) & 15) | ((Z >> 2) & 0x30));
+    const int sb = low ? (Y1 & 63) : ((W1 & 15) | ((Y1 >> 2) & 0x30));
+    const int mb = low ? (Z1 & 63) : (((W1 >> 4) & 15) | ((Z1 >> 2) & 0x30));
+    // xs * (d*(s*iqx) - dmin*(m*ix)): the integer products are exact
+    // (|s*iqx| <= 63*32*15*127 < 2^22) and become floats by exponent bias
+    float a = X.xsa * (d * i22_to_float(sa * ia) - dmin * i22_to_float(ma * X.sma));
+    a += X.xsb * (d * i22_to_float(sb * ib) - dmin * i22_to_float(mb * X.smb));
+    acc[r] = r < nrows ? a : 0.f;
   }
 }
 
@@ -317,27 +412,56 @@ __device__ __forceinline__ void q4k_unit(const uint8_t* st, int nrows, int m, co
 // 128n + 16k + i (scale group 8n + k), high nibbles 128n + 64 + 16k + i (group
 // 8n + 4 + k); their two high bits sit in qh[32n + 16(k&1) + i] at bits 0/2
 // and 4/6 — the element map of dequant_q6_K (src/quant.c:94-123).
-struct Q6X {
-  float lo[2][16], hi[2][16];
+struct Q6L {
+  uint4 l0[2][2], l1[2][2], l2[2][2];  // [pass][lo/hi group]
+  float2 lp[2][2];
 };
 
-__device__ __forceinline__ void q6x_load(const float* xf, int c, int nb, Q6X& X) {
+__device__ __forceinline__ void q6l_load(const Act& A, int c, int nb, Q6L& X) {
   const int lane = threadIdx.x & 31, bq = lane >> 3, n = (lane >> 2) & 1, k = lane & 3;
 #pragma unroll
   for (int pass = 0; pass < 2; pass++) {
     const int b = min(CHUNK_BLOCKS * c + 4 * pass + bq, nb - 1);
-    const float4* xl4 = reinterpret_cast<const float4*>(xf + 256 * b + 128 * n + 16 * k);
-    const float4* xh4 = reinterpret_cast<const float4*>(xf + 256 * b + 128 * n + 64 + 16 * k);
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const float4 a = xl4[i], e = xh4[i];
-      X.lo[pass][4 * i] = a.x; X.lo[pass][4 * i + 1] = a.y; X.lo[pass][4 * i + 2] = a.z; X.lo[pass][4 * i + 3] = a.w;
-      X.hi[pass][4 * i] = e.x; X.hi[pass][4 * i + 1] = e.y; X.hi[pass][4 * i + 2] = e.z; X.hi[pass][4 * i + 3] = e.w;
+    for (int h = 0; h < 2; h++) {
+      const int e = 256 * b + 128 * n + 64 * h + 16 * k;  // first element of the lane's group
+      const int pos = limb_pos(e);
+      X.l0[pass][h] = *reinterpret_cast<const uint4*>(A.l0 + pos);
+      X.l1[pass][h] = *reinterpret_cast<const uint4*>(A.l1 + pos);
+      X.l2[pass][h] = *reinterpret_cast<const uint4*>(A.l2 + pos);
+      X.lp[pass][h] = A.lp[e >> 4];
     }
   }
 }
 
-__device__ __forceinline__ void q6k_unit(const uint8_t* st, int nrows, int m, const Q6X& X, float acc[4]) {
+// sum over 16 codes of q * X for one limb plane: 4 dp4a
+__device__ __forceinline__ int dot16u(const uint32_t q[4], const uint4& l) {
+  unsigned r = __dp4a(q[0], l.x, 0u);
+  r = __dp4a(q[1], l.y, r);
+  r = __dp4a(q[2], l.z, r);
+  r = __dp4a(q[3], l.w, r);
+  return (int)r;
+}
+__device__ __forceinline__ int dot16s(const uint32_t q[4], const uint4& l) {
+  int r = __dp4a((int)q[0], (int)l.x, 0);
+  r = __dp4a((int)q[1], (int)l.y, r);
+  r = __dp4a((int)q[2], (int)l.z, r);
+  r = __dp4a((int)q[3], (int)l.w, r);
+  return r;
+}
+
+// sum((q - 32) * X) of one 16-group from its three limb dot products; the
+// partial sums are exact integers below 2^22, the combine is fp32
+__device__ __forceinline__ float group_dot(const uint32_t q[4], const uint4& l0, const uint4& l1, const uint4& l2,
+                                           float xs32) {
+  const float s0 = i22_to_float(dot16u(q, l0));
+  const float s1 = i22_to_float(dot16u(q, l1));
+  const float s2 = i22_to_float(dot16s(q, l2));
+  return fmaf(s2, 65536.0f, fmaf(s1, 256.0f, s0)) - xs32;
+}
+
+__device__ __forceinline__ void q6k_unit(const uint8_t* st, int rstride, int nrows, int m, const Q6L& X,
+                                         float acc[4]) {
   const int lane = threadIdx.x & 31, bq = lane >> 3, n = (lane >> 2) & 1, k = lane & 3;
   const int sh_lo = (k < 2) ? 0 : 2, sh_hi = (k < 2) ? 4 : 6;
 #pragma unroll
@@ -346,32 +470,34 @@ __device__ __forceinline__ void q6k_unit(const uint8_t* st, int nrows, int m, co
   for (int pass = 0; pass < 2; pass++) {
     const int bl = 4 * pass + bq;
     if (bl >= m) continue;
+    uint4 ql[4], qh[4];
+    uint2 sc[4];
+    float d[4];
+#pragma unroll
+    for (int r = 0; r < 4; r++) {  // rows past nrows re-read row 0, result unused
+      const uint8_t* chunk = st + (r < nrows ? r : 0) * rstride;
+      const uint8_t* body = chunk + bl * Q6K_BODY;
+      ql[r] = *reinterpret_cast<const uint4*>(body + 64 * n + 16 * k);
+      qh[r] = *reinterpret_cast<const uint4*>(body + 128 + 32 * n + 16 * (k & 1));
+      sc[r] = *reinterpret_cast<const uint2*>(body + 192 + 8 * n);
+      d[r] = __half2float(*reinterpret_cast<const __half*>(chunk + m * Q6K_BODY + 2 * bl));
+    }
 #pragma unroll
     for (int r = 0; r < 4; r++) {
-      if (r < nrows) {
-        const uint8_t* chunk = st + r * Q6K_CHUNK;
-        const uint8_t* body = chunk + bl * Q6K_BODY;
-        const uint4 ql = *reinterpret_cast<const uint4*>(body + 64 * n + 16 * k);
-        const uint4 qh = *reinterpret_cast<const uint4*>(body + 128 + 32 * n + 16 * (k & 1));
-        const uint2 sc = *reinterpret_cast<const uint2*>(body + 192 + 8 * n);
-        const float d = __half2float(*reinterpret_cast<const __half*>(chunk + m * Q6K_BODY + 2 * bl));
-        const uint32_t lw[4] = {ql.x, ql.y, ql.z, ql.w};
-        const uint32_t hw[4] = {qh.x, qh.y, qh.z, qh.w};
-        float slo = 0.f, shi = 0.f;
+      const uint32_t lw[4] = {ql[r].x, ql[r].y, ql[r].z, ql[r].w};
+      const uint32_t hw[4] = {qh[r].x, qh[r].y, qh[r].z, qh[r].w};
+      uint32_t qlo[4], qhi[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const uint32_t lo = (lw[i] & 0x0F0F0F0Fu) | (((hw[i] >> sh_lo) & 0x03030303u) << 4);
-          const uint32_t hi = ((lw[i] >> 4) & 0x0F0F0F0Fu) | (((hw[i] >> sh_hi) & 0x03030303u) << 4);
-#pragma unroll
-          for (int t = 0; t < 4; t++) {
-            slo = fmaf(q6_val(lo, t), X.lo[pass][4 * i + t], slo);
-            shi = fmaf(q6_val(hi, t), X.hi[pass][4 * i + t], shi);
-          }
-        }
-        // scales: sc[8n + k] is byte k of word 0 of this half, sc[8n + 4 + k] byte k of word 1
-        const float sl = (float)(int8_t)(sc.x >> (8 * k)), sh = (float)(int8_t)(sc.y >> (8 * k));
-        acc[r] += d * sl * slo + d * sh * shi;
+      for (int i = 0; i < 4; i++) {
+        qlo[i] = (lw[i] & 0x0F0F0F0Fu) | (((hw[i] >> sh_lo) << 4) & 0x30303030u);
+        qhi[i] = ((lw[i] >> 4) & 0x0F0F0F0Fu) | (((hw[i] >> sh_hi) << 4) & 0x30303030u);
       }
+      const float tlo = group_dot(qlo, X.l0[pass][0], X.l1[pass][0], X.l2[pass][0], X.lp[pass][0].x);
+      const float thi = group_dot(qhi, X.l0[pass][1], X.l1[pass][1], X.l2[pass][1], X.lp[pass][1].x);
+      // scales: sc[8n + k] is byte k of word 0 of this half, sc[8n + 4 + k] byte k of word 1
+      const float sl = (float)(int8_t)(sc[r].x >> (8 * k)), sh = (float)(int8_t)(sc[r].y >> (8 * k));
+      const float v = d[r] * (sl * X.lp[pass][0].y * tlo + sh * X.lp[pass][1].y * thi);
+      acc[r] += r < nrows ? v : 0.f;
     }
   }
 }
@@ -482,12 +608,11 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
   const int S_ = p.n_stages, SB = p.stage_bytes;
   uint8_t* ring = smem + SMEM_HEADER;
   const int K = p.n_in, nb = K / QK, nsb = K / 32;
-  float* xf = reinterpret_cast<float*>(ring + (size_t)S_ * SB);
-  int8_t* xq = reinterpret_cast<int8_t*>(xf + K);
-  float* xs = reinterpret_cast<float*>(xq + K);
-  int* xsum = reinterpret_cast<int*>(xs + nsb);
-  float* part = reinterpret_cast<float*>(xsum + nsb);
+  uint8_t* act = ring + (size_t)S_ * SB;
+  const Act A = carve_act(act, K, p.need_q8, p.need_q6);
+  float* part = reinterpret_cast<float*>(act + act_bytes(K, p.need_q8, p.need_q6));
   float* red = part + p.part_floats;
+  (void)nsb;
 
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -495,7 +620,7 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
   if (threadIdx.x == 0) {
     for (int i = 0; i < S_; i++) {
       mbar_init(smem_addr(&full[i]), 1);
-      mbar_init(smem_addr(&empty[i]), UNITS);
+      mbar_init(smem_addr(&empty[i]), CONSUMER_WARPS / phase_groups(nb));
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -513,25 +638,22 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       const Seg& S = p.seg[s];
       const int type = (KINDS == 1) ? W_Q4K : (KINDS == 2) ? W_Q6K : S.type;
       const size_t rowB = dev_row_bytes(type, nb);
-      const int stride = type == W_Q4K ? Q4K_CHUNK : Q6K_CHUNK;
-      for (int rt = sr[s].row0; rt < sr[s].row1 && !failed; rt += TILE_ROWS) {
-        const int nr = min(TILE_ROWS, sr[s].row1 - rt);
-        for (int c = 0; c < sr[s].nch; c++, i++) {
-          const int slot = i % S_;
-          if (i >= S_) {
-            bool ok = true;
-            if (lane == 0) ok = mbar_wait(smem_addr(&empty[slot]), ((i / S_) - 1) & 1);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) { failed = true; break; }
-          }
-          const int cb = chunk_bytes(type, nb, c);
-          if (lane == 0) mbar_expect_tx(smem_addr(&full[slot]), (uint32_t)(nr * cb));
-          __syncwarp();
-          if (lane < nr)
-            bulk_g2s(smem_addr(ring + (size_t)slot * SB + lane * stride),
-                     S.w + (size_t)(rt + lane) * rowB + (size_t)c * stride, (uint32_t)cb,
-                     smem_addr(&full[slot]));
+      const int R = stage_rows(type, nb);
+      for (int rt = sr[s].row0; rt < sr[s].row1; rt += R, i++) {
+        const int nr = min(R, sr[s].row1 - rt);
+        const int slot = i % S_;
+        if (i >= S_) {
+          bool ok = true;
+          if (lane == 0) ok = mbar_wait(smem_addr(&empty[slot]), ((i / S_) - 1) & 1);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) { failed = true; break; }
         }
+        if (lane == 0) {
+          const uint32_t bytes = (uint32_t)(nr * rowB);
+          mbar_expect_tx(smem_addr(&full[slot]), bytes);
+          bulk_g2s(smem_addr(ring + (size_t)slot * SB), S.w + (size_t)rt * rowB, bytes, smem_addr(&full[slot]));
+        }
+        __syncwarp();
       }
     }
     if (lane == 0) TRACE(5);
@@ -558,62 +680,67 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
       }
     }
     pdl_wait();
-    build_activation(p, wpre, xf, xq, xs, xsum, red);
+    build_activation(p, wpre, A, red);
     if (threadIdx.x == 32) TRACE(1);
-    const int cw = warp - 1, mine = cw >> 2, unit = cw & 3;
+    const int groups = phase_groups(nb), wpg = CONSUMER_WARPS / groups;
+    const int cw = warp - 1, mine = cw / wpg, unit = cw % wpg;
     bool first = true;
     // short rows: the lane's activation slice stays in registers for the kernel
     const int nch_all = n_chunks(nb);
     constexpr bool c4 = CACHE && (KINDS & 1);
     constexpr bool c6 = CACHE && KINDS == 2;
     Q4X x4c0, x4c1;
-    Q6X x6c;
+    Q6L x6c;
     if constexpr (c4) {
-      x4c0 = q4x_load(xq, xs, xsum, 0, nb);
-      x4c1 = nch_all > 1 ? q4x_load(xq, xs, xsum, 1, nb) : x4c0;
+      x4c0 = q4x_load(A.xq, A.xs, A.xsum, 0, nb);
+      x4c1 = nch_all > 1 ? q4x_load(A.xq, A.xs, A.xsum, 1, nb) : x4c0;
     }
-    if constexpr (c6) q6x_load(xf, 0, nb, x6c);
+    if constexpr (c6) q6l_load(A, 0, nb, x6c);
     int i = 0;
     for (int s = 0; s < p.n_seg && !failed; s++) {
       const int type = (KINDS == 1) ? W_Q4K : (KINDS == 2) ? W_Q6K : p.seg[s].type;
-      for (int rt = sr[s].row0; rt < sr[s].row1 && !failed; rt += TILE_ROWS) {
-        const int nr = min(TILE_ROWS, sr[s].row1 - rt);
-        for (int c = 0; c < sr[s].nch; c++, i++) {
-          if (i % GROUPS != mine) continue;
-          const int slot = i % S_;
-          if (!mbar_wait(smem_addr(&full[slot]), (i / S_) & 1)) { failed = true; break; }
-          if (first && threadIdx.x == 32) TRACE(2);
-          first = false;
-          const int t0 = 4 * unit, nru = min(4, nr - t0);
-          if (nru > 0) {
-            const uint8_t* st = ring + (size_t)slot * SB;
-            const int m = q6_chunk_blocks(nb, c);
-            float acc[4];
+      const int rowB = (int)dev_row_bytes(type, nb);
+      const int R = stage_rows(type, nb), nch = sr[s].nch;
+      const int chunkB = type == W_Q4K ? Q4K_CHUNK : Q6K_CHUNK;
+      const int n_units = ((R + 3) / 4) * nch;  // (4-row group, chunk) cells of a stage
+      for (int rt = sr[s].row0; rt < sr[s].row1; rt += R, i++) {
+        if (i % groups != mine) continue;
+        const int nr = min(R, sr[s].row1 - rt);
+        const int slot = i % S_;
+        if (!mbar_wait(smem_addr(&full[slot]), (i / S_) & 1)) { failed = true; break; }
+        if (first && threadIdx.x == 32) TRACE(2);
+        first = false;
+        const uint8_t* stage = ring + (size_t)slot * SB;
+        for (int u = unit; u < n_units; u += wpg) {
+          const int c = u % nch, t0 = 4 * (u / nch), nru = min(4, nr - t0);
+          if (nru <= 0) continue;
+          const uint8_t* st = stage + (size_t)t0 * rowB + (size_t)c * chunkB;
+          const int m = q6_chunk_blocks(nb, c);
+          float acc[4];
 #pragma unroll
-            for (int r = 0; r < 4; r++) acc[r] = 0.f;
-            if (type == W_Q4K) {
-              if constexpr (KINDS & 1) {
-                if constexpr (c4) q4k_unit(st + t0 * Q4K_CHUNK, nru, m, c == 0 ? x4c0 : x4c1, acc);
-                else q4k_unit(st + t0 * Q4K_CHUNK, nru, m, q4x_load(xq, xs, xsum, c, nb), acc);
-              }
-            } else {
-              if constexpr (KINDS & 2) {
-                if constexpr (c6) {
-                  q6k_unit(st + t0 * Q6K_CHUNK, nru, m, x6c, acc);
-                } else {
-                  Q6X X;
-                  q6x_load(xf, c, nb, X);
-                  q6k_unit(st + t0 * Q6K_CHUNK, nru, m, X, acc);
-                }
+          for (int r = 0; r < 4; r++) acc[r] = 0.f;
+          if (type == W_Q4K) {
+            if constexpr (KINDS & 1) {
+              if constexpr (c4) q4k_unit(st, rowB, nru, m, c == 0 ? x4c0 : x4c1, acc);
+              else q4k_unit(st, rowB, nru, m, q4x_load(A.xq, A.xs, A.xsum, c, nb), acc);
+            }
+          } else {
+            if constexpr (KINDS & 2) {
+              if constexpr (c6) {
+                q6k_unit(st, rowB, nru, m, x6c, acc);
+              } else {
+                Q6L X;
+                q6l_load(A, c, nb, X);
+                q6k_unit(st, rowB, nru, m, X, acc);
               }
             }
-            const float tot = reduce4(acc);
-            if ((lane & 7) == 0 && (lane >> 3) < nru)
-              part[sr[s].part_base + (rt - sr[s].row0 + t0 + (lane >> 3)) * sr[s].nch + c] = tot;
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_addr(&empty[slot]));
+          const float tot = reduce4(acc);
+          if ((lane & 7) == 0 && (lane >> 3) < nru)
+            part[sr[s].part_base + (rt - sr[s].row0 + t0 + (lane >> 3)) * nch + c] = tot;
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&empty[slot]));
       }
     }
     consumers_sync();
@@ -665,23 +792,28 @@ static int phase_grid_size(const PhaseParams& p, int num_sms) {
 // Fills n_stages / stage_bytes / part_floats; returns the dynamic smem size.
 static size_t plan(PhaseParams& q, int grid) {
   const int K = q.n_in, nb = K / QK;
-  int stride = 0, part = 0;
+  size_t slot = 0;
+  int part = 0;
   for (int s = 0; s < q.n_seg; s++) {
-    const int st = q.seg[s].type == W_Q4K ? Q4K_CHUNK : Q6K_CHUNK;
-    stride = st > stride ? st : stride;
+    const size_t sb = (size_t)stage_rows(q.seg[s].type, nb) * dev_row_bytes(q.seg[s].type, nb);
+    slot = sb > slot ? sb : slot;
     const int G = (q.seg[s].n_rows + 3) / 4;
     part += ((G + grid - 1) / grid) * 4 * n_chunks(nb);
   }
-  q.stage_bytes = TILE_ROWS * stride;
+  q.stage_bytes = (int)slot;
   q.part_floats = (part + 3) & ~3;
-  const size_t fixed = SMEM_HEADER + (size_t)K * 4 + K + (size_t)(K / 32) * 8 + (size_t)q.part_floats * 4 + 64 * 4;
-  // Stage i lives in slot i % S and is consumed by group i % GROUPS. S must
-  // be a multiple of GROUPS: then every slot belongs to one group, which waits
+  const size_t fixed = SMEM_HEADER + act_bytes(K, q.need_q8, q.need_q6) + (size_t)q.part_floats * 4 + 64 * 4;
+  // Stage i lives in slot i % S and is consumed by group i % groups. S must
+  // be a multiple of groups: then every slot belongs to one group, which waits
   // on that slot's phases strictly in order — a parity wait can never see a
   // phase two behind and alias.
+  const int groups = phase_groups(nb);
   const long avail = (long)PHASE_BUDGET - (long)fixed;
-  const int k = avail >= 3L * GROUPS * q.stage_bytes ? 3 : (avail >= 2L * GROUPS * q.stage_bytes ? 2 : 1);
-  q.n_stages = k * GROUPS;
+  int k = (int)(avail / ((long)groups * q.stage_bytes));
+  const int kmax = groups == 1 ? 6 : 3;
+  k = k < 1 ? 1 : (k > kmax ? kmax : k);
+  if (groups == 1 && k < 2 && avail >= 2L * q.stage_bytes) k = 2;
+  q.n_stages = k * groups;
   return fixed + (size_t)q.n_stages * q.stage_bytes;
 }
 
