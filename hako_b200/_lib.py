@@ -48,6 +48,7 @@ SIGNATURES = {
     "hakmc_rmsnorm": (_i, [_vp, _vp, _vp, _i, _f, _vp]),
     "hakmc_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "hakmc_rope_neox": (_i, [_vp, _i, _i, _i, _f, _vp]),
+    "hakmc_attention_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
 }
 
 

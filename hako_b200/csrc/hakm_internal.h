@@ -135,6 +135,10 @@ struct AttnParams {
 };
 constexpr int ATTN_CHUNK = 64;   // positions per attention CTA
 cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl);
+// hakmc_attention_noalloc: scratch in a static device array, no allocation
+cudaError_t attention_noalloc(float* out, const float* q, const float* kc, const float* vc, int pos, int n_heads,
+                              int n_kv, int head_dim, cudaStream_t stream);
+size_t noalloc_part_floats();
 size_t attention_scratch_floats(int n_kv, int n_split, int group, int head_dim);
 
 }  // namespace hakm

@@ -4,6 +4,8 @@
 // attention. The streaming GEMV phases live in hakm_stream.cu.
 #include "hakm_device.cuh"
 
+#include <mutex>
+
 namespace hakm {
 
 // Block-wide sum over blockDim.x threads (<= 1024). `red` holds 32 floats.
@@ -358,6 +360,62 @@ cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl) {
   if (a.head_dim == 128) return launch_attn<128>(a, s, pdl);
   if (a.head_dim == 64) return launch_attn<64>(a, s, pdl);
   return cudaErrorInvalidValue;
+}
+
+// ------------------------------------------------------------ allocation-free attention
+
+// Scratch of hakmc_attention_noalloc: split partials, per-kv-head tickets and
+// the position word, in one file-scope device array. Every GPU that loads the
+// library holds it (about 1 MiB) until the process exits.
+constexpr size_t NOALLOC_PART_FLOATS = 256 * 1024;  // 1 MiB of split partials
+constexpr int NOALLOC_TICKETS = 64;
+struct NoAllocScratch {
+  float part[NOALLOC_PART_FLOATS];
+  unsigned tickets[NOALLOC_TICKETS];
+  int pos;
+};
+static __device__ __align__(256) NoAllocScratch g_noalloc;
+
+// Host code cannot use &g_noalloc (a host-side stand-in, not a device
+// address): the device address comes from cudaGetSymbolAddress, once per
+// device, with that device current.
+static std::mutex g_noalloc_mu;
+static NoAllocScratch* g_noalloc_dev[64];
+
+__global__ void noalloc_prepare_kernel(NoAllocScratch* s, int pos) {
+  if (threadIdx.x < NOALLOC_TICKETS) s->tickets[threadIdx.x] = 0u;  // must start at zero
+  if (threadIdx.x == 0) s->pos = pos;
+}
+
+size_t noalloc_part_floats() { return NOALLOC_PART_FLOATS; }
+
+cudaError_t attention_noalloc(float* out, const float* q, const float* kc, const float* vc, int pos, int n_heads,
+                              int n_kv, int head_dim, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  NoAllocScratch* s = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_dev[dev]) {
+      void* ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_noalloc);
+      if (e != cudaSuccess) return e;
+      g_noalloc_dev[dev] = static_cast<NoAllocScratch*>(ptr);
+    }
+    s = g_noalloc_dev[dev];
+  }
+  noalloc_prepare_kernel<<<1, NOALLOC_TICKETS, 0, stream>>>(s, pos);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  AttnParams a = {};
+  a.q = q; a.k_cache = kc; a.v_cache = vc; a.out = out; a.pos_dev = &s->pos;
+  a.n_heads = n_heads; a.n_kv = n_kv; a.head_dim = head_dim; a.scale = 1.0f / sqrtf((float)head_dim);
+  a.n_split = pos / ATTN_CHUNK + 1;
+  a.part = s->part;
+  a.counters = s->tickets;
+  return launch_attention(a, stream, false);
 }
 
 }  // namespace hakm

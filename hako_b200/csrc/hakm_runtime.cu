@@ -964,6 +964,24 @@ extern "C" int hakmc_attention(float* out, const float* q, const float* kc, cons
   return 0;
 }
 
+extern "C" int hakmc_attention_noalloc(float* out, const float* q, const float* kc, const float* vc, int pos,
+                                       int n_heads, int n_kv, int head_dim, void* stream) {
+  if (!out || !q || !kc || !vc || pos < 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > 8 ||
+      (head_dim != 64 && head_dim != 128) || n_kv > 64) {
+    set_err("attention_noalloc: unsupported arguments");
+    return HAKMC_EINVAL;
+  }
+  const int n_split = pos / ATTN_CHUNK + 1;
+  const size_t need = attention_scratch_floats(n_kv, n_split, n_heads / n_kv, head_dim);
+  if (need > noalloc_part_floats()) {
+    set_err("attention_noalloc: %d heads x %d positions need %zu scratch floats, the fixed array holds %zu "
+            "(use hakmc_attention)", n_heads, pos + 1, need, noalloc_part_floats());
+    return HAKMC_ERANGE;
+  }
+  CKL(attention_noalloc(out, q, kc, vc, pos, n_heads, n_kv, head_dim, (cudaStream_t)stream));
+  return 0;
+}
+
 extern "C" int hakmc_rope_neox(float* x, int n_heads, int head_dim, int pos, float theta, void* stream) {
   if (!x || n_heads <= 0 || head_dim <= 0 || head_dim % 2 || pos < 0) return HAKMC_EINVAL;
   const int half = head_dim / 2;

@@ -188,6 +188,23 @@ int hakmc_rmsnorm(float *y, const float *x, const float *w, int n, float eps, vo
 int hakmc_attention(float *out, const float *q, const float *k_cache, const float *v_cache,
                     int pos, int n_heads, int n_kv, int head_dim, void *stream);
 
+/* hakmc_attention without any device allocation, for callers that cannot
+ * allocate GPU memory once they are running: a host that has handed the
+ * whole device budget to another framework's memory pool, or a latency-bound
+ * loop that must not take cudaMalloc's implicit device synchronisation. It
+ * launches the same kernel as hakmc_attention, but its scratch (split
+ * partials, tickets, the position word) lives in one fixed array of about
+ * 1 MiB inside this library, which every GPU that loads the library holds
+ * until the process exits. Limit: n_heads * ceil((pos + 1) / 64) *
+ * (head_dim + 2) <= 262144 floats (for example 16 heads of 128 up to 8064
+ * positions, 28 heads up to 4608); larger calls return HAKMC_ERANGE. The
+ * first call on a device looks the array up (cudaGetSymbolAddress), so make
+ * it before any stream capture. All calls share the array and it keeps the
+ * last call's contents: calls that overlap on the GPU (other streams, other
+ * threads) race, so serialise them. No counterpart in the reference. */
+int hakmc_attention_noalloc(float *out, const float *q, const float *k_cache, const float *v_cache,
+                            int pos, int n_heads, int n_kv, int head_dim, void *stream);
+
 /* NeoX RoPE in place on n_heads heads of head_dim at position pos
  * (src/nn.c:32-42), angles from a table built on the host with the
  * reference's formula. */
