@@ -31,6 +31,7 @@ SIGNATURES = {
     "hakmc_decode": (_i, [_vp, _i, _vp]),
     "hakmc_time_phase": (_i, [_vp, _i, _i, _vp]),
     "hakmc_trace_phase": (_i, [_vp, _i, _i, _vp, _i]),
+    "hakmc_trace_step": (_i, [_vp, _vp, _i]),
     "hakmc_set_layers": (_i, [_vp, _i]),
     "hakmc_hidden": (_i, [_vp, _i, _vp]),
     "hakmc_fill_kv": (_i, [_vp, _i, _vp, _vp, _i]),

@@ -34,12 +34,14 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t h16) {
 
 // Float -> int8 as the reference's (int)lrintf + clamp compiles with its own
 // flags (src/quant.c:138-141): round half to even through a 64-bit
-// conversion truncated to 32 bits, so NaN / out-of-range (INT64_MIN) give 0.
+// conversion truncated to 32 bits; NaN and infinities give 0 (the 64-bit
+// result is INT64_MIN). Here r = x * (127/amax) with |x| <= amax, so r is
+// either within 127 * (1 + 2^-22), or infinite (127/amax overflowed for
+// amax < 2^-121), or NaN: on that set a 32-bit round-to-nearest-even
+// conversion behind a range check gives the same integers.
 __device__ __forceinline__ int q8_round(float r) {
-  if (!(fabsf(r) < 9223372036854775808.0f)) return 0;
-  const long long v = __float2ll_rn(r);
-  const int v32 = (int)(unsigned)((unsigned long long)v & 0xFFFFFFFFull);
-  return v32 > 127 ? 127 : (v32 < -127 ? -127 : v32);
+  const int v = fabsf(r) < 2147483648.0f ? __float2int_rn(r) : 0;
+  return v > 127 ? 127 : (v < -127 ? -127 : v);
 }
 
 // Per-32 quantization step of quantize_row_q8_32 as built with -ffast-math:

@@ -141,4 +141,74 @@ cudaError_t attention_noalloc(float* out, const float* q, const float* kc, const
 size_t noalloc_part_floats();
 size_t attention_scratch_floats(int n_kv, int n_split, int group, int head_dim);
 
+// Rows of one segment that one CTA computes, and where its per-(row, chunk)
+// partial sums start in shared memory.
+struct SegRange {
+  int row0, row1, nch, part_base;
+};
+
+// ---- persistent decode-step kernel (hakm_step.cu) ----
+enum PhaseKind { PK_GEMV = 0, PK_ATTN = 1 };
+
+// One phase of the device-resident step program. Phases exchange vectors as
+// tagged words: uint64 = (tag << 32) | float bits, tag = tag_base + step *
+// (n_phases + 1) + index of the writing phase (0 = embedding, prog[i] = i+1).
+struct PhaseDesc {
+  int kind;          // PhaseKind
+  int skip_forced;   // skipped on forced (prompt) steps whose pick is not needed: lm_head
+  PhaseParams g;     // PK_GEMV geometry, weights, biases, caches, norm and rope tables
+  AttnParams a;      // PK_ATTN geometry, caches, split scratch (n_split / pos_dev / q / out unused)
+  const uint64_t* x_ll;  // input vector (GEMV activation; attention q)
+  int x_src;             // index of the phase that wrote it
+  const uint64_t* res_ll;  // EPI_RESID: previous residual; attention: current k row
+  int res_src;
+  const uint64_t* v_ll;  // attention: current v row (written by phase x_src)
+  uint64_t* out_ll[MAX_SEGS];  // per segment: q / v / xb / h; attention: att
+  uint64_t* out2_ll;     // EPI_ROPE_QK: k
+  int layer;             // attention: layer index (split tickets)
+};
+
+struct StepArgs {
+  const PhaseDesc* prog;   // device array, n_phases entries (one decode step)
+  int n_phases;
+  int n_steps;             // decode steps run by the launch
+  int pos0;                // position of step 0
+  int n_forced;            // steps 0..n_forced-1 take forced[step] as input token
+  const int* forced;
+  int* token_dev;          // in: input of step 0 when n_forced == 0; out: last pick
+  int* pos_dev;            // out: pos0 + n_steps
+  int* token_log;          // pick of step j at token_log[j - log_base] (may be null)
+  int token_log_cap;
+  int log_base;
+  unsigned long long* keys;  // [3] running argmax keys, by step % 3
+  unsigned int* bar;       // step barrier counter, zero at launch
+  unsigned int* tickets;   // attention split tickets [n_kv], zero at launch, monotonic
+  const SegRange* ranges;  // [n_phases][grid][MAX_SEGS]: each CTA's rows of each GEMV phase
+  int* err_flag;
+  const uint8_t* tok_embd; // Q6_K embedding rows (device layout)
+  uint64_t* xb_ll;         // embedding output (xb buffer 0)
+  float* xb_plain;         // final residual as plain floats (CTA 0, lm_head phase)
+  int D;
+  int n_layers;            // attention phases per step (split tickets)
+  int skip_last;           // the last phase (lm_head) is skipped on forced steps but the last
+  int head_dim;            // attention head size (64 or 128): selects the kernel instance
+  uint32_t tag_base;
+  // shared-memory plan (plan_step)
+  int n_stages, slot_bytes, region_bytes, part_floats;
+  // measurement hook: per CTA and phase k < trace_k, %globaltimer stamps
+  // [cta][k][4] = phase start, activation built, stages done, epilogue done
+  unsigned long long* trace;
+  int trace_k;
+};
+
+// Fills the shared-memory plan of `a` for this program; false if it cannot fit.
+bool plan_step(const PhaseDesc* prog_host, int n_phases, int grid, StepArgs& a);
+// The row table of StepArgs::ranges for this program and grid.
+void step_ranges(const PhaseDesc* prog_host, int n_phases, int grid, SegRange* out);
+size_t step_smem_bytes(const StepArgs& a);
+cudaError_t launch_step(const StepArgs& a, int grid, cudaStream_t s);
+// Unpacks n tagged words into floats (debug reads of the exchange buffers).
+cudaError_t launch_ll_unpack(float* out, const uint64_t* in, int n, cudaStream_t s);
+constexpr int STEP_SMEM_MAX = 225 * 1024;  // dynamic; the opt-in limit (227 KB) also covers static smem
+
 }  // namespace hakm

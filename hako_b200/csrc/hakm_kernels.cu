@@ -2,6 +2,7 @@
 // activation quantizer, exact Q4_K integer sub-block sums, Q6_K re-layout,
 // dequantization, rmsnorm, embedding lookup, NeoX RoPE and GQA decode
 // attention. The streaming GEMV phases live in hakm_stream.cu.
+#include "hakm_attn.cuh"
 #include "hakm_device.cuh"
 
 #include <mutex>
@@ -28,7 +29,9 @@ __global__ void quantize_q8_kernel(const float* __restrict__ x, int n, int8_t* _
   const int b = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (32 * b >= n) return;
   const float v = x[32 * b + lane];
-  const float amax = warp_max(fabsf(v));
+  // NaN elements do not raise amax (src/quant.c:131-133 keeps the larger of
+  // amax and |x| with a comparison that a NaN never wins)
+  const float amax = warp_max(fmaxf(0.0f, fabsf(v)));
   const float scale = amax * (1.0f / 127.0f);
   const float inv = q8_inv(amax, scale);
   xq[32 * b + lane] = (int8_t)q8_round(v * inv);
@@ -191,139 +194,17 @@ cudaError_t launch_rope(float* x, const float* rope_cs, const int* pos_dev, int 
 
 // ------------------------------------------------------------ attention
 
-// GQA decode attention (src/model.c:124-142, softmax src/nn.c:20-27). One CTA
-// per (kv head, chunk of ATTN_CHUNK positions) serves the G query heads that
-// share the kv head. The chunk's K and V rows are staged in shared memory
-// with every load in flight at once (rows padded by 4 floats so float4 reads
-// down a column of positions are bank-conflict free); scores, softmax and the
-// weighted V sum then run out of shared memory. Chunks combine flash-decode
-// style (max / sum rescale); the last CTA of a kv head (atomic ticket) merges
-// them, so one launch suffices at any context length.
+// Standalone attention launch: one CTA per (kv head, chunk).
+struct BlockSync {
+  __device__ void operator()() const { __syncthreads(); }
+};
+
 template <int HD>
 __global__ void __launch_bounds__(256) attention_kernel(const AttnParams a) {
   extern __shared__ __align__(16) float sm[];
-  constexpr int MAXG = 8, KP = HD + 4;
-  const int G = a.n_heads / a.n_kv;
-  const int kvh = blockIdx.x, split = blockIdx.y;
-  const int kv_dim = a.n_kv * HD;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-  float* qs = sm;                     // [G][HD]
-  float* ks = qs + MAXG * HD;         // [ATTN_CHUNK][KP]
-  float* vs = ks + ATTN_CHUNK * KP;   // [ATTN_CHUNK][HD]
-  float* sc = vs + ATTN_CHUNK * HD;   // [G][ATTN_CHUNK]
-  __shared__ float stat_m[MAXG], stat_l[MAXG];
-  __shared__ bool last;
-
   pdl_launch_dependents();
   pdl_wait();
-  const int pos = *a.pos_dev;
-  const int s0 = split * ATTN_CHUNK;
-  const int ns = min(ATTN_CHUNK, pos + 1 - s0);  // may be <= 0 for chunks past pos
-
-  // stage q, K and V (all loads issued before any use)
-  constexpr int R4 = HD / 4;
-  const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)kvh * G * HD);
-  for (int i = tid; i < G * R4; i += blockDim.x) reinterpret_cast<float4*>(qs)[i] = q4[i];
-  if (ns > 0) {
-    const float* kb = a.k_cache + (size_t)s0 * kv_dim + kvh * HD;
-    const float* vb = a.v_cache + (size_t)s0 * kv_dim + kvh * HD;
-    for (int i = tid; i < ns * R4; i += blockDim.x) {
-      const int r = i / R4, c4 = i % R4;
-      const float4 kv = *reinterpret_cast<const float4*>(kb + (size_t)r * kv_dim + 4 * c4);
-      const float4 vv = *reinterpret_cast<const float4*>(vb + (size_t)r * kv_dim + 4 * c4);
-      *reinterpret_cast<float4*>(ks + r * KP + 4 * c4) = kv;
-      *reinterpret_cast<float4*>(vs + r * HD + 4 * c4) = vv;
-    }
-  }
-  __syncthreads();
-
-  // scores: one (head, position) pair per thread iteration, positions fastest
-  for (int i = tid; i < G * ATTN_CHUNK; i += blockDim.x) {
-    const int g = i / ATTN_CHUNK, r = i % ATTN_CHUNK;
-    if (r < ns) {
-      const float4* kr = reinterpret_cast<const float4*>(ks + r * KP);
-      const float4* qr = reinterpret_cast<const float4*>(qs + g * HD);
-      float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-      for (int c4 = 0; c4 < R4; c4 += 2) {
-        const float4 k0 = kr[c4], k1 = kr[c4 + 1], x0 = qr[c4], x1 = qr[c4 + 1];
-        d0 = fmaf(x0.x, k0.x, d0); d0 = fmaf(x0.y, k0.y, d0); d0 = fmaf(x0.z, k0.z, d0); d0 = fmaf(x0.w, k0.w, d0);
-        d1 = fmaf(x1.x, k1.x, d1); d1 = fmaf(x1.y, k1.y, d1); d1 = fmaf(x1.z, k1.z, d1); d1 = fmaf(x1.w, k1.w, d1);
-      }
-      sc[g * ATTN_CHUNK + r] = (d0 + d1) * a.scale;
-    }
-  }
-  __syncthreads();
-
-  // per-head max and exp-sum (warp g handles head g)
-  for (int g = warp; g < G; g += nw) {
-    float m = -CUDART_INF_F;
-    for (int i = lane; i < ns; i += 32) m = fmaxf(m, sc[g * ATTN_CHUNK + i]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int i = lane; i < ns; i += 32) {
-      const float e = expf(sc[g * ATTN_CHUNK + i] - m);
-      sc[g * ATTN_CHUNK + i] = e;
-      l += e;
-    }
-    l = warp_sum(l);
-    if (lane == 0) { stat_m[g] = m; stat_l[g] = l; }
-  }
-  __syncthreads();
-
-  // weighted V: one (head, 4 dims) pair per thread iteration
-  const bool single = (a.n_split == 1);
-  for (int i = tid; i < G * R4; i += blockDim.x) {
-    const int g = i / R4, c4 = i % R4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int r = 0; r < ns; r++) {
-      const float e = sc[g * ATTN_CHUNK + r];
-      const float4 v = *reinterpret_cast<const float4*>(vs + r * HD + 4 * c4);
-      acc.x = fmaf(e, v.x, acc.x); acc.y = fmaf(e, v.y, acc.y);
-      acc.z = fmaf(e, v.z, acc.z); acc.w = fmaf(e, v.w, acc.w);
-    }
-    if (single) {
-      const float inv = 1.0f / stat_l[g];
-      float4 o;
-      o.x = acc.x * inv; o.y = acc.y * inv; o.z = acc.z * inv; o.w = acc.w * inv;
-      *reinterpret_cast<float4*>(a.out + (size_t)(kvh * G + g) * HD + 4 * c4) = o;
-    } else {
-      float* pp = a.part + ((size_t)(kvh * a.n_split + split) * G + g) * (HD + 2);
-      pp[2 + 4 * c4] = acc.x; pp[3 + 4 * c4] = acc.y; pp[4 + 4 * c4] = acc.z; pp[5 + 4 * c4] = acc.w;
-      if (c4 == 0) { pp[0] = ns > 0 ? stat_m[g] : -CUDART_INF_F; pp[1] = ns > 0 ? stat_l[g] : 0.f; }
-    }
-  }
-  if (!single) {
-    __syncthreads();
-    if (tid == 0) {
-      __threadfence();
-      const unsigned prev = atomicAdd(&a.counters[kvh], 1u);
-      last = (prev == (unsigned)a.n_split - 1);
-    }
-    __syncthreads();
-    if (last) {
-      __threadfence();
-      for (int i = tid; i < G * HD; i += blockDim.x) {
-        const int g = i / HD, d = i % HD;
-        float m = -CUDART_INF_F;
-        for (int sp = 0; sp < a.n_split; sp++) {
-          const volatile float* pp = a.part + ((size_t)(kvh * a.n_split + sp) * G + g) * (HD + 2);
-          m = fmaxf(m, pp[0]);
-        }
-        float l = 0.f, acc = 0.f;
-        for (int sp = 0; sp < a.n_split; sp++) {
-          const volatile float* pp = a.part + ((size_t)(kvh * a.n_split + sp) * G + g) * (HD + 2);
-          if (pp[1] > 0.f) {
-            const float f = expf(pp[0] - m);
-            l += pp[1] * f;
-            acc += pp[2 + d] * f;
-          }
-        }
-        a.out[(kvh * G + g) * HD + d] = acc / l;
-      }
-      if (tid == 0) a.counters[kvh] = 0u;
-    }
-  }
+  attn_item<HD, false>(a, blockIdx.x, blockIdx.y, *a.pos_dev, sm, threadIdx.x, blockDim.x, BlockSync());
 }
 
 size_t attention_scratch_floats(int n_kv, int n_split, int group, int head_dim) {
@@ -332,8 +213,7 @@ size_t attention_scratch_floats(int n_kv, int n_split, int group, int head_dim) 
 
 template <int HD>
 static cudaError_t launch_attn(const AttnParams& a, cudaStream_t s, bool pdl) {
-  constexpr int MAXG = 8;
-  const size_t smem = (size_t)(MAXG * HD + ATTN_CHUNK * (HD + 4) + ATTN_CHUNK * HD + MAXG * ATTN_CHUNK) * 4;
+  const size_t smem = attn_smem_bytes(HD);
   static unsigned done = 0;
   int dev = 0;
   cudaGetDevice(&dev);

@@ -156,6 +156,22 @@ struct hakmc_ctx {
   int pos = 0;                // host mirror of *pos_dev
   int run_layers = 0;
   std::map<int, cudaGraphExec_t> graphs;  // keyed by attention split count
+  // persistent step kernel: device program of one step for run_layers layers
+  bool use_step = true;        // HAKMC_STEP=0 selects the per-phase graphs
+  PhaseDesc* prog_dev = nullptr;
+  int prog_cap = 0, prog_layers = -1;
+  SegRange* ranges_dev = nullptr;  // [phase][cta][segment] rows of the step program
+  size_t ranges_cap = 0;
+  StepArgs step = {};
+  unsigned int* step_bar = nullptr;
+  unsigned int* step_tickets = nullptr;
+  unsigned long long* step_keys = nullptr;
+  // tagged exchange vectors of the step kernel: xb (two buffers), q, k, v, att, h
+  uint64_t *xb_ll = nullptr, *q_ll = nullptr, *k_ll = nullptr, *v_ll = nullptr, *att_ll = nullptr,
+           *h_ll = nullptr;
+  size_t ll_words = 0;         // all of them, contiguous from xb_ll
+  uint32_t tag_base = 1;       // first tag of the next launch
+  bool step_ran = false;       // the exchange vectors hold the latest q/k/v/att/h
 };
 
 static int dalloc(hakmc_ctx* c, void** p, size_t n) {
@@ -272,23 +288,21 @@ static void finish_params(PhaseParams& p) {
 
 static unsigned long long* g_trace = nullptr;  // set only inside hakmc_trace_phase
 
-static cudaError_t run_phase(hakmc_ctx* c, PhaseParams& p) {
-  finish_params(p);
-  p.err_flag = c->err_flag;
-  p.trace = g_trace;
-  return launch_phase(p, c->num_sms, c->stream, c->pdl);
-}
 
 enum { PH_QKV = 0, PH_ATTN = 1, PH_WO = 2, PH_FFN = 3, PH_DOWN = 4, PH_LMHEAD = 5 };
 
-// Enqueue one phase of layer l (l ignored for PH_LMHEAD). `timing` strips the
-// step-finalisation side effects so a phase can be relaunched on its own.
-static cudaError_t enqueue_phase(hakmc_ctx* c, int l, int ph, int n_split, bool timing) {
+// One phase of layer l (l ignored for PH_LMHEAD) as a PhaseDesc. `timing`
+// leaves out the step-finalisation side effects of the per-phase lm_head
+// kernel, so a phase can be relaunched on its own (and the step program,
+// which finalises inside the step kernel, uses it too).
+static PhaseDesc make_phase(hakmc_ctx* c, int l, int ph, int n_split, bool timing) {
   const size_t lstride = (size_t)c->max_seq * c->KV;
   DevLayer& y = c->layers[l < c->L ? l : 0];
   float* kc = c->k_cache + (size_t)l * lstride;
   float* vc = c->v_cache + (size_t)l * lstride;
-  PhaseParams p = {};
+  PhaseDesc d = {};
+  d.kind = PK_GEMV;
+  PhaseParams& p = d.g;
   switch (ph) {
     case PH_QKV:
       p.n_in = c->D; p.act = ACT_RMS; p.x = c->xb; p.norm_w = y.attn_norm; p.eps = c->eps;
@@ -298,42 +312,56 @@ static cudaError_t enqueue_phase(hakmc_ctx* c, int l, int ph, int n_split, bool 
       p.seg[1] = make_seg(y.wv, EPI_V_CACHE, c->v);
       p.seg[1].cache = vc; p.seg[1].bias = y.bv;
       p.rope_cs = c->rope_cs; p.pos_dev = c->pos_dev; p.head_dim = c->hd; p.kv_dim = c->KV;
-      return run_phase(c, p);
+      break;
     case PH_ATTN: {
-      AttnParams a = {};
+      d.kind = PK_ATTN;
+      AttnParams& a = d.a;
       a.q = c->q; a.k_cache = kc; a.v_cache = vc; a.out = c->att; a.pos_dev = c->pos_dev;
       a.n_heads = c->H; a.n_kv = c->KVH; a.head_dim = c->hd; a.scale = 1.0f / sqrtf((float)c->hd);
       a.n_split = n_split; a.part = c->attn_part; a.counters = c->attn_counters;
-      return launch_attention(a, c->stream, c->pdl);
+      break;
     }
     case PH_WO:
       p.n_in = c->D; p.act = ACT_F32; p.x = c->att;
       p.n_seg = 1;
       p.seg[0] = make_seg(y.wo, EPI_RESID, c->xb);
-      return run_phase(c, p);
+      break;
     case PH_FFN:
       p.n_in = c->D; p.act = ACT_RMS; p.x = c->xb; p.norm_w = y.ffn_norm; p.eps = c->eps;
       p.n_seg = 1;
       p.seg[0] = make_seg(y.wgu, EPI_SWIGLU, c->hbuf);
-      return run_phase(c, p);
+      break;
     case PH_DOWN:
       p.n_in = c->F; p.act = ACT_F32; p.x = c->hbuf;
       p.n_seg = 1;
       p.seg[0] = make_seg(y.down, EPI_RESID, c->xb);
-      return run_phase(c, p);
-    default:  // final norm + lm_head + argmax + step finalisation
+      break;
+    default:  // final norm + lm_head + argmax (+ step finalisation)
       p.n_in = c->D; p.act = ACT_RMS; p.x = c->xb; p.norm_w = c->out_norm; p.eps = c->eps;
       p.n_seg = 1;
       p.seg[0] = make_seg(c->lm_head, EPI_ARGMAX, c->logits);
       p.argmax_key = c->argmax_key;
+      d.skip_forced = 1;
       if (!timing) {
         p.done_counter = c->done_counter;
         p.next_token = c->token_dev; p.token_log = c->token_log; p.step_dev = c->step_dev;
         p.token_log_cap = c->token_log_cap;
         p.pos_inc = c->pos_dev;
       }
-      return run_phase(c, p);
+      break;
   }
+  if (d.kind == PK_GEMV) {
+    finish_params(p);
+    p.err_flag = c->err_flag;
+  }
+  return d;
+}
+
+static cudaError_t enqueue_phase(hakmc_ctx* c, int l, int ph, int n_split, bool timing) {
+  PhaseDesc d = make_phase(c, l, ph, n_split, timing);
+  if (d.kind == PK_ATTN) return launch_attention(d.a, c->stream, c->pdl);
+  d.g.trace = g_trace;
+  return launch_phase(d.g, c->num_sms, c->stream, c->pdl);
 }
 
 // Enqueue one decode step for sequence 0 on c->stream.
@@ -405,6 +433,134 @@ static int launch_one(hakmc_ctx* c) {
   return 0;
 }
 
+// Device program of one decode step for run_layers layers (rebuilt when that
+// changes) and its shared-memory plan. Phase i of the program has tag index
+// i + 1 (0 is the embedding); each phase names the index of the phase whose
+// output it reads.
+static int ensure_program(hakmc_ctx* c) {
+  if (c->prog_layers == c->run_layers) return 0;
+  std::vector<PhaseDesc> prog;
+  uint64_t* xb0 = c->xb_ll;
+  uint64_t* xb1 = c->xb_ll + c->D;
+  int xb0_src = 0;  // phase that last wrote xb buffer 0 (the embedding first)
+  for (int l = 0; l < c->run_layers; l++) {
+    const int base = 5 * l + 1;  // tag index of this layer's qkv phase
+    PhaseDesc qkv = make_phase(c, l, PH_QKV, 1, true);
+    qkv.x_ll = xb0; qkv.x_src = xb0_src;
+    qkv.out_ll[0] = c->q_ll; qkv.out2_ll = c->k_ll; qkv.out_ll[1] = c->v_ll;
+    PhaseDesc at = make_phase(c, l, PH_ATTN, 1, true);
+    at.x_ll = c->q_ll; at.res_ll = c->k_ll; at.v_ll = c->v_ll; at.x_src = base;
+    at.out_ll[0] = c->att_ll; at.layer = l;
+    at.a.counters = c->step_tickets;
+    PhaseDesc wo = make_phase(c, l, PH_WO, 1, true);
+    wo.x_ll = c->att_ll; wo.x_src = base + 1;
+    wo.res_ll = xb0; wo.res_src = xb0_src; wo.out_ll[0] = xb1;
+    PhaseDesc ffn = make_phase(c, l, PH_FFN, 1, true);
+    ffn.x_ll = xb1; ffn.x_src = base + 2; ffn.out_ll[0] = c->h_ll;
+    PhaseDesc down = make_phase(c, l, PH_DOWN, 1, true);
+    down.x_ll = c->h_ll; down.x_src = base + 3;
+    down.res_ll = xb1; down.res_src = base + 2; down.out_ll[0] = xb0;
+    xb0_src = base + 4;
+    prog.push_back(qkv); prog.push_back(at); prog.push_back(wo); prog.push_back(ffn); prog.push_back(down);
+  }
+  PhaseDesc lm = make_phase(c, 0, PH_LMHEAD, 1, true);
+  lm.x_ll = xb0; lm.x_src = xb0_src;
+  prog.push_back(lm);
+  StepArgs a = {};
+  if (!plan_step(prog.data(), (int)prog.size(), c->num_sms, a)) {
+    set_err("step kernel: shapes do not fit its shared-memory plan");
+    return HAKMC_EINVAL;
+  }
+  if ((int)prog.size() > c->prog_cap) {
+    void* p = nullptr;
+    const int r = dalloc(c, &p, prog.size() * sizeof(PhaseDesc));
+    if (r) return r;
+    c->prog_dev = (PhaseDesc*)p;
+    c->prog_cap = (int)prog.size();
+  }
+  CK(cudaMemcpy(c->prog_dev, prog.data(), prog.size() * sizeof(PhaseDesc), cudaMemcpyHostToDevice));
+  {
+    std::vector<SegRange> tab(prog.size() * (size_t)c->num_sms * MAX_SEGS);
+    step_ranges(prog.data(), (int)prog.size(), c->num_sms, tab.data());
+    if (tab.size() > c->ranges_cap) {
+      void* p = nullptr;
+      const int r = dalloc(c, &p, tab.size() * sizeof(SegRange));
+      if (r) return r;
+      c->ranges_dev = (SegRange*)p;
+      c->ranges_cap = tab.size();
+    }
+    CK(cudaMemcpy(c->ranges_dev, tab.data(), tab.size() * sizeof(SegRange), cudaMemcpyHostToDevice));
+  }
+  a.prog = c->prog_dev;
+  a.ranges = c->ranges_dev;
+  a.n_phases = (int)prog.size();
+  a.token_dev = c->token_dev;
+  a.pos_dev = c->pos_dev;
+  a.token_log = c->token_log;
+  a.token_log_cap = c->token_log_cap;
+  a.keys = c->step_keys;
+  a.bar = c->step_bar;
+  a.tickets = c->step_tickets;
+  a.err_flag = c->err_flag;
+  a.tok_embd = c->tok_embd.w;
+  a.xb_ll = c->xb_ll;
+  a.xb_plain = c->xb;
+  a.D = c->D;
+  a.n_layers = c->run_layers;
+  a.skip_last = 1;  // the program ends with lm_head
+  a.head_dim = c->hd;
+  c->step = a;
+  c->prog_layers = c->run_layers;
+  return 0;
+}
+
+// n_steps decode steps from the host-mirrored position in one launch of the
+// step kernel. Steps 0..n_forced-1 take forced_dev[] as input (else step 0
+// takes token_dev); the pick of step j goes to token_log[j - log_base].
+static int run_steps(hakmc_ctx* c, int n_steps, int n_forced, const int* forced_dev, int log_base,
+                     unsigned long long* trace = nullptr, int trace_k = 0) {
+  if (n_steps <= 0) return 0;
+  if (c->pos + n_steps > c->max_seq) { set_err("position %d beyond max_seq %d", c->pos + n_steps, c->max_seq); return HAKMC_ERANGE; }
+  int r = ensure_program(c);
+  if (r) return r;
+  StepArgs a = c->step;
+  a.n_steps = n_steps;
+  a.pos0 = c->pos;
+  a.n_forced = n_forced;
+  a.forced = forced_dev;
+  a.log_base = log_base;
+  a.trace = trace;
+  a.trace_k = trace_k;
+  // tags of this launch: tag_base .. tag_base + n_steps * (n_phases + 1) - 1;
+  // before they would wrap, the vectors are cleared and tags restart at 1
+  const uint64_t span = (uint64_t)n_steps * (uint64_t)(a.n_phases + 1);
+  if ((uint64_t)c->tag_base + span >= 0xFFFFFFF0ull) {
+    CK(cudaMemsetAsync(c->xb_ll, 0, c->ll_words * 8, c->stream));
+    c->tag_base = 1;
+  }
+  a.tag_base = c->tag_base;
+  c->tag_base += (uint32_t)span;
+  CK(cudaMemsetAsync(c->step_bar, 0, 4, c->stream));
+  CK(cudaMemsetAsync(c->step_tickets, 0, 64 * 4, c->stream));
+  CK(cudaMemsetAsync(c->step_keys, 0, 3 * 8, c->stream));
+  CK(launch_step(a, c->num_sms, c->stream));
+  c->pos += n_steps;
+  c->step_ran = true;
+  return 0;
+}
+
+// After a synchronised call: a kernel whose bounded wait gave up leaves the
+// error flag set (and its outputs unusable).
+static int check_flag(hakmc_ctx* c) {
+  CK(cudaMemcpy(&c->h_pinned[4], c->err_flag, 4, cudaMemcpyDeviceToHost));
+  if (c->h_pinned[4]) {
+    CK(cudaMemset(c->err_flag, 0, 4));
+    set_err("a kernel wait timed out; outputs of this call are invalid");
+    return HAKMC_ETIMEOUT;
+  }
+  return 0;
+}
+
 extern "C" void hakmc_destroy(hakmc_ctx* c) {
   if (!c) return;
   cudaSetDevice(c->device);
@@ -450,6 +606,8 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
   CK(cudaEventCreate(&c->ev1));
   const char* pe = getenv("HAKMC_PDL");
   c->pdl = !(pe && pe[0] == '0');
+  const char* se = getenv("HAKMC_STEP");
+  c->use_step = !(se && se[0] == '0');
 
   const MTensor *te = need("token_embd.weight"), *on = need("output_norm.weight");
   if (!te || !on) return HAKMC_EFORMAT;
@@ -546,6 +704,25 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
   if ((r = dalloc(c, (void**)&c->argmax_key, 8 * B))) return r;
   if ((r = dalloc(c, (void**)&c->done_counter, 4 * B))) return r;
   if ((r = dalloc(c, (void**)&c->err_flag, 16))) return r;
+  if ((r = dalloc(c, (void**)&c->step_bar, 16))) return r;
+  if ((r = dalloc(c, (void**)&c->step_keys, 32))) return r;
+  if ((r = dalloc(c, (void**)&c->step_tickets, 64 * 4))) return r;
+  CK(cudaMemset(c->step_bar, 0, 16));
+  CK(cudaMemset(c->step_keys, 0, 32));
+  CK(cudaMemset(c->step_tickets, 0, 64 * 4));
+  {
+    // exchange vectors, 16-byte aligned pieces of one allocation
+    auto up2 = [](size_t n) { return (n + 1) & ~(size_t)1; };
+    const size_t nD = up2(c->D), nKV = up2(c->KV), nF = up2(c->F);
+    c->ll_words = 2 * nD + nD + 2 * nKV + nD + nF;
+    if ((r = dalloc(c, (void**)&c->xb_ll, c->ll_words * 8))) return r;
+    CK(cudaMemset(c->xb_ll, 0, c->ll_words * 8));
+    c->q_ll = c->xb_ll + 2 * nD;
+    c->k_ll = c->q_ll + nD;
+    c->v_ll = c->k_ll + nKV;
+    c->att_ll = c->v_ll + nKV;
+    c->h_ll = c->att_ll + nD;
+  }
   CK(cudaMemset(c->err_flag, 0, 16));
   CK(cudaMemset(c->token_dev, 0, 16 * B));
   CK(cudaMemset(c->pos_dev, 0, 16 * B));
@@ -629,13 +806,14 @@ extern "C" int hakmc_forward(hakmc_ctx* c, int token, float* logits, int* argmax
   c->h_pinned[0] = token;
   CK(cudaEventRecord(c->ev0, c->stream));
   CK(cudaMemcpyAsync(c->token_dev, &c->h_pinned[0], 4, cudaMemcpyHostToDevice, c->stream));
-  int r = launch_one(c);
+  int r = c->use_step ? run_steps(c, 1, 1, c->token_dev, 0) : launch_one(c);
   if (r) return r;
   CK(cudaMemcpyAsync(&c->h_pinned[1], c->token_dev, 4, cudaMemcpyDeviceToHost, c->stream));
   if (logits) CK(cudaMemcpyAsync(c->logits_pinned, c->logits, (size_t)c->V * 4, cudaMemcpyDeviceToHost, c->stream));
   CK(cudaEventRecord(c->ev1, c->stream));
   CK(cudaStreamSynchronize(c->stream));
   CK(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
+  if ((r = check_flag(c))) return r;
   if (argmax) *argmax = c->h_pinned[1];
   if (logits) memcpy(logits, c->logits_pinned, (size_t)c->V * 4);
   return 0;
@@ -655,7 +833,7 @@ extern "C" int hakmc_generate(hakmc_ctx* c, const int* prompt, int n_prompt, int
     c->prompt_dev = (int*)p;
     c->prompt_cap = n_prompt;
   }
-  {
+  if (!c->use_step) {
     const int r = ensure_graphs(c, c->pos, c->pos + n_prompt + n_gen);
     if (r) return r;
   }
@@ -663,21 +841,30 @@ extern "C" int hakmc_generate(hakmc_ctx* c, const int* prompt, int n_prompt, int
   CK(cudaMemcpyAsync(c->prompt_dev, pp.data(), (size_t)n_prompt * 4, cudaMemcpyHostToDevice, c->stream));
   CK(cudaMemsetAsync(c->step_dev, 0, 4, c->stream));
   CK(cudaEventRecord(c->ev0, c->stream));
-  for (int i = 0; i < n_prompt; i++) {
-    CK(cudaMemcpyAsync(c->token_dev, c->prompt_dev + i, 4, cudaMemcpyDeviceToDevice, c->stream));
-    int r = launch_one(c);
+  int log_off = n_prompt - 1;  // token_log index of the first generated token
+  if (c->use_step) {
+    // prompt and generation in one launch: the pick of the last prompt step
+    // is the first generated token
+    const int r = run_steps(c, n_prompt + (n_gen > 0 ? n_gen : 1) - 1, n_prompt, c->prompt_dev, n_prompt - 1);
     if (r) return r;
-  }
-  for (int g = 1; g < n_gen; g++) {
-    int r = launch_one(c);
-    if (r) return r;
+    log_off = 0;
+  } else {
+    for (int i = 0; i < n_prompt; i++) {
+      CK(cudaMemcpyAsync(c->token_dev, c->prompt_dev + i, 4, cudaMemcpyDeviceToDevice, c->stream));
+      int r = launch_one(c);
+      if (r) return r;
+    }
+    for (int g = 1; g < n_gen; g++) {
+      int r = launch_one(c);
+      if (r) return r;
+    }
   }
   CK(cudaEventRecord(c->ev1, c->stream));
   if (n_gen > 0)
-    CK(cudaMemcpyAsync(out, c->token_log + (n_prompt - 1), (size_t)n_gen * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(out, c->token_log + log_off, (size_t)n_gen * 4, cudaMemcpyDeviceToHost, c->stream));
   CK(cudaStreamSynchronize(c->stream));
   CK(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
-  return 0;
+  return check_flag(c);
 }
 
 extern "C" int hakmc_decode(hakmc_ctx* c, int n_steps, int* out) {
@@ -685,7 +872,10 @@ extern "C" int hakmc_decode(hakmc_ctx* c, int n_steps, int* out) {
   if (c->pos + n_steps > c->max_seq) { set_err("sequence exceeds max_seq"); return HAKMC_ERANGE; }
   if (n_steps > c->token_log_cap) { set_err("token log too small"); return HAKMC_ERANGE; }
   CK(cudaSetDevice(c->device));
-  {
+  if (c->use_step) {
+    const int r = ensure_program(c);
+    if (r) return r;
+  } else {
     const int r = ensure_graphs(c, c->pos, c->pos + n_steps);
     if (r) return r;
   }
@@ -694,16 +884,21 @@ extern "C" int hakmc_decode(hakmc_ctx* c, int n_steps, int* out) {
   CK(cudaMemsetAsync(c->step_dev, 0, 4, c->stream));
   if (out && n_steps > 0) CK(cudaMemcpyAsync(out, c->token_dev, 4, cudaMemcpyDeviceToHost, c->stream));
   CK(cudaEventRecord(c->ev0, c->stream));
-  for (int i = 0; i < n_steps; i++) {
-    int r = launch_one(c);
+  if (c->use_step) {
+    const int r = run_steps(c, n_steps, 0, nullptr, 0);
     if (r) return r;
+  } else {
+    for (int i = 0; i < n_steps; i++) {
+      int r = launch_one(c);
+      if (r) return r;
+    }
   }
   CK(cudaEventRecord(c->ev1, c->stream));
   if (out && n_steps > 1)
     CK(cudaMemcpyAsync(out + 1, c->token_log, (size_t)(n_steps - 1) * 4, cudaMemcpyDeviceToHost, c->stream));
   CK(cudaStreamSynchronize(c->stream));
   CK(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
-  return 0;
+  return check_flag(c);
 }
 
 extern "C" int hakmc_time_phase(hakmc_ctx* c, int phase, int iters, float* avg_ms) {
@@ -740,6 +935,26 @@ extern "C" int hakmc_trace_phase(hakmc_ctx* c, int phase, int layer, unsigned lo
   return max_ctas < c->num_sms ? max_ctas : c->num_sms;
 }
 
+extern "C" int hakmc_trace_step(hakmc_ctx* c, unsigned long long* stamps, int max_phases) {
+  if (!c || !stamps || max_phases <= 0) return HAKMC_EINVAL;
+  if (c->pos >= c->max_seq) { set_err("position beyond max_seq"); return HAKMC_ERANGE; }
+  CK(cudaSetDevice(c->device));
+  const size_t n = (size_t)c->num_sms * max_phases * 4;
+  unsigned long long* d = nullptr;
+  CK(cudaMalloc(&d, n * 8));
+  cudaError_t e = cudaMemset(d, 0, n * 8);
+  int r = e == cudaSuccess ? run_steps(c, 1, 0, nullptr, 0, d, max_phases) : HAKMC_ECUDA;
+  if (r == 0) {
+    e = cudaStreamSynchronize(c->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(stamps, d, n * 8, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) { set_err("trace_step: %s", cudaGetErrorString(e)); r = HAKMC_ECUDA; }
+  }
+  cudaFree(d);
+  if (r) return r;
+  if ((r = check_flag(c))) return r;
+  return c->num_sms;
+}
+
 extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* pos, int n_seq,
                                    float* logits, int* argmax) {
   (void)tokens; (void)pos; (void)logits; (void)argmax;
@@ -762,6 +977,11 @@ extern "C" int hakmc_debug_read(hakmc_ctx* c, int which, float* out) {
   const int n[7] = {c->D, c->D, c->KV, c->KV, c->D, c->F, c->V};
   if (which < 0 || which > 6) return HAKMC_EINVAL;
   CK(cudaSetDevice(c->device));
+  if (c->step_ran && which >= 1 && which <= 5) {
+    // the step kernel keeps these as tagged words: unpack into the plain buffer
+    const uint64_t* ll[6] = {nullptr, c->q_ll, c->k_ll, c->v_ll, c->att_ll, c->h_ll};
+    CK(launch_ll_unpack(const_cast<float*>(src[which]), ll[which], n[which], c->stream));
+  }
   CK(cudaMemcpyAsync(out, src[which], (size_t)n[which] * 4, cudaMemcpyDeviceToHost, c->stream));
   CK(cudaStreamSynchronize(c->stream));
   return 0;

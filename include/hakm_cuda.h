@@ -119,6 +119,16 @@ int hakmc_time_phase(hakmc_ctx *c, int phase, int iters, float *avg_ms);
  * code. No counterpart in the reference. */
 int hakmc_trace_phase(hakmc_ctx *c, int phase, int layer, unsigned long long *stamps, int max_ctas);
 
+/* Measurement hook: one decode step (input token in the context, as for
+ * hakmc_decode) through the persistent step kernel with %globaltimer stamps
+ * written to [host] stamps, laid out [cta][phase][4] for the first
+ * max_phases grid phases of the step (embedding, then per layer qkv,
+ * attention, attn-output, ffn gate/up, ffn down, then lm_head): barrier
+ * passed, activation built, stages consumed, arrived. Advances the position
+ * by one. Returns the CTA count or a negative code. No counterpart in the
+ * reference. */
+int hakmc_trace_step(hakmc_ctx *c, unsigned long long *stamps, int max_phases);
+
 /* Time of the last hakmc_forward / hakmc_generate / hakmc_forward_batch
  * call's device work in milliseconds (CUDA events on the context stream). */
 float hakmc_last_device_ms(const hakmc_ctx *c);

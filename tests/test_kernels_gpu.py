@@ -87,6 +87,19 @@ def test_quantize_random_bit_exact(cuda, reference):
         assert np.array_equal(xq.cpu().numpy(), rq) and np.array_equal(xs.cpu().numpy(), rs)
 
 
+def test_quantize_special_values_bit_exact(cuda, reference):
+    import torch
+    from test_oracle import special_q8_blocks
+    x = special_q8_blocks()
+    xq = empty(x.size, torch.int8, cuda)
+    xs = empty(x.size // 32, torch.float32, cuda)
+    check(lib.hakmc_quantize_q8_32(P(dev(x, cuda)), x.size, P(xq), P(xs), None))
+    sync()
+    rq, rs = reference.quantize_q8_32(x)
+    assert np.array_equal(xq.cpu().numpy(), rq)
+    assert np.array_equal(xs.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+
+
 def test_q4k_integer_sums_pinned(cuda):
     import torch
     g = golden_npz("q4k.npz")

@@ -120,3 +120,28 @@ def test_synth_quantizers_roundtrip(oracle):
         lib.synth_quantize_q6k_block(C.c_void_p(x[256 * i:].ctypes.data), C.c_void_p(b6[210 * i:].ctypes.data))
     assert rel_l2(oracle.dequant(b4, 12, x.size), x) < 0.12
     assert rel_l2(oracle.dequant(b6, 14, x.size), x) < 0.03
+
+
+def special_q8_blocks():
+    """Blocks whose scale path leaves the normal range: 127/amax overflows
+    (amax below 2^-121), infinities, NaN, FLT_MAX, subnormals."""
+    rng = np.random.default_rng(11)
+    blocks = []
+    for amax in (1e-38, 3e-37, 4e-37, 1e-30, 3.4e38):
+        b = rng.uniform(-1, 1, 32).astype(np.float32) * np.float32(amax)
+        b[3] = np.float32(amax)
+        blocks.append(b)
+    b = rng.standard_normal(32).astype(np.float32); b[5] = np.inf; blocks.append(b)
+    b = rng.standard_normal(32).astype(np.float32); b[7] = -np.inf; b[8] = np.inf; blocks.append(b)
+    b = rng.standard_normal(32).astype(np.float32); b[9] = np.nan; blocks.append(b)
+    b = np.full(32, np.nan, np.float32); blocks.append(b)
+    b = np.full(32, 1e-45, np.float32); b[::2] = -1e-45; blocks.append(b)
+    return np.concatenate(blocks).astype(np.float32)
+
+
+def test_q8_special_values_match_reference(oracle, reference):
+    x = special_q8_blocks()
+    oq, os_ = oracle.quantize_q8_32(x)
+    rq, rs = reference.quantize_q8_32(x)
+    assert np.array_equal(oq, rq)
+    assert np.array_equal(os_.view(np.uint32), rs.view(np.uint32))
