@@ -10,12 +10,13 @@ untimed; exactly K decode steps are timed with CUDA events, bracketed by a
 barrier and a device synchronize. Weights (2.03 GB) exceed the 126 MB L2, so
 every step streams them from HBM.
 
-- value: K / device time of the device-resident decode loop (hakmc_decode).
+- value: K / device time of one hakmc_decode call, which runs all K steps
+  in one launch of the persistent step kernel (CUDA events on its stream).
 - e2e: the same K steps through the reference-facing per-token call
   (hakmc_forward: host token in, host argmax out, synchronous), wall clock.
-- roofline: the FFN gate/up GEMV phase (the largest launch of the step),
-  timed live with CUDA events on the context stream over launches rotating
-  through the layers.
+- roofline: that step-kernel launch (the only kernel of the decode path):
+  algorithmic bytes = every step's weights + its K/V reads at that
+  position, over the launch's device time.
 - cpu_baseline: the reference engine's own compiled decode (oracle/_ref) on
   this host's cores, on a bounded sample of the same workload.
 
@@ -250,21 +251,18 @@ def main():
     e2e_s = reduce_max(pg, time.perf_counter() - t0, device)
     e2e = world * args.steps / e2e_s
 
-    # roofline: FFN gate/up phase (largest launch), live CUDA-event timing
+    # roofline: the step-kernel launch of the timed region
     pk, pk_kind = peaks()
-    ffn_ms = C.c_float(0)
-    lib.hakmc_time_phase(ctx._h, 3, 4 * cfg.n_layers, C.byref(ffn_ms))
-    ffn_bytes = 2 * cfg.ffn_dim * (cfg.d_model // 256) * 144 + cfg.d_model * 8 + cfg.ffn_dim * 4
-    achieved = ffn_bytes / (ffn_ms.value / 1e3) / 1e9
-    # token-level: all weights + KV read per step
-    pos_mid = pos0 + args.steps // 2
-    tok_bytes = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(pos_mid)
-    tok_gbs = tok_bytes * (args.steps / (dev_ms / 1e3)) / 1e9
+    alg_bytes = sum(cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(pos0 + i) for i in range(args.steps))
+    achieved = alg_bytes / (dev_ms / 1e3) / 1e9
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
         with open(tpath) as f:
-            traffic = json.load(f).get(f"ffn_gate_up_{args.model}")
+            per_tok = json.load(f).get(f"step_kernel_{args.model}_bytes_per_token")
+        if per_tok:
+            traffic = per_tok * args.steps
+    tok_bytes = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(pos0 + args.steps // 2)
 
     line = {"metric": "decode tok/s (batch 1)", "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
@@ -272,19 +270,18 @@ def main():
             "dtype": "int8 x int4/int6 dot, fp32 accumulate", "data": "synthetic (seeded random-init weights, seeded prompt ids)",
             "config": config_block(args, world),
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-            "gpu_launches": (2 + 5 * cfg.n_layers) * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "phase_kernel (ffn gate/up, Q4_K)", "achieved": achieved,
-                         "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                         "peak_source": pk_kind, "traffic": traffic, "bytes_per_launch": ffn_bytes,
-                         "launch_ms": ffn_ms.value},
-            "token_roofline": {"bytes_per_token": tok_bytes, "achieved": tok_gbs, "peak": pk["hbm_gbs"],
-                               "unit": "GB/s", "frac": tok_gbs / pk["hbm_gbs"],
-                               "roofline_tok_s": pk["hbm_gbs"] * 1e9 / tok_bytes},
+            "gpu_launches": 1,
+            "roofline": {"bound": "hbm", "kernel": "step_kernel (whole decode steps, one launch)",
+                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / pk["hbm_gbs"], "peak_source": pk_kind, "traffic": traffic,
+                         "bytes_per_launch": alg_bytes, "launch_ms": dev_ms,
+                         "roofline_tok_s": pk["hbm_gbs"] * 1e9 / tok_bytes},
             "clocks": clk.summary(), "wall_s": wall}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, cores = cpu_reference_decode(path, args.model, 6, max_seq)
+        n_cpu = 96 if args.model == "3b" else 48
+        v, cores = cpu_reference_decode(path, args.model, n_cpu, len(prompt) + n_cpu + 8)
         line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
-                                "sample": f"6 greedy decode steps after the {len(prompt)}-id prompt "
+                                "sample": f"{n_cpu} greedy decode steps after the {len(prompt)}-id prompt "
                                           "(reference hakm_forward, oracle/_ref)"}
     ctx.close()
     if rank == 0:

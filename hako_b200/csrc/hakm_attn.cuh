@@ -34,6 +34,12 @@ struct AttnLL {
   const int* err;
 };
 
+// Most splits the merge can combine: their statistics (2 per split and
+// head, plus one per head) live in the space of the staged K/V tiles.
+__host__ __device__ inline int attn_max_splits(int hd, int group) {
+  return (ATTN_CHUNK * (2 * hd + 4) - group) / (2 * group);
+}
+
 __host__ __device__ inline size_t attn_smem_bytes(int hd) {
   return (size_t)(ATTN_MAXG * hd + ATTN_CHUNK * (hd + 4) + ATTN_CHUNK * hd + ATTN_MAXG * ATTN_CHUNK +
                   2 * ATTN_MAXG + 4) * 4;
@@ -164,24 +170,46 @@ __device__ bool attn_item(const AttnParams& a, int kvh, int split, int pos, floa
     sync();
     if (*last) {
       __threadfence();
+      // merge: every split's (max, exp-sum) into shared memory at once,
+      // one rescale weight per (split, head), then the weighted sum of the
+      // partial vectors with independent L2 loads. The staged K/V tiles are
+      // no longer needed: their space holds the statistics.
+      const int ns_all = a.n_split * G;
+      float* mw = ks;               // [n_split * G]: split max, then its weight
+      float* ls = ks + ns_all;      // [n_split * G]: split exp-sum
+      float* head_l = ls + ns_all;  // [G]: merged exp-sum
+      for (int i = tid; i < ns_all; i += nthr) {
+        const float* pp = a.part + ((size_t)kvh * a.n_split * G + i) * (HD + 2);
+        mw[i] = __ldcg(pp);
+        ls[i] = __ldcg(pp + 1);
+      }
+      sync();
+      for (int g = warp; g < G; g += nw) {
+        float m = -CUDART_INF_F;
+        for (int sp = lane; sp < a.n_split; sp += 32) m = fmaxf(m, mw[sp * G + g]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int sp = lane; sp < a.n_split; sp += 32) {
+          const float li = ls[sp * G + g];
+          const float f = li > 0.f ? expf(mw[sp * G + g] - m) : 0.f;
+          mw[sp * G + g] = f;
+          l += li * f;
+        }
+        l = warp_sum(l);
+        if (lane == 0) head_l[g] = l;
+      }
+      sync();
       for (int i = tid; i < G * HD; i += nthr) {
         const int g = i / HD, d = i % HD;
-        float m = -CUDART_INF_F;
+        const float* pp = a.part + ((size_t)kvh * a.n_split * G + g) * (HD + 2) + 2 + d;
+        float acc = 0.f;
         for (int sp = 0; sp < a.n_split; sp++) {
-          const volatile float* pp = a.part + ((size_t)(kvh * a.n_split + sp) * G + g) * (HD + 2);
-          m = fmaxf(m, pp[0]);
+          const float f = mw[sp * G + g];
+          if (f != 0.f) acc = fmaf(f, __ldcg(pp + (size_t)sp * G * (HD + 2)), acc);
         }
-        float l = 0.f, acc = 0.f;
-        for (int sp = 0; sp < a.n_split; sp++) {
-          const volatile float* pp = a.part + ((size_t)(kvh * a.n_split + sp) * G + g) * (HD + 2);
-          if (pp[1] > 0.f) {
-            const float f = expf(pp[0] - m);
-            l += pp[1] * f;
-            acc += pp[2 + d] * f;
-          }
-        }
-        if constexpr (LL) ll_st1(T.out + (kvh * G + g) * HD + d, ll_word(acc / l, T.out_tag));
-        else a.out[(kvh * G + g) * HD + d] = acc / l;
+        const float o = acc / head_l[g];
+        if constexpr (LL) ll_st1(T.out + (kvh * G + g) * HD + d, ll_word(o, T.out_tag));
+        else a.out[(kvh * G + g) * HD + d] = o;
       }
       if (!LL && tid == 0) a.counters[kvh] = 0u;
     }

@@ -133,13 +133,15 @@ struct AttnParams {
   float* part;           // scratch [n_kv][n_split][G][2 + hd]
   unsigned int* counters;  // [n_kv], self-resetting
 };
-constexpr int ATTN_CHUNK = 64;   // positions per attention CTA
+constexpr int ATTN_CHUNK = 32;   // positions per attention work item
 cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl);
 // hakmc_attention_noalloc: scratch in a static device array, no allocation
 cudaError_t attention_noalloc(float* out, const float* q, const float* kc, const float* vc, int pos, int n_heads,
                               int n_kv, int head_dim, cudaStream_t stream);
 size_t noalloc_part_floats();
 size_t attention_scratch_floats(int n_kv, int n_split, int group, int head_dim);
+// Most ATTN_CHUNK-position splits one attention merge combines.
+int attention_max_splits(int head_dim, int group);
 
 // Rows of one segment that one CTA computes, and where its per-(row, chunk)
 // partial sums start in shared memory.

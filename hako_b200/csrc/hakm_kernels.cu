@@ -207,6 +207,8 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttnParams a) {
   attn_item<HD, false>(a, blockIdx.x, blockIdx.y, *a.pos_dev, sm, threadIdx.x, blockDim.x, BlockSync());
 }
 
+int attention_max_splits(int head_dim, int group) { return attn_max_splits(head_dim, group); }
+
 size_t attention_scratch_floats(int n_kv, int n_split, int group, int head_dim) {
   return (size_t)n_kv * n_split * group * (head_dim + 2);
 }

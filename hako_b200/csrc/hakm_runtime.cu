@@ -691,6 +691,10 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
   if ((r = dalloc(c, (void**)&c->hbuf, (size_t)B * c->F * 4))) return r;
   if ((r = dalloc(c, (void**)&c->logits, (size_t)B * c->V * 4))) return r;
   const int max_split = (c->max_seq + ATTN_CHUNK - 1) / ATTN_CHUNK;
+  if (max_split > attention_max_splits(c->hd, c->H / c->KVH)) {
+    set_err("max_seq %d: beyond what one attention split merge combines", c->max_seq);
+    return HAKMC_EINVAL;
+  }
   if ((r = dalloc(c, (void**)&c->attn_part,
                   attention_scratch_floats(c->KVH, max_split, c->H / c->KVH, c->hd) * 4 * B)))
     return r;
@@ -1170,6 +1174,10 @@ extern "C" int hakmc_attention(float* out, const float* q, const float* kc, cons
     return HAKMC_EINVAL;
   }
   const int n_split = pos / ATTN_CHUNK + 1;
+  if (n_split > attention_max_splits(head_dim, n_heads / n_kv)) {
+    set_err("attention: position %d beyond what one split merge combines", pos);
+    return HAKMC_ERANGE;
+  }
   DevScratch* s;
   int r = scratch(&s, attention_scratch_floats(n_kv, n_split, n_heads / n_kv, head_dim), 0);
   if (r) return r;
@@ -1192,6 +1200,10 @@ extern "C" int hakmc_attention_noalloc(float* out, const float* q, const float* 
     return HAKMC_EINVAL;
   }
   const int n_split = pos / ATTN_CHUNK + 1;
+  if (n_split > attention_max_splits(head_dim, n_heads / n_kv)) {
+    set_err("attention_noalloc: position %d beyond what one split merge combines", pos);
+    return HAKMC_ERANGE;
+  }
   const size_t need = attention_scratch_floats(n_kv, n_split, n_heads / n_kv, head_dim);
   if (need > noalloc_part_floats()) {
     set_err("attention_noalloc: %d heads x %d positions need %zu scratch floats, the fixed array holds %zu "
