@@ -19,6 +19,8 @@ SIGNATURES = {
     "hakmc_version": (_i, []),
     "hakmc_create": (_vp, [_vp, _sz, _i, _i, _i]),
     "hakmc_destroy": (None, [_vp]),
+    "hakmc_free": (None, [_vp]),
+    "hakmc_prefill": (_i, [_vp, _vp, _i, _vp, _vp]),
     "hakmc_reset": (None, [_vp]),
     "hakmc_pos": (_i, [_vp]),
     "hakmc_set_pos": (_i, [_vp, _i]),

@@ -871,6 +871,46 @@ extern "C" int hakmc_generate(hakmc_ctx* c, const int* prompt, int n_prompt, int
   return check_flag(c);
 }
 
+extern "C" int hakmc_prefill(hakmc_ctx* c, const int* tokens, int n, float* logits, int* argmax) {
+  if (!c || !tokens || n <= 0) { set_err("prefill: need at least one token"); return HAKMC_EINVAL; }
+  if (c->pos + n > c->max_seq) { set_err("prefill: sequence exceeds max_seq"); return HAKMC_ERANGE; }
+  for (int i = 0; i < n; i++)
+    if (tokens[i] < 0 || tokens[i] >= c->V) { set_err("prefill: token %d out of range", tokens[i]); return HAKMC_EINVAL; }
+  CK(cudaSetDevice(c->device));
+  if (n > c->prompt_cap) {
+    void* p = nullptr;
+    const int r = dalloc(c, &p, (size_t)n * 4);
+    if (r) return r;
+    c->prompt_dev = (int*)p;
+    c->prompt_cap = n;
+  }
+  std::vector<int> pp(tokens, tokens + n);
+  CK(cudaMemcpyAsync(c->prompt_dev, pp.data(), (size_t)n * 4, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaEventRecord(c->ev0, c->stream));
+  if (c->use_step) {
+    const int r = run_steps(c, n, n, c->prompt_dev, n - 1);
+    if (r) return r;
+  } else {
+    for (int i = 0; i < n; i++) {
+      CK(cudaMemcpyAsync(c->token_dev, c->prompt_dev + i, 4, cudaMemcpyDeviceToDevice, c->stream));
+      const int r = launch_one(c);
+      if (r) return r;
+    }
+  }
+  CK(cudaEventRecord(c->ev1, c->stream));
+  CK(cudaMemcpyAsync(&c->h_pinned[1], c->token_dev, 4, cudaMemcpyDeviceToHost, c->stream));
+  if (logits) CK(cudaMemcpyAsync(c->logits_pinned, c->logits, (size_t)c->V * 4, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  CK(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
+  const int r = check_flag(c);
+  if (r) return r;
+  if (argmax) *argmax = c->h_pinned[1];
+  if (logits) memcpy(logits, c->logits_pinned, (size_t)c->V * 4);
+  return 0;
+}
+
+extern "C" void hakmc_free(hakmc_ctx* c) { hakmc_destroy(c); }
+
 extern "C" int hakmc_decode(hakmc_ctx* c, int n_steps, int* out) {
   if (!c || n_steps < 0) return HAKMC_EINVAL;
   if (c->pos + n_steps > c->max_seq) { set_err("sequence exceeds max_seq"); return HAKMC_ERANGE; }

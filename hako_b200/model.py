@@ -91,6 +91,16 @@ class HakmCtx:
                                 C.byref(am)), "forward")
         return logits, am.value
 
+    def prefill(self, tokens, want_logits: bool = True):
+        """Feed a prompt in one device launch (hakmc_prefill); returns the
+        last position's (logits or None, argmax)."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        logits = np.empty(self.vocab, np.float32) if want_logits else None
+        am = C.c_int(0)
+        check(lib.hakmc_prefill(self._h, C.c_void_p(t.ctypes.data), len(t),
+                                C.c_void_p(logits.ctypes.data) if want_logits else None, C.byref(am)), "prefill")
+        return logits, int(am.value)
+
     def generate(self, prompt, n_gen: int) -> list[int]:
         """Greedy: feed the prompt one position at a time, then n_gen tokens."""
         p = np.ascontiguousarray(np.asarray(prompt, dtype=np.int32))

@@ -48,6 +48,8 @@ hakmc_ctx *hakmc_create(const void *mlf2_image, size_t image_size,
                         int max_seq, int max_batch, int device);
 /* Replaces hakm_ctx_free (src/model.c:78-86). */
 void hakmc_destroy(hakmc_ctx *c);
+/* The same as hakmc_destroy, under the name of the boundary's free call. */
+void hakmc_free(hakmc_ctx *c);
 /* Replaces hakm_reset (src/model.c:88): every sequence back to position 0. */
 void hakmc_reset(hakmc_ctx *c);
 int  hakmc_pos(const hakmc_ctx *c);          /* hakm_ctx.pos (model.h:20)     */
@@ -69,6 +71,13 @@ int hakmc_forward(hakmc_ctx *c, int token, float *logits, int *argmax);
  * into [host] out_tokens. No host round trip between tokens. */
 int hakmc_generate(hakmc_ctx *c, const int *prompt, int n_prompt, int n_gen,
                    int *out_tokens);
+
+/* Prompt processing: feeds n [host] ids at consecutive positions (as the
+ * reference's feed loop calls hakm_forward per id, cli/main.c:56-60) in one
+ * device launch; only the last id's lm_head runs. [host] logits (vocab
+ * floats, may be NULL) and argmax (may be NULL) receive the last step's.
+ * Advances the position by n. 0 or a negative code. */
+int hakmc_prefill(hakmc_ctx *c, const int *tokens, int n, float *logits, int *argmax);
 
 /* Continue the greedy stream of the current sequence for n_steps positions
  * without returning to the host between steps (the decode half of

@@ -19,16 +19,21 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "_build", "libhakm_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libhakm_ref.so")
 REF_CLI = os.path.join(HERE, "_ref", "hakm")
+DROPIN_CLI = os.path.join(HERE, "_ref", "hakm_cuda")  # the same CLI over the CUDA drop-in
 REF_SRC = os.environ.get("HAKM_REF_SRC", "/root/reference")
 
 _vp, _i, _f = C.c_void_p, C.c_int, C.c_float
 
 
 def build(ref: bool = True) -> None:
-    """Compile the restatement, and the reference too when its sources exist."""
+    """Compile the restatement, and the reference too when its sources exist
+    (with the reference CLI relinked over the CUDA drop-in once
+    libhakm_cuda is built)."""
     targets = ["all"]
     if ref and os.path.isdir(os.path.join(REF_SRC, "src")):
         targets.append("ref")
+        if os.path.exists(os.path.join(os.path.dirname(HERE), "hako_b200", "_lib", "libhakm_cuda.so")):
+            targets.append("dropin")
     subprocess.run(["make", "-s", "-C", HERE, *targets, f"REF={REF_SRC}"], check=True)
 
 

@@ -179,3 +179,35 @@ def test_big_model_stream(cuda, name, max_seq):
     with HakmCtx(path, max_seq=max_seq) as ctx:
         toks = ctx.generate(fx["prompt"], fx["n_gen"])
     check_stream(toks, fx)
+
+
+def test_prefill_matches_per_token_feed(cuda, small_path):
+    """hakmc_prefill (one launch, lm_head only on the last id) leaves the same
+    state as feeding the ids one hakm_forward at a time: same last logits,
+    same continuation; and its logits match the reference's."""
+    from oracle.oracle import RefModel
+    prompt = [11, 4000, 256, 259, 1, 2, 3, 77, 9, 123]
+    with HakmCtx(small_path, max_seq=64) as a, HakmCtx(small_path, max_seq=64) as b:
+        la, ama = a.prefill(prompt)
+        lb = amb = None
+        for t in prompt:
+            lb, amb = b.forward(t)
+        assert a.pos == b.pos == len(prompt)
+        assert ama == amb
+        assert rel_l2(la, lb) < 1e-6
+        assert a.generate([ama], 8) == b.generate([amb], 8)
+    ref = RefModel(small_path, 64)
+    lr = None
+    for t in prompt:
+        lr, _ = ref.forward(t)
+    ref.close()
+    assert rel_l2(la, lr) < 2e-2
+
+
+def test_prefill_rejects_bad_input(cuda, small_path):
+    with HakmCtx(small_path, max_seq=8) as ctx:
+        with pytest.raises(HakmcError):
+            ctx.prefill([1] * 9)
+        with pytest.raises(HakmcError):
+            ctx.prefill([1, 10 ** 7])
+        assert ctx.pos == 0
