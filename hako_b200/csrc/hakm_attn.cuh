@@ -3,13 +3,13 @@
 // range of threads of one CTA: the standalone attention kernel and the
 // persistent decode-step kernel both call it.
 //
-// One work item = (kv head, chunk of ATTN_CHUNK positions) and serves the G
-// query heads sharing that kv head. The chunk's K and V rows are staged in
-// shared memory with every load in flight at once (rows padded by 4 floats so
-// float4 reads down a column of positions are bank-conflict free); scores,
-// softmax and the weighted V sum run out of shared memory. Chunks combine
-// flash-decode style (max / sum rescale); the last item of a kv head to
-// finish (atomic ticket) merges them. Inputs are read with L2-coherent loads:
+// One work item = (kv head, group of its query heads, chunk of ATTN_CHUNK
+// positions). The chunk's K and V rows are staged in shared memory with every
+// load in flight at once (rows padded by 4 floats so float4 reads down a
+// column of positions are bank-conflict free); scores, softmax and the
+// weighted V sum run out of shared memory. Chunks combine flash-decode style
+// (max / sum rescale); the last item of a (kv head, head group) to finish
+// (atomic ticket) merges them. Inputs are read with L2-coherent loads:
 // other SMs may have written them earlier in the same kernel.
 #pragma once
 #include "hakm_device.cuh"
@@ -47,12 +47,16 @@ __host__ __device__ inline size_t attn_smem_bytes(int hd) {
 
 // tid in [0, nthr); sync() synchronises exactly those nthr threads. In
 // tagged mode returns false if a wait for a tagged input gave up.
+// Work unit u = (kv head, group of a.head_group query heads): query heads
+// [u * head_group, (u + 1) * head_group), all of kv head u / (groups per kv
+// head).
 template <int HD, bool LL, class Sync>
-__device__ bool attn_item(const AttnParams& a, int kvh, int split, int pos, float* sm, int tid, int nthr,
+__device__ bool attn_item(const AttnParams& a, int u, int split, int pos, float* sm, int tid, int nthr,
                           Sync sync, const AttnLL& T = AttnLL()) {
   bool ok = true;
   constexpr int KP = HD + 4, R4 = HD / 4;
-  const int G = a.n_heads / a.n_kv;
+  const int G = a.head_group;  // query heads of this item
+  const int kvh = u / (a.n_heads / a.n_kv / G);
   const int kv_dim = a.n_kv * HD;
   const int lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
   float* qs = sm;                          // [G][HD]
@@ -69,11 +73,11 @@ __device__ bool attn_item(const AttnParams& a, int kvh, int split, int pos, floa
   if constexpr (LL) {
     for (int i = tid; i < G * R4; i += nthr) {
       float v4[4];
-      ok &= ll_get<4>(T.q + (size_t)kvh * G * HD + 4 * i, T.in_tag, v4, T.err);
+      ok &= ll_get<4>(T.q + (size_t)u * G * HD + 4 * i, T.in_tag, v4, T.err);
       reinterpret_cast<float4*>(qs)[i] = make_float4(v4[0], v4[1], v4[2], v4[3]);
     }
   } else {
-    const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)kvh * G * HD);
+    const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)u * G * HD);
     for (int i = tid; i < G * R4; i += nthr) reinterpret_cast<float4*>(qs)[i] = __ldcg(q4 + i);
   }
   if (ns > 0) {
@@ -148,14 +152,14 @@ __device__ bool attn_item(const AttnParams& a, int kvh, int split, int pos, floa
       float4 o;
       o.x = acc.x * inv; o.y = acc.y * inv; o.z = acc.z * inv; o.w = acc.w * inv;
       if constexpr (LL) {
-        uint64_t* dst = T.out + (size_t)(kvh * G + g) * HD + 4 * c4;
+        uint64_t* dst = T.out + (size_t)(u * G + g) * HD + 4 * c4;
         ll_put2(dst, o.x, o.y, T.out_tag);
         ll_put2(dst + 2, o.z, o.w, T.out_tag);
       } else {
-        *reinterpret_cast<float4*>(a.out + (size_t)(kvh * G + g) * HD + 4 * c4) = o;
+        *reinterpret_cast<float4*>(a.out + (size_t)(u * G + g) * HD + 4 * c4) = o;
       }
     } else {
-      float* pp = a.part + ((size_t)(kvh * a.n_split + split) * G + g) * (HD + 2);
+      float* pp = a.part + ((size_t)(u * a.n_split + split) * G + g) * (HD + 2);
       pp[2 + 4 * c4] = acc.x; pp[3 + 4 * c4] = acc.y; pp[4 + 4 * c4] = acc.z; pp[5 + 4 * c4] = acc.w;
       if (c4 == 0) { pp[0] = ns > 0 ? stat_m[g] : -CUDART_INF_F; pp[1] = ns > 0 ? stat_l[g] : 0.f; }
     }
@@ -164,7 +168,7 @@ __device__ bool attn_item(const AttnParams& a, int kvh, int split, int pos, floa
     sync();
     if (tid == 0) {
       __threadfence();
-      const unsigned prev = atomicAdd(&a.counters[kvh], 1u);
+      const unsigned prev = atomicAdd(&a.counters[u], 1u);
       *last = LL ? (prev + 1u == T.ticket_target) : (prev == (unsigned)a.n_split - 1);
     }
     sync();
@@ -179,7 +183,7 @@ __device__ bool attn_item(const AttnParams& a, int kvh, int split, int pos, floa
       float* ls = ks + ns_all;      // [n_split * G]: split exp-sum
       float* head_l = ls + ns_all;  // [G]: merged exp-sum
       for (int i = tid; i < ns_all; i += nthr) {
-        const float* pp = a.part + ((size_t)kvh * a.n_split * G + i) * (HD + 2);
+        const float* pp = a.part + ((size_t)u * a.n_split * G + i) * (HD + 2);
         mw[i] = __ldcg(pp);
         ls[i] = __ldcg(pp + 1);
       }
@@ -201,17 +205,17 @@ __device__ bool attn_item(const AttnParams& a, int kvh, int split, int pos, floa
       sync();
       for (int i = tid; i < G * HD; i += nthr) {
         const int g = i / HD, d = i % HD;
-        const float* pp = a.part + ((size_t)kvh * a.n_split * G + g) * (HD + 2) + 2 + d;
+        const float* pp = a.part + ((size_t)u * a.n_split * G + g) * (HD + 2) + 2 + d;
         float acc = 0.f;
         for (int sp = 0; sp < a.n_split; sp++) {
           const float f = mw[sp * G + g];
           if (f != 0.f) acc = fmaf(f, __ldcg(pp + (size_t)sp * G * (HD + 2)), acc);
         }
         const float o = acc / head_l[g];
-        if constexpr (LL) ll_st1(T.out + (kvh * G + g) * HD + d, ll_word(o, T.out_tag));
-        else a.out[(kvh * G + g) * HD + d] = o;
+        if constexpr (LL) ll_st1(T.out + (u * G + g) * HD + d, ll_word(o, T.out_tag));
+        else a.out[(u * G + g) * HD + d] = o;
       }
-      if (!LL && tid == 0) a.counters[kvh] = 0u;
+      if (!LL && tid == 0) a.counters[u] = 0u;
     }
     sync();
   }

@@ -69,10 +69,17 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     if (clock64() - t0 > WAIT_LIMIT) return false;
   return true;
 }
+// Weight rows are read once per token: the copy carries an L2 evict-first
+// policy so the stream does not push the small hot data (exchanged vectors,
+// K/V rows, norm weights, descriptors) out of L2.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(bar)
-               : "memory");
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+      : "memory");
 }
 __device__ __forceinline__ unsigned long long gtime() {
   unsigned long long t;

@@ -130,8 +130,9 @@ struct AttnParams {
   int n_heads, n_kv, head_dim;
   float scale;
   int n_split;           // grid.y; chunks of ATTN_CHUNK positions
-  float* part;           // scratch [n_kv][n_split][G][2 + hd]
-  unsigned int* counters;  // [n_kv], self-resetting
+  float* part;           // scratch [n_heads / head_group][n_split][head_group][2 + hd]
+  unsigned int* counters;  // [n_heads / head_group], self-resetting
+  int head_group;        // query heads per work item (divides n_heads / n_kv); 0: all of them
 };
 constexpr int ATTN_CHUNK = 32;   // positions per attention work item
 cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl);
@@ -155,7 +156,7 @@ enum PhaseKind { PK_GEMV = 0, PK_ATTN = 1 };
 // One phase of the device-resident step program. Phases exchange vectors as
 // tagged words: uint64 = (tag << 32) | float bits, tag = tag_base + step *
 // (n_phases + 1) + index of the writing phase (0 = embedding, prog[i] = i+1).
-struct PhaseDesc {
+struct alignas(16) PhaseDesc {  // copied to shared memory as 16-byte words
   int kind;          // PhaseKind
   int skip_forced;   // skipped on forced (prompt) steps whose pick is not needed: lm_head
   PhaseParams g;     // PK_GEMV geometry, weights, biases, caches, norm and rope tables

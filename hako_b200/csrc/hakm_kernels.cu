@@ -237,8 +237,10 @@ static cudaError_t launch_attn(const AttnParams& a, cudaStream_t s, bool pdl) {
   return cudaLaunchKernelEx(&cfg, attention_kernel<HD>, a);
 }
 
-cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl) {
-  if (a.n_heads % a.n_kv || a.n_heads / a.n_kv > 8) return cudaErrorInvalidValue;
+cudaError_t launch_attention(const AttnParams& a0, cudaStream_t s, bool pdl) {
+  if (a0.n_heads % a0.n_kv || a0.n_heads / a0.n_kv > 8) return cudaErrorInvalidValue;
+  AttnParams a = a0;
+  a.head_group = a.n_heads / a.n_kv;  // one block per kv head and split
   if (a.head_dim == 128) return launch_attn<128>(a, s, pdl);
   if (a.head_dim == 64) return launch_attn<64>(a, s, pdl);
   return cudaErrorInvalidValue;

@@ -452,6 +452,15 @@ static int ensure_program(hakmc_ctx* c) {
     at.x_ll = c->q_ll; at.res_ll = c->k_ll; at.v_ll = c->v_ll; at.x_src = base;
     at.out_ll[0] = c->att_ll; at.layer = l;
     at.a.counters = c->step_tickets;
+    {
+      // query heads per attention work item: split each kv head's group so
+      // that at least 8 items run even at one position split
+      const int G = c->H / c->KVH;
+      int nhg = G;
+      for (int d = 1; d <= G; d++)
+        if (G % d == 0 && c->KVH * d >= 8) { nhg = d; break; }
+      at.a.head_group = G / nhg;
+    }
     PhaseDesc wo = make_phase(c, l, PH_WO, 1, true);
     wo.x_ll = c->att_ll; wo.x_src = base + 1;
     wo.res_ll = xb0; wo.res_src = xb0_src; wo.out_ll[0] = xb1;

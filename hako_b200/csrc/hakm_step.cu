@@ -569,12 +569,11 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         T.out_tag = tag;
         T.ticket_target = tick;
         T.err = err;
-        const int items = a.n_kv * a.n_split;
+        const int n_units = a.n_heads / a.head_group;  // (kv head, query-head group) pairs
+        const int items = n_units * a.n_split;
         float* sm = reinterpret_cast<float*>(region);
-        for (int it = blockIdx.x; it < items; it += grid) {
-          const int kvh = it % a.n_kv, sp = it / a.n_kv;
-          bad |= !attn_item<HD, true>(a, kvh, sp, pos, sm, t, nt, ConsumerSync(), T);
-        }
+        for (int it = blockIdx.x; it < items; it += grid)
+          bad |= !attn_item<HD, true>(a, it % n_units, it / n_units, pos, sm, t, nt, ConsumerSync(), T);
       }
       stamp(3);
       kph++;
@@ -645,6 +644,8 @@ bool plan_step(const PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
     const PhaseDesc& D = prog[ph];
     if (D.kind == PK_ATTN) {
       if (D.a.n_heads % D.a.n_kv || D.a.n_heads / D.a.n_kv > ATTN_MAXG) return false;
+      if (D.a.head_group <= 0 || (D.a.n_heads / D.a.n_kv) % D.a.head_group || D.a.n_heads / D.a.head_group > 64)
+        return false;
       if (D.a.head_dim != 64 && D.a.head_dim != 128) return false;
       region = std::max(region, attn_smem_bytes(D.a.head_dim));
       continue;
