@@ -169,6 +169,9 @@ struct alignas(16) PhaseDesc {  // copied to shared memory as 16-byte words
   uint64_t* out_ll[MAX_SEGS];  // per segment: q / v / xb / h; attention: att
   uint64_t* out2_ll;     // EPI_ROPE_QK: k
   int layer;             // attention: layer index (split tickets)
+  // stage geometry of each GEMV segment (plan_step): rows per stage, row
+  // bytes, chunks per row, and ceil(2^16 / chunks) for unit -> (group, chunk)
+  int st_rows[MAX_SEGS], st_row_bytes[MAX_SEGS], st_nch[MAX_SEGS], st_rn[MAX_SEGS];
 };
 
 struct StepArgs {
@@ -205,7 +208,7 @@ struct StepArgs {
 };
 
 // Fills the shared-memory plan of `a` for this program; false if it cannot fit.
-bool plan_step(const PhaseDesc* prog_host, int n_phases, int grid, StepArgs& a);
+bool plan_step(PhaseDesc* prog_host, int n_phases, int grid, StepArgs& a);
 // The row table of StepArgs::ranges for this program and grid.
 void step_ranges(const PhaseDesc* prog_host, int n_phases, int grid, SegRange* out);
 size_t step_smem_bytes(const StepArgs& a);

@@ -146,15 +146,15 @@ struct EpiPre {
 struct SegGeo {
   int type, rowB, R, nch, chunkB, rn;
 };
-__device__ __forceinline__ SegGeo seg_geo(const PhaseParams& P, int s, int slot_bytes) {
+// Read from the descriptor (computed by plan_step on the host).
+__device__ __forceinline__ SegGeo seg_geo(const PhaseDesc& D, int s) {
   SegGeo g;
-  const int nb = P.n_in / QK;
-  g.type = P.seg[s].type;
-  g.rowB = (int)dev_row_bytes(g.type, nb);
-  g.R = stage_rows_for(g.type, nb, slot_bytes);
-  g.nch = n_chunks(nb);
+  g.type = D.g.seg[s].type;
+  g.rowB = D.st_row_bytes[s];
+  g.R = D.st_rows[s];
+  g.nch = D.st_nch[s];
   g.chunkB = g.type == W_Q4K ? Q4K_CHUNK : Q6K_CHUNK;
-  g.rn = (65536 + g.nch - 1) / g.nch;
+  g.rn = D.st_rn[s];
   return g;
 }
 
@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         if (D.kind != PK_GEMV || !phase_runs(A, ph, step)) continue;
         const SegRange* rtab = A.ranges + ((size_t)ph * grid + blockIdx.x) * MAX_SEGS;
         for (int s = 0; s < D.g.n_seg && ok; s++) {
-          const SegGeo G = seg_geo(D.g, s, SB);
+          const SegGeo G = seg_geo(D, s);
           const uint8_t* w = D.g.seg[s].w;
           const int4 rr = __ldg(reinterpret_cast<const int4*>(rtab + s));
           for (int rt = rr.x; rt < rr.y; rt += G.R) {
@@ -514,7 +514,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         stamp(1);
         bool failed = false;
         for (int s = 0; s < P.n_seg && !failed; s++) {
-          const SegGeo G = seg_geo(P, s, SB);
+          const SegGeo G = seg_geo(D, s);
           const int n_units_full = ((G.R + 3) / 4) * G.nch;
           float* ps = part + sr[s].part_base;
           for (int rt = sr[s].row0; rt < sr[s].row1; rt += G.R) {
@@ -637,7 +637,7 @@ size_t step_smem_bytes(const StepArgs& a) {
   return SMEM_HEADER + (size_t)a.n_stages * a.slot_bytes + a.region_bytes + (size_t)a.part_floats * 4 + 64 * 4;
 }
 
-bool plan_step(const PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
+bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
   size_t region = 0, max_row = 0;
   int part = 0;
   for (int ph = 0; ph < n_phases; ph++) {
@@ -684,6 +684,18 @@ bool plan_step(const PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
   }
   a.n_stages = S;
   a.slot_bytes = (int)slot;
+  for (int ph = 0; ph < n_phases; ph++) {
+    PhaseDesc& D = prog[ph];
+    if (D.kind != PK_GEMV) continue;
+    const int nb = D.g.n_in / QK;
+    for (int s = 0; s < D.g.n_seg; s++) {
+      D.st_rows[s] = stage_rows_for(D.g.seg[s].type, nb, a.slot_bytes);
+      D.st_row_bytes[s] = (int)dev_row_bytes(D.g.seg[s].type, nb);
+      D.st_nch[s] = n_chunks(nb);
+      D.st_rn[s] = (65536 + D.st_nch[s] - 1) / D.st_nch[s];
+      if (D.st_rows[s] < 1) return false;
+    }
+  }
   return step_smem_bytes(a) <= (size_t)STEP_SMEM_MAX;
 }
 
