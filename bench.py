@@ -20,8 +20,10 @@ every step streams them from HBM.
 - cpu_baseline: the reference engine's own compiled decode (oracle/_ref) on
   this host's cores, on a bounded sample of the same workload.
 
-N > 1 (torchrun): one independent replica per GPU (no collective on this
-path yet); value = all ranks' tokens / the slowest rank's time.
+N > 1 (torchrun): one tensor-parallel group over the N GPUs (hakmc_tp_*):
+every GEMV phase's rows split over all GPUs' CTAs, outputs all-gathered by
+peer stores inside the step kernel; one sequence, so scaling is "strong" and
+value = its tokens / the slowest rank's device time.
 """
 from __future__ import annotations
 
@@ -189,8 +191,8 @@ def config_block(args, world):
                         f"Q4_K_M greedy decode, batch 1",
             "model": f"qwen2-{args.model}-synthetic", "layers": cfg.n_layers, "d_model": cfg.d_model,
             "heads": f"{cfg.n_heads}/{cfg.n_kv_heads}", "ffn": cfg.ffn_dim, "vocab": cfg.vocab,
-            "prompt_len": len(prompt_ids(args.model)), "global_batch": world, "seq_len": None,
-            "parallelism": "replicas" if world > 1 else "single",
+            "prompt_len": len(prompt_ids(args.model)), "global_batch": 1, "seq_len": None,
+            "parallelism": f"tp{world} (rows of every phase over all GPUs, peer-store all-gather)" if world > 1 else "single",
             "l2": "weights stream from HBM every step (2.03 GB > 126 MB L2)"}
 
 
@@ -217,6 +219,9 @@ def main():
     prompt = prompt_ids(args.model)
     max_seq = len(prompt) + 2 * (args.warmup + args.steps) + 16
     ctx = HakmCtx(path, max_seq=max_seq, device=local)
+    if world > 1:
+        from hako_b200 import tp
+        tp.connect(ctx)
 
     # prompt + warm-up (untimed)
     for t in prompt:
@@ -239,7 +244,7 @@ def main():
         raise RuntimeError(f"hakmc_decode failed: {rc}")
     dev_ms = float(ctx.last_device_ms)
     max_ms = reduce_max(pg, dev_ms, device)
-    value = world * args.steps / (max_ms / 1e3)
+    value = args.steps / (max_ms / 1e3)  # one sequence, whatever the GPU count
 
     # e2e: the same number of steps through the per-token host call
     ctx.set_pos(pos0)
@@ -249,12 +254,13 @@ def main():
     for _ in range(args.steps):
         _, am = ctx.forward(am, want_logits=False)
     e2e_s = reduce_max(pg, time.perf_counter() - t0, device)
-    e2e = world * args.steps / e2e_s
+    e2e = args.steps / e2e_s
 
     # roofline: the step-kernel launch of the timed region
     pk, pk_kind = peaks()
-    alg_bytes = sum(cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(pos0 + i) for i in range(args.steps))
-    achieved = alg_bytes / (dev_ms / 1e3) / 1e9
+    # per GPU: with tensor parallelism each GPU streams 1/world of the weights
+    alg_bytes = sum(cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(pos0 + i) for i in range(args.steps)) / world
+    achieved = alg_bytes / (max_ms / 1e3) / 1e9
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
     if os.path.exists(tpath):
@@ -266,7 +272,7 @@ def main():
 
     line = {"metric": "decode tok/s (batch 1)", "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
             "dtype": "int8 x int4/int6 dot, fp32 accumulate", "data": "synthetic (seeded random-init weights, seeded prompt ids)",
             "config": config_block(args, world),
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
@@ -275,7 +281,7 @@ def main():
                          "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / pk["hbm_gbs"], "peak_source": pk_kind, "traffic": traffic,
                          "bytes_per_launch": alg_bytes, "launch_ms": dev_ms,
-                         "roofline_tok_s": pk["hbm_gbs"] * 1e9 / tok_bytes},
+                         "roofline_tok_s": world * pk["hbm_gbs"] * 1e9 / tok_bytes},
             "clocks": clk.summary(), "wall_s": wall}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         n_cpu = 96 if args.model == "3b" else 48

@@ -32,7 +32,18 @@ struct AttnLL {
   uint32_t in_tag, out_tag;
   unsigned ticket_target;
   const int* err;
+  int n_dst;                      // GPUs the output goes to (tensor parallelism), 1 otherwise
+  long long out_delta[8];         // byte offset of each GPU's copy of `out`
 };
+
+// Tagged output words to every destination GPU.
+__device__ __forceinline__ void attn_put1(const AttnLL& T, uint64_t* p, uint64_t w) {
+  for (int r = 0; r < T.n_dst; r++) ll_st1(reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(p) + T.out_delta[r]), w);
+}
+__device__ __forceinline__ void attn_put2(const AttnLL& T, uint64_t* p, float a, float b) {
+  for (int r = 0; r < T.n_dst; r++)
+    ll_put2(reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(p) + T.out_delta[r]), a, b, T.out_tag);
+}
 
 // Most splits the merge can combine: their statistics (2 per split and
 // head, plus one per head) live in the space of the staged K/V tiles.
@@ -153,8 +164,8 @@ __device__ bool attn_item(const AttnParams& a, int u, int split, int pos, float*
       o.x = acc.x * inv; o.y = acc.y * inv; o.z = acc.z * inv; o.w = acc.w * inv;
       if constexpr (LL) {
         uint64_t* dst = T.out + (size_t)(u * G + g) * HD + 4 * c4;
-        ll_put2(dst, o.x, o.y, T.out_tag);
-        ll_put2(dst + 2, o.z, o.w, T.out_tag);
+        attn_put2(T, dst, o.x, o.y);
+        attn_put2(T, dst + 2, o.z, o.w);
       } else {
         *reinterpret_cast<float4*>(a.out + (size_t)(u * G + g) * HD + 4 * c4) = o;
       }
@@ -212,7 +223,7 @@ __device__ bool attn_item(const AttnParams& a, int u, int split, int pos, float*
           if (f != 0.f) acc = fmaf(f, __ldcg(pp + (size_t)sp * G * (HD + 2)), acc);
         }
         const float o = acc / head_l[g];
-        if constexpr (LL) ll_st1(T.out + (u * G + g) * HD + d, ll_word(o, T.out_tag));
+        if constexpr (LL) attn_put1(T, T.out + (u * G + g) * HD + d, ll_word(o, T.out_tag));
         else a.out[(u * G + g) * HD + d] = o;
       }
       if (!LL && tid == 0) a.counters[u] = 0u;

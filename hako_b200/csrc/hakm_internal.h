@@ -151,6 +151,12 @@ struct SegRange {
 };
 
 // ---- persistent decode-step kernel (hakm_step.cu) ----
+
+// Tensor parallelism: device regions every GPU of a group can address in
+// every other (identical sizes on all ranks, so an address moves to rank r
+// by that region's byte offset).
+constexpr int TP_MAX = 8;
+enum XRegion { XR_LL = 0, XR_KCACHE = 1, XR_VCACHE = 2, XR_LOGITS = 3, XR_KEYS = 4, XR_XBAR = 5, XR_COUNT = 6 };
 enum PhaseKind { PK_GEMV = 0, PK_ATTN = 1 };
 
 // One phase of the device-resident step program. Phases exchange vectors as
@@ -197,6 +203,12 @@ struct StepArgs {
   int D;
   int n_layers;            // attention phases per step (split tickets)
   int skip_last;           // the last phase (lm_head) is skipped on forced steps but the last
+  // tensor parallelism (tp_world 1: none). Rows of every GEMV phase are split
+  // over the tp_world * grid CTAs of all GPUs; outputs go to every GPU.
+  int tp_rank, tp_world;
+  long long tp_delta[TP_MAX][XR_COUNT];  // byte offset from this GPU's region to rank r's
+  unsigned int* xbar;      // cross-GPU step counter (XR_XBAR): +1 per GPU per step, never reset
+  unsigned int xbar_base;  // steps completed before this launch
   int head_dim;            // attention head size (64 or 128): selects the kernel instance
   uint32_t tag_base;
   // shared-memory plan (plan_step)
@@ -209,8 +221,9 @@ struct StepArgs {
 
 // Fills the shared-memory plan of `a` for this program; false if it cannot fit.
 bool plan_step(PhaseDesc* prog_host, int n_phases, int grid, StepArgs& a);
-// The row table of StepArgs::ranges for this program and grid.
-void step_ranges(const PhaseDesc* prog_host, int n_phases, int grid, SegRange* out);
+// The row table of StepArgs::ranges for this program: the rows of CTAs
+// cta0 .. cta0 + n_ctas - 1 of a grid of `grid` CTAs (all GPUs' CTAs).
+void step_ranges(const PhaseDesc* prog_host, int n_phases, int grid, int cta0, int n_ctas, SegRange* out);
 size_t step_smem_bytes(const StepArgs& a);
 cudaError_t launch_step(const StepArgs& a, int grid, cudaStream_t s);
 // Unpacks n tagged words into floats (debug reads of the exchange buffers).

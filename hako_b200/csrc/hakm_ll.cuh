@@ -2,9 +2,10 @@
 // the persistent step kernel without a grid barrier.
 //
 // A word is (tag << 32) | float bits, written and read as single 8-byte
-// relaxed accesses at gpu scope (pairs of words as one 16-byte vector
+// relaxed accesses at system scope (pairs of words as one 16-byte vector
 // access, each aligned 8-byte element single-copy atomic), the flag-in-data
-// scheme of NCCL's LL protocol. A reader that sees the
+// scheme of NCCL's LL protocol. System scope, because with tensor
+// parallelism the writer may sit on another GPU (peer stores over NVLink). A reader that sees the
 // tag it expects sees the value written with it; it polls until every word
 // it needs carries that tag. Tags grow by one per phase instance, so a stale
 // word can never match.
@@ -26,13 +27,13 @@ __device__ __forceinline__ float ll_value(uint64_t w) { return __uint_as_float((
 __device__ __forceinline__ bool ll_has(uint64_t w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
 
 __device__ __forceinline__ void ll_ld2(const uint64_t* p, uint64_t& a, uint64_t& b) {
-  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 __device__ __forceinline__ void ll_st2(uint64_t* p, uint64_t a, uint64_t b) {
-  asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
 __device__ __forceinline__ void ll_st1(uint64_t* p, uint64_t a) {
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
 }
 __device__ __forceinline__ void ll_put2(uint64_t* p, float a, float b, uint32_t tag) {
   ll_st2(p, ll_word(a, tag), ll_word(b, tag));
@@ -60,7 +61,7 @@ __device__ __forceinline__ bool ll_get(const uint64_t* p, uint32_t tag, float* o
     for (;;) {
       if (!ll_has(w[0], tag)) {
         __nanosleep(64);
-        asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w[0]) : "l"(p) : "memory");
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[0]) : "l"(p) : "memory");
       } else {
         ok = true;
 #pragma unroll
@@ -106,13 +107,13 @@ __device__ __forceinline__ bool ll_finish8(const uint64_t* p, uint32_t tag, uint
 // One tagged float (p 8-byte aligned).
 __device__ __forceinline__ bool ll_get1(const uint64_t* p, uint32_t tag, float& out, const int* err) {
   uint64_t w;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
   if (!ll_has(w, tag)) {
     const long long t0 = clock64();
     long long next = t0 + 4096;
     while (!ll_has(w, tag)) {
       __nanosleep(64);
-      asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
       const long long now = clock64();
       if (now > next) {
         if (ll_aborted(err) || now - t0 > LL_WAIT_LIMIT) { out = 0.f; return false; }

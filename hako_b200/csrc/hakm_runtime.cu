@@ -21,6 +21,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <unistd.h>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -172,6 +173,14 @@ struct hakmc_ctx {
   size_t ll_words = 0;         // all of them, contiguous from xb_ll
   uint32_t tag_base = 1;       // first tag of the next launch
   bool step_ran = false;       // the exchange vectors hold the latest q/k/v/att/h
+  // tensor parallelism (hakmc_tp_connect): regions every rank addresses
+  int tp_rank = 0, tp_world = 1;
+  unsigned int* step_xbar = nullptr;  // cross-GPU step counter, never reset
+  unsigned int xbar_base = 0;         // steps run in tensor-parallel launches so far
+  void* xr_ptr[XR_COUNT] = {};
+  size_t xr_size[XR_COUNT] = {};
+  void* peer_ptr[TP_MAX][XR_COUNT] = {};
+  bool peer_ipc[TP_MAX] = {};         // opened through IPC (closed at destroy)
 };
 
 static int dalloc(hakmc_ctx* c, void** p, size_t n) {
@@ -490,7 +499,8 @@ static int ensure_program(hakmc_ctx* c) {
   CK(cudaMemcpy(c->prog_dev, prog.data(), prog.size() * sizeof(PhaseDesc), cudaMemcpyHostToDevice));
   {
     std::vector<SegRange> tab(prog.size() * (size_t)c->num_sms * MAX_SEGS);
-    step_ranges(prog.data(), (int)prog.size(), c->num_sms, tab.data());
+    step_ranges(prog.data(), (int)prog.size(), c->num_sms * c->tp_world, c->tp_rank * c->num_sms, c->num_sms,
+                tab.data());
     if (tab.size() > c->ranges_cap) {
       void* p = nullptr;
       const int r = dalloc(c, &p, tab.size() * sizeof(SegRange));
@@ -544,9 +554,20 @@ static int run_steps(hakmc_ctx* c, int n_steps, int n_forced, const int* forced_
   // before they would wrap, the vectors are cleared and tags restart at 1
   const uint64_t span = (uint64_t)n_steps * (uint64_t)(a.n_phases + 1);
   if ((uint64_t)c->tag_base + span >= 0xFFFFFFF0ull) {
+    // peers write into these words without a host round trip: clearing them
+    // under tensor parallelism could erase a peer's early write
+    if (c->tp_world > 1) { set_err("tag space of the tensor-parallel group used up: recreate the contexts"); return HAKMC_ERANGE; }
     CK(cudaMemsetAsync(c->xb_ll, 0, c->ll_words * 8, c->stream));
     c->tag_base = 1;
   }
+  a.tp_rank = c->tp_rank;
+  a.tp_world = c->tp_world;
+  for (int rr = 0; rr < c->tp_world; rr++)
+    for (int x = 0; x < XR_COUNT; x++)
+      a.tp_delta[rr][x] = rr == c->tp_rank ? 0
+                                           : (long long)((const char*)c->peer_ptr[rr][x] - (const char*)c->xr_ptr[x]);
+  a.xbar = c->step_xbar;
+  a.xbar_base = c->xbar_base;
   a.tag_base = c->tag_base;
   c->tag_base += (uint32_t)span;
   CK(cudaMemsetAsync(c->step_bar, 0, 4, c->stream));
@@ -555,6 +576,7 @@ static int run_steps(hakmc_ctx* c, int n_steps, int n_forced, const int* forced_
   CK(launch_step(a, c->num_sms, c->stream));
   c->pos += n_steps;
   c->step_ran = true;
+  if (c->tp_world > 1) c->xbar_base += (unsigned)n_steps;
   return 0;
 }
 
@@ -575,6 +597,10 @@ extern "C" void hakmc_destroy(hakmc_ctx* c) {
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
   drop_graphs(c);
+  for (int rr = 0; rr < TP_MAX; rr++)
+    if (c->peer_ipc[rr])
+      for (int x = 0; x < XR_COUNT; x++)
+        if (c->peer_ptr[rr][x]) cudaIpcCloseMemHandle(c->peer_ptr[rr][x]);
   for (void* p : c->allocs) cudaFree(p);
   if (c->h_pinned) cudaFreeHost(c->h_pinned);
   if (c->logits_pinned) cudaFreeHost(c->logits_pinned);
@@ -720,6 +746,8 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
   if ((r = dalloc(c, (void**)&c->step_bar, 16))) return r;
   if ((r = dalloc(c, (void**)&c->step_keys, 32))) return r;
   if ((r = dalloc(c, (void**)&c->step_tickets, 64 * 4))) return r;
+  if ((r = dalloc(c, (void**)&c->step_xbar, 16))) return r;
+  CK(cudaMemset(c->step_xbar, 0, 16));
   CK(cudaMemset(c->step_bar, 0, 16));
   CK(cudaMemset(c->step_keys, 0, 32));
   CK(cudaMemset(c->step_tickets, 0, 64 * 4));
@@ -736,6 +764,12 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
     c->att_ll = c->v_ll + nKV;
     c->h_ll = c->att_ll + nD;
   }
+  c->xr_ptr[XR_LL] = c->xb_ll;          c->xr_size[XR_LL] = c->ll_words * 8;
+  c->xr_ptr[XR_KCACHE] = c->k_cache;    c->xr_size[XR_KCACHE] = kv * 4;
+  c->xr_ptr[XR_VCACHE] = c->v_cache;    c->xr_size[XR_VCACHE] = kv * 4;
+  c->xr_ptr[XR_LOGITS] = c->logits;     c->xr_size[XR_LOGITS] = (size_t)B * c->V * 4;
+  c->xr_ptr[XR_KEYS] = c->step_keys;    c->xr_size[XR_KEYS] = 32;
+  c->xr_ptr[XR_XBAR] = c->step_xbar;    c->xr_size[XR_XBAR] = 16;
   CK(cudaMemset(c->err_flag, 0, 16));
   CK(cudaMemset(c->token_dev, 0, 16 * B));
   CK(cudaMemset(c->pos_dev, 0, 16 * B));
@@ -987,6 +1021,93 @@ extern "C" int hakmc_trace_phase(hakmc_ctx* c, int phase, int layer, unsigned lo
   if (e != cudaSuccess) { set_err("trace: %s", cudaGetErrorString(e)); return HAKMC_ECUDA; }
   return max_ctas < c->num_sms ? max_ctas : c->num_sms;
 }
+
+// ------------------------------------------------------------ tensor parallelism
+
+namespace {
+struct TpHandle {
+  uint32_t magic, version;
+  int32_t pid, device;
+  int32_t vocab, dim, layers, max_seq, max_batch, pad;
+  uint64_t size[XR_COUNT];
+  uint64_t ptr[XR_COUNT];                // for ranks in the same process
+  cudaIpcMemHandle_t ipc[XR_COUNT];      // for ranks in other processes
+};
+constexpr uint32_t TP_MAGIC = 0x48414b54u;  // "HAKT"
+}  // namespace
+
+extern "C" size_t hakmc_tp_handle_bytes(void) { return sizeof(TpHandle); }
+
+extern "C" int hakmc_tp_export(hakmc_ctx* c, void* handle) {
+  if (!c || !handle) return HAKMC_EINVAL;
+  CK(cudaSetDevice(c->device));
+  TpHandle h;
+  memset(&h, 0, sizeof h);
+  h.magic = TP_MAGIC; h.version = 1; h.pid = (int32_t)getpid(); h.device = c->device;
+  h.vocab = c->V; h.dim = c->D; h.layers = c->L; h.max_seq = c->max_seq; h.max_batch = c->max_batch;
+  for (int x = 0; x < XR_COUNT; x++) {
+    h.size[x] = c->xr_size[x];
+    h.ptr[x] = (uint64_t)(uintptr_t)c->xr_ptr[x];
+    CK(cudaIpcGetMemHandle(&h.ipc[x], c->xr_ptr[x]));
+  }
+  memcpy(handle, &h, sizeof h);
+  return 0;
+}
+
+extern "C" int hakmc_tp_connect(hakmc_ctx* c, int rank, int world, const void* handles) {
+  if (!c || !handles || world < 1 || world > TP_MAX || rank < 0 || rank >= world) {
+    set_err("tp_connect: world must be 1..%d and rank within it", TP_MAX);
+    return HAKMC_EINVAL;
+  }
+  if (!c->use_step) { set_err("tp_connect: tensor parallelism needs the step kernel (HAKMC_STEP unset)"); return HAKMC_EINVAL; }
+  if (c->tp_world > 1) { set_err("tp_connect: already connected"); return HAKMC_EINVAL; }
+  CK(cudaSetDevice(c->device));
+  const TpHandle* hs = static_cast<const TpHandle*>(handles);
+  for (int rr = 0; rr < world; rr++) {
+    const TpHandle& h = hs[rr];
+    if (h.magic != TP_MAGIC || h.version != 1 || h.vocab != c->V || h.dim != c->D || h.layers != c->L ||
+        h.max_seq != c->max_seq || h.max_batch != c->max_batch) {
+      set_err("tp_connect: rank %d's context differs (model, max_seq or max_batch)", rr);
+      return HAKMC_EINVAL;
+    }
+    for (int x = 0; x < XR_COUNT; x++)
+      if (h.size[x] != c->xr_size[x]) { set_err("tp_connect: rank %d's regions differ in size", rr); return HAKMC_EINVAL; }
+  }
+  if (hs[rank].pid != (int32_t)getpid() || hs[rank].device != c->device ||
+      hs[rank].ptr[XR_LL] != (uint64_t)(uintptr_t)c->xr_ptr[XR_LL]) {
+    set_err("tp_connect: handle %d is not this context's", rank);
+    return HAKMC_EINVAL;
+  }
+  CK(cudaDeviceSynchronize());
+  for (int rr = 0; rr < world; rr++) {
+    if (rr == rank) continue;
+    const TpHandle& h = hs[rr];
+    if (h.pid == (int32_t)getpid()) {
+      int can = 0;
+      CK(cudaDeviceCanAccessPeer(&can, c->device, h.device));
+      if (!can) { set_err("tp_connect: device %d cannot access device %d", c->device, h.device); return HAKMC_EINVAL; }
+      cudaError_t e = cudaDeviceEnablePeerAccess(h.device, 0);
+      if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled) {
+        set_err("tp_connect: peer access to device %d: %s", h.device, cudaGetErrorString(e));
+        return HAKMC_ECUDA;
+      }
+      cudaGetLastError();
+      for (int x = 0; x < XR_COUNT; x++) c->peer_ptr[rr][x] = (void*)(uintptr_t)h.ptr[x];
+    } else {
+      c->peer_ipc[rr] = true;
+      for (int x = 0; x < XR_COUNT; x++)
+        CK(cudaIpcOpenMemHandle(&c->peer_ptr[rr][x], h.ipc[x], cudaIpcMemLazyEnablePeerAccess));
+    }
+  }
+  for (int x = 0; x < XR_COUNT; x++) c->peer_ptr[rank][x] = c->xr_ptr[x];
+  c->tp_rank = rank;
+  c->tp_world = world;
+  c->prog_layers = -1;  // rebuild the program: rows over all GPUs' CTAs
+  return 0;
+}
+
+extern "C" int hakmc_tp_rank(const hakmc_ctx* c) { return c ? c->tp_rank : -1; }
+extern "C" int hakmc_tp_world(const hakmc_ctx* c) { return c ? c->tp_world : -1; }
 
 extern "C" int hakmc_trace_step(hakmc_ctx* c, unsigned long long* stamps, int max_phases) {
   if (!c || !stamps || max_phases <= 0) return HAKMC_EINVAL;

@@ -65,21 +65,24 @@ __device__ __forceinline__ bool consumers_sync_or(bool v) {
 
 // Called by one thread after a consumers_sync. The release add is cumulative:
 // the CTA's writes that this thread observed through the named barrier are
-// visible to whoever acquires the count.
+// visible to whoever acquires the count. System scope (here and in
+// grid_wait): with tensor parallelism the writes include other GPUs' memory
+// and the waiters include other GPUs' threads; once per step, so the cost of
+// the wider scope does not matter.
 __device__ __forceinline__ void grid_arrive(unsigned* bar) {
-  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+  asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
 }
 
-// Bounded poll of the step counter (relaxed loads, one acquire fence once it
+// Bounded poll of a step counter (relaxed loads, one acquire fence once it
 // is reached); the error flag is looked at every 2^12 cycles.
-static __device__ __noinline__ bool grid_wait(const unsigned* bar, unsigned target, const int* err) {
+__device__ __forceinline__ bool grid_wait(const unsigned* bar, unsigned target, const int* err) {
   unsigned v;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
   if (v < target) {
     const long long t0 = clock64();
     long long next = t0 + 4096;
     for (;;) {
-      asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+      asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
       if (v >= target) break;
       const long long now = clock64();
       if (now > next) {
@@ -88,7 +91,7 @@ static __device__ __noinline__ bool grid_wait(const unsigned* bar, unsigned targ
       }
     }
   }
-  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
   return true;
 }
 
@@ -108,6 +111,16 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint32_t bar, uint32_t parity
 
 __device__ __forceinline__ int key_pick(const unsigned long long* key) {
   return argmax_key_index(__ldcg(key));
+}
+
+// Address p (in region `region` of this GPU) in rank r's copy.
+template <class T>
+__device__ __forceinline__ T* on_rank(const StepArgs& A, T* p, int region, int r) {
+  return reinterpret_cast<T*>(reinterpret_cast<char*>(p) + A.tp_delta[r][region]);
+}
+// A tagged word to every GPU's copy of an exchange vector.
+__device__ __forceinline__ void put_all(const StepArgs& A, uint64_t* p, uint64_t w) {
+  for (int r = 0; r < A.tp_world; r++) ll_st1(on_rank(A, p, XR_LL, r), w);
 }
 
 __device__ __forceinline__ bool phase_runs(const StepArgs& A, int ph, int step) {
@@ -243,9 +256,10 @@ __device__ bool build_activation_ll(const PhaseParams& p, const uint64_t* x, uin
 // vector outputs written as tagged words. res: this thread's prefetched
 // previous residual for row r.row0 + t (EPI_RESID). Returns false if a wait
 // gave up.
-__device__ bool epilogue_ll(const PhaseDesc& D, const SegRange* sr, const float* part, int pos,
+__device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRange* sr, const float* part, int pos,
                             unsigned long long* key, uint32_t tag, uint32_t res_tag, float res, const EpiPre& pre,
                             const int* err) {
+  const int W = A.tp_world;
   const PhaseParams& p = D.g;
   const int t = threadIdx.x - 32, nt = CONSUMER_WARPS * 32;
   unsigned long long best = 0ull;
@@ -260,7 +274,7 @@ __device__ bool epilogue_ll(const PhaseDesc& D, const SegRange* sr, const float*
         const float a0 = row_total(part, r, dr), a1 = row_total(part, r, dr + 1);
         if (S.epi == EPI_SWIGLU) {
           // src/model.c:154 with silu_f (src/nn.c:29)
-          ll_st1(out + (dr >> 1), ll_word(a0 / (1.0f + expf(-a0)) * a1, tag));
+          put_all(A, out + (dr >> 1), ll_word(a0 / (1.0f + expf(-a0)) * a1, tag));
         } else {
           const bool first = q == t;
           const float x0 = S.bias ? a0 + (first ? pre.b0 : S.bias[dr]) : a0;
@@ -275,11 +289,14 @@ __device__ bool epilogue_ll(const PhaseDesc& D, const SegRange* sr, const float*
           const float r1 = x0 * cs.y + x1 * cs.x;
           const int o0 = head * hd + pi, o1 = o0 + half;
           uint64_t* dst = is_k ? D.out2_ll : out;
-          ll_st1(dst + o0, ll_word(r0, tag));
-          ll_st1(dst + o1, ll_word(r1, tag));
+          put_all(A, dst + o0, ll_word(r0, tag));
+          put_all(A, dst + o1, ll_word(r1, tag));
           if (is_k) {
-            S.cache[(size_t)pos * p.kv_dim + o0] = r0;
-            S.cache[(size_t)pos * p.kv_dim + o1] = r1;
+            float* kc = S.cache + (size_t)pos * p.kv_dim;
+            for (int r = 0; r < W; r++) {
+              on_rank(A, kc, XR_KCACHE, r)[o0] = r0;
+              on_rank(A, kc, XR_KCACHE, r)[o1] = r1;
+            }
           }
         }
       }
@@ -290,23 +307,25 @@ __device__ bool epilogue_ll(const PhaseDesc& D, const SegRange* sr, const float*
           case EPI_RESID: {
             float old = res;
             if (row != r.row0 + t) ok &= ll_get1(D.res_ll + row, res_tag, old, err);
-            ll_st1(out + row, ll_word(old + v, tag));
+            put_all(A, out + row, ll_word(old + v, tag));
             break;
           }
           case EPI_V_CACHE: {
             const float o = S.bias ? v + (row == r.row0 + t ? pre.bv : S.bias[row]) : v;
-            ll_st1(out + row, ll_word(o, tag));
-            S.cache[(size_t)pos * p.kv_dim + row] = o;
+            put_all(A, out + row, ll_word(o, tag));
+            float* vc = S.cache + (size_t)pos * p.kv_dim + row;
+            for (int rr = 0; rr < W; rr++) *on_rank(A, vc, XR_VCACHE, rr) = o;
             break;
           }
           case EPI_ARGMAX: {
-            if (S.out) S.out[row] = v;
+            if (S.out)
+              for (int rr = 0; rr < W; rr++) on_rank(A, S.out, XR_LOGITS, rr)[row] = v;
             const unsigned long long kk = argmax_key(v, row);
             best = kk > best ? kk : best;
             break;
           }
           default:
-            ll_st1(out + row, ll_word(S.bias ? v + S.bias[row] : v, tag));
+            put_all(A, out + row, ll_word(S.bias ? v + S.bias[row] : v, tag));
             break;
         }
       }
@@ -318,7 +337,11 @@ __device__ bool epilogue_ll(const PhaseDesc& D, const SegRange* sr, const float*
       const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
       best = other > best ? other : best;
     }
-    if ((t & 31) == 0 && best) atomicMax(key, best);
+    if ((t & 31) == 0 && best) {
+      if (W == 1) atomicMax(key, best);
+      else
+        for (int r = 0; r < W; r++) atomicMax_system(on_rank(A, key, XR_KEYS, r), best);
+    }
   }
   return ok;
 }
@@ -418,8 +441,11 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
   for (int step = 0; step < A.n_steps; step++) {
     const int pos = A.pos0 + step;
     // ---- step barrier: the previous step's pick and K/V rows are complete
+    // (with tensor parallelism: on every GPU, through the cross-GPU counter)
     if (step > 0) {
-      if (t == 0) s_ok = grid_wait(A.bar, (unsigned)step * grid, err);
+      if (t == 0)
+        s_ok = A.tp_world == 1 ? grid_wait(A.bar, (unsigned)step * grid, err)
+                               : grid_wait(A.xbar, (A.xbar_base + (unsigned)step) * (unsigned)A.tp_world, err);
       consumers_sync();
       if (!s_ok) bad = true;
     }
@@ -441,11 +467,12 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
       }
       const int nbD = A.D / QK;
       const uint8_t* row = A.tok_embd + (size_t)token * dev_row_bytes(W_Q6K, nbD);
-      const int per = (A.D + (int)grid - 1) / (int)grid;
-      const int e1 = min(A.D, ((int)blockIdx.x + 1) * per);
+      const int gc = A.tp_rank * (int)grid + (int)blockIdx.x, n_gc = A.tp_world * (int)grid;
+      const int per = (A.D + n_gc - 1) / n_gc;
+      const int e1 = min(A.D, (gc + 1) * per);
       const uint32_t tg = tag_of(step, 0);
-      for (int e = (int)blockIdx.x * per + t; e < e1; e += nt)
-        ll_st1(A.xb_ll + e, ll_word(q6k_dequant_packed(row, nbD, e), tg));
+      for (int e = gc * per + t; e < e1; e += nt)
+        put_all(A, A.xb_ll + e, ll_word(q6k_dequant_packed(row, nbD, e), tg));
     }
     stamp(3);
     kph++;
@@ -553,7 +580,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         if (failed) { atomicExch(A.err_flag, 1); bad = true; }
         if (consumers_sync_or(bad)) goto fail;
         stamp(2);
-        bad |= !epilogue_ll(D, sr, part, pos, P.argmax_key ? A.keys + step % 3 : nullptr, tag, res_tag, res, pre,
+        bad |= !epilogue_ll(A, D, sr, part, pos, P.argmax_key ? A.keys + step % 3 : nullptr, tag, res_tag, res, pre,
                             err);
       } else {
         consumers_sync();  // the next descriptor is staged; CTAs without items have no other barrier here
@@ -569,22 +596,42 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         T.out_tag = tag;
         T.ticket_target = tick;
         T.err = err;
-        const int n_units = a.n_heads / a.head_group;  // (kv head, query-head group) pairs
-        const int items = n_units * a.n_split;
+        T.n_dst = A.tp_world;
+        for (int r = 0; r < A.tp_world; r++) T.out_delta[r] = A.tp_delta[r][XR_LL];
+        // (kv head, query-head group) units; with tensor parallelism this GPU
+        // runs units rank, rank + world, ... (all splits of a unit stay here)
+        const int n_units = a.n_heads / a.head_group;
+        const int n_loc = (n_units - A.tp_rank + A.tp_world - 1) / A.tp_world;
+        const int items = n_loc * a.n_split;
         float* sm = reinterpret_cast<float*>(region);
         for (int it = blockIdx.x; it < items; it += grid)
-          bad |= !attn_item<HD, true>(a, it % n_units, it / n_units, pos, sm, t, nt, ConsumerSync(), T);
+          bad |= !attn_item<HD, true>(a, A.tp_rank + A.tp_world * (it % n_loc), it / n_loc, pos, sm, t, nt,
+                                      ConsumerSync(), T);
       }
       stamp(3);
       kph++;
     }
     // ---- end of step: every CTA's pick and cache rows are in
     if (consumers_sync_or(bad)) goto fail;
-    if (t == 0) grid_arrive(A.bar);
+    if (t == 0) {
+      grid_arrive(A.bar);
+      if (A.tp_world > 1 && blockIdx.x == 0) {
+        // this GPU's CTAs are done: signal every GPU's cross-GPU counter
+        if (grid_wait(A.bar, (unsigned)(step + 1) * grid, err)) {
+          for (int r = 0; r < A.tp_world; r++)
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(on_rank(A, A.xbar, XR_XBAR, r)) : "memory");
+        } else {
+          atomicExch(A.err_flag, 1);
+        }
+      }
+    }
   }
   // the last step's pick: next input token, token log, position
   if (blockIdx.x == 0 && t == 0) {
-    if (grid_wait(A.bar, (unsigned)A.n_steps * grid, err)) {
+    const bool done = A.tp_world == 1
+                          ? grid_wait(A.bar, (unsigned)A.n_steps * grid, err)
+                          : grid_wait(A.xbar, (A.xbar_base + (unsigned)A.n_steps) * (unsigned)A.tp_world, err);
+    if (done) {
       const int tok = key_pick(A.keys + (A.n_steps - 1) % 3);
       *A.token_dev = tok;
       const int j = A.n_steps - 1 - A.log_base;
@@ -608,10 +655,11 @@ __global__ void ll_unpack_kernel(float* out, const uint64_t* in, int n) {
 
 // Host copy of cta_ranges (hakm_gemv.cuh): a segment's 4-row groups split
 // evenly over the grid, each segment's split rotated by the groups before it.
-void step_ranges(const PhaseDesc* prog, int n_phases, int grid, SegRange* out) {
+void step_ranges(const PhaseDesc* prog, int n_phases, int grid, int cta0, int n_ctas, SegRange* out) {
   for (int ph = 0; ph < n_phases; ph++)
-    for (int cta = 0; cta < grid; cta++) {
-      SegRange* sr = out + ((size_t)ph * grid + cta) * MAX_SEGS;
+    for (int lc = 0; lc < n_ctas; lc++) {
+      const int cta = cta0 + lc;
+      SegRange* sr = out + ((size_t)ph * n_ctas + lc) * MAX_SEGS;
       for (int s = 0; s < MAX_SEGS; s++) sr[s] = SegRange{0, 0, 1, 0};
       if (prog[ph].kind != PK_GEMV) continue;
       const PhaseParams& p = prog[ph].g;

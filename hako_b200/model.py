@@ -91,6 +91,18 @@ class HakmCtx:
                                 C.byref(am)), "forward")
         return logits, am.value
 
+    # -- tensor parallelism (hakmc_tp_*)
+    def tp_export(self) -> bytes:
+        """This rank's exchange handle, to be gathered by every rank."""
+        buf = C.create_string_buffer(lib.hakmc_tp_handle_bytes())
+        check(lib.hakmc_tp_export(self._h, buf), "tp_export")
+        return buf.raw
+
+    def tp_connect(self, rank: int, handles) -> None:
+        """Join the group: `handles` are all ranks' tp_export() bytes in rank order."""
+        blob = b"".join(handles)
+        check(lib.hakmc_tp_connect(self._h, rank, len(handles), blob), "tp_connect")
+
     def prefill(self, tokens, want_logits: bool = True):
         """Feed a prompt in one device launch (hakmc_prefill); returns the
         last position's (logits or None, argmax)."""

@@ -130,10 +130,17 @@ def cached_model(cfg: ModelConfig, directory: str | None = None) -> str:
     d = directory or ("/dev/shm" if os.path.isdir("/dev/shm") else "/tmp")
     tag = hashlib.sha1(repr(dataclasses.astuple(cfg)).encode()).hexdigest()[:12]
     path = os.path.join(d, f"hakm_synth_{cfg.name}_{tag}.mlf2")
-    if not os.path.exists(path) or os.path.getsize(path) != model_size(cfg):
-        tmp = path + ".part"
-        write_model(tmp, cfg)
-        os.replace(tmp, path)
+    if os.path.exists(path) and os.path.getsize(path) == model_size(cfg):
+        return path
+    import fcntl
+    # one writer per machine: concurrent callers (e.g. the ranks of a
+    # multi-GPU job) wait for it instead of writing the same file
+    with open(path + ".lock", "w") as lk:
+        fcntl.flock(lk, fcntl.LOCK_EX)
+        if not os.path.exists(path) or os.path.getsize(path) != model_size(cfg):
+            tmp = path + f".{os.getpid()}.part"
+            write_model(tmp, cfg)
+            os.replace(tmp, path)
     return path
 
 

@@ -94,6 +94,25 @@ int hakmc_decode(hakmc_ctx *c, int n_steps, int *out_tokens);
 int hakmc_forward_batch(hakmc_ctx *c, const int *tokens, const int *pos,
                         int n_seq, float *logits, int *argmax);
 
+/* Tensor parallelism over `world` GPUs of one node (no counterpart in the
+ * reference, whose engine runs on one CPU). Every rank creates its own
+ * context with hakmc_create on its own device (same model, max_seq and
+ * max_batch), exports a handle, and hands all ranks' handles (rank order,
+ * world * hakmc_tp_handle_bytes() bytes, e.g. all-gathered over the job's
+ * own transport) to hakmc_tp_connect. From then on every GEMV phase's rows
+ * are split over all GPUs' CTAs and each output vector is written into
+ * every GPU's memory by peer stores over NVLink inside the step kernel (the
+ * float sums are those of one GPU, so results do not change with world).
+ * All ranks must then make the same calls (forward / prefill / generate /
+ * decode / reset with the same arguments) concurrently; every rank gets the
+ * same tokens and logits. Ranks may be threads of one process or separate
+ * processes (CUDA IPC). 0 or a negative code. */
+size_t hakmc_tp_handle_bytes(void);
+int hakmc_tp_export(hakmc_ctx *c, void *handle);
+int hakmc_tp_connect(hakmc_ctx *c, int rank, int world, const void *handles);
+int hakmc_tp_rank(const hakmc_ctx *c);
+int hakmc_tp_world(const hakmc_ctx *c);
+
 /* Test hooks. Run only the first n layers of each forward (the residual
  * stream is then what the reference holds in hakm_ctx.xb after that many
  * layers, src/model.c:102-157); n < 0 restores all layers. */
