@@ -267,7 +267,7 @@ def main():
         with open(tpath) as f:
             per_tok = json.load(f).get(f"step_kernel_{args.model}_bytes_per_token")
         if per_tok:
-            traffic = per_tok * args.steps
+            traffic = per_tok * args.steps / world  # per GPU, like bytes_per_launch
     tok_bytes = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(pos0 + args.steps // 2)
 
     line = {"metric": "decode tok/s (batch 1)", "value": value, "unit": "tok/s", "n_gpus": world,
