@@ -33,16 +33,23 @@ struct AttnLL {
   unsigned ticket_target;
   const int* err;
   int n_dst;                      // GPUs the output goes to (tensor parallelism), 1 otherwise
-  long long out_delta[8];         // byte offset of each GPU's copy of `out`
+  // byte offset of GPU r's copy of `out`: out_delta[r * delta_stride] (a
+  // pointer into the kernel's parameters, so no per-thread copy is made)
+  const long long* out_delta;
+  int delta_stride;
 };
 
 // Tagged output words to every destination GPU.
 __device__ __forceinline__ void attn_put1(const AttnLL& T, uint64_t* p, uint64_t w) {
-  for (int r = 0; r < T.n_dst; r++) ll_st1(reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(p) + T.out_delta[r]), w);
+  if (T.n_dst == 1) { ll_st1(p, w); return; }
+  for (int r = 0; r < T.n_dst; r++)
+    ll_st1(reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(p) + T.out_delta[r * T.delta_stride]), w);
 }
 __device__ __forceinline__ void attn_put2(const AttnLL& T, uint64_t* p, float a, float b) {
+  if (T.n_dst == 1) { ll_put2(p, a, b, T.out_tag); return; }
   for (int r = 0; r < T.n_dst; r++)
-    ll_put2(reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(p) + T.out_delta[r]), a, b, T.out_tag);
+    ll_put2(reinterpret_cast<uint64_t*>(reinterpret_cast<char*>(p) + T.out_delta[r * T.delta_stride]), a, b,
+            T.out_tag);
 }
 
 // Most splits the merge can combine: their statistics (2 per split and

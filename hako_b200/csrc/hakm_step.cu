@@ -118,8 +118,13 @@ template <class T>
 __device__ __forceinline__ T* on_rank(const StepArgs& A, T* p, int region, int r) {
   return reinterpret_cast<T*>(reinterpret_cast<char*>(p) + A.tp_delta[r][region]);
 }
+// GPUs an output goes to: compile-time 1 in the single-GPU kernel instance.
+template <bool TP>
+__device__ __forceinline__ int n_ranks(const StepArgs& A) { return TP ? A.tp_world : 1; }
 // A tagged word to every GPU's copy of an exchange vector.
+template <bool TP>
 __device__ __forceinline__ void put_all(const StepArgs& A, uint64_t* p, uint64_t w) {
+  if (!TP) { ll_st1(p, w); return; }
   for (int r = 0; r < A.tp_world; r++) ll_st1(on_rank(A, p, XR_LL, r), w);
 }
 
@@ -256,10 +261,11 @@ __device__ bool build_activation_ll(const PhaseParams& p, const uint64_t* x, uin
 // vector outputs written as tagged words. res: this thread's prefetched
 // previous residual for row r.row0 + t (EPI_RESID). Returns false if a wait
 // gave up.
+template <bool TP>
 __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRange* sr, const float* part, int pos,
                             unsigned long long* key, uint32_t tag, uint32_t res_tag, float res, const EpiPre& pre,
                             const int* err) {
-  const int W = A.tp_world;
+  const int W = n_ranks<TP>(A);
   const PhaseParams& p = D.g;
   const int t = threadIdx.x - 32, nt = CONSUMER_WARPS * 32;
   unsigned long long best = 0ull;
@@ -274,7 +280,7 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
         const float a0 = row_total(part, r, dr), a1 = row_total(part, r, dr + 1);
         if (S.epi == EPI_SWIGLU) {
           // src/model.c:154 with silu_f (src/nn.c:29)
-          put_all(A, out + (dr >> 1), ll_word(a0 / (1.0f + expf(-a0)) * a1, tag));
+          put_all<TP>(A, out + (dr >> 1), ll_word(a0 / (1.0f + expf(-a0)) * a1, tag));
         } else {
           const bool first = q == t;
           const float x0 = S.bias ? a0 + (first ? pre.b0 : S.bias[dr]) : a0;
@@ -289,8 +295,8 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
           const float r1 = x0 * cs.y + x1 * cs.x;
           const int o0 = head * hd + pi, o1 = o0 + half;
           uint64_t* dst = is_k ? D.out2_ll : out;
-          put_all(A, dst + o0, ll_word(r0, tag));
-          put_all(A, dst + o1, ll_word(r1, tag));
+          put_all<TP>(A, dst + o0, ll_word(r0, tag));
+          put_all<TP>(A, dst + o1, ll_word(r1, tag));
           if (is_k) {
             float* kc = S.cache + (size_t)pos * p.kv_dim;
             for (int r = 0; r < W; r++) {
@@ -307,12 +313,12 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
           case EPI_RESID: {
             float old = res;
             if (row != r.row0 + t) ok &= ll_get1(D.res_ll + row, res_tag, old, err);
-            put_all(A, out + row, ll_word(old + v, tag));
+            put_all<TP>(A, out + row, ll_word(old + v, tag));
             break;
           }
           case EPI_V_CACHE: {
             const float o = S.bias ? v + (row == r.row0 + t ? pre.bv : S.bias[row]) : v;
-            put_all(A, out + row, ll_word(o, tag));
+            put_all<TP>(A, out + row, ll_word(o, tag));
             float* vc = S.cache + (size_t)pos * p.kv_dim + row;
             for (int rr = 0; rr < W; rr++) *on_rank(A, vc, XR_VCACHE, rr) = o;
             break;
@@ -325,7 +331,7 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
             break;
           }
           default:
-            put_all(A, out + row, ll_word(S.bias ? v + S.bias[row] : v, tag));
+            put_all<TP>(A, out + row, ll_word(S.bias ? v + S.bias[row] : v, tag));
             break;
         }
       }
@@ -346,7 +352,7 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
   return ok;
 }
 
-template <int HD>
+template <int HD, bool TP>
 __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant__ StepArgs A) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -472,7 +478,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
       const int e1 = min(A.D, (gc + 1) * per);
       const uint32_t tg = tag_of(step, 0);
       for (int e = gc * per + t; e < e1; e += nt)
-        put_all(A, A.xb_ll + e, ll_word(q6k_dequant_packed(row, nbD, e), tg));
+        put_all<TP>(A, A.xb_ll + e, ll_word(q6k_dequant_packed(row, nbD, e), tg));
     }
     stamp(3);
     kph++;
@@ -580,7 +586,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         if (failed) { atomicExch(A.err_flag, 1); bad = true; }
         if (consumers_sync_or(bad)) goto fail;
         stamp(2);
-        bad |= !epilogue_ll(A, D, sr, part, pos, P.argmax_key ? A.keys + step % 3 : nullptr, tag, res_tag, res, pre,
+        bad |= !epilogue_ll<TP>(A, D, sr, part, pos, P.argmax_key ? A.keys + step % 3 : nullptr, tag, res_tag, res, pre,
                             err);
       } else {
         consumers_sync();  // the next descriptor is staged; CTAs without items have no other barrier here
@@ -596,8 +602,9 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         T.out_tag = tag;
         T.ticket_target = tick;
         T.err = err;
-        T.n_dst = A.tp_world;
-        for (int r = 0; r < A.tp_world; r++) T.out_delta[r] = A.tp_delta[r][XR_LL];
+        T.n_dst = n_ranks<TP>(A);
+        T.out_delta = &A.tp_delta[0][XR_LL];
+        T.delta_stride = XR_COUNT;
         // (kv head, query-head group) units; with tensor parallelism this GPU
         // runs units rank, rank + world, ... (all splits of a unit stay here)
         const int n_units = a.n_heads / a.head_group;
@@ -747,13 +754,13 @@ bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
   return step_smem_bytes(a) <= (size_t)STEP_SMEM_MAX;
 }
 
-template <int HD>
+template <int HD, bool TP>
 static cudaError_t launch_step_hd(const StepArgs& a, int grid, cudaStream_t s) {
   static unsigned done = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 32 && !(done & (1u << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(step_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, STEP_SMEM_MAX);
+    cudaError_t e = cudaFuncSetAttribute(step_kernel<HD, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, STEP_SMEM_MAX);
     if (e != cudaSuccess) return e;
     done |= 1u << dev;
   }
@@ -767,12 +774,13 @@ static cudaError_t launch_step_hd(const StepArgs& a, int grid, cudaStream_t s) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, step_kernel<HD>, a);
+  return cudaLaunchKernelEx(&cfg, step_kernel<HD, TP>, a);
 }
 
 cudaError_t launch_step(const StepArgs& a, int grid, cudaStream_t s) {
-  if (a.head_dim == 128) return launch_step_hd<128>(a, grid, s);
-  if (a.head_dim == 64) return launch_step_hd<64>(a, grid, s);
+  const bool tp = a.tp_world > 1;
+  if (a.head_dim == 128) return tp ? launch_step_hd<128, true>(a, grid, s) : launch_step_hd<128, false>(a, grid, s);
+  if (a.head_dim == 64) return tp ? launch_step_hd<64, true>(a, grid, s) : launch_step_hd<64, false>(a, grid, s);
   return cudaErrorInvalidValue;
 }
 
