@@ -50,6 +50,14 @@ __device__ __forceinline__ float q8_inv(float amax, float scale) {
   return scale > 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
 }
 
+// NeoX RoPE rotation of the pair (a, b) with the roundings of the reference
+// as built (src/nn.c:38-40 under gcc -O3 -ffast-math with FMA): the b
+// products are rounded on their own, the a products fused:
+//   a' = fma(a, c, -(b*s)),  b' = fma(a, s, b*c).
+__device__ __forceinline__ float2 rope_rotate(float a, float b, float c, float s) {
+  return make_float2(__fmaf_rn(a, c, -__fmul_rn(b, s)), __fmaf_rn(a, s, __fmul_rn(b, c)));
+}
+
 // Monotonic key for argmax: larger value wins, equal values -> lower index.
 __device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
   uint32_t u = __float_as_uint(v);

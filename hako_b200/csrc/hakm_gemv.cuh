@@ -573,8 +573,8 @@ static __device__ void epilogue(const PhaseParams& p, const SegRange* sr, const 
           const int head = lr / hd, pi = (lr % hd) >> 1;
           const float2 cs = reinterpret_cast<const float2*>(p.rope_cs)[(size_t)pos * half + pi];
           // src/nn.c:38-40
-          const float r0 = x0 * cs.x - x1 * cs.y;
-          const float r1 = x0 * cs.y + x1 * cs.x;
+          const float2 rr = rope_rotate(x0, x1, cs.x, cs.y);
+          const float r0 = rr.x, r1 = rr.y;
           const int o0 = head * hd + pi, o1 = o0 + half;
           float* dst = is_k ? S.out2 : S.out;
           dst[o0] = r0;

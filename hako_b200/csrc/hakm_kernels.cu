@@ -181,8 +181,9 @@ __global__ void rope_kernel(float* x, const float* rope_cs, const int* pos_dev, 
   const int pos = pos_dev ? *pos_dev : 0;
   const float2 cs = reinterpret_cast<const float2*>(rope_cs)[(size_t)pos * half + i];
   const float a = x[h * hd + i], b = x[h * hd + i + half];
-  x[h * hd + i] = a * cs.x - b * cs.y;
-  x[h * hd + i + half] = a * cs.y + b * cs.x;
+  const float2 r = rope_rotate(a, b, cs.x, cs.y);
+  x[h * hd + i] = r.x;
+  x[h * hd + i + half] = r.y;
 }
 
 cudaError_t launch_rope(float* x, const float* rope_cs, const int* pos_dev, int n_heads, int head_dim,

@@ -257,6 +257,98 @@ __device__ bool build_activation_ll(const PhaseParams& p, const uint64_t* x, uin
   return ok;
 }
 
+// Epilogue record of one thread for one segment: its first output item,
+// prepared at the start of the phase (off the critical path) so that after
+// the last unit only the partial sums remain to be read. kind: 0 none, else
+// an Epi code (EPI_ROPE_QK split into q and k by EPI_ROPE_K) | nch << 8.
+constexpr int EPI_ROPE_K = 16;
+struct __align__(16) EpiRec {
+  int kind, pidx, o0, o1;
+  float f0, f1, f2, f3;  // ROPE: bias pair, (cos, sin); RESID: residual; V / STORE: bias
+};
+constexpr int EPI_RECS = 2;  // segments with records
+
+__device__ __forceinline__ EpiRec epi_prepare(const PhaseDesc& D, const SegRange* sr, int s, int pos, int t,
+                                              uint32_t res_tag, bool& ok, const int* err) {
+  const PhaseParams& p = D.g;
+  const Seg& S = p.seg[s];
+  const SegRange& r = sr[s];
+  EpiRec e = {0, 0, 0, 0, 0.f, 0.f, 0.f, 0.f};
+  if (S.epi == EPI_ROPE_QK || S.epi == EPI_SWIGLU) {
+    if (2 * t + 1 >= r.row1 - r.row0) return e;
+    const int dr = r.row0 + 2 * t;
+    e.pidx = r.part_base + 2 * t * r.nch;
+    if (S.epi == EPI_SWIGLU) {
+      e.kind = EPI_SWIGLU | (r.nch << 8);
+      e.o0 = dr >> 1;
+      return e;
+    }
+    const bool is_k = dr >= S.split;
+    const int lr = is_k ? dr - S.split : dr;
+    const int hd = p.head_dim, half = hd >> 1;
+    const int head = lr / hd, pi = (lr % hd) >> 1;
+    e.kind = (is_k ? EPI_ROPE_K : EPI_ROPE_QK) | (r.nch << 8);
+    e.o0 = head * hd + pi;
+    e.o1 = e.o0 + half;
+    if (S.bias) { e.f0 = __ldg(S.bias + dr); e.f1 = __ldg(S.bias + dr + 1); }
+    const float2 cs = __ldg(reinterpret_cast<const float2*>(p.rope_cs) + (size_t)pos * half + pi);
+    e.f2 = cs.x;
+    e.f3 = cs.y;
+    return e;
+  }
+  const int row = r.row0 + t;
+  if (row >= r.row1 || S.epi == EPI_ARGMAX) return e;
+  e.kind = S.epi | (r.nch << 8);
+  e.pidx = r.part_base + t * r.nch;
+  e.o0 = row;
+  if (S.epi == EPI_RESID) ok &= ll_get1(D.res_ll + row, res_tag, e.f0, err);
+  else if (S.bias) e.f0 = __ldg(S.bias + row);
+  return e;
+}
+
+// The prepared first items: partial sums, arithmetic, stores.
+template <bool TP>
+__device__ __forceinline__ void epi_apply(const StepArgs& A, const PhaseDesc& D, int s, const EpiRec& e,
+                                          const float* part, int pos, uint32_t tag) {
+  const int kind = e.kind & 255, nch = e.kind >> 8;
+  if (!kind) return;
+  const PhaseParams& p = D.g;
+  const float* pp = part + e.pidx;
+  float a0 = pp[0];
+  for (int c = 1; c < nch; c++) a0 += pp[c];
+  if (kind == EPI_SWIGLU || kind == EPI_ROPE_QK || kind == EPI_ROPE_K) {
+    float a1 = pp[nch];
+    for (int c = 1; c < nch; c++) a1 += pp[nch + c];
+    if (kind == EPI_SWIGLU) {
+      // src/model.c:154 with silu_f (src/nn.c:29)
+      put_all<TP>(A, D.out_ll[s] + e.o0, ll_word(a0 / (1.0f + expf(-a0)) * a1, tag));
+      return;
+    }
+    const float x0 = a0 + e.f0, x1 = a1 + e.f1;
+    // src/nn.c:38-40
+    const float2 rr = rope_rotate(x0, x1, e.f2, e.f3);
+    const float r0 = rr.x, r1 = rr.y;
+    const bool is_k = kind == EPI_ROPE_K;
+    uint64_t* dst = is_k ? D.out2_ll : D.out_ll[s];
+    put_all<TP>(A, dst + e.o0, ll_word(r0, tag));
+    put_all<TP>(A, dst + e.o1, ll_word(r1, tag));
+    if (is_k) {
+      float* kc = p.seg[s].cache + (size_t)pos * p.kv_dim;
+      for (int r = 0; r < n_ranks<TP>(A); r++) {
+        on_rank(A, kc, XR_KCACHE, r)[e.o0] = r0;
+        on_rank(A, kc, XR_KCACHE, r)[e.o1] = r1;
+      }
+    }
+    return;
+  }
+  const float o = a0 + e.f0;  // residual or bias (0 when none)
+  put_all<TP>(A, D.out_ll[s] + e.o0, ll_word(o, tag));
+  if (kind == EPI_V_CACHE) {
+    float* vc = p.seg[s].cache + (size_t)pos * p.kv_dim + e.o0;
+    for (int r = 0; r < n_ranks<TP>(A); r++) *on_rank(A, vc, XR_VCACHE, r) = o;
+  }
+}
+
 // Epilogue of a GEMV phase of the step program: as epilogue(), with the
 // vector outputs written as tagged words. res: this thread's prefetched
 // previous residual for row r.row0 + t (EPI_RESID). Returns false if a wait
@@ -264,7 +356,7 @@ __device__ bool build_activation_ll(const PhaseParams& p, const uint64_t* x, uin
 template <bool TP>
 __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRange* sr, const float* part, int pos,
                             unsigned long long* key, uint32_t tag, uint32_t res_tag, float res, const EpiPre& pre,
-                            const int* err) {
+                            const int* err, int n_done = 0) {
   const int W = n_ranks<TP>(A);
   const PhaseParams& p = D.g;
   const int t = threadIdx.x - 32, nt = CONSUMER_WARPS * 32;
@@ -274,8 +366,9 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
     const Seg& S = p.seg[s];
     const SegRange& r = sr[s];
     uint64_t* out = D.out_ll[s];
+    const int first = s < n_done ? nt : 0;  // items done from the records
     if (S.epi == EPI_ROPE_QK || S.epi == EPI_SWIGLU) {
-      for (int q = t; 2 * q + 1 < r.row1 - r.row0; q += nt) {
+      for (int q = t + first; 2 * q + 1 < r.row1 - r.row0; q += nt) {
         const int dr = r.row0 + 2 * q;
         const float a0 = row_total(part, r, dr), a1 = row_total(part, r, dr + 1);
         if (S.epi == EPI_SWIGLU) {
@@ -291,8 +384,8 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
           const int head = lr / hd, pi = (lr % hd) >> 1;
           const float2 cs = first ? pre.cs : reinterpret_cast<const float2*>(p.rope_cs)[(size_t)pos * half + pi];
           // src/nn.c:38-40
-          const float r0 = x0 * cs.x - x1 * cs.y;
-          const float r1 = x0 * cs.y + x1 * cs.x;
+          const float2 rr = rope_rotate(x0, x1, cs.x, cs.y);
+          const float r0 = rr.x, r1 = rr.y;
           const int o0 = head * hd + pi, o1 = o0 + half;
           uint64_t* dst = is_k ? D.out2_ll : out;
           put_all<TP>(A, dst + o0, ll_word(r0, tag));
@@ -307,7 +400,7 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
         }
       }
     } else {
-      for (int row = r.row0 + t; row < r.row1; row += nt) {
+      for (int row = r.row0 + t + (S.epi == EPI_ARGMAX ? 0 : first); row < r.row1; row += nt) {
         const float v = row_total(part, r, row);
         switch (S.epi) {
           case EPI_RESID: {
@@ -526,20 +619,31 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
           }
         }
         float res = 0.f;
+        bool ok_pre = true;
         const uint32_t res_tag = tag_of(step, D.res_src);
-        if (P.seg[0].epi == EPI_RESID && sr[0].row0 + t < sr[0].row1)
-          bad |= !ll_get1(D.res_ll + sr[0].row0 + t, res_tag, res, err);
+        // epilogue records of this thread (its own slots: no barrier needed)
+        int n_rec = 0;
+        EpiRec* recs = nullptr;
         EpiPre pre;
-        if (P.seg[0].epi == EPI_ROPE_QK && 2 * t + 1 < sr[0].row1 - sr[0].row0) {
-          const Seg& S0 = P.seg[0];
-          const int dr = sr[0].row0 + 2 * t;
-          if (S0.bias) { pre.b0 = __ldg(S0.bias + dr); pre.b1 = __ldg(S0.bias + dr + 1); }
-          const int lr = dr >= S0.split ? dr - S0.split : dr;
-          const int half = P.head_dim >> 1;
-          pre.cs = __ldg(reinterpret_cast<const float2*>(P.rope_cs) + (size_t)pos * half + ((lr % P.head_dim) >> 1));
+        if (D.epi_rec_off >= 0) {
+          recs = reinterpret_cast<EpiRec*>(region + D.epi_rec_off) + t * EPI_RECS;
+          n_rec = min(P.n_seg, EPI_RECS);
+          for (int s = 0; s < n_rec; s++) recs[s] = epi_prepare(D, sr, s, pos, t, res_tag, ok_pre, err);
+        } else {
+          // no room for records: the first items' operands in registers
+          if (P.seg[0].epi == EPI_RESID && sr[0].row0 + t < sr[0].row1)
+            bad |= !ll_get1(D.res_ll + sr[0].row0 + t, res_tag, res, err);
+          if (P.seg[0].epi == EPI_ROPE_QK && 2 * t + 1 < sr[0].row1 - sr[0].row0) {
+            const Seg& S0 = P.seg[0];
+            const int dr = sr[0].row0 + 2 * t;
+            if (S0.bias) { pre.b0 = __ldg(S0.bias + dr); pre.b1 = __ldg(S0.bias + dr + 1); }
+            const int lr = dr >= S0.split ? dr - S0.split : dr;
+            const int half = P.head_dim >> 1;
+            pre.cs = __ldg(reinterpret_cast<const float2*>(P.rope_cs) + (size_t)pos * half + ((lr % P.head_dim) >> 1));
+          }
+          if (P.n_seg > 1 && P.seg[1].epi == EPI_V_CACHE && P.seg[1].bias && sr[1].row0 + t < sr[1].row1)
+            pre.bv = __ldg(P.seg[1].bias + sr[1].row0 + t);
         }
-        if (P.n_seg > 1 && P.seg[1].epi == EPI_V_CACHE && P.seg[1].bias && sr[1].row0 + t < sr[1].row1)
-          pre.bv = __ldg(P.seg[1].bias + sr[1].row0 + t);
         const Act X = carve_act(region, K, P.need_q8, P.need_q6);
         float* plain = (P.seg[0].epi == EPI_ARGMAX && blockIdx.x == 0) ? A.xb_plain : nullptr;
         bad |= !build_activation_ll(P, D.x_ll, tag_of(step, D.x_src), wpre, X, red, err, plain);
@@ -586,8 +690,12 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         if (failed) { atomicExch(A.err_flag, 1); bad = true; }
         if (consumers_sync_or(bad)) goto fail;
         stamp(2);
+        for (int s = 0; s < n_rec; s++) epi_apply<TP>(A, D, s, recs[s], part, pos, tag);
+        bad |= !ok_pre;
         bad |= !epilogue_ll<TP>(A, D, sr, part, pos, P.argmax_key ? A.keys + step % 3 : nullptr, tag, res_tag, res, pre,
-                            err);
+                                err, n_rec);
+        // the next phase's activation may be built over these records
+        if (n_rec) consumers_sync();
       } else {
         consumers_sync();  // the next descriptor is staged; CTAs without items have no other barrier here
         AttnParams a = D.a;
@@ -614,6 +722,9 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         for (int it = blockIdx.x; it < items; it += grid)
           bad |= !attn_item<HD, true>(a, A.tp_rank + A.tp_world * (it % n_loc), it / n_loc, pos, sm, t, nt,
                                       ConsumerSync(), T);
+        // the next phase writes the shared region (activation, epilogue
+        // records): every thread must be done with the attention tiles
+        consumers_sync();
       }
       stamp(3);
       kph++;
@@ -741,7 +852,14 @@ bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
   a.slot_bytes = (int)slot;
   for (int ph = 0; ph < n_phases; ph++) {
     PhaseDesc& D = prog[ph];
+    D.epi_rec_off = -1;
     if (D.kind != PK_GEMV) continue;
+    {
+      // per-thread epilogue records past the activation, when they fit
+      const size_t act = (act_bytes(D.g.n_in, D.g.need_q8, D.g.need_q6) + 15) & ~(size_t)15;
+      const size_t recs = (size_t)CONSUMER_WARPS * 32 * EPI_RECS * sizeof(EpiRec);
+      if (act + recs <= (size_t)a.region_bytes) D.epi_rec_off = (int)act;
+    }
     const int nb = D.g.n_in / QK;
     for (int s = 0; s < D.g.n_seg; s++) {
       D.st_rows[s] = stage_rows_for(D.g.seg[s].type, nb, a.slot_bytes);

@@ -232,8 +232,10 @@ void orc_rope_neox(float *vec, int head_dim, int pos, float theta) {
 		float ang = (float)pos * freq;
 		float c = cosf(ang), s = sinf(ang);
 		float a = vec[i], b = vec[i + half];
-		vec[i] = a * c - b * s;
-		vec[i + half] = a * s + b * c;
+		/* the roundings of the reference as built (-ffast-math with FMA):
+		 * the b products rounded on their own, the a products fused */
+		vec[i] = fmaf(a, c, -(b * s));
+		vec[i + half] = fmaf(a, s, b * c);
 	}
 }
 
