@@ -385,6 +385,9 @@ __device__ __forceinline__ Q4X q4x_load(const int8_t* xq, const float* xs, const
   return X;
 }
 
+// NR rows (4, or 2 for phases with few rows per CTA: half the latency of a
+// unit); acc[NR..3] stay 0.
+template <int NR = 4>
 __device__ __forceinline__ void q4k_unit(const uint8_t* st, int rstride, int nrows, int m, const Q4X& X,
                                          float acc[4]) {
   const int lane = threadIdx.x & 31, bl = lane >> 2, g = lane & 3;
@@ -392,9 +395,9 @@ __device__ __forceinline__ void q4k_unit(const uint8_t* st, int rstride, int nro
   for (int r = 0; r < 4; r++) acc[r] = 0.f;
   if (bl >= m) return;
   // all four rows' loads first (rows past nrows re-read row 0, result unused)
-  uint4 hd[4], q0[4], q1[4];
+  uint4 hd[NR], q0[NR], q1[NR];
 #pragma unroll
-  for (int r = 0; r < 4; r++) {
+  for (int r = 0; r < NR; r++) {
     const uint8_t* blk = st + (r < nrows ? r : 0) * rstride + bl * Q4K_BYTES;
     hd[r] = *reinterpret_cast<const uint4*>(blk);
     q0[r] = *reinterpret_cast<const uint4*>(blk + 16 + 32 * g);
@@ -403,7 +406,7 @@ __device__ __forceinline__ void q4k_unit(const uint8_t* st, int rstride, int nro
   const int shf = 16 * (g & 1);  // scale bytes of j = 2g, 2g+1 within their words
   const bool low = g < 2;        // j < 4: plain 6-bit fields (src/quant.c:59-61)
 #pragma unroll
-  for (int r = 0; r < 4; r++) {
+  for (int r = 0; r < NR; r++) {
     const uint32_t qw[8] = {q0[r].x, q0[r].y, q0[r].z, q0[r].w, q1[r].x, q1[r].y, q1[r].z, q1[r].w};
     int ia = 0, ib = 0;
 #pragma unroll
@@ -481,6 +484,7 @@ __device__ __forceinline__ float group_dot(const uint32_t q[4], const uint4& l0,
   return fmaf(s2, 65536.0f, fmaf(s1, 256.0f, s0)) - xs32;
 }
 
+template <int NR = 4>
 __device__ __forceinline__ void q6k_unit(const uint8_t* st, int rstride, int nrows, int m, const Q6L& X,
                                          float acc[4]) {
   const int lane = threadIdx.x & 31, bq = lane >> 3, n = (lane >> 2) & 1, k = lane & 3;
@@ -491,11 +495,11 @@ __device__ __forceinline__ void q6k_unit(const uint8_t* st, int rstride, int nro
   for (int pass = 0; pass < 2; pass++) {
     const int bl = 4 * pass + bq;
     if (bl >= m) continue;
-    uint4 ql[4], qh[4];
-    uint2 sc[4];
-    float d[4];
+    uint4 ql[NR], qh[NR];
+    uint2 sc[NR];
+    float d[NR];
 #pragma unroll
-    for (int r = 0; r < 4; r++) {  // rows past nrows re-read row 0, result unused
+    for (int r = 0; r < NR; r++) {  // rows past nrows re-read row 0, result unused
       const uint8_t* chunk = st + (r < nrows ? r : 0) * rstride;
       const uint8_t* body = chunk + bl * Q6K_BODY;
       ql[r] = *reinterpret_cast<const uint4*>(body + 64 * n + 16 * k);
@@ -504,7 +508,7 @@ __device__ __forceinline__ void q6k_unit(const uint8_t* st, int rstride, int nro
       d[r] = __half2float(*reinterpret_cast<const __half*>(chunk + m * Q6K_BODY + 2 * bl));
     }
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
+    for (int r = 0; r < NR; r++) {
       const uint32_t lw[4] = {ql[r].x, ql[r].y, ql[r].z, ql[r].w};
       const uint32_t hw[4] = {qh[r].x, qh[r].y, qh[r].z, qh[r].w};
       uint32_t qlo[4], qhi[4];

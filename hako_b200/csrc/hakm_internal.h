@@ -178,6 +178,7 @@ struct alignas(16) PhaseDesc {  // copied to shared memory as 16-byte words
   // stage geometry of each GEMV segment (plan_step): rows per stage, row
   // bytes, chunks per row, and ceil(2^16 / chunks) for unit -> (group, chunk)
   int st_rows[MAX_SEGS], st_row_bytes[MAX_SEGS], st_nch[MAX_SEGS], st_rn[MAX_SEGS];
+  int st_unit_rows[MAX_SEGS];  // rows per unit: 4, or 2 where a CTA holds few rows (shorter latency)
   // byte offset, within the shared activation region, of the per-thread
   // epilogue records (past this phase's activation); -1: no room, no records
   int epi_rec_off;

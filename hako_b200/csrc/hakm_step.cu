@@ -162,7 +162,7 @@ struct EpiPre {
 // rows per stage (one bulk copy), units of 4 rows x one chunk. unit -> (row
 // group, chunk) uses a multiply-shift (exact for unit < 2^16 / nch).
 struct SegGeo {
-  int type, rowB, R, nch, chunkB, rn;
+  int type, rowB, R, nch, chunkB, rn, ur;
 };
 // Read from the descriptor (computed by plan_step on the host).
 __device__ __forceinline__ SegGeo seg_geo(const PhaseDesc& D, int s) {
@@ -173,6 +173,7 @@ __device__ __forceinline__ SegGeo seg_geo(const PhaseDesc& D, int s) {
   g.nch = D.st_nch[s];
   g.chunkB = g.type == W_Q4K ? Q4K_CHUNK : Q6K_CHUNK;
   g.rn = D.st_rn[s];
+  g.ur = D.st_unit_rows[s];
   return g;
 }
 
@@ -652,7 +653,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         bool failed = false;
         for (int s = 0; s < P.n_seg && !failed; s++) {
           const SegGeo G = seg_geo(D, s);
-          const int n_units_full = ((G.R + 3) / 4) * G.nch;
+          const int n_units_full = ((G.R + G.ur - 1) / G.ur) * G.nch;
           float* ps = part + sr[s].part_base;
           for (int rt = sr[s].row0; rt < sr[s].row1; rt += G.R) {
             if (!mbar_wait_or_abort(smem_addr(&full[rc.slot]), rc.par, err)) {
@@ -665,17 +666,20 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
             const int first = (int)((unsigned)(cw + CONSUMER_WARPS) - ucount % CONSUMER_WARPS) % CONSUMER_WARPS;
             for (int u = first; u < n_units_full; u += CONSUMER_WARPS) {
               const int grp = (u * G.rn) >> 16, c = u - grp * G.nch;
-              const int t0 = 4 * grp, nru = min(4, nr - t0);
+              const int t0 = G.ur * grp, nru = min(G.ur, nr - t0);
               if (nru <= 0) continue;
               const uint8_t* st = stage + t0 * G.rowB + c * G.chunkB;
               const int m = q6_chunk_blocks(nb, c);
               float acc[4];
               if (G.type == W_Q4K) {
-                q4k_unit(st, G.rowB, nru, m, q4x_load(X.xq, X.xs, X.xsum, c, nb), acc);
+                const Q4X xq = q4x_load(X.xq, X.xs, X.xsum, c, nb);
+                if (G.ur == 2) q4k_unit<2>(st, G.rowB, nru, m, xq, acc);
+                else q4k_unit<4>(st, G.rowB, nru, m, xq, acc);
               } else {
                 Q6L L;
                 q6l_load(X, c, nb, L);
-                q6k_unit(st, G.rowB, nru, m, L, acc);
+                if (G.ur == 2) q6k_unit<2>(st, G.rowB, nru, m, L, acc);
+                else q6k_unit<4>(st, G.rowB, nru, m, L, acc);
               }
               const float tot = reduce4(acc);
               if ((lane & 7) == 0 && (lane >> 3) < nru)
@@ -867,6 +871,11 @@ bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
       D.st_nch[s] = n_chunks(nb);
       D.st_rn[s] = (65536 + D.st_nch[s] - 1) / D.st_nch[s];
       if (D.st_rows[s] < 1) return false;
+      // a segment that gives each CTA a single 4-row unit (the 3B attn_v
+      // rows) runs as two 2-row units on two warps: half the latency. With
+      // more units per CTA the extra activation loads cost more (measured).
+      const int max_groups = ((D.g.seg[s].n_rows + 3) / 4 + grid - 1) / grid;
+      D.st_unit_rows[s] = max_groups * D.st_nch[s] == 1 ? 2 : 4;
     }
   }
   return step_smem_bytes(a) <= (size_t)STEP_SMEM_MAX;
