@@ -184,6 +184,94 @@ def run_reference_arm(args):
     return 0
 
 
+GEMV_SHAPES = [(2048, 2048), (256, 2048), (11008, 2048), (2048, 11008), (18944, 3584), (3584, 18944)]
+GEMV_BATCHES = (1, 4, 16, 64)
+LMHEAD_SHAPES = [(151936, 2048), (152064, 3584)]
+
+
+def _graph_us(torch, stream, launch, reps):
+    """Per-launch device time of `reps` back-to-back launches captured in one
+    CUDA graph (no host launch cost), replayed 3 times between CUDA events."""
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            launch(i)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for i in range(reps):
+            launch(i)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / (3 * reps) * 1e3
+    del g
+    return us
+
+
+def gemv_sweep(device, hbm_gbs):
+    """Config 1 (batched Q4_K x q8_32 matmul) and config 2 (Q6_K lm_head +
+    greedy argmax): achieved HBM GB/s of the C-ABI kernels. Algorithmic bytes
+    = rows*(K/256)*144 + N*(K + 4K/32) + N*rows*4 (Q4_K) and the Q6_K rows +
+    the activation (lm_head). Each launch reads a different weight copy
+    (copies together > 300 MB, beyond the 126 MB L2)."""
+    import ctypes as C
+    import torch
+    from hako_b200 import check, lib, synth
+    P = lambda t: C.c_void_p(t.data_ptr())
+    s = torch.cuda.Stream(device)
+    sp = C.c_void_p(s.cuda_stream)
+    rows_out = []
+    for rows, k in GEMV_SHAPES:
+        wb = rows * (k // 256) * 144
+        ncopy = max(2, -(-300_000_000 // wb))
+        w0 = torch.from_numpy(synth.random_q4k(rows, k, rows + k)).to(device)
+        ws = [w0] + [w0.clone() for _ in range(ncopy - 1)]
+        for n in GEMV_BATCHES:
+            g = torch.Generator(device="cpu").manual_seed(n)
+            xq = torch.randint(-127, 128, (n, k), dtype=torch.int8, generator=g).to(device)
+            xs = (torch.rand((n, k // 32), generator=g) * 0.01).to(device)
+            out = torch.empty((n, rows), dtype=torch.float32, device=device)
+            nbytes = lib.hakmc_gemv_q4k_q8_batch_scratch(rows, k, n)
+            sc = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+            launch = lambda i: check(lib.hakmc_gemv_q4k_q8_batch(P(out), P(ws[i % ncopy]), P(xq), P(xs), None,
+                                                                 rows, k, n, P(sc), nbytes, sp))
+            us = _graph_us(torch, s, launch, max(ncopy, 20))
+            byt = wb + n * (k + 4 * k // 32) + n * rows * 4
+            rows_out.append({"shape": f"{rows}x{k}", "batch": n, "us": round(us, 2),
+                             "gbs": round(byt / us / 1e3, 1), "frac": round(byt / us / 1e3 / hbm_gbs, 3)})
+        del ws, w0
+        torch.cuda.empty_cache()
+    lm = []
+    for rows, k in LMHEAD_SHAPES:
+        w = synth.random_q6k(rows, k, rows + k)
+        src = torch.from_numpy(w).to(device)
+        packed = torch.empty(lib.hakmc_q6k_packed_bytes(rows, k), dtype=torch.uint8, device=device)
+        check(lib.hakmc_q6k_pack(P(packed), P(src), rows, k, None))
+        del src, w
+        x = torch.from_numpy(synth.normal(k, 9)).to(device)
+        logits = torch.empty(rows, dtype=torch.float32, device=device)
+        am = torch.empty(1, dtype=torch.int32, device=device)
+        launch = lambda i: check(lib.hakmc_lmhead_argmax(P(logits), P(am), P(packed), P(x), None, 0.0,
+                                                         rows, k, sp))
+        us = _graph_us(torch, s, launch, 10)
+        byt = rows * (k // 256) * 210 + 4 * k + 4 * rows
+        lm.append({"shape": f"{rows}x{k}", "us": round(us, 2), "gbs": round(byt / us / 1e3, 1),
+                   "frac": round(byt / us / 1e3 / hbm_gbs, 3)})
+        del packed
+        torch.cuda.empty_cache()
+    return {"kernel": "q4k_batch_kernel (hakmc_gemv_q4k_q8_batch); lm_head: stream_kernel (hakmc_lmhead_argmax)",
+            "unit": "GB/s", "peak": hbm_gbs,
+            "timing": "per launch, CUDA graph of back-to-back launches (programmatic dependent launch), "
+                      "each on a different weight copy beyond L2",
+            "q4k": rows_out, "lmhead_q6k_argmax": lm}
+
+
 def config_block(args, world):
     from hako_b200 import synth
     cfg = synth.PRESETS[args.model]
@@ -204,6 +292,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="3b", choices=["3b", "7b"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemv-sweep", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -290,6 +379,8 @@ def main():
                                 "sample": f"{n_cpu} greedy decode steps after the {len(prompt)}-id prompt "
                                           "(reference hakm_forward, oracle/_ref)"}
     ctx.close()
+    if rank == 0 and world == 1 and not args.no_gemv_sweep:
+        line["gemv_sweep"] = gemv_sweep(device, pk["hbm_gbs"])
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:

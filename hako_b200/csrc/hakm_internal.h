@@ -111,6 +111,13 @@ constexpr int PHASE_SMEM_MAX = 220 * 1024;
 // ---- small kernels (hakm_kernels.cu) ----
 
 cudaError_t launch_quantize_q8(const float* x, int n, int8_t* xq, float* xs, cudaStream_t s);
+// Batched Q4_K x q8_32 matmul (hakm_batch.cu). scratch: scratch_bytes,
+// the words from ticket_offset on zero (the launches leave them zero).
+cudaError_t launch_q4k_batch(float* out, const uint8_t* w, const int8_t* xq, const float* xs, const float* bias,
+                             int n_out, int n_in, int n_batch, void* scratch, int* err_flag, int num_sms,
+                             cudaStream_t st);
+size_t q4k_batch_scratch_bytes(int n_out, int n_in, int n_batch, int num_sms);
+size_t q4k_batch_ticket_offset(int n_out, int n_in, int n_batch, int num_sms);
 cudaError_t launch_q4k_subsums(int32_t* iqx, int32_t* ix, const uint8_t* w, const int8_t* xq,
                                int n_out, int n_in, cudaStream_t s);
 cudaError_t launch_q6k_pack(uint8_t* dst, const uint8_t* src, int n_rows, int n_in, cudaStream_t s);

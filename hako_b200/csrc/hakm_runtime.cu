@@ -1273,6 +1273,46 @@ extern "C" int hakmc_gemv_q4k_q8(float* out, const void* w, const int8_t* xq, co
   return gemv_common(out, w, W_Q4K, nullptr, xq, xs, bias, n_out, n_in, ACT_Q8, stream);
 }
 
+static int device_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+extern "C" size_t hakmc_gemv_q4k_q8_batch_scratch(int n_out, int n_in, int n_batch) {
+  if (n_out <= 0 || n_in <= 0 || n_in % QK || n_batch <= 0) return 0;
+  return q4k_batch_scratch_bytes(n_out, n_in, n_batch, device_sms());
+}
+
+extern "C" int hakmc_gemv_q4k_q8_batch(float* out, const void* w, const int8_t* xq, const float* xs,
+                                       const float* bias, int n_out, int n_in, int n_batch, void* scratch,
+                                       size_t scratch_bytes, void* stream) {
+  if (!out || !w || !xq || !xs || n_out <= 0 || n_in <= 0 || n_in % QK || n_batch <= 0) {
+    set_err("gemv batch: n_in must be a positive multiple of 256, n_batch >= 1");
+    return HAKMC_EINVAL;
+  }
+  if (!aligned16(w) || !aligned16(xq)) { set_err("gemv batch: w and xq must be 16-byte aligned"); return HAKMC_EINVAL; }
+  const int sms = device_sms();
+  const size_t bytes = q4k_batch_scratch_bytes(n_out, n_in, n_batch, sms);
+  if (scratch && (scratch_bytes < bytes || !aligned16(scratch))) {
+    set_err("gemv batch: scratch needs %zu bytes, 16-byte aligned", bytes);
+    return HAKMC_EINVAL;
+  }
+  const cudaStream_t st = (cudaStream_t)stream;
+  void* s = scratch;
+  if (!s) {  // stream-ordered scratch for callers that pass none
+    CKL(cudaMallocAsync(&s, bytes, st));
+    const size_t t0 = q4k_batch_ticket_offset(n_out, n_in, n_batch, sms);
+    const cudaError_t e = cudaMemsetAsync((char*)s + t0, 0, bytes - t0, st);
+    if (e != cudaSuccess) { cudaFreeAsync(s, st); CKL(e); }
+  }
+  const cudaError_t e = launch_q4k_batch(out, (const uint8_t*)w, xq, xs, bias, n_out, n_in, n_batch, s, nullptr,
+                                         sms, st);
+  if (!scratch) CKL(cudaFreeAsync(s, st));
+  CKL(e);
+  return 0;
+}
+
 extern "C" int hakmc_gemv_q4k(float* out, const void* w, const float* x, const float* bias, int n_out, int n_in,
                               void* stream) {
   if (!x) return HAKMC_EINVAL;

@@ -180,6 +180,24 @@ int hakmc_quantize_q8_32(const float *x, int n, int8_t *xq, float *xs, void *str
 int hakmc_gemv_q4k_q8(float *out, const void *w, const int8_t *xq, const float *xs,
                       const float *bias, int n_out, int n_in, void *stream);
 
+/* Batched Q4_K matmul: out[n*n_out + r] = q4k_vec_dot(w row r, xq + n*n_in,
+ * xs + n*(n_in/32)) (+ bias[r]) for n < n_batch, r < n_out — the reference's
+ * Q4_K matmul (src/nn.c:76-82, src/quant.c:150-232) applied to n_batch
+ * activations; the reference has no batched call (it runs one vector per
+ * hakm_forward). Each weight byte is read once per 16 activations. [dev]
+ * buffers; w and xq 16-byte aligned; n_in % 256 == 0.
+ * scratch: [dev] hakmc_gemv_q4k_q8_batch_scratch(n_out, n_in, n_batch)
+ * bytes, 16-byte aligned, zeroed before its first use (a call leaves it
+ * reusable; zero it again after a failed call); one call at a time per
+ * scratch. NULL takes a scratch from the stream-ordered allocator.
+ * The kernel is launched as a programmatic dependent of the preceding
+ * kernel in the stream and may read w before that kernel has finished, so
+ * w must not be written by the immediately preceding kernel. */
+size_t hakmc_gemv_q4k_q8_batch_scratch(int n_out, int n_in, int n_batch);
+int hakmc_gemv_q4k_q8_batch(float *out, const void *w, const int8_t *xq, const float *xs,
+                            const float *bias, int n_out, int n_in, int n_batch,
+                            void *scratch, size_t scratch_bytes, void *stream);
+
 /* The whole Q4_K matmul of src/nn.c:179-210: quantizes the fp32 [dev] x once
  * (quantize_row_q8_32), then the int8 row dots. Same layout rules. */
 int hakmc_gemv_q4k(float *out, const void *w, const float *x, const float *bias,
