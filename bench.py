@@ -265,7 +265,8 @@ def gemv_sweep(device, hbm_gbs):
                    "frac": round(byt / us / 1e3 / hbm_gbs, 3)})
         del packed
         torch.cuda.empty_cache()
-    return {"kernel": "q4k_batch_kernel (hakmc_gemv_q4k_q8_batch); lm_head: stream_kernel (hakmc_lmhead_argmax)",
+    return {"kernel": "hakmc_gemv_q4k_q8_batch: q4k_batch_kernel (dp4a) for N <= 16, q4k_mma_kernel "
+                      "(tcgen05 kind::i8) above; lm_head: stream_kernel (hakmc_lmhead_argmax)",
             "unit": "GB/s", "peak": hbm_gbs,
             "timing": "per launch, CUDA graph of back-to-back launches (programmatic dependent launch), "
                       "each on a different weight copy beyond L2",

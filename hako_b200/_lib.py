@@ -48,6 +48,8 @@ SIGNATURES = {
     "hakmc_gemv_q4k_q8": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp]),
     "hakmc_gemv_q4k_q8_batch_scratch": (_sz, [_i, _i, _i]),
     "hakmc_gemv_q4k_q8_batch": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
+    "hakmc_gemm_q4k_q8_scratch": (_sz, [_i, _i, _i]),
+    "hakmc_gemm_q4k_q8": (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _sz, _vp]),
     "hakmc_gemv_q4k": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "hakmc_q4k_subsums": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp]),
     "hakmc_q6k_pack": (_i, [_vp, _vp, _i, _i, _vp]),

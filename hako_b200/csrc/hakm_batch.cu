@@ -359,6 +359,22 @@ __global__ void __launch_bounds__(256) q4k_batch_sum_kernel(float* out, const fl
 
 // ------------------------------------------------------------------ host
 
+// The chunk-sum kernel as a programmatic dependent of the kernel before it.
+cudaError_t launch_chunk_sum(float* out, const float* part, const float* bias, int n_out, int n_batch, int nch,
+                             int num_sms, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  const int total = n_batch * n_out;
+  cfg.gridDim = dim3((unsigned)std::min((total + 255) / 256, 4 * num_sms));
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, q4k_batch_sum_kernel, out, part, bias, n_out, n_batch, nch);
+}
+
 namespace {
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -507,17 +523,7 @@ cudaError_t launch_q4k_batch(float* out, const uint8_t* w, const int8_t* xq, con
     }
     if (e != cudaSuccess) return e;
     if (!P.tile_order && a.nch > 1) {
-      cudaLaunchConfig_t cfg = {};
-      const int total = nbt * n_out;
-      cfg.gridDim = dim3((unsigned)std::min((total + 255) / 256, 4 * num_sms));
-      cfg.blockDim = dim3(256);
-      cfg.stream = st;
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-      attr[0].val.programmaticStreamSerializationAllowed = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      e = cudaLaunchKernelEx(&cfg, q4k_batch_sum_kernel, a.out, (const float*)a.part, bias, n_out, nbt, a.nch);
+      e = launch_chunk_sum(a.out, a.part, bias, n_out, nbt, a.nch, num_sms, st);
       if (e != cudaSuccess) return e;
     }
   }

@@ -118,6 +118,15 @@ cudaError_t launch_q4k_batch(float* out, const uint8_t* w, const int8_t* xq, con
                              cudaStream_t st);
 size_t q4k_batch_scratch_bytes(int n_out, int n_in, int n_batch, int num_sms);
 size_t q4k_batch_ticket_offset(int n_out, int n_in, int n_batch, int num_sms);
+// out[n][r] = sum over c < nch of part[c][n][r] (+ bias[r]), in order.
+cudaError_t launch_chunk_sum(float* out, const float* part, const float* bias, int n_out, int n_batch, int nch,
+                             int num_sms, cudaStream_t st);
+// Tensor-core (tcgen05 kind::i8) batched Q4_K x q8_32 matmul (hakm_mma.cu);
+// part: q4k_mma_scratch_bytes (split-K partials), may be null when that is 0.
+cudaError_t launch_q4k_mma(float* out, const uint8_t* w, const int8_t* xq, const float* xs, const float* bias,
+                           int n_out, int n_in, int n_batch, float* part, int* err_flag, int num_sms,
+                           cudaStream_t st);
+size_t q4k_mma_scratch_bytes(int n_out, int n_in, int n_batch, int num_sms);
 cudaError_t launch_q4k_subsums(int32_t* iqx, int32_t* ix, const uint8_t* w, const int8_t* xq,
                                int n_out, int n_in, cudaStream_t s);
 cudaError_t launch_q6k_pack(uint8_t* dst, const uint8_t* src, int n_rows, int n_in, cudaStream_t s);

@@ -1279,9 +1279,16 @@ static int device_sms() {
   return sms;
 }
 
+// Batches above 16 activations go to the tensor cores (hakm_mma.cu): their
+// MMAs take the integer work that bounds the dp4a kernel from there on.
+constexpr int TC_MIN_BATCH = 17;
+
 extern "C" size_t hakmc_gemv_q4k_q8_batch_scratch(int n_out, int n_in, int n_batch) {
   if (n_out <= 0 || n_in <= 0 || n_in % QK || n_batch <= 0) return 0;
-  return q4k_batch_scratch_bytes(n_out, n_in, n_batch, device_sms());
+  const int sms = device_sms();
+  // the dp4a kernel's partials and tickets, then the tensor-core partials
+  const size_t dp = (q4k_batch_scratch_bytes(n_out, n_in, n_batch, sms) + 255) & ~(size_t)255;
+  return dp + (n_batch >= TC_MIN_BATCH ? q4k_mma_scratch_bytes(n_out, n_in, n_batch, sms) : (size_t)0);
 }
 
 extern "C" int hakmc_gemv_q4k_q8_batch(float* out, const void* w, const int8_t* xq, const float* xs,
@@ -1293,12 +1300,23 @@ extern "C" int hakmc_gemv_q4k_q8_batch(float* out, const void* w, const int8_t* 
   }
   if (!aligned16(w) || !aligned16(xq)) { set_err("gemv batch: w and xq must be 16-byte aligned"); return HAKMC_EINVAL; }
   const int sms = device_sms();
-  const size_t bytes = q4k_batch_scratch_bytes(n_out, n_in, n_batch, sms);
+  const size_t bytes = hakmc_gemv_q4k_q8_batch_scratch(n_out, n_in, n_batch);
   if (scratch && (scratch_bytes < bytes || !aligned16(scratch))) {
     set_err("gemv batch: scratch needs %zu bytes, 16-byte aligned", bytes);
     return HAKMC_EINVAL;
   }
   const cudaStream_t st = (cudaStream_t)stream;
+  if (n_batch >= TC_MIN_BATCH && aligned16(xs)) {
+    // the tensor-core path uses only its K-split partials, after the dp4a part
+    const size_t tb = q4k_mma_scratch_bytes(n_out, n_in, n_batch, sms);
+    void* s = scratch ? (char*)scratch + (bytes - tb) : nullptr;
+    if (!scratch && tb) CKL(cudaMallocAsync(&s, tb, st));
+    const cudaError_t e = launch_q4k_mma(out, (const uint8_t*)w, xq, xs, bias, n_out, n_in, n_batch, (float*)s,
+                                         nullptr, sms, st);
+    if (!scratch && tb) CKL(cudaFreeAsync(s, st));
+    CKL(e);
+    return 0;
+  }
   void* s = scratch;
   if (!s) {  // stream-ordered scratch for callers that pass none
     CKL(cudaMallocAsync(&s, bytes, st));
@@ -1309,6 +1327,38 @@ extern "C" int hakmc_gemv_q4k_q8_batch(float* out, const void* w, const int8_t* 
   const cudaError_t e = launch_q4k_batch(out, (const uint8_t*)w, xq, xs, bias, n_out, n_in, n_batch, s, nullptr,
                                          sms, st);
   if (!scratch) CKL(cudaFreeAsync(s, st));
+  CKL(e);
+  return 0;
+}
+
+extern "C" size_t hakmc_gemm_q4k_q8_scratch(int n_out, int n_in, int n_batch) {
+  if (n_out <= 0 || n_in <= 0 || n_in % QK || n_batch <= 0) return 0;
+  return q4k_mma_scratch_bytes(n_out, n_in, n_batch, device_sms());
+}
+
+extern "C" int hakmc_gemm_q4k_q8(float* out, const void* w, const int8_t* xq, const float* xs, const float* bias,
+                                 int n_out, int n_in, int n_batch, void* scratch, size_t scratch_bytes,
+                                 void* stream) {
+  if (!out || !w || !xq || !xs || n_out <= 0 || n_in <= 0 || n_in % QK || n_batch <= 0) {
+    set_err("gemm: n_in must be a positive multiple of 256, n_batch >= 1");
+    return HAKMC_EINVAL;
+  }
+  if (!aligned16(w) || !aligned16(xq) || !aligned16(xs)) {
+    set_err("gemm: w, xq and xs must be 16-byte aligned");
+    return HAKMC_EINVAL;
+  }
+  const int sms = device_sms();
+  const size_t bytes = q4k_mma_scratch_bytes(n_out, n_in, n_batch, sms);
+  if (scratch && bytes && (scratch_bytes < bytes || !aligned16(scratch))) {
+    set_err("gemm: scratch needs %zu bytes, 16-byte aligned", bytes);
+    return HAKMC_EINVAL;
+  }
+  const cudaStream_t st = (cudaStream_t)stream;
+  void* s = scratch;
+  if (!s && bytes) CKL(cudaMallocAsync(&s, bytes, st));  // stream-ordered scratch for callers that pass none
+  const cudaError_t e = launch_q4k_mma(out, (const uint8_t*)w, xq, xs, bias, n_out, n_in, n_batch, (float*)s,
+                                       nullptr, sms, st);
+  if (!scratch && bytes) CKL(cudaFreeAsync(s, st));
   CKL(e);
   return 0;
 }

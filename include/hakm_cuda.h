@@ -184,7 +184,9 @@ int hakmc_gemv_q4k_q8(float *out, const void *w, const int8_t *xq, const float *
  * xs + n*(n_in/32)) (+ bias[r]) for n < n_batch, r < n_out — the reference's
  * Q4_K matmul (src/nn.c:76-82, src/quant.c:150-232) applied to n_batch
  * activations; the reference has no batched call (it runs one vector per
- * hakm_forward). Each weight byte is read once per 16 activations. [dev]
+ * hakm_forward). Up to 16 activations: dp4a, each weight byte read once
+ * per 16 activations; larger batches run on the tensor cores as
+ * hakmc_gemm_q4k_q8 does (xs 16-byte aligned; else dp4a in launches of 16). [dev]
  * buffers; w and xq 16-byte aligned; n_in % 256 == 0.
  * scratch: [dev] hakmc_gemv_q4k_q8_batch_scratch(n_out, n_in, n_batch)
  * bytes, 16-byte aligned, zeroed before its first use (a call leaves it
@@ -197,6 +199,21 @@ size_t hakmc_gemv_q4k_q8_batch_scratch(int n_out, int n_in, int n_batch);
 int hakmc_gemv_q4k_q8_batch(float *out, const void *w, const int8_t *xq, const float *xs,
                             const float *bias, int n_out, int n_in, int n_batch,
                             void *scratch, size_t scratch_bytes, void *stream);
+
+/* The same product on the tensor cores (tcgen05 kind::i8): the per-32
+ * integer sums q*xq are exact int32 MMA results, combined in fp32 as
+ * q4k_vec_dot does (src/quant.c:224-227). For batches (batched decode,
+ * prompt processing); any n_batch >= 1, tiles of 16, 32 or 64 activations;
+ * shapes with few row tiles split K over several CTAs and add the splits
+ * in order in a second kernel. [dev] w, xq and xs 16-byte aligned;
+ * n_in % 256 == 0. scratch: [dev] hakmc_gemm_q4k_q8_scratch(n_out, n_in,
+ * n_batch) bytes (0 when no split is needed), any contents; NULL takes it
+ * from the stream-ordered allocator. Launched as a programmatic dependent
+ * of the preceding kernel (it waits for that kernel before reading). */
+size_t hakmc_gemm_q4k_q8_scratch(int n_out, int n_in, int n_batch);
+int hakmc_gemm_q4k_q8(float *out, const void *w, const int8_t *xq, const float *xs,
+                      const float *bias, int n_out, int n_in, int n_batch,
+                      void *scratch, size_t scratch_bytes, void *stream);
 
 /* The whole Q4_K matmul of src/nn.c:179-210: quantizes the fp32 [dev] x once
  * (quantize_row_q8_32), then the int8 row dots. Same layout rules. */

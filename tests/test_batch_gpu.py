@@ -85,3 +85,47 @@ def test_gemv_q4k_batch_rejects_bad_shapes(cuda):
     assert lib.hakmc_gemv_q4k_q8_batch(p, C.c_void_p(buf.data_ptr() + 8), p, p, None, 4, 256, 1,
                                        None, 0, None) < 0  # unaligned w
     assert lib.hakmc_gemv_q4k_q8_batch(p, p, p, p, None, 64, 4096, 4, p, 16, None) < 0  # scratch too small
+
+
+def run_tc(cuda, w, xq, xs, bias, rows, k, n):
+    import torch
+    wd = torch.from_numpy(w).to(cuda)
+    xqd = torch.from_numpy(np.ascontiguousarray(xq)).to(cuda)
+    xsd = torch.from_numpy(np.ascontiguousarray(xs)).to(cuda)
+    bd = torch.from_numpy(bias).to(cuda) if bias is not None else None
+    out = torch.full((n, rows), float("nan"), dtype=torch.float32, device=cuda)
+    check(lib.hakmc_gemm_q4k_q8(P(out), P(wd), P(xqd), P(xsd), P(bd), rows, k, n, None, 0, None))
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+# tensor-core path: activation tiles of 16, 32, 64 or 128; ragged rows (not
+# a multiple of the 128-row tile), ragged batches, one super-block, K split
+# over several CTAs (few row tiles)
+TC_CASES = [(256, 2048, 16), (2048, 2048, 64), (11008, 2048, 64), (2048, 11008, 64), (3584, 18944, 16),
+            (300, 512, 100), (5, 256, 1), (130, 2304, 130), (512, 3584, 256), (1000, 1024, 30), (18944, 3584, 4)]
+
+
+@pytest.mark.parametrize("rows,k,n", TC_CASES)
+def test_gemm_q4k_tensor_cores_match_reference(cuda, reference, rows, k, n):
+    w = synth.random_q4k(rows, k, 11 * rows + k + n)
+    xs_f = [synth.normal(k, 2000 + 17 * i + k) for i in range(n)]
+    q = [reference.quantize_q8_32(x) for x in xs_f]
+    xq = np.stack([a for a, _ in q])
+    xs = np.stack([b for _, b in q])
+    bias = synth.normal(rows, 81) if n % 2 == 0 else None
+    out = run_tc(cuda, w, xq, xs, bias, rows, k, n)
+    for i in range(n):
+        ref = reference.matmul(w, 12, xs_f[i], rows, k, bias=bias)
+        assert rel_l2(out[i], ref) < TOL, i
+
+
+def test_gemm_q4k_tensor_cores_deterministic(cuda, reference):
+    rows, k, n = 2048, 3584, 64
+    w = synth.random_q4k(rows, k, 6)
+    q = [reference.quantize_q8_32(synth.normal(k, 70 + i)) for i in range(n)]
+    xq = np.stack([a for a, _ in q])
+    xs = np.stack([b for _, b in q])
+    a = run_tc(cuda, w, xq, xs, None, rows, k, n)
+    b = run_tc(cuda, w, xq, xs, None, rows, k, n)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
