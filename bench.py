@@ -273,6 +273,26 @@ def gemv_sweep(device, hbm_gbs):
             "q4k": rows_out, "lmhead_q6k_argmax": lm}
 
 
+def gemv_one(rows, k, n):
+    """Three launches of the batched Q4_K matmul on one shape (seeded data)."""
+    import ctypes as C
+    import torch
+    from hako_b200 import check, lib, synth
+    P = lambda t: C.c_void_p(t.data_ptr())
+    dev = torch.device("cuda:0")
+    w = torch.from_numpy(synth.random_q4k(rows, k, rows + k)).to(dev)
+    g = torch.Generator(device="cpu").manual_seed(n)
+    xq = torch.randint(-127, 128, (n, k), dtype=torch.int8, generator=g).to(dev)
+    xs = (torch.rand((n, k // 32), generator=g) * 0.01).to(dev)
+    out = torch.empty((n, rows), dtype=torch.float32, device=dev)
+    nbytes = lib.hakmc_gemv_q4k_q8_batch_scratch(rows, k, n)
+    sc = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        check(lib.hakmc_gemv_q4k_q8_batch(P(out), P(w), P(xq), P(xs), None, rows, k, n, P(sc), nbytes, None))
+    torch.cuda.synchronize()
+    return 0
+
+
 def config_block(args, world):
     from hako_b200 import synth
     cfg = synth.PRESETS[args.model]
@@ -294,8 +314,13 @@ def main():
     ap.add_argument("--model", default="3b", choices=["3b", "7b"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv-sweep", action="store_true")
+    ap.add_argument("--gemv-shape", default=None,
+                    help="ROWSxKxN: only run three launches of hakmc_gemv_q4k_q8_batch on that shape "
+                         "(a small case for a profiler), print nothing else")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.gemv_shape:
+        return gemv_one(*(int(v) for v in args.gemv_shape.split("x")))
     if args.impl == "reference":
         return run_reference_arm(args)
 
