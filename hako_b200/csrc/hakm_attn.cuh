@@ -37,6 +37,7 @@ struct AttnLL {
   // pointer into the kernel's parameters, so no per-thread copy is made)
   const long long* out_delta;
   int delta_stride;
+  long long kv_off;  // elements from the cache pointers to this sequence's cache (0: the first)
 };
 
 // Tagged output words to every destination GPU.
@@ -99,8 +100,8 @@ __device__ bool attn_item(const AttnParams& a, int u, int split, int pos, float*
     for (int i = tid; i < G * R4; i += nthr) reinterpret_cast<float4*>(qs)[i] = __ldcg(q4 + i);
   }
   if (ns > 0) {
-    const float* kb = a.k_cache + (size_t)s0 * kv_dim + kvh * HD;
-    const float* vb = a.v_cache + (size_t)s0 * kv_dim + kvh * HD;
+    const float* kb = a.k_cache + T.kv_off + (size_t)s0 * kv_dim + kvh * HD;
+    const float* vb = a.v_cache + T.kv_off + (size_t)s0 * kv_dim + kvh * HD;
     for (int i = tid; i < ns * R4; i += nthr) {
       const int r = i / R4, c4 = i % R4;
       float4 kv, vv;

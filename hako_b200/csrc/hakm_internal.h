@@ -209,6 +209,7 @@ struct StepArgs {
   const int* forced;
   int* token_dev;          // in: input of step 0 when n_forced == 0; out: last pick
   int* pos_dev;            // out: pos0 + n_steps
+  long long kv_off;        // elements from the K/V cache pointers to this launch's sequence
   int* token_log;          // pick of step j at token_log[j - log_base] (may be null)
   int token_log_cap;
   int log_base;

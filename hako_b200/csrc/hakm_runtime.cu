@@ -537,12 +537,13 @@ static int ensure_program(hakmc_ctx* c) {
 // step kernel. Steps 0..n_forced-1 take forced_dev[] as input (else step 0
 // takes token_dev); the pick of step j goes to token_log[j - log_base].
 static int run_steps(hakmc_ctx* c, int n_steps, int n_forced, const int* forced_dev, int log_base,
-                     unsigned long long* trace = nullptr, int trace_k = 0) {
+                     unsigned long long* trace = nullptr, int trace_k = 0, int seq = 0) {
   if (n_steps <= 0) return 0;
   if (c->pos + n_steps > c->max_seq) { set_err("position %d beyond max_seq %d", c->pos + n_steps, c->max_seq); return HAKMC_ERANGE; }
   int r = ensure_program(c);
   if (r) return r;
   StepArgs a = c->step;
+  a.kv_off = (long long)seq * c->L * c->max_seq * c->KV;  // cache layout [seq][layer][max_seq][KV]
   a.n_steps = n_steps;
   a.pos0 = c->pos;
   a.n_forced = n_forced;
@@ -1131,10 +1132,38 @@ extern "C" int hakmc_trace_step(hakmc_ctx* c, unsigned long long* stamps, int ma
 
 extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* pos, int n_seq,
                                    float* logits, int* argmax) {
-  (void)tokens; (void)pos; (void)logits; (void)argmax;
-  if (!c || n_seq <= 0 || n_seq > c->max_batch) { set_err("bad batch"); return HAKMC_EINVAL; }
-  set_err("batched decode is not built yet");
-  return HAKMC_EINVAL;
+  if (!c || !tokens || !pos || n_seq <= 0 || n_seq > c->max_batch) { set_err("bad batch"); return HAKMC_EINVAL; }
+  if (!c->use_step) { set_err("forward_batch runs on the step kernel (HAKMC_STEP=0 is set)"); return HAKMC_EINVAL; }
+  for (int i = 0; i < n_seq; i++) {
+    if (tokens[i] < 0 || tokens[i] >= c->V) { set_err("token %d out of range", tokens[i]); return HAKMC_EINVAL; }
+    if (pos[i] < 0 || pos[i] >= c->max_seq) { set_err("position %d beyond max_seq %d", pos[i], c->max_seq); return HAKMC_ERANGE; }
+  }
+  CK(cudaSetDevice(c->device));
+  // sequence 0 is also the single-sequence API's: its position and last pick
+  // (the input hakmc_decode continues from) are restored afterwards
+  const int saved_pos = c->pos;
+  CK(cudaMemcpyAsync(c->token_dev + 2, c->token_dev, 4, cudaMemcpyDeviceToDevice, c->stream));
+  int r = 0;
+  for (int i = 0; i < n_seq && !r; i++) {
+    c->pos = pos[i];
+    c->h_pinned[0] = tokens[i];
+    CK(cudaMemcpyAsync(c->token_dev, &c->h_pinned[0], 4, cudaMemcpyHostToDevice, c->stream));
+    r = run_steps(c, 1, 1, c->token_dev, 0, nullptr, 0, i);
+    if (r) break;
+    CK(cudaMemcpyAsync(&c->h_pinned[1], c->token_dev, 4, cudaMemcpyDeviceToHost, c->stream));
+    if (logits) CK(cudaMemcpyAsync(c->logits_pinned, c->logits, (size_t)c->V * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    r = check_flag(c);
+    if (r) break;
+    if (argmax) argmax[i] = c->h_pinned[1];
+    if (logits) memcpy(logits + (size_t)i * c->V, c->logits_pinned, (size_t)c->V * 4);
+  }
+  c->pos = saved_pos;
+  c->h_pinned[2] = saved_pos;
+  CK(cudaMemcpyAsync(c->pos_dev, &c->h_pinned[2], 4, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaMemcpyAsync(c->token_dev, c->token_dev + 2, 4, cudaMemcpyDeviceToDevice, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  return r;
 }
 
 extern "C" int hakmc_hidden(hakmc_ctx* c, int seq, float* out) {

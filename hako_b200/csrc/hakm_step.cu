@@ -334,7 +334,7 @@ __device__ __forceinline__ void epi_apply(const StepArgs& A, const PhaseDesc& D,
     put_all<TP>(A, dst + e.o0, ll_word(r0, tag));
     put_all<TP>(A, dst + e.o1, ll_word(r1, tag));
     if (is_k) {
-      float* kc = p.seg[s].cache + (size_t)pos * p.kv_dim;
+      float* kc = p.seg[s].cache + A.kv_off + (size_t)pos * p.kv_dim;
       for (int r = 0; r < n_ranks<TP>(A); r++) {
         on_rank(A, kc, XR_KCACHE, r)[e.o0] = r0;
         on_rank(A, kc, XR_KCACHE, r)[e.o1] = r1;
@@ -345,7 +345,7 @@ __device__ __forceinline__ void epi_apply(const StepArgs& A, const PhaseDesc& D,
   const float o = a0 + e.f0;  // residual or bias (0 when none)
   put_all<TP>(A, D.out_ll[s] + e.o0, ll_word(o, tag));
   if (kind == EPI_V_CACHE) {
-    float* vc = p.seg[s].cache + (size_t)pos * p.kv_dim + e.o0;
+    float* vc = p.seg[s].cache + A.kv_off + (size_t)pos * p.kv_dim + e.o0;
     for (int r = 0; r < n_ranks<TP>(A); r++) *on_rank(A, vc, XR_VCACHE, r) = o;
   }
 }
@@ -392,7 +392,7 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
           put_all<TP>(A, dst + o0, ll_word(r0, tag));
           put_all<TP>(A, dst + o1, ll_word(r1, tag));
           if (is_k) {
-            float* kc = S.cache + (size_t)pos * p.kv_dim;
+            float* kc = S.cache + A.kv_off + (size_t)pos * p.kv_dim;
             for (int r = 0; r < W; r++) {
               on_rank(A, kc, XR_KCACHE, r)[o0] = r0;
               on_rank(A, kc, XR_KCACHE, r)[o1] = r1;
@@ -413,7 +413,7 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
           case EPI_V_CACHE: {
             const float o = S.bias ? v + (row == r.row0 + t ? pre.bv : S.bias[row]) : v;
             put_all<TP>(A, out + row, ll_word(o, tag));
-            float* vc = S.cache + (size_t)pos * p.kv_dim + row;
+            float* vc = S.cache + A.kv_off + (size_t)pos * p.kv_dim + row;
             for (int rr = 0; rr < W; rr++) *on_rank(A, vc, XR_VCACHE, rr) = o;
             break;
           }
@@ -717,6 +717,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         T.n_dst = n_ranks<TP>(A);
         T.out_delta = &A.tp_delta[0][XR_LL];
         T.delta_stride = XR_COUNT;
+        T.kv_off = A.kv_off;
         // (kv head, query-head group) units; with tensor parallelism this GPU
         // runs units rank, rank + world, ... (all splits of a unit stay here)
         const int n_units = a.n_heads / a.head_group;

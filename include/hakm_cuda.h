@@ -87,10 +87,14 @@ int hakmc_prefill(hakmc_ctx *c, const int *tokens, int n, float *logits, int *ar
 int hakmc_decode(hakmc_ctx *c, int n_steps, int *out_tokens);
 
 /* Batched decode: one step for n_seq independent sequences (n_seq <=
- * max_batch), sequence i at position pos[i] with input tokens[i] ([host]).
- * The reference decodes one sequence at a time; each row of this call equals
- * hakm_forward on a context holding that sequence's cache. argmax [host] gets
- * n_seq ids; logits [host] (may be NULL) n_seq*vocab floats. */
+ * max_batch), sequence i at position pos[i] with input tokens[i] ([host]),
+ * using KV-cache slot i (slot 0 is also the single-sequence calls' cache;
+ * their position and last pick are left as they were). The reference
+ * decodes one sequence at a time; each row of this call equals hakm_forward
+ * on a context holding that sequence's cache (bit for bit: the same step
+ * kernel runs each sequence in turn). argmax [host] gets n_seq ids; logits
+ * [host] (may be NULL) n_seq*vocab floats. 0, HAKMC_ERANGE for a position
+ * beyond max_seq, or another negative code. */
 int hakmc_forward_batch(hakmc_ctx *c, const int *tokens, const int *pos,
                         int n_seq, float *logits, int *argmax);
 

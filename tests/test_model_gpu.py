@@ -232,3 +232,53 @@ def test_prefill_rejects_bad_input(cuda, small_path):
         with pytest.raises(HakmcError):
             ctx.prefill([1, 10 ** 7])
         assert ctx.pos == 0
+
+
+def test_forward_batch_rows_equal_single_sequence_contexts(cuda, small_path):
+    """hakmc_forward_batch: row i is hakm_forward on a context holding
+    sequence i's cache (slot i) — bit for bit, since the same step kernel
+    runs each sequence. Three sequences with different prompts, fed and then
+    decoded greedily in lockstep; sequence 2 starts two positions later."""
+    prompts = [[11, 22, 33, 44], [500, 600, 700, 800], [3000, 17, 42, 9]]
+    n_gen, start = 6, [0, 0, 2]
+    batch = HakmCtx(small_path, max_seq=64, max_batch=3)
+    singles = [HakmCtx(small_path, max_seq=64) for _ in prompts]
+    try:
+        nxt = [None, None, None]
+        feed = [list(p) for p in prompts]
+        pos = [0, 0, 0]
+        for rnd in range(len(prompts[0]) + n_gen + 2):
+            toks, poss, rows = [], [], []
+            for i in range(3):
+                active = rnd >= start[i] and pos[i] < len(prompts[i]) + n_gen
+                tok = (feed[i].pop(0) if feed[i] else nxt[i]) if active else 1
+                toks.append(tok)
+                poss.append(pos[i] if active else 63)  # idle rows write position 63 only
+                rows.append(active)
+            logits, am = batch.forward_batch(toks, poss, want_logits=True)
+            for i in range(3):
+                if not rows[i]:
+                    continue
+                ref_logits, ref_am = singles[i].forward(toks[i])
+                assert np.array_equal(logits[i].view(np.uint32), ref_logits.view(np.uint32)), (rnd, i)
+                assert am[i] == ref_am
+                nxt[i] = int(am[i])
+                pos[i] += 1
+        assert batch.pos == 0  # the single-sequence state is left alone
+    finally:
+        batch.close()
+        for s in singles:
+            s.close()
+
+
+def test_forward_batch_rejects_bad_input(cuda, tiny_path):
+    ctx = HakmCtx(tiny_path, max_seq=16, max_batch=2)
+    try:
+        with pytest.raises(HakmcError):
+            ctx.forward_batch([1, 2], [0, 16])  # position beyond max_seq
+        with pytest.raises(HakmcError):
+            ctx.forward_batch([1, 2, 3], [0, 0, 0])  # more sequences than max_batch
+        with pytest.raises(HakmcError):
+            ctx.forward_batch([1, -5], [0, 0])  # token out of range
+    finally:
+        ctx.close()
