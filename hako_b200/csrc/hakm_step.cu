@@ -12,7 +12,7 @@
 //               only for free slots, so the next phases' weights are loading
 //               while the consumers wait for inputs, run attention or write
 //               an epilogue.
-//   warps 1..12 consumers: per phase, fetch the inputs, rebuild the
+//   warps 1..11 consumers: per phase, fetch the inputs, rebuild the
 //               activation (norm weights fetched first), consume the phase's
 //               stages, run the epilogue. Every consumer warp visits every
 //               stage (waits its full barrier, does the 4-row units that fall
