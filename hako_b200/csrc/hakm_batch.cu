@@ -34,9 +34,7 @@
 // order and adds the bias: deterministic for any grid, and no fence or
 // ticket in the streaming kernel.
 #include "hakm_gemv.cuh"
-
-#include <cuda.h>
-#include <cudaTypedefs.h>
+#include "hakm_tmap.h"
 
 #include <atomic>
 
@@ -375,19 +373,26 @@ cudaError_t launch_chunk_sum(float* out, const float* part, const float* bias, i
   return cudaLaunchKernelEx(&cfg, q4k_batch_sum_kernel, out, part, bias, n_out, n_batch, nch);
 }
 
-namespace {
-
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+bool encode_tmap_2d(CUtensorMap* m, CUtensorMapDataType type, const void* base, uint64_t d0, uint64_t d1,
+                    uint64_t stride1, uint32_t b0, uint32_t b1, CUtensorMapSwizzle swizzle) {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return false;
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   }
-  return fn;
+  const cuuint64_t dims[2] = {d0, d1};
+  const cuuint64_t strides[1] = {stride1};
+  const cuuint32_t box[2] = {b0, b1};
+  const cuuint32_t es[2] = {1, 1};
+  return fn(m, type, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+namespace {
 
 constexpr size_t BT_SMEM_MAX = 227 * 1024;
 
@@ -477,18 +482,11 @@ size_t ticket_offset(size_t part_floats) { return ((part_floats * 4 + 255) & ~(s
 cudaError_t launch_q4k_batch(float* out, const uint8_t* w, const int8_t* xq, const float* xs, const float* bias,
                              int n_out, int n_in, int n_batch, void* scratch, int* err_flag, int num_sms,
                              cudaStream_t st) {
-  auto fn = encode_fn();
-  if (!fn) return cudaErrorNotSupported;
   const int nb = n_in / QK;
   const size_t rowB = (size_t)nb * Q4K_BYTES;
   CUtensorMap m;
-  const cuuint64_t dims[2] = {(cuuint64_t)(rowB / 8), (cuuint64_t)n_out};
-  const cuuint64_t strides[1] = {(cuuint64_t)rowB};
-  const cuuint32_t box[2] = {Q4K_CHUNK / 8, BT_ROWS};
-  const cuuint32_t es[2] = {1, 1};
-  if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<uint8_t*>(w), dims, strides, box, es,
-         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+  if (!encode_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, rowB / 8, (uint64_t)n_out, rowB, Q4K_CHUNK / 8,
+                      BT_ROWS))
     return cudaErrorInvalidValue;
   BatchArgs a = {};
   a.err_flag = err_flag;

@@ -33,9 +33,7 @@
 // down (all issued MMAs and copies complete before tensor memory is freed
 // and the CTA exits).
 #include "hakm_gemv.cuh"
-
-#include <cuda.h>
-#include <cudaTypedefs.h>
+#include "hakm_tmap.h"
 
 #include <atomic>
 
@@ -481,35 +479,11 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
 
 namespace {
 
-PFN_cuTensorMapEncodeTiled_v12000 mm_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-bool encode_2d(CUtensorMap* m, CUtensorMapDataType type, const void* base, uint64_t d0, uint64_t d1,
-               uint64_t stride1, uint32_t b0, uint32_t b1,
-               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE) {
-  auto fn = mm_encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[2] = {d0, d1};
-  const cuuint64_t strides[1] = {stride1};
-  const cuuint32_t box[2] = {b0, b1};
-  const cuuint32_t es[2] = {1, 1};
-  return fn(m, type, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
+// Activation tile width for a batch.
+int mma_bn(int n_batch) { return n_batch <= 16 ? 16 : n_batch <= 32 ? 32 : 64; }
 
 // Super-blocks per split so that row tiles x activation tiles x splits
 // covers the SMs (each split at least 4 super-blocks).
-int mma_bn(int n_batch) { return n_batch <= 16 ? 16 : n_batch <= 32 ? 32 : 64; }
-
 int mma_split(int n_out, int n_in, int n_batch, int num_sms, int* per) {
   const int bn = mma_bn(n_batch);
   const int nsb = n_in / QK, tiles = ((n_out + MM_ROWS - 1) / MM_ROWS) * ((n_batch + bn - 1) / bn);
@@ -524,10 +498,10 @@ cudaError_t launch_mma_bn(const uint8_t* w, const int8_t* xq, const float* xs, c
   using L = MmaLayout<BN>;
   CUtensorMap wm, xm, sm;
   const uint64_t rowB = (uint64_t)(a.n_in / QK) * Q4K_BYTES;
-  if (!encode_2d(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, rowB / 8, (uint64_t)a.n_out, rowB, Q4K_BYTES / 8, MM_ROWS) ||
-      !encode_2d(&xm, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, (uint64_t)a.n_in, (uint64_t)a.n_batch, (uint64_t)a.n_in, 128,
+  if (!encode_tmap_2d(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT64, w, rowB / 8, (uint64_t)a.n_out, rowB, Q4K_BYTES / 8, MM_ROWS) ||
+      !encode_tmap_2d(&xm, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, (uint64_t)a.n_in, (uint64_t)a.n_batch, (uint64_t)a.n_in, 128,
                  BN, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_2d(&sm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xs, (uint64_t)(a.n_in / 32), (uint64_t)a.n_batch,
+      !encode_tmap_2d(&sm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, xs, (uint64_t)(a.n_in / 32), (uint64_t)a.n_batch,
                  (uint64_t)(a.n_in / 32) * 4, 8, BN))
     return cudaErrorInvalidValue;
   static std::atomic<unsigned long long> ready{0};
