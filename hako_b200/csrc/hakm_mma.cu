@@ -487,7 +487,9 @@ int mma_bn(int n_batch) { return n_batch <= 16 ? 16 : n_batch <= 32 ? 32 : 64; }
 int mma_split(int n_out, int n_in, int n_batch, int num_sms, int* per) {
   const int bn = mma_bn(n_batch);
   const int nsb = n_in / QK, tiles = ((n_out + MM_ROWS - 1) / MM_ROWS) * ((n_batch + bn - 1) / bn);
-  int split = std::max(1, std::min((num_sms + tiles - 1) / tiles, nsb / 4));
+  // one wave: tiles x split <= SMs (a second, partial wave costs a whole
+  // CTA's time for a few CTAs)
+  int split = std::max(1, std::min(num_sms / tiles, nsb / 4));
   *per = (nsb + split - 1) / split;
   return (nsb + *per - 1) / *per;
 }

@@ -1308,16 +1308,21 @@ static int device_sms() {
   return sms;
 }
 
-// Batches above 16 activations go to the tensor cores (hakm_mma.cu): their
-// MMAs take the integer work that bounds the dp4a kernel from there on.
-constexpr int TC_MIN_BATCH = 17;
+// Which batches go to the tensor cores (hakm_mma.cu): their MMAs take the
+// integer work that bounds the dp4a kernel as the batch grows. Measured on
+// the config-1 shapes: above 16 activations always; from 9 (where the dp4a
+// kernel runs its 16-wide instance) once the matrix has 16M weights or more;
+// small matrices stay on dp4a, whose launch is lighter.
+static bool use_tensor_cores(int n_out, int n_in, int n_batch) {
+  return n_batch > 16 || (n_batch > 8 && (long long)n_out * n_in >= (16ll << 20));
+}
 
 extern "C" size_t hakmc_gemv_q4k_q8_batch_scratch(int n_out, int n_in, int n_batch) {
   if (n_out <= 0 || n_in <= 0 || n_in % QK || n_batch <= 0) return 0;
   const int sms = device_sms();
   // the dp4a kernel's partials and tickets, then the tensor-core partials
   const size_t dp = (q4k_batch_scratch_bytes(n_out, n_in, n_batch, sms) + 255) & ~(size_t)255;
-  return dp + (n_batch >= TC_MIN_BATCH ? q4k_mma_scratch_bytes(n_out, n_in, n_batch, sms) : (size_t)0);
+  return dp + (use_tensor_cores(n_out, n_in, n_batch) ? q4k_mma_scratch_bytes(n_out, n_in, n_batch, sms) : (size_t)0);
 }
 
 extern "C" int hakmc_gemv_q4k_q8_batch(float* out, const void* w, const int8_t* xq, const float* xs,
@@ -1335,7 +1340,7 @@ extern "C" int hakmc_gemv_q4k_q8_batch(float* out, const void* w, const int8_t* 
     return HAKMC_EINVAL;
   }
   const cudaStream_t st = (cudaStream_t)stream;
-  if (n_batch >= TC_MIN_BATCH && aligned16(xs)) {
+  if (use_tensor_cores(n_out, n_in, n_batch) && aligned16(xs)) {
     // the tensor-core path uses only its K-split partials, after the dp4a part
     const size_t tb = q4k_mma_scratch_bytes(n_out, n_in, n_batch, sms);
     void* s = scratch ? (char*)scratch + (bytes - tb) : nullptr;

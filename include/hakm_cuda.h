@@ -188,9 +188,10 @@ int hakmc_gemv_q4k_q8(float *out, const void *w, const int8_t *xq, const float *
  * xs + n*(n_in/32)) (+ bias[r]) for n < n_batch, r < n_out — the reference's
  * Q4_K matmul (src/nn.c:76-82, src/quant.c:150-232) applied to n_batch
  * activations; the reference has no batched call (it runs one vector per
- * hakm_forward). Up to 16 activations: dp4a, each weight byte read once
- * per 16 activations; larger batches run on the tensor cores as
- * hakmc_gemm_q4k_q8 does (xs 16-byte aligned; else dp4a in launches of 16). [dev]
+ * hakm_forward). Small batches: dp4a, each weight byte read once per 16
+ * activations; batches above 16 (above 8 for matrices of 16M weights or
+ * more) run on the tensor cores as hakmc_gemm_q4k_q8 does (when xs is
+ * 16-byte aligned; else dp4a in launches of 16). [dev]
  * buffers; w and xq 16-byte aligned; n_in % 256 == 0.
  * scratch: [dev] hakmc_gemv_q4k_q8_batch_scratch(n_out, n_in, n_batch)
  * bytes, 16-byte aligned, zeroed before its first use (a call leaves it
