@@ -293,6 +293,21 @@ def gemv_one(rows, k, n):
     return 0
 
 
+def step_profile(model):
+    """The step-kernel launches a profiler summary is taken from: launch 1 =
+    a 4-id prompt plus 2 greedy ids (one launch), launches 2 and 3 = one
+    decode step each."""
+    import ctypes as C
+    from hako_b200 import HakmCtx, check, lib, synth
+    ctx = HakmCtx(synth.cached_model(synth.PRESETS[model]), max_seq=128)
+    ctx.generate(list(range(100, 104)), 2)
+    out = np.zeros(1, np.int32)
+    for _ in range(2):
+        check(lib.hakmc_decode(ctx._h, 1, C.c_void_p(out.ctypes.data)))
+    ctx.close()
+    return 0
+
+
 def config_block(args, world):
     from hako_b200 import synth
     cfg = synth.PRESETS[args.model]
@@ -314,6 +329,9 @@ def main():
     ap.add_argument("--model", default="3b", choices=["3b", "7b"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv-sweep", action="store_true")
+    ap.add_argument("--step-profile", action="store_true",
+                    help="only a 4-id prompt, 2 generated ids, then two one-step hakmc_decode launches "
+                         "(the last is the one a profiler captures: -k step_kernel -s 2 -c 1)")
     ap.add_argument("--gemv-shape", default=None,
                     help="ROWSxKxN: only run three launches of hakmc_gemv_q4k_q8_batch on that shape "
                          "(a small case for a profiler), print nothing else")
@@ -321,6 +339,8 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.gemv_shape:
         return gemv_one(*(int(v) for v in args.gemv_shape.split("x")))
+    if args.step_profile:
+        return step_profile(args.model)
     if args.impl == "reference":
         return run_reference_arm(args)
 
