@@ -200,6 +200,8 @@ struct alignas(16) PhaseDesc {  // copied to shared memory as 16-byte words
   int epi_rec_off;
 };
 
+constexpr int STEP_SEQ_MAX = 2;  // sequences one step-kernel launch can carry
+
 struct StepArgs {
   const PhaseDesc* prog;   // device array, n_phases entries (one decode step)
   int n_phases;
@@ -210,6 +212,13 @@ struct StepArgs {
   int* token_dev;          // in: input of step 0 when n_forced == 0; out: last pick
   int* pos_dev;            // out: pos0 + n_steps
   long long kv_off;        // elements from the K/V cache pointers to this launch's sequence
+  // several sequences per launch (n_seq > 1, one GPU): sequence h runs on
+  // CTAs [h * grid / n_seq, (h + 1) * grid / n_seq) with program
+  // prog + h * n_phases, exchange words xb_ll + h * ll_stride, counters
+  // bar + 8h, keys + 4h, token_dev[h], pos_dev[h], forced + h * n_forced
+  int n_seq;
+  int seq_pos0[STEP_SEQ_MAX];
+  long long ll_stride;
   int* token_log;          // pick of step j at token_log[j - log_base] (may be null)
   int token_log_cap;
   int log_base;

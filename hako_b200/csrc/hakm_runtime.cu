@@ -15,6 +15,7 @@
 #include "../../include/hakm_cuda.h"
 #include "hakm_internal.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -164,6 +165,15 @@ struct hakmc_ctx {
   SegRange* ranges_dev = nullptr;  // [phase][cta][segment] rows of the step program
   size_t ranges_cap = 0;
   StepArgs step = {};
+  // forward_batch: two sequences per launch, each on half the SMs with its
+  // own program (exchange vectors, cache slot, logits, counters)
+  PhaseDesc* prog2_dev = nullptr;
+  int prog2_cap = 0, prog2_layers = -1;
+  SegRange* ranges2_dev = nullptr;
+  size_t ranges2_cap = 0;
+  StepArgs step2 = {};
+  int* seq_tokens_dev = nullptr;  // input tokens of a multi-sequence launch
+  size_t attn_part_floats = 0;    // attention scratch of one sequence
   unsigned int* step_bar = nullptr;
   unsigned int* step_tickets = nullptr;
   unsigned long long* step_keys = nullptr;
@@ -304,11 +314,12 @@ enum { PH_QKV = 0, PH_ATTN = 1, PH_WO = 2, PH_FFN = 3, PH_DOWN = 4, PH_LMHEAD = 
 // leaves out the step-finalisation side effects of the per-phase lm_head
 // kernel, so a phase can be relaunched on its own (and the step program,
 // which finalises inside the step kernel, uses it too).
-static PhaseDesc make_phase(hakmc_ctx* c, int l, int ph, int n_split, bool timing) {
+static PhaseDesc make_phase(hakmc_ctx* c, int l, int ph, int n_split, bool timing, int seq = 0) {
   const size_t lstride = (size_t)c->max_seq * c->KV;
   DevLayer& y = c->layers[l < c->L ? l : 0];
-  float* kc = c->k_cache + (size_t)l * lstride;
-  float* vc = c->v_cache + (size_t)l * lstride;
+  // cache slot `seq` (the step program of a multi-sequence launch)
+  float* kc = c->k_cache + ((size_t)seq * c->L + l) * lstride;
+  float* vc = c->v_cache + ((size_t)seq * c->L + l) * lstride;
   PhaseDesc d = {};
   d.kind = PK_GEMV;
   PhaseParams& p = d.g;
@@ -327,7 +338,7 @@ static PhaseDesc make_phase(hakmc_ctx* c, int l, int ph, int n_split, bool timin
       AttnParams& a = d.a;
       a.q = c->q; a.k_cache = kc; a.v_cache = vc; a.out = c->att; a.pos_dev = c->pos_dev;
       a.n_heads = c->H; a.n_kv = c->KVH; a.head_dim = c->hd; a.scale = 1.0f / sqrtf((float)c->hd);
-      a.n_split = n_split; a.part = c->attn_part; a.counters = c->attn_counters;
+      a.n_split = n_split; a.part = c->attn_part + (size_t)seq * c->attn_part_floats; a.counters = c->attn_counters;
       break;
     }
     case PH_WO:
@@ -348,7 +359,7 @@ static PhaseDesc make_phase(hakmc_ctx* c, int l, int ph, int n_split, bool timin
     default:  // final norm + lm_head + argmax (+ step finalisation)
       p.n_in = c->D; p.act = ACT_RMS; p.x = c->xb; p.norm_w = c->out_norm; p.eps = c->eps;
       p.n_seg = 1;
-      p.seg[0] = make_seg(c->lm_head, EPI_ARGMAX, c->logits);
+      p.seg[0] = make_seg(c->lm_head, EPI_ARGMAX, c->logits + (size_t)seq * c->V);
       p.argmax_key = c->argmax_key;
       d.skip_forced = 1;
       if (!timing) {
@@ -446,21 +457,25 @@ static int launch_one(hakmc_ctx* c) {
 // changes) and its shared-memory plan. Phase i of the program has tag index
 // i + 1 (0 is the embedding); each phase names the index of the phase whose
 // output it reads.
-static int ensure_program(hakmc_ctx* c) {
-  if (c->prog_layers == c->run_layers) return 0;
-  std::vector<PhaseDesc> prog;
-  uint64_t* xb0 = c->xb_ll;
-  uint64_t* xb1 = c->xb_ll + c->D;
+// The step program of sequence `seq` (its exchange vectors, cache slot,
+// logits, attention scratch and tickets) for run_layers layers.
+static void build_program(hakmc_ctx* c, int seq, std::vector<PhaseDesc>& prog) {
+  prog.clear();
+  const size_t lo = (size_t)seq * c->ll_words;
+  uint64_t* xb0 = c->xb_ll + lo;
+  uint64_t* xb1 = c->xb_ll + lo + c->D;
+  uint64_t *q_ll = c->q_ll + lo, *k_ll = c->k_ll + lo, *v_ll = c->v_ll + lo, *att_ll = c->att_ll + lo,
+           *h_ll = c->h_ll + lo;
   int xb0_src = 0;  // phase that last wrote xb buffer 0 (the embedding first)
   for (int l = 0; l < c->run_layers; l++) {
     const int base = 5 * l + 1;  // tag index of this layer's qkv phase
-    PhaseDesc qkv = make_phase(c, l, PH_QKV, 1, true);
+    PhaseDesc qkv = make_phase(c, l, PH_QKV, 1, true, seq);
     qkv.x_ll = xb0; qkv.x_src = xb0_src;
-    qkv.out_ll[0] = c->q_ll; qkv.out2_ll = c->k_ll; qkv.out_ll[1] = c->v_ll;
-    PhaseDesc at = make_phase(c, l, PH_ATTN, 1, true);
-    at.x_ll = c->q_ll; at.res_ll = c->k_ll; at.v_ll = c->v_ll; at.x_src = base;
-    at.out_ll[0] = c->att_ll; at.layer = l;
-    at.a.counters = c->step_tickets;
+    qkv.out_ll[0] = q_ll; qkv.out2_ll = k_ll; qkv.out_ll[1] = v_ll;
+    PhaseDesc at = make_phase(c, l, PH_ATTN, 1, true, seq);
+    at.x_ll = q_ll; at.res_ll = k_ll; at.v_ll = v_ll; at.x_src = base;
+    at.out_ll[0] = att_ll; at.layer = l;
+    at.a.counters = c->step_tickets + 64 * seq;
     {
       // query heads per attention work item: split each kv head's group so
       // that at least 8 items run even at one position split
@@ -470,20 +485,30 @@ static int ensure_program(hakmc_ctx* c) {
         if (G % d == 0 && c->KVH * d >= 8) { nhg = d; break; }
       at.a.head_group = G / nhg;
     }
-    PhaseDesc wo = make_phase(c, l, PH_WO, 1, true);
-    wo.x_ll = c->att_ll; wo.x_src = base + 1;
+    PhaseDesc wo = make_phase(c, l, PH_WO, 1, true, seq);
+    wo.x_ll = att_ll; wo.x_src = base + 1;
     wo.res_ll = xb0; wo.res_src = xb0_src; wo.out_ll[0] = xb1;
-    PhaseDesc ffn = make_phase(c, l, PH_FFN, 1, true);
-    ffn.x_ll = xb1; ffn.x_src = base + 2; ffn.out_ll[0] = c->h_ll;
-    PhaseDesc down = make_phase(c, l, PH_DOWN, 1, true);
-    down.x_ll = c->h_ll; down.x_src = base + 3;
+    PhaseDesc ffn = make_phase(c, l, PH_FFN, 1, true, seq);
+    ffn.x_ll = xb1; ffn.x_src = base + 2; ffn.out_ll[0] = h_ll;
+    PhaseDesc down = make_phase(c, l, PH_DOWN, 1, true, seq);
+    down.x_ll = h_ll; down.x_src = base + 3;
     down.res_ll = xb1; down.res_src = base + 2; down.out_ll[0] = xb0;
     xb0_src = base + 4;
     prog.push_back(qkv); prog.push_back(at); prog.push_back(wo); prog.push_back(ffn); prog.push_back(down);
   }
-  PhaseDesc lm = make_phase(c, 0, PH_LMHEAD, 1, true);
+  PhaseDesc lm = make_phase(c, 0, PH_LMHEAD, 1, true, seq);
   lm.x_ll = xb0; lm.x_src = xb0_src;
   prog.push_back(lm);
+}
+
+// Device program of one decode step for run_layers layers (rebuilt when that
+// changes) and its shared-memory plan. Phase i of the program has tag index
+// i + 1 (0 is the embedding); each phase names the index of the phase whose
+// output it reads.
+static int ensure_program(hakmc_ctx* c) {
+  if (c->prog_layers == c->run_layers) return 0;
+  std::vector<PhaseDesc> prog;
+  build_program(c, 0, prog);
   StepArgs a = {};
   if (!plan_step(prog.data(), (int)prog.size(), c->num_sms, a)) {
     set_err("step kernel: shapes do not fit its shared-memory plan");
@@ -528,8 +553,105 @@ static int ensure_program(hakmc_ctx* c) {
   a.n_layers = c->run_layers;
   a.skip_last = 1;  // the program ends with lm_head
   a.head_dim = c->hd;
+  a.n_seq = 1;
   c->step = a;
   c->prog_layers = c->run_layers;
+  return 0;
+}
+
+// The programs of sequences 0 and 1 for a two-sequence launch: each runs on
+// half the SMs (the shared-memory plan and row table are those of that
+// half-grid), with its own exchange vectors, cache slot, logits and
+// counters. The row sums do not depend on which CTA computes a row, so each
+// sequence's results are those of a single-sequence launch, bit for bit.
+static int ensure_program2(hakmc_ctx* c) {
+  if (c->prog2_layers == c->run_layers) return 0;
+  const int vgrid = c->num_sms / 2;
+  std::vector<PhaseDesc> p0, p1;
+  build_program(c, 0, p0);
+  build_program(c, 1, p1);
+  StepArgs a = {}, a1 = {};
+  if (!plan_step(p0.data(), (int)p0.size(), vgrid, a) || !plan_step(p1.data(), (int)p1.size(), vgrid, a1)) {
+    set_err("step kernel: shapes do not fit its shared-memory plan at %d CTAs", vgrid);
+    return HAKMC_EINVAL;
+  }
+  std::vector<PhaseDesc> both(p0);
+  both.insert(both.end(), p1.begin(), p1.end());
+  if ((int)both.size() > c->prog2_cap) {
+    void* p = nullptr;
+    const int r = dalloc(c, &p, both.size() * sizeof(PhaseDesc));
+    if (r) return r;
+    c->prog2_dev = (PhaseDesc*)p;
+    c->prog2_cap = (int)both.size();
+  }
+  CK(cudaMemcpy(c->prog2_dev, both.data(), both.size() * sizeof(PhaseDesc), cudaMemcpyHostToDevice));
+  {
+    std::vector<SegRange> tab(p0.size() * (size_t)vgrid * MAX_SEGS);
+    step_ranges(p0.data(), (int)p0.size(), vgrid, 0, vgrid, tab.data());
+    if (tab.size() > c->ranges2_cap) {
+      void* p = nullptr;
+      const int r = dalloc(c, &p, tab.size() * sizeof(SegRange));
+      if (r) return r;
+      c->ranges2_dev = (SegRange*)p;
+      c->ranges2_cap = tab.size();
+    }
+    CK(cudaMemcpy(c->ranges2_dev, tab.data(), tab.size() * sizeof(SegRange), cudaMemcpyHostToDevice));
+  }
+  a.prog = c->prog2_dev;
+  a.ranges = c->ranges2_dev;
+  a.n_phases = (int)p0.size();
+  a.token_dev = c->token_dev;  // [sequence]
+  a.pos_dev = c->pos_dev;      // [sequence]
+  a.token_log = nullptr;
+  a.keys = c->step_keys;
+  a.bar = c->step_bar;
+  a.tickets = c->step_tickets;
+  a.err_flag = c->err_flag;
+  a.tok_embd = c->tok_embd.w;
+  a.xb_ll = c->xb_ll;
+  a.ll_stride = (long long)c->ll_words;
+  a.xb_plain = c->xb;
+  a.D = c->D;
+  a.n_layers = c->run_layers;
+  a.skip_last = 1;
+  a.head_dim = c->hd;
+  c->step2 = a;
+  c->prog2_layers = c->run_layers;
+  return 0;
+}
+
+// One decode step of sequences 0 and 1 (cache slots 0 and 1) at positions
+// pos[0], pos[1] with input tokens tokens[0], tokens[1], in one launch; the
+// picks land in token_dev[0..1], the logits in logits + i * vocab.
+static int run_pair(hakmc_ctx* c, const int* tokens, const int* pos) {
+  int r = ensure_program2(c);
+  if (r) return r;
+  StepArgs a = c->step2;
+  a.n_seq = 2;
+  a.n_steps = 1;
+  a.n_forced = 1;
+  a.forced = c->seq_tokens_dev;
+  a.seq_pos0[0] = pos[0];
+  a.seq_pos0[1] = pos[1];
+  a.pos0 = pos[0];
+  a.log_base = 0;
+  const uint64_t span = (uint64_t)(a.n_phases + 1);
+  if ((uint64_t)c->tag_base + span >= 0xFFFFFFF0ull) {
+    CK(cudaMemsetAsync(c->xb_ll, 0, c->ll_words * 8 * STEP_SEQ_MAX, c->stream));
+    c->tag_base = 1;
+  }
+  a.tp_rank = 0;
+  a.tp_world = 1;
+  a.tag_base = c->tag_base;
+  c->tag_base += (uint32_t)span;
+  c->h_pinned[8] = tokens[0];
+  c->h_pinned[9] = tokens[1];
+  CK(cudaMemcpyAsync(c->seq_tokens_dev, &c->h_pinned[8], 8, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaMemsetAsync(c->step_bar, 0, 32 * STEP_SEQ_MAX, c->stream));
+  CK(cudaMemsetAsync(c->step_tickets, 0, 64 * 4 * STEP_SEQ_MAX, c->stream));
+  CK(cudaMemsetAsync(c->step_keys, 0, 32 * STEP_SEQ_MAX, c->stream));
+  CK(launch_step(a, 2 * (c->num_sms / 2), c->stream));
+  c->step_ran = true;
   return 0;
 }
 
@@ -558,7 +680,7 @@ static int run_steps(hakmc_ctx* c, int n_steps, int n_forced, const int* forced_
     // peers write into these words without a host round trip: clearing them
     // under tensor parallelism could erase a peer's early write
     if (c->tp_world > 1) { set_err("tag space of the tensor-parallel group used up: recreate the contexts"); return HAKMC_ERANGE; }
-    CK(cudaMemsetAsync(c->xb_ll, 0, c->ll_words * 8, c->stream));
+    CK(cudaMemsetAsync(c->xb_ll, 0, c->ll_words * 8 * STEP_SEQ_MAX, c->stream));
     c->tag_base = 1;
   }
   a.tp_rank = c->tp_rank;
@@ -731,9 +853,8 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
     set_err("max_seq %d: beyond what one attention split merge combines", c->max_seq);
     return HAKMC_EINVAL;
   }
-  if ((r = dalloc(c, (void**)&c->attn_part,
-                  attention_scratch_floats(c->KVH, max_split, c->H / c->KVH, c->hd) * 4 * B)))
-    return r;
+  c->attn_part_floats = attention_scratch_floats(c->KVH, max_split, c->H / c->KVH, c->hd);
+  if ((r = dalloc(c, (void**)&c->attn_part, c->attn_part_floats * 4 * std::max(B, STEP_SEQ_MAX)))) return r;
   if ((r = dalloc(c, (void**)&c->attn_counters, 64 * 4 * B))) return r;
   CK(cudaMemset(c->attn_counters, 0, 64 * 4 * B));
   if ((r = dalloc(c, (void**)&c->token_dev, 16 * B))) return r;
@@ -744,21 +865,24 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
   if ((r = dalloc(c, (void**)&c->argmax_key, 8 * B))) return r;
   if ((r = dalloc(c, (void**)&c->done_counter, 4 * B))) return r;
   if ((r = dalloc(c, (void**)&c->err_flag, 16))) return r;
-  if ((r = dalloc(c, (void**)&c->step_bar, 16))) return r;
-  if ((r = dalloc(c, (void**)&c->step_keys, 32))) return r;
-  if ((r = dalloc(c, (void**)&c->step_tickets, 64 * 4))) return r;
+  // per sequence of a launch: bar 8 words, keys 4, tickets 64 (the kernel's strides)
+  if ((r = dalloc(c, (void**)&c->step_bar, 32 * STEP_SEQ_MAX))) return r;
+  if ((r = dalloc(c, (void**)&c->step_keys, 32 * STEP_SEQ_MAX))) return r;
+  if ((r = dalloc(c, (void**)&c->step_tickets, 64 * 4 * STEP_SEQ_MAX))) return r;
+  if ((r = dalloc(c, (void**)&c->seq_tokens_dev, 4 * STEP_SEQ_MAX))) return r;
   if ((r = dalloc(c, (void**)&c->step_xbar, 16))) return r;
   CK(cudaMemset(c->step_xbar, 0, 16));
-  CK(cudaMemset(c->step_bar, 0, 16));
-  CK(cudaMemset(c->step_keys, 0, 32));
-  CK(cudaMemset(c->step_tickets, 0, 64 * 4));
+  CK(cudaMemset(c->step_bar, 0, 32 * STEP_SEQ_MAX));
+  CK(cudaMemset(c->step_keys, 0, 32 * STEP_SEQ_MAX));
+  CK(cudaMemset(c->step_tickets, 0, 64 * 4 * STEP_SEQ_MAX));
   {
     // exchange vectors, 16-byte aligned pieces of one allocation
     auto up2 = [](size_t n) { return (n + 1) & ~(size_t)1; };
     const size_t nD = up2(c->D), nKV = up2(c->KV), nF = up2(c->F);
     c->ll_words = 2 * nD + nD + 2 * nKV + nD + nF;
-    if ((r = dalloc(c, (void**)&c->xb_ll, c->ll_words * 8))) return r;
-    CK(cudaMemset(c->xb_ll, 0, c->ll_words * 8));
+    // one copy per sequence of a multi-sequence launch, ll_words apart
+    if ((r = dalloc(c, (void**)&c->xb_ll, c->ll_words * 8 * STEP_SEQ_MAX))) return r;
+    CK(cudaMemset(c->xb_ll, 0, c->ll_words * 8 * STEP_SEQ_MAX));
     c->q_ll = c->xb_ll + 2 * nD;
     c->k_ll = c->q_ll + nD;
     c->v_ll = c->k_ll + nKV;
@@ -1144,7 +1268,24 @@ extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* p
   const int saved_pos = c->pos;
   CK(cudaMemcpyAsync(c->token_dev + 2, c->token_dev, 4, cudaMemcpyDeviceToDevice, c->stream));
   int r = 0;
-  for (int i = 0; i < n_seq && !r; i++) {
+  int i = 0;
+  // pairs of sequences share one launch (one GPU, step kernel, two cache slots)
+  const bool pairs = c->tp_world == 1 && c->max_batch >= 2;
+  for (; pairs && i + 1 < n_seq && !r; i += 2) {
+    if (i > 0) {
+      // slots 2 and 3 onwards: the pair's programs address slots 0 and 1
+      break;
+    }
+    r = run_pair(c, tokens + i, pos + i);
+    if (r) break;
+    CK(cudaMemcpyAsync(&c->h_pinned[10], c->token_dev, 8, cudaMemcpyDeviceToHost, c->stream));
+    if (logits) CK(cudaMemcpyAsync(logits + (size_t)i * c->V, c->logits, (size_t)2 * c->V * 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    r = check_flag(c);
+    if (r) break;
+    if (argmax) { argmax[i] = c->h_pinned[10]; argmax[i + 1] = c->h_pinned[11]; }
+  }
+  for (; i < n_seq && !r; i++) {
     c->pos = pos[i];
     c->h_pinned[0] = tokens[i];
     CK(cudaMemcpyAsync(c->token_dev, &c->h_pinned[0], 4, cudaMemcpyHostToDevice, c->stream));

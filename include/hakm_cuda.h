@@ -91,10 +91,12 @@ int hakmc_decode(hakmc_ctx *c, int n_steps, int *out_tokens);
  * using KV-cache slot i (slot 0 is also the single-sequence calls' cache;
  * their position and last pick are left as they were). The reference
  * decodes one sequence at a time; each row of this call equals hakm_forward
- * on a context holding that sequence's cache (bit for bit: the same step
- * kernel runs each sequence in turn). argmax [host] gets n_seq ids; logits
- * [host] (may be NULL) n_seq*vocab floats. 0, HAKMC_ERANGE for a position
- * beyond max_seq, or another negative code. */
+ * on a context holding that sequence's cache. Sequences 0 and 1 share one
+ * step-kernel launch, each on half the SMs (one GPU, max_batch >= 2): their
+ * rows agree with single-sequence runs to fp32 rounding (rel 1e-6); further
+ * sequences run one launch each, bit for bit. argmax [host] gets n_seq ids;
+ * logits [host] (may be NULL) n_seq*vocab floats. 0, HAKMC_ERANGE for a
+ * position beyond max_seq, or another negative code. */
 int hakmc_forward_batch(hakmc_ctx *c, const int *tokens, const int *pos,
                         int n_seq, float *logits, int *argmax);
 

@@ -236,8 +236,12 @@ def test_prefill_rejects_bad_input(cuda, small_path):
 
 def test_forward_batch_rows_equal_single_sequence_contexts(cuda, small_path):
     """hakmc_forward_batch: row i is hakm_forward on a context holding
-    sequence i's cache (slot i) — bit for bit, since the same step kernel
-    runs each sequence. Three sequences with different prompts, fed and then
+    sequence i's cache (slot i). Sequences 0 and 1 share one launch, each on
+    half the SMs: their logits agree with the single-sequence runs to fp32
+    rounding (rel-L2 <= 1e-6; the half-grid plan is not the same
+    computation bit for bit), and their picks agree unless the two best
+    logits are within that noise. Sequence 2 runs alone, on the whole grid:
+    bit for bit. Three sequences with different prompts, fed and then
     decoded greedily in lockstep; sequence 2 starts two positions later."""
     prompts = [[11, 22, 33, 44], [500, 600, 700, 800], [3000, 17, 42, 9]]
     n_gen, start = 6, [0, 0, 2]
@@ -260,8 +264,13 @@ def test_forward_batch_rows_equal_single_sequence_contexts(cuda, small_path):
                 if not rows[i]:
                     continue
                 ref_logits, ref_am = singles[i].forward(toks[i])
-                assert np.array_equal(logits[i].view(np.uint32), ref_logits.view(np.uint32)), (rnd, i)
-                assert am[i] == ref_am
+                if i >= 2:
+                    assert np.array_equal(logits[i].view(np.uint32), ref_logits.view(np.uint32)), (rnd, i)
+                    assert am[i] == ref_am
+                else:
+                    assert rel_l2(logits[i], ref_logits) < 1e-6, (rnd, i)
+                    top = np.sort(ref_logits)[-2:]
+                    assert am[i] == ref_am or top[1] - top[0] < 1e-5 * abs(top[1]), (rnd, i)
                 nxt[i] = int(am[i])
                 pos[i] += 1
         assert batch.pos == 0  # the single-sequence state is left alone
