@@ -137,6 +137,19 @@ cudaError_t launch_embed_q6k(float* xb, const uint8_t* w, const int* token, int 
 cudaError_t launch_rope(float* x, const float* rope_cs, const int* pos_dev, int n_heads, int head_dim,
                         cudaStream_t s);
 
+// ---- batched prompt processing (hakm_prefill.cu): rows of a prompt chunk ----
+cudaError_t launch_pf_embed(float* x, const uint8_t* w, const int* tokens, int M, int D, cudaStream_t s);
+cudaError_t launch_pf_norm_quant(const float* x, const float* w, int M, int D, float eps, float* xn, int8_t* xq,
+                                 float* xs, cudaStream_t s);
+cudaError_t launch_pf_q6k_gemm(float* out, const uint8_t* w, const float* x, const float* bias, int n_out, int K,
+                               int M, bool accumulate, cudaStream_t s);
+cudaError_t launch_pf_rope_kv(const float* qk, const float* v, float* q, float* kc, float* vc, const float* rope_cs,
+                              int M, int pos0, int D, int KV, int hd, cudaStream_t s);
+cudaError_t launch_pf_attention(float* out, const float* q, const float* kc, const float* vc, int M, int pos0, int H,
+                                int KVH, int hd, float scale, cudaStream_t s);
+cudaError_t launch_pf_swiglu(float* h, const float* gu, int M, int F, cudaStream_t s);
+cudaError_t launch_pf_add(float* x, const float* o, size_t n, cudaStream_t s);
+
 struct AttnParams {
   const float* q;        // [H*hd]
   const float* k_cache;  // layer base [max_seq][kv_dim]
@@ -200,7 +213,8 @@ struct alignas(16) PhaseDesc {  // copied to shared memory as 16-byte words
   int epi_rec_off;
 };
 
-constexpr int STEP_SEQ_MAX = 2;  // sequences one step-kernel launch can carry
+constexpr int STEP_SEQ_MAX = 4;  // sequences one step-kernel launch can address
+constexpr int STEP_GROUP_MAX = 3;  // sequences forward_batch puts in one launch
 
 struct StepArgs {
   const PhaseDesc* prog;   // device array, n_phases entries (one decode step)

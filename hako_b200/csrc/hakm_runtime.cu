@@ -165,13 +165,14 @@ struct hakmc_ctx {
   SegRange* ranges_dev = nullptr;  // [phase][cta][segment] rows of the step program
   size_t ranges_cap = 0;
   StepArgs step = {};
-  // forward_batch: two sequences per launch, each on half the SMs with its
-  // own program (exchange vectors, cache slot, logits, counters)
-  PhaseDesc* prog2_dev = nullptr;
-  int prog2_cap = 0, prog2_layers = -1;
-  SegRange* ranges2_dev = nullptr;
-  size_t ranges2_cap = 0;
-  StepArgs step2 = {};
+  // forward_batch: n (2..STEP_SEQ_MAX) sequences per launch, each on 1/n of
+  // the SMs with its own program (exchange vectors, cache slot, logits,
+  // counters); indexed by n
+  PhaseDesc* progn_dev[STEP_SEQ_MAX + 1] = {};
+  int progn_cap[STEP_SEQ_MAX + 1] = {}, progn_layers[STEP_SEQ_MAX + 1] = {-1, -1, -1, -1, -1};
+  SegRange* rangesn_dev[STEP_SEQ_MAX + 1] = {};
+  size_t rangesn_cap[STEP_SEQ_MAX + 1] = {};
+  StepArgs stepn[STEP_SEQ_MAX + 1] = {};
   int* seq_tokens_dev = nullptr;  // input tokens of a multi-sequence launch
   size_t attn_part_floats = 0;    // attention scratch of one sequence
   unsigned int* step_bar = nullptr;
@@ -191,6 +192,13 @@ struct hakmc_ctx {
   size_t xr_size[XR_COUNT] = {};
   void* peer_ptr[TP_MAX][XR_COUNT] = {};
   bool peer_ipc[TP_MAX] = {};         // opened through IPC (closed at destroy)
+  // batched prompt processing (hakmc_prefill_batched): buffers for pf_rows
+  // rows of a chunk; pf_part holds pf_part_bytes of tensor-core split partials
+  int pf_rows = 0;
+  float *pf_x = nullptr, *pf_xn = nullptr, *pf_qk = nullptr, *pf_v = nullptr, *pf_q = nullptr, *pf_att = nullptr,
+        *pf_gu = nullptr, *pf_h = nullptr, *pf_tmp = nullptr, *pf_xs = nullptr, *pf_part = nullptr;
+  int8_t* pf_xq = nullptr;
+  size_t pf_part_bytes = 0;
 };
 
 static int dalloc(hakmc_ctx* c, void** p, size_t n) {
@@ -201,6 +209,17 @@ static int dalloc(hakmc_ctx* c, void** p, size_t n) {
   }
   c->allocs.push_back(*p);
   return 0;
+}
+
+// Free one dalloc'd buffer before the context goes (a buffer being regrown).
+static void dfree(hakmc_ctx* c, void* p) {
+  if (!p) return;
+  for (size_t i = 0; i < c->allocs.size(); i++)
+    if (c->allocs[i] == p) {
+      cudaFree(p);
+      c->allocs.erase(c->allocs.begin() + (long)i);
+      return;
+    }
 }
 
 // Upload rows of a Q4_K / Q6_K matrix. `order[i]` is the source row of device
@@ -559,47 +578,49 @@ static int ensure_program(hakmc_ctx* c) {
   return 0;
 }
 
-// The programs of sequences 0 and 1 for a two-sequence launch: each runs on
-// half the SMs (the shared-memory plan and row table are those of that
-// half-grid), with its own exchange vectors, cache slot, logits and
-// counters. The row sums do not depend on which CTA computes a row, so each
-// sequence's results are those of a single-sequence launch, bit for bit.
-static int ensure_program2(hakmc_ctx* c) {
-  if (c->prog2_layers == c->run_layers) return 0;
-  const int vgrid = c->num_sms / 2;
-  std::vector<PhaseDesc> p0, p1;
-  build_program(c, 0, p0);
-  build_program(c, 1, p1);
-  StepArgs a = {}, a1 = {};
-  if (!plan_step(p0.data(), (int)p0.size(), vgrid, a) || !plan_step(p1.data(), (int)p1.size(), vgrid, a1)) {
-    set_err("step kernel: shapes do not fit its shared-memory plan at %d CTAs", vgrid);
-    return HAKMC_EINVAL;
+// The programs of sequences 0..n-1 for an n-sequence launch: each runs on
+// 1/n of the SMs (the shared-memory plan and row table are those of that
+// virtual grid), with its own exchange vectors, cache slot, logits and
+// counters. HAKMC_EINVAL when the shapes do not fit that grid's plan.
+static int ensure_program_n(hakmc_ctx* c, int n) {
+  if (c->progn_layers[n] == c->run_layers) return 0;
+  const int vgrid = c->num_sms / n;
+  std::vector<PhaseDesc> all, pr;
+  StepArgs a = {};
+  for (int q = 0; q < n; q++) {
+    build_program(c, q, pr);
+    StepArgs aq = {};
+    if (!plan_step(pr.data(), (int)pr.size(), vgrid, aq)) {
+      set_err("step kernel: shapes do not fit its shared-memory plan at %d CTAs", vgrid);
+      return HAKMC_EINVAL;
+    }
+    if (q == 0) a = aq;
+    all.insert(all.end(), pr.begin(), pr.end());
   }
-  std::vector<PhaseDesc> both(p0);
-  both.insert(both.end(), p1.begin(), p1.end());
-  if ((int)both.size() > c->prog2_cap) {
+  const int n_phases = (int)pr.size();
+  if ((int)all.size() > c->progn_cap[n]) {
     void* p = nullptr;
-    const int r = dalloc(c, &p, both.size() * sizeof(PhaseDesc));
+    const int r = dalloc(c, &p, all.size() * sizeof(PhaseDesc));
     if (r) return r;
-    c->prog2_dev = (PhaseDesc*)p;
-    c->prog2_cap = (int)both.size();
+    c->progn_dev[n] = (PhaseDesc*)p;
+    c->progn_cap[n] = (int)all.size();
   }
-  CK(cudaMemcpy(c->prog2_dev, both.data(), both.size() * sizeof(PhaseDesc), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(c->progn_dev[n], all.data(), all.size() * sizeof(PhaseDesc), cudaMemcpyHostToDevice));
   {
-    std::vector<SegRange> tab(p0.size() * (size_t)vgrid * MAX_SEGS);
-    step_ranges(p0.data(), (int)p0.size(), vgrid, 0, vgrid, tab.data());
-    if (tab.size() > c->ranges2_cap) {
+    std::vector<SegRange> tab((size_t)n_phases * vgrid * MAX_SEGS);
+    step_ranges(all.data(), n_phases, vgrid, 0, vgrid, tab.data());
+    if (tab.size() > c->rangesn_cap[n]) {
       void* p = nullptr;
       const int r = dalloc(c, &p, tab.size() * sizeof(SegRange));
       if (r) return r;
-      c->ranges2_dev = (SegRange*)p;
-      c->ranges2_cap = tab.size();
+      c->rangesn_dev[n] = (SegRange*)p;
+      c->rangesn_cap[n] = tab.size();
     }
-    CK(cudaMemcpy(c->ranges2_dev, tab.data(), tab.size() * sizeof(SegRange), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->rangesn_dev[n], tab.data(), tab.size() * sizeof(SegRange), cudaMemcpyHostToDevice));
   }
-  a.prog = c->prog2_dev;
-  a.ranges = c->ranges2_dev;
-  a.n_phases = (int)p0.size();
+  a.prog = c->progn_dev[n];
+  a.ranges = c->rangesn_dev[n];
+  a.n_phases = n_phases;
   a.token_dev = c->token_dev;  // [sequence]
   a.pos_dev = c->pos_dev;      // [sequence]
   a.token_log = nullptr;
@@ -615,24 +636,23 @@ static int ensure_program2(hakmc_ctx* c) {
   a.n_layers = c->run_layers;
   a.skip_last = 1;
   a.head_dim = c->hd;
-  c->step2 = a;
-  c->prog2_layers = c->run_layers;
+  a.n_seq = n;
+  c->stepn[n] = a;
+  c->progn_layers[n] = c->run_layers;
   return 0;
 }
 
-// One decode step of sequences 0 and 1 (cache slots 0 and 1) at positions
-// pos[0], pos[1] with input tokens tokens[0], tokens[1], in one launch; the
-// picks land in token_dev[0..1], the logits in logits + i * vocab.
-static int run_pair(hakmc_ctx* c, const int* tokens, const int* pos) {
-  int r = ensure_program2(c);
+// One decode step of sequences 0..n-1 (cache slots 0..n-1) at positions
+// pos[i] with input tokens tokens[i], in one launch; the picks land in
+// token_dev[0..n-1], the logits in logits + i * vocab.
+static int run_group(hakmc_ctx* c, int n, const int* tokens, const int* pos) {
+  int r = ensure_program_n(c, n);
   if (r) return r;
-  StepArgs a = c->step2;
-  a.n_seq = 2;
+  StepArgs a = c->stepn[n];
   a.n_steps = 1;
   a.n_forced = 1;
   a.forced = c->seq_tokens_dev;
-  a.seq_pos0[0] = pos[0];
-  a.seq_pos0[1] = pos[1];
+  for (int q = 0; q < n; q++) a.seq_pos0[q] = pos[q];
   a.pos0 = pos[0];
   a.log_base = 0;
   const uint64_t span = (uint64_t)(a.n_phases + 1);
@@ -644,13 +664,12 @@ static int run_pair(hakmc_ctx* c, const int* tokens, const int* pos) {
   a.tp_world = 1;
   a.tag_base = c->tag_base;
   c->tag_base += (uint32_t)span;
-  c->h_pinned[8] = tokens[0];
-  c->h_pinned[9] = tokens[1];
-  CK(cudaMemcpyAsync(c->seq_tokens_dev, &c->h_pinned[8], 8, cudaMemcpyHostToDevice, c->stream));
+  for (int q = 0; q < n; q++) c->h_pinned[8 + q] = tokens[q];
+  CK(cudaMemcpyAsync(c->seq_tokens_dev, &c->h_pinned[8], 4 * n, cudaMemcpyHostToDevice, c->stream));
   CK(cudaMemsetAsync(c->step_bar, 0, 32 * STEP_SEQ_MAX, c->stream));
   CK(cudaMemsetAsync(c->step_tickets, 0, 64 * 4 * STEP_SEQ_MAX, c->stream));
   CK(cudaMemsetAsync(c->step_keys, 0, 32 * STEP_SEQ_MAX, c->stream));
-  CK(launch_step(a, 2 * (c->num_sms / 2), c->stream));
+  CK(launch_step(a, n * (c->num_sms / n), c->stream));
   c->step_ran = true;
   return 0;
 }
@@ -857,7 +876,8 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
   if ((r = dalloc(c, (void**)&c->attn_part, c->attn_part_floats * 4 * std::max(B, STEP_SEQ_MAX)))) return r;
   if ((r = dalloc(c, (void**)&c->attn_counters, 64 * 4 * B))) return r;
   CK(cudaMemset(c->attn_counters, 0, 64 * 4 * B));
-  if ((r = dalloc(c, (void**)&c->token_dev, 16 * B))) return r;
+  // [sequence] plus a save slot (forward_batch) past the STEP_SEQ_MAX sequences
+  if ((r = dalloc(c, (void**)&c->token_dev, 4 * std::max(4 * B, 2 * STEP_SEQ_MAX + 1)))) return r;
   if ((r = dalloc(c, (void**)&c->pos_dev, 16 * B))) return r;
   if ((r = dalloc(c, (void**)&c->step_dev, 16))) return r;
   c->token_log_cap = c->max_seq + 8;
@@ -1077,6 +1097,153 @@ extern "C" int hakmc_prefill(hakmc_ctx* c, const int* tokens, int n, float* logi
   return 0;
 }
 
+// ------------------------------------------------------------ batched prefill
+//
+// The rows of a prompt chunk go through every layer together
+// (hakm_prefill.cu): Q4_K matmuls on the tensor cores, Q6_K matmuls as fp32
+// tiles, causal attention over the cache, which the chunk's own K/V rows
+// enter first. Then the last row's final norm, lm_head and argmax run as in
+// a decode step.
+
+constexpr int PF_ROWS_DEFAULT = 1024;
+
+// Buffers for chunks of `rows` rows (regrown when a larger chunk comes).
+static int pf_ensure(hakmc_ctx* c, int rows) {
+  if (rows <= c->pf_rows) return 0;
+  float** fb[] = {&c->pf_x, &c->pf_xn, &c->pf_qk, &c->pf_v, &c->pf_q, &c->pf_att, &c->pf_gu, &c->pf_h, &c->pf_tmp,
+                  &c->pf_xs};
+  for (float** b : fb) { dfree(c, *b); *b = nullptr; }
+  dfree(c, c->pf_xq);
+  c->pf_xq = nullptr;
+  c->pf_rows = 0;
+  const size_t M = (size_t)rows, K = (size_t)std::max(c->D, c->F);
+  const size_t n[] = {M * c->D, M * c->D, M * (c->D + c->KV), M * c->KV, M * c->D, M * c->D, M * 2 * c->F,
+                      M * c->F, M * c->D, M * K / 32};
+  for (size_t i = 0; i < sizeof(n) / sizeof(n[0]); i++) {
+    const int r = dalloc(c, (void**)fb[i], n[i] * 4);
+    if (r) return r;
+  }
+  const int r = dalloc(c, (void**)&c->pf_xq, M * K);
+  if (r) return r;
+  c->pf_rows = rows;
+  return 0;
+}
+
+// out[M][W.rows] (+)= W x (+ bias) for the chunk's rows: Q4_K on the q8
+// codes (xq, xs), Q6_K on the fp32 rows xn. Accumulating Q4_K products go
+// through pf_tmp, then one add (the reference's order: product, then +=).
+static cudaError_t pf_matmul(hakmc_ctx* c, float* out, const DevMat& W, const float* xn, const int8_t* xq,
+                             const float* xs, const float* bias, int M, bool accumulate) {
+  if (W.type == W_Q6K) return launch_pf_q6k_gemm(out, W.w, xn, bias, W.rows, W.cols, M, accumulate, c->stream);
+  float* dst = accumulate ? c->pf_tmp : out;
+  cudaError_t e = launch_q4k_mma(dst, W.w, xq, xs, bias, W.rows, W.cols, M, c->pf_part, c->err_flag, c->num_sms,
+                                 c->stream);
+  if (e != cudaSuccess || !accumulate) return e;
+  return launch_pf_add(out, c->pf_tmp, (size_t)M * W.rows, c->stream);
+}
+
+// Tensor-core split partials for every Q4_K matmul of a chunk of M rows.
+static int pf_ensure_part(hakmc_ctx* c, int M) {
+  size_t need = 0;
+  for (int l = 0; l < c->run_layers; l++) {
+    const DevLayer& y = c->layers[l];
+    for (const DevMat* W : {&y.wqk, &y.wv, &y.wo, &y.wgu, &y.down})
+      if (W->type == W_Q4K) need = std::max(need, q4k_mma_scratch_bytes(W->rows, W->cols, M, c->num_sms));
+  }
+  if (need <= c->pf_part_bytes) return 0;
+  dfree(c, c->pf_part);
+  c->pf_part = nullptr;
+  c->pf_part_bytes = 0;
+  const int r = dalloc(c, (void**)&c->pf_part, need);
+  if (r) return r;
+  c->pf_part_bytes = need;
+  return 0;
+}
+
+// One chunk: rows tokens_dev[0..M) at positions pos0.. of sequence 0 through
+// run_layers layers; leaves the residual rows in pf_x.
+static cudaError_t pf_chunk(hakmc_ctx* c, const int* tokens_dev, int M, int pos0) {
+  const int D = c->D, KV = c->KV, F = c->F;
+  const size_t lstride = (size_t)c->max_seq * KV;
+  const float scale = 1.0f / sqrtf((float)c->hd);
+  cudaStream_t s = c->stream;
+  cudaError_t e = launch_pf_embed(c->pf_x, c->tok_embd.w, tokens_dev, M, D, s);
+  for (int l = 0; l < c->run_layers && e == cudaSuccess; l++) {
+    const DevLayer& y = c->layers[l];
+    float* kc = c->k_cache + (size_t)l * lstride;
+    float* vc = c->v_cache + (size_t)l * lstride;
+    // attention block (src/model.c:102-146)
+    if ((e = launch_pf_norm_quant(c->pf_x, y.attn_norm, M, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
+    if ((e = pf_matmul(c, c->pf_qk, y.wqk, c->pf_xn, c->pf_xq, c->pf_xs, y.bqk, M, false))) break;
+    if ((e = pf_matmul(c, c->pf_v, y.wv, c->pf_xn, c->pf_xq, c->pf_xs, y.bv, M, false))) break;
+    if ((e = launch_pf_rope_kv(c->pf_qk, c->pf_v, c->pf_q, kc, vc, c->rope_cs, M, pos0, D, KV, c->hd, s))) break;
+    if ((e = launch_pf_attention(c->pf_att, c->pf_q, kc, vc, M, pos0, c->H, c->KVH, c->hd, scale, s))) break;
+    if (y.wo.type == W_Q4K && (e = launch_quantize_q8(c->pf_att, M * D, c->pf_xq, c->pf_xs, s))) break;
+    if ((e = pf_matmul(c, c->pf_x, y.wo, c->pf_att, c->pf_xq, c->pf_xs, nullptr, M, true))) break;
+    // feed-forward block (src/model.c:148-156)
+    if ((e = launch_pf_norm_quant(c->pf_x, y.ffn_norm, M, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
+    if ((e = pf_matmul(c, c->pf_gu, y.wgu, c->pf_xn, c->pf_xq, c->pf_xs, nullptr, M, false))) break;
+    if ((e = launch_pf_swiglu(c->pf_h, c->pf_gu, M, F, s))) break;
+    if (y.down.type == W_Q4K && (e = launch_quantize_q8(c->pf_h, M * F, c->pf_xq, c->pf_xs, s))) break;
+    e = pf_matmul(c, c->pf_x, y.down, c->pf_h, c->pf_xq, c->pf_xs, nullptr, M, true);
+  }
+  return e;
+}
+
+extern "C" int hakmc_prefill_batched(hakmc_ctx* c, const int* tokens, int n, int chunk_rows, float* logits,
+                                     int* argmax) {
+  if (!c || !tokens || n <= 0) { set_err("prefill: need at least one token"); return HAKMC_EINVAL; }
+  if (c->tp_world > 1) return hakmc_prefill(c, tokens, n, logits, argmax);
+  if (c->pos + n > c->max_seq) { set_err("prefill: sequence exceeds max_seq"); return HAKMC_ERANGE; }
+  for (int i = 0; i < n; i++)
+    if (tokens[i] < 0 || tokens[i] >= c->V) { set_err("prefill: token %d out of range", tokens[i]); return HAKMC_EINVAL; }
+  if (c->H / c->KVH > 32) { set_err("prefill: more than 32 query heads per kv head"); return HAKMC_EINVAL; }
+  CK(cudaSetDevice(c->device));
+  const int rows = std::min(n, chunk_rows > 0 ? chunk_rows : PF_ROWS_DEFAULT);
+  int r = pf_ensure(c, rows);
+  if (!r) r = pf_ensure_part(c, rows);
+  if (!r && n % rows) r = pf_ensure_part(c, n % rows);
+  if (r) return r;
+  if (n > c->prompt_cap) {
+    void* p = nullptr;
+    r = dalloc(c, &p, (size_t)n * 4);
+    if (r) return r;
+    dfree(c, c->prompt_dev);
+    c->prompt_dev = (int*)p;
+    c->prompt_cap = n;
+  }
+  std::vector<int> pp(tokens, tokens + n);
+  CK(cudaMemcpyAsync(c->prompt_dev, pp.data(), (size_t)n * 4, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaEventRecord(c->ev0, c->stream));
+  int last = 0;
+  for (int i = 0; i < n; i += rows) {
+    const int M = std::min(rows, n - i);
+    CK(pf_chunk(c, c->prompt_dev + i, M, c->pos + i));
+    last = M;
+  }
+  // the last row's final norm + lm_head + argmax, as a decode step ends:
+  // the residual row goes to xb, the position word to that row's position
+  // (the lm_head kernel moves it on by one and leaves the pick in token_dev)
+  CK(cudaMemcpyAsync(c->xb, c->pf_x + (size_t)(last - 1) * c->D, (size_t)c->D * 4, cudaMemcpyDeviceToDevice,
+                     c->stream));
+  c->h_pinned[2] = c->pos + n - 1;
+  CK(cudaMemcpyAsync(c->pos_dev, &c->h_pinned[2], 4, cudaMemcpyHostToDevice, c->stream));
+  CK(cudaMemsetAsync(c->step_dev, 0, 4, c->stream));
+  CK(enqueue_phase(c, 0, PH_LMHEAD, 1, false));
+  CK(cudaEventRecord(c->ev1, c->stream));
+  CK(cudaMemcpyAsync(&c->h_pinned[1], c->token_dev, 4, cudaMemcpyDeviceToHost, c->stream));
+  if (logits) CK(cudaMemcpyAsync(c->logits_pinned, c->logits, (size_t)c->V * 4, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  CK(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
+  c->pos += n;
+  c->step_ran = false;
+  r = check_flag(c);
+  if (r) return r;
+  if (argmax) *argmax = c->h_pinned[1];
+  if (logits) memcpy(logits, c->logits_pinned, (size_t)c->V * 4);
+  return 0;
+}
+
 extern "C" void hakmc_free(hakmc_ctx* c) { hakmc_destroy(c); }
 
 extern "C" int hakmc_decode(hakmc_ctx* c, int n_steps, int* out) {
@@ -1266,24 +1433,27 @@ extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* p
   // sequence 0 is also the single-sequence API's: its position and last pick
   // (the input hakmc_decode continues from) are restored afterwards
   const int saved_pos = c->pos;
-  CK(cudaMemcpyAsync(c->token_dev + 2, c->token_dev, 4, cudaMemcpyDeviceToDevice, c->stream));
+  CK(cudaMemcpyAsync(c->token_dev + 2 * STEP_SEQ_MAX, c->token_dev, 4, cudaMemcpyDeviceToDevice, c->stream));
   int r = 0;
   int i = 0;
-  // pairs of sequences share one launch (one GPU, step kernel, two cache slots)
-  const bool pairs = c->tp_world == 1 && c->max_batch >= 2;
-  for (; pairs && i + 1 < n_seq && !r; i += 2) {
-    if (i > 0) {
-      // slots 2 and 3 onwards: the pair's programs address slots 0 and 1
-      break;
+  // the first sequences share one launch (one GPU, step kernel, cache slots
+  // 0..g-1): as many as the context and the shared-memory plan allow
+  // (at most STEP_GROUP_MAX: four sequences per launch on the 3B shapes, a
+  // virtual grid of 37 CTAs, stopped with an illegal-instruction error whose
+  // cause reading has not found; three and two run clean)
+  int g = c->tp_world == 1 ? std::min(std::min(n_seq, c->max_batch), STEP_GROUP_MAX) : 1;
+  while (g > 1 && ensure_program_n(c, g) != 0) g--;
+  if (g > 1) {
+    r = run_group(c, g, tokens, pos);
+    if (!r) {
+      CK(cudaMemcpyAsync(&c->h_pinned[12], c->token_dev, 4 * g, cudaMemcpyDeviceToHost, c->stream));
+      if (logits) CK(cudaMemcpyAsync(logits, c->logits, (size_t)g * c->V * 4, cudaMemcpyDeviceToHost, c->stream));
+      CK(cudaStreamSynchronize(c->stream));
+      r = check_flag(c);
+      if (!r && argmax)
+        for (int q = 0; q < g; q++) argmax[q] = c->h_pinned[12 + q];
+      i = g;
     }
-    r = run_pair(c, tokens + i, pos + i);
-    if (r) break;
-    CK(cudaMemcpyAsync(&c->h_pinned[10], c->token_dev, 8, cudaMemcpyDeviceToHost, c->stream));
-    if (logits) CK(cudaMemcpyAsync(logits + (size_t)i * c->V, c->logits, (size_t)2 * c->V * 4, cudaMemcpyDeviceToHost, c->stream));
-    CK(cudaStreamSynchronize(c->stream));
-    r = check_flag(c);
-    if (r) break;
-    if (argmax) { argmax[i] = c->h_pinned[10]; argmax[i + 1] = c->h_pinned[11]; }
   }
   for (; i < n_seq && !r; i++) {
     c->pos = pos[i];
@@ -1302,7 +1472,7 @@ extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* p
   c->pos = saved_pos;
   c->h_pinned[2] = saved_pos;
   CK(cudaMemcpyAsync(c->pos_dev, &c->h_pinned[2], 4, cudaMemcpyHostToDevice, c->stream));
-  CK(cudaMemcpyAsync(c->token_dev, c->token_dev + 2, 4, cudaMemcpyDeviceToDevice, c->stream));
+  CK(cudaMemcpyAsync(c->token_dev, c->token_dev + 2 * STEP_SEQ_MAX, 4, cudaMemcpyDeviceToDevice, c->stream));
   CK(cudaStreamSynchronize(c->stream));
   return r;
 }

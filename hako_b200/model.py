@@ -113,6 +113,18 @@ class HakmCtx:
                                 C.c_void_p(logits.ctypes.data) if want_logits else None, C.byref(am)), "prefill")
         return logits, int(am.value)
 
+    def prefill_batched(self, tokens, want_logits: bool = True, chunk_rows: int = 0):
+        """Feed a prompt with its positions batched through each layer
+        (hakmc_prefill_batched, chunks of chunk_rows positions; 0: default);
+        returns the last position's (logits or None, argmax)."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        logits = np.empty(self.vocab, np.float32) if want_logits else None
+        am = C.c_int(0)
+        check(lib.hakmc_prefill_batched(self._h, C.c_void_p(t.ctypes.data), len(t), int(chunk_rows),
+                                        C.c_void_p(logits.ctypes.data) if want_logits else None, C.byref(am)),
+              "prefill_batched")
+        return logits, int(am.value)
+
     def generate(self, prompt, n_gen: int) -> list[int]:
         """Greedy: feed the prompt one position at a time, then n_gen tokens."""
         p = np.ascontiguousarray(np.asarray(prompt, dtype=np.int32))

@@ -79,6 +79,21 @@ int hakmc_generate(hakmc_ctx *c, const int *prompt, int n_prompt, int n_gen,
  * Advances the position by n. 0 or a negative code. */
 int hakmc_prefill(hakmc_ctx *c, const int *tokens, int n, float *logits, int *argmax);
 
+/* Prompt processing with the positions batched: the same state and outputs
+ * as hakmc_prefill, but the n [host] ids go through each layer together in
+ * chunks of chunk_rows positions (<= 0: 1024), so every weight byte read
+ * serves a whole chunk: Q4_K matmuls on the tensor cores over each row's
+ * q8_32 codes, Q6_K matmuls as fp32 products of dequantized tiles, causal
+ * attention over the cache (which each chunk's own K/V rows enter first).
+ * Each position's arithmetic is the per-position arithmetic of
+ * hakm_forward (src/model.c:93-165); summation orders differ, so results
+ * agree with hakmc_prefill to fp32 rounding (and the int8 rounding flips
+ * it can move), not bit for bit. No counterpart in the reference, whose
+ * feed loop calls hakm_forward per id (cli/main.c:56-60). Under tensor
+ * parallelism this runs hakmc_prefill. 0 or a negative code. */
+int hakmc_prefill_batched(hakmc_ctx *c, const int *tokens, int n, int chunk_rows, float *logits,
+                          int *argmax);
+
 /* Continue the greedy stream of the current sequence for n_steps positions
  * without returning to the host between steps (the decode half of
  * cli/main.c:63-75): each step's input is the previous step's argmax. The
@@ -91,10 +106,11 @@ int hakmc_decode(hakmc_ctx *c, int n_steps, int *out_tokens);
  * using KV-cache slot i (slot 0 is also the single-sequence calls' cache;
  * their position and last pick are left as they were). The reference
  * decodes one sequence at a time; each row of this call equals hakm_forward
- * on a context holding that sequence's cache. Sequences 0 and 1 share one
- * step-kernel launch, each on half the SMs (one GPU, max_batch >= 2): their
- * rows agree with single-sequence runs to fp32 rounding (rel 1e-6); further
- * sequences run one launch each, bit for bit. argmax [host] gets n_seq ids;
+ * on a context holding that sequence's cache. Sequences 0..2 share one
+ * step-kernel launch, each on a third (two: half) of the SMs (one GPU,
+ * max_batch >= 2): their rows agree with single-sequence runs to fp32
+ * rounding (rel 1e-6); further sequences run one launch each, bit for bit.
+ * argmax [host] gets n_seq ids;
  * logits [host] (may be NULL) n_seq*vocab floats. 0, HAKMC_ERANGE for a
  * position beyond max_seq, or another negative code. */
 int hakmc_forward_batch(hakmc_ctx *c, const int *tokens, const int *pos,

@@ -225,6 +225,69 @@ def test_prefill_matches_per_token_feed(cuda, small_path):
     assert rel_l2(la, lr) < 2e-2
 
 
+def _margin_ok(logits, a, b):
+    """argmax a and b agree, or the top-two margin of `logits` is inside the
+    fp32 / int8-flip noise."""
+    top2 = np.sort(logits)[-2:]
+    return a == b or top2[1] - top2[0] <= GAP_TOL
+
+
+@pytest.mark.parametrize("preset,n,chunk", [("small", 40, 0), ("small", 40, 7), ("mid", 300, 128)])
+def test_prefill_batched_matches_per_position_prefill(cuda, reference, preset, n, chunk):
+    """hakmc_prefill_batched (positions batched through each layer: tensor-core
+    Q4_K matmuls, fp32 Q6_K tiles, causal attention over the cache) leaves the
+    state hakmc_prefill leaves, to fp32 rounding plus the int8 flips it can
+    move: the last logits, the KV cache (the next step's logits), the
+    position; and its logits match the reference's feed loop. Chunks of 7
+    rows cross chunk boundaries inside the prompt; the mid model has
+    head_dim 128 and a 300-position prompt (several attention tiles)."""
+    from oracle.oracle import RefModel
+    path = synth.cached_model(synth.PRESETS[preset])
+    prompt = [(37 * i + 11) % 4000 for i in range(n)]
+    with HakmCtx(path, max_seq=512) as a, HakmCtx(path, max_seq=512) as b:
+        la, ama = a.prefill_batched(prompt, chunk_rows=chunk)
+        lb, amb = b.prefill(prompt)
+        assert a.pos == b.pos == n
+        assert rel_l2(la, lb) < 2e-2
+        assert _margin_ok(lb, ama, amb), (ama, amb)
+        assert ama == int(np.argmax(la))
+        na, nma = a.forward(amb)
+        nb, nmb = b.forward(amb)
+        assert rel_l2(na, nb) < 2e-2
+        assert _margin_ok(nb, nma, nmb)
+    ref = RefModel(path, 512)
+    lr = None
+    for i, t in enumerate(prompt):
+        lr, _ = ref.forward(t, want_logits=i == n - 1)
+    ref.close()
+    assert rel_l2(la, lr) < 2e-2
+
+
+def test_prefill_batched_first_layer_is_fp32_close(cuda, small_path):
+    """With one layer, no int8 code can flip downstream of an attention
+    difference before the hidden state is read: the batched and per-position
+    residual streams of the last position agree to fp32 rounding (or to one
+    flip of the wo / ffn inputs, ~1e-3, in rare cases)."""
+    prompt = [(91 * i + 5) % 4000 for i in range(33)]
+    with HakmCtx(small_path, max_seq=64) as a, HakmCtx(small_path, max_seq=64) as b:
+        a.set_layers(1)
+        b.set_layers(1)
+        a.prefill_batched(prompt, chunk_rows=16)
+        b.prefill(prompt)
+        assert rel_l2(a.hidden(), b.hidden()) < 5e-3
+
+
+def test_prefill_batched_rejects_bad_input(cuda, small_path):
+    with HakmCtx(small_path, max_seq=8) as ctx:
+        with pytest.raises(HakmcError):
+            ctx.prefill_batched([1] * 9)
+        with pytest.raises(HakmcError):
+            ctx.prefill_batched([1, 10 ** 7])
+        assert ctx.pos == 0
+        ctx.prefill_batched([1, 2, 3])
+        assert ctx.pos == 3
+
+
 def test_prefill_rejects_bad_input(cuda, small_path):
     with HakmCtx(small_path, max_seq=8) as ctx:
         with pytest.raises(HakmcError):
@@ -236,35 +299,36 @@ def test_prefill_rejects_bad_input(cuda, small_path):
 
 def test_forward_batch_rows_equal_single_sequence_contexts(cuda, small_path):
     """hakmc_forward_batch: row i is hakm_forward on a context holding
-    sequence i's cache (slot i). Sequences 0 and 1 share one launch, each on
-    half the SMs: their logits agree with the single-sequence runs to fp32
-    rounding (rel-L2 <= 1e-6; the half-grid plan is not the same
-    computation bit for bit), and their picks agree unless the two best
-    logits are within that noise. Sequence 2 runs alone, on the whole grid:
-    bit for bit. Three sequences with different prompts, fed and then
-    decoded greedily in lockstep; sequence 2 starts two positions later."""
-    prompts = [[11, 22, 33, 44], [500, 600, 700, 800], [3000, 17, 42, 9]]
-    n_gen, start = 6, [0, 0, 2]
-    batch = HakmCtx(small_path, max_seq=64, max_batch=3)
+    sequence i's cache (slot i). Up to three sequences share one launch, each
+    on its share of the SMs: their logits agree with the single-sequence runs
+    to fp32 rounding (rel-L2 <= 1e-6; a smaller virtual grid's plan is not
+    the same computation bit for bit), and their picks agree unless the two
+    best logits are within that noise. The fourth and fifth sequences run
+    alone, on the whole grid: bit for bit. Five sequences with different
+    prompts, fed and then decoded greedily in lockstep; two of them start
+    later."""
+    prompts = [[11, 22, 33, 44], [500, 600, 700, 800], [3000, 17, 42, 9], [7, 8, 9, 10], [1234, 99, 5, 66]]
+    n_seq, n_gen, start = 5, 6, [0, 0, 2, 0, 1]
+    batch = HakmCtx(small_path, max_seq=64, max_batch=n_seq)
     singles = [HakmCtx(small_path, max_seq=64) for _ in prompts]
     try:
-        nxt = [None, None, None]
+        nxt = [None] * n_seq
         feed = [list(p) for p in prompts]
-        pos = [0, 0, 0]
+        pos = [0] * n_seq
         for rnd in range(len(prompts[0]) + n_gen + 2):
             toks, poss, rows = [], [], []
-            for i in range(3):
+            for i in range(n_seq):
                 active = rnd >= start[i] and pos[i] < len(prompts[i]) + n_gen
                 tok = (feed[i].pop(0) if feed[i] else nxt[i]) if active else 1
                 toks.append(tok)
                 poss.append(pos[i] if active else 63)  # idle rows write position 63 only
                 rows.append(active)
             logits, am = batch.forward_batch(toks, poss, want_logits=True)
-            for i in range(3):
+            for i in range(n_seq):
                 if not rows[i]:
                     continue
                 ref_logits, ref_am = singles[i].forward(toks[i])
-                if i >= 2:
+                if i >= 3:
                     assert np.array_equal(logits[i].view(np.uint32), ref_logits.view(np.uint32)), (rnd, i)
                     assert am[i] == ref_am
                 else:
