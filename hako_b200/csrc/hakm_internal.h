@@ -141,10 +141,16 @@ cudaError_t launch_rope(float* x, const float* rope_cs, const int* pos_dev, int 
 cudaError_t launch_pf_embed(float* x, const uint8_t* w, const int* tokens, int M, int D, cudaStream_t s);
 cudaError_t launch_pf_norm_quant(const float* x, const float* w, int M, int D, float eps, float* xn, int8_t* xq,
                                  float* xs, cudaStream_t s);
+// Q6_K x fp32 rows; short batches split K: the partials go to `part`
+// (pf_q6k_part_floats floats; null: no split) and, when accumulating, the
+// sum through `tmp` (M * n_out floats).
 cudaError_t launch_pf_q6k_gemm(float* out, const uint8_t* w, const float* x, const float* bias, int n_out, int K,
-                               int M, bool accumulate, cudaStream_t s);
+                               int M, bool accumulate, float* part, size_t part_floats, float* tmp, cudaStream_t s);
+size_t pf_q6k_part_floats(int n_out, int K, int M);
 cudaError_t launch_pf_rope_kv(const float* qk, const float* v, float* q, float* kc, float* vc, const float* rope_cs,
-                              int M, int pos0, int D, int KV, int hd, cudaStream_t s);
+                              int M, int pos0, const int* row_pos, size_t slot_stride, int D, int KV, int hd,
+                              cudaStream_t s);
+cudaError_t launch_pf_argmax(int* out, const float* logits, int M, int V, cudaStream_t s);
 cudaError_t launch_pf_attention(float* out, const float* q, const float* kc, const float* vc, int M, int pos0, int H,
                                 int KVH, int hd, float scale, cudaStream_t s);
 cudaError_t launch_pf_swiglu(float* h, const float* gu, int M, int F, cudaStream_t s);
@@ -165,6 +171,9 @@ struct AttnParams {
 };
 constexpr int ATTN_CHUNK = 32;   // positions per attention work item
 cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl);
+// One query row per sequence, n_rows sequences (grid z); see hakm_kernels.cu.
+cudaError_t launch_attention_rows(const AttnParams& a, const int* row_pos, int n_rows, size_t kv_stride,
+                                  size_t part_stride, cudaStream_t s);
 // hakmc_attention_noalloc: scratch in a static device array, no allocation
 cudaError_t attention_noalloc(float* out, const float* q, const float* kc, const float* vc, int pos, int n_heads,
                               int n_kv, int head_dim, cudaStream_t stream);
@@ -214,7 +223,13 @@ struct alignas(16) PhaseDesc {  // copied to shared memory as 16-byte words
 };
 
 constexpr int STEP_SEQ_MAX = 4;  // sequences one step-kernel launch can address
-constexpr int STEP_GROUP_MAX = 3;  // sequences forward_batch puts in one launch
+// Sequences forward_batch puts in one step-kernel launch. 1: multi-sequence
+// launches are off. With two or three sequences per launch (7B and 3B shapes)
+// a call now and then stopped with an illegal-instruction error after many
+// clean ones; a build whose step kernel checked every bulk copy (size,
+// alignment, slot bounds), its shared-memory carve and every partial-sum
+// range found nothing out of bounds, so the cause is not known.
+constexpr int STEP_GROUP_MAX = 1;
 
 struct StepArgs {
   const PhaseDesc* prog;   // device array, n_phases entries (one decode step)

@@ -14,6 +14,8 @@
 // summation orders differ (fp32 rounding, as between any two fp32 orders).
 #include "hakm_device.cuh"
 
+#include <algorithm>
+
 namespace hakm {
 
 namespace {
@@ -87,96 +89,209 @@ cudaError_t launch_pf_norm_quant(const float* x, const float* w, int M, int D, f
 // once. The dequantized weights (d * sc) * (q - 32) are exact in fp32 (an
 // 11-bit d times an 8-bit scale times a 6-bit code), so only the order of
 // the k sum differs from the reference's: here one fma chain per output in
-// k order. CTA tile 128 weight rows x 64 activation rows, k tiles of 32 (two
-// 16-element scale groups); thread tile 8 weight rows x 4 activation rows.
-constexpr int G6_BN = 128, G6_BM = 64, G6_BK = 32;
+// k order.
+// CTA tile 128 weight rows x BM activation rows (128, or 64 for short
+// batches), k tiles of 32 (two 16-element scale groups); thread tile 8 weight
+// rows x BM/16 activation rows, read as float4 pairs 64 apart (conflict-free
+// shared loads). Double-buffered: the next k tile's raw weight bytes and
+// activations are loaded into registers while the current one is
+// multiplied, then dequantized into the other buffer; one barrier per tile.
+constexpr int G6_BN = 128, G6_BK = 32;
 
-__global__ void __launch_bounds__(256) pf_q6k_gemm_kernel(float* __restrict__ out, const uint8_t* __restrict__ w,
+template <int BM>
+struct G6Tile {
+  float w[2][G6_BK][G6_BN];
+  float x[2][G6_BK][BM + 4];
+};
+
+template <int BM>
+__global__ void __launch_bounds__(256, BM == 128 ? 2 : 3) pf_q6k_gemm_kernel(float* __restrict__ out, const uint8_t* __restrict__ w,
                                                           const float* __restrict__ x, const float* __restrict__ bias,
-                                                          int n_out, int K, int M, int accumulate) {
-  __shared__ __align__(16) float Ws[G6_BK][G6_BN];
-  __shared__ __align__(16) float Xs[G6_BK][G6_BM + 4];
+                                                          int n_out, int K, int M, int accumulate, int kt_per) {
+  constexpr int TM = BM / 16;                // activation rows per thread
+  constexpr int XV = BM * G6_BK / 256 / 4;   // float4 activation loads per thread and tile
+  constexpr int XPR = G6_BK / (4 * XV);      // threads per activation row
+  extern __shared__ __align__(16) float g6_smem[];
+  G6Tile<BM>& S = *reinterpret_cast<G6Tile<BM>*>(g6_smem);
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-  const int n0 = blockIdx.x * G6_BN, m0 = blockIdx.y * G6_BM;
+  const int n0 = blockIdx.x * G6_BN, m0 = blockIdx.y * BM;
   const int nb = K / QK;
+  // this CTA's k tiles: [kt0, kt0 + nk) (split over grid z)
+  const int kt0 = blockIdx.z * kt_per, nk = min(K / G6_BK - kt0, kt_per);
   const size_t rowB = dev_row_bytes(W_Q6K, nb);
   // dequantization: weight row lr, 16 values at k0 + 16 * hf (one scale group)
   const int lr = tid >> 1, hf = tid & 1;
   const uint8_t* wrow = w + (size_t)min(n0 + lr, n_out - 1) * rowB;
-  // activations: row xm, 8 values at k0 + xk
-  const int xm = tid >> 2, xk = (tid & 3) * 8;
+  // activations: row xm, 4 * XV values at k0 + xk
+  const int xm = tid / XPR, xk = (tid % XPR) * 4 * XV;
   const float* xrow = x + (size_t)min(m0 + xm, M - 1) * K;
-  float acc[4][8];
+
+  uint4 rlo, rhi;
+  float rds;
+  float4 rx[XV];
+  auto load = [&](int k0) {
+    const int kk = k0 + 16 * hf;
+    const int b = kk / QK, i0 = kk % QK;
+    const int c = b >> 3, j = b & 7, m = q6_chunk_blocks(nb, c);
+    const uint8_t* chunk = wrow + (size_t)c * Q6K_CHUNK;
+    const uint8_t* body = chunk + j * Q6K_BODY;
+    const float d = half_bits_to_float((uint32_t)chunk[m * Q6K_BODY + 2 * j] |
+                                       ((uint32_t)chunk[m * Q6K_BODY + 2 * j + 1] << 8));
+    rds = __fmul_rn(d, (float)(int8_t)body[192 + (i0 >> 4)]);
+    const int nh = i0 >> 7, qd = (i0 >> 5) & 3, l0 = i0 & 31;
+    rlo = *reinterpret_cast<const uint4*>(body + 64 * nh + 32 * (qd & 1) + l0);
+    rhi = *reinterpret_cast<const uint4*>(body + 128 + 32 * nh + l0);
 #pragma unroll
-  for (int i = 0; i < 4; i++)
+    for (int v = 0; v < XV; v++) rx[v] = *reinterpret_cast<const float4*>(xrow + k0 + xk + 4 * v);
+  };
+  auto store = [&](int buf, int k0) {
+    const int qd = (((k0 + 16 * hf) % QK) >> 5) & 3;
+    const uint32_t lw[4] = {rlo.x, rlo.y, rlo.z, rlo.w}, hw[4] = {rhi.x, rhi.y, rhi.z, rhi.w};
+#pragma unroll
+    for (int e = 0; e < 16; e++) {
+      const uint32_t lb = (lw[e >> 2] >> (8 * (e & 3))) & 0xFFu, hb = (hw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+      const int nib = qd < 2 ? (int)(lb & 15u) : (int)(lb >> 4);
+      const int q = (nib | (int)(((hb >> (2 * qd)) & 3u) << 4)) - 32;
+      S.w[buf][16 * hf + e][lr] = __fmul_rn(rds, (float)q);
+    }
+#pragma unroll
+    for (int v = 0; v < XV; v++) {
+      S.x[buf][xk + 4 * v + 0][xm] = rx[v].x;
+      S.x[buf][xk + 4 * v + 1][xm] = rx[v].y;
+      S.x[buf][xk + 4 * v + 2][xm] = rx[v].z;
+      S.x[buf][xk + 4 * v + 3][xm] = rx[v].w;
+    }
+  };
+
+  float acc[TM][8];
+#pragma unroll
+  for (int i = 0; i < TM; i++)
 #pragma unroll
     for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
-
-  for (int k0 = 0; k0 < K; k0 += G6_BK) {
-    {
-      const int kk = k0 + 16 * hf;
-      const int b = kk / QK, i0 = kk % QK;
-      const int c = b >> 3, j = b & 7, m = q6_chunk_blocks(nb, c);
-      const uint8_t* chunk = wrow + (size_t)c * Q6K_CHUNK;
-      const uint8_t* body = chunk + j * Q6K_BODY;
-      const float d = half_bits_to_float((uint32_t)chunk[m * Q6K_BODY + 2 * j] |
-                                         ((uint32_t)chunk[m * Q6K_BODY + 2 * j + 1] << 8));
-      const float ds = __fmul_rn(d, (float)(int8_t)body[192 + (i0 >> 4)]);
-      const int nh = i0 >> 7, qd = (i0 >> 5) & 3, l0 = i0 & 31;
-      const uint4 lo = *reinterpret_cast<const uint4*>(body + 64 * nh + 32 * (qd & 1) + l0);
-      const uint4 hi = *reinterpret_cast<const uint4*>(body + 128 + 32 * nh + l0);
-      const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w}, hw[4] = {hi.x, hi.y, hi.z, hi.w};
-#pragma unroll
-      for (int e = 0; e < 16; e++) {
-        const uint32_t lb = (lw[e >> 2] >> (8 * (e & 3))) & 0xFFu, hb = (hw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
-        const int nib = qd < 2 ? (int)(lb & 15u) : (int)(lb >> 4);
-        const int q = (nib | (int)(((hb >> (2 * qd)) & 3u) << 4)) - 32;
-        Ws[16 * hf + e][lr] = __fmul_rn(ds, (float)q);
-      }
-    }
-    {
-      const float4 a = *reinterpret_cast<const float4*>(xrow + k0 + xk);
-      const float4 b = *reinterpret_cast<const float4*>(xrow + k0 + xk + 4);
-      Xs[xk + 0][xm] = a.x; Xs[xk + 1][xm] = a.y; Xs[xk + 2][xm] = a.z; Xs[xk + 3][xm] = a.w;
-      Xs[xk + 4][xm] = b.x; Xs[xk + 5][xm] = b.y; Xs[xk + 6][xm] = b.z; Xs[xk + 7][xm] = b.w;
-    }
-    __syncthreads();
-#pragma unroll 8
+  load(kt0 * G6_BK);
+  store(0, kt0 * G6_BK);
+  __syncthreads();
+  for (int t = 0; t < nk; t++) {
+    const int buf = t & 1;
+    if (t + 1 < nk) load((kt0 + t + 1) * G6_BK);
+#pragma unroll 4
     for (int kk = 0; kk < G6_BK; kk++) {
-      const float4 w0 = *reinterpret_cast<const float4*>(&Ws[kk][tx * 8]);
-      const float4 w1 = *reinterpret_cast<const float4*>(&Ws[kk][tx * 8 + 4]);
-      const float4 xv = *reinterpret_cast<const float4*>(&Xs[kk][ty * 4]);
+      const float4 w0 = *reinterpret_cast<const float4*>(&S.w[buf][kk][tx * 4]);
+      const float4 w1 = *reinterpret_cast<const float4*>(&S.w[buf][kk][64 + tx * 4]);
       const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-      const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+      float xa[TM];
 #pragma unroll
-      for (int i = 0; i < 4; i++)
+      for (int h = 0; h < TM / 4; h++) {
+        const float4 xv = *reinterpret_cast<const float4*>(&S.x[buf][kk][64 * h + ty * 4]);
+        xa[4 * h] = xv.x; xa[4 * h + 1] = xv.y; xa[4 * h + 2] = xv.z; xa[4 * h + 3] = xv.w;
+      }
+#pragma unroll
+      for (int i = 0; i < TM; i++)
 #pragma unroll
         for (int j = 0; j < 8; j++) acc[i][j] = __fmaf_rn(xa[i], wv[j], acc[i][j]);
     }
+    if (t + 1 < nk) store(buf ^ 1, (kt0 + t + 1) * G6_BK);
     __syncthreads();
   }
+  // a K split writes its partial sums to out[split][m][n] (added in order by
+  // the chunk-sum kernel)
+  const bool split = gridDim.z > 1;
+  if (split) out += (size_t)blockIdx.z * M * n_out;
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int m = m0 + ty * 4 + i;
+  for (int i = 0; i < TM; i++) {
+    const int m = m0 + 64 * (i >> 2) + ty * 4 + (i & 3);
     if (m >= M) continue;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
-      const int n = n0 + tx * 8 + j;
+      const int n = n0 + 64 * (j >> 2) + tx * 4 + (j & 3);
       if (n >= n_out) continue;
       float v = acc[i][j];
-      if (bias) v += bias[n];
       float* o = out + (size_t)m * n_out + n;
+      if (split) {
+        *o = v;
+        continue;
+      }
+      if (bias) v += bias[n];
       *o = accumulate ? *o + v : v;
     }
   }
 }
 
-cudaError_t launch_pf_q6k_gemm(float* out, const uint8_t* w, const float* x, const float* bias, int n_out, int K,
-                               int M, bool accumulate, cudaStream_t s) {
-  if (K % QK || n_out <= 0 || M <= 0) return cudaErrorInvalidValue;
-  const dim3 grid((n_out + G6_BN - 1) / G6_BN, (M + G6_BM - 1) / G6_BM);
-  pf_q6k_gemm_kernel<<<grid, 256, 0, s>>>(out, w, x, bias, n_out, K, M, accumulate ? 1 : 0);
+template <int BM>
+static cudaError_t launch_g6(dim3 grid, float* out, const uint8_t* w, const float* x, const float* bias, int n_out,
+                             int K, int M, bool accumulate, int kt_per, cudaStream_t s) {
+  static unsigned done = 0;  // attribute set, per device
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 32 && !(done & (1u << dev))) {
+    e = cudaFuncSetAttribute(pf_q6k_gemm_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(G6Tile<BM>));
+    if (e != cudaSuccess) return e;
+    done |= 1u << dev;
+  }
+  pf_q6k_gemm_kernel<BM><<<grid, 256, sizeof(G6Tile<BM>), s>>>(out, w, x, bias, n_out, K, M, accumulate ? 1 : 0,
+                                                               kt_per);
   return cudaGetLastError();
+}
+
+namespace {
+
+struct G6Plan {
+  int bm, tn, tm, split, kt_per;
+};
+
+// Tile height and K split: the height that wastes least of the last wave (2
+// CTAs of 128 or 3 of 64 per SM; a 64-row tile does ~15% less work per
+// instruction); when the tiles fill less than one wave (short batches), the
+// k tiles are split over CTAs (at least 8 per CTA).
+G6Plan g6_plan(int n_out, int K, int M, int sms) {
+  G6Plan p;
+  p.tn = (n_out + G6_BN - 1) / G6_BN;
+  const long t128 = (long)p.tn * ((M + 127) / 128), t64 = (long)p.tn * ((M + 63) / 64);
+  const double c128 = (double)((t128 + 2L * sms - 1) / (2L * sms)) * 128.0;
+  const double c64 = (double)((t64 + 3L * sms - 1) / (3L * sms)) * 64.0 * 1.15;
+  p.bm = (M > 64 && c128 <= c64) ? 128 : 64;
+  p.tm = (M + p.bm - 1) / p.bm;
+  const long tiles = (long)p.tn * p.tm, slots = (p.bm == 128 ? 2L : 3L) * sms;
+  const int nk = K / G6_BK;
+  int split = tiles < slots ? (int)std::min<long>(slots / tiles, nk / 8) : 1;
+  split = std::max(split, 1);
+  p.kt_per = (nk + split - 1) / split;
+  p.split = (nk + p.kt_per - 1) / p.kt_per;
+  return p;
+}
+
+int g6_sms() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+}  // namespace
+
+size_t pf_q6k_part_floats(int n_out, int K, int M) {
+  const G6Plan p = g6_plan(n_out, K, M, g6_sms());
+  return p.split > 1 ? (size_t)p.split * M * n_out : 0;
+}
+
+cudaError_t launch_pf_q6k_gemm(float* out, const uint8_t* w, const float* x, const float* bias, int n_out, int K,
+                               int M, bool accumulate, float* part, size_t part_floats, float* tmp, cudaStream_t s) {
+  if (K % QK || n_out <= 0 || M <= 0) return cudaErrorInvalidValue;
+  const int sms = g6_sms();
+  G6Plan p = g6_plan(n_out, K, M, sms);
+  if (p.split > 1 && (!part || part_floats < (size_t)p.split * M * n_out || (accumulate && !tmp))) {
+    p.split = 1;  // no room for the partials: one CTA per tile takes all of K
+    p.kt_per = K / G6_BK;
+  }
+  const dim3 grid((unsigned)p.tn, (unsigned)p.tm, (unsigned)p.split);
+  float* dst = p.split > 1 ? part : out;
+  cudaError_t e = p.bm == 128 ? launch_g6<128>(grid, dst, w, x, bias, n_out, K, M, accumulate, p.kt_per, s)
+                              : launch_g6<64>(grid, dst, w, x, bias, n_out, K, M, accumulate, p.kt_per, s);
+  if (e != cudaSuccess || p.split == 1) return e;
+  e = launch_chunk_sum(accumulate ? tmp : out, part, bias, n_out, M, p.split, sms, s);
+  if (e != cudaSuccess || !accumulate) return e;
+  return launch_pf_add(out, tmp, (size_t)M * n_out, s);
 }
 
 // ---------------------------------------------------------------- RoPE + KV
@@ -185,11 +300,19 @@ cudaError_t launch_pf_q6k_gemm(float* out, const uint8_t* w, const float* x, con
 // (within a head, rows 2i and 2i + 1 are the pair (i, i + hd/2) that NeoX
 // RoPE rotates, src/nn.c:32-42), bias already added; v: [M][KV]. Writes q
 // (rotated, natural order) to q[M][D] and k, v to the cache rows
-// pos0 + r (src/model.c:118-121).
+// pos0 + r (src/model.c:118-121). With row_pos (batched decode: row r is
+// sequence r) the position is row_pos[r] and the cache rows those of slot r,
+// slot_stride floats apart.
 __global__ void pf_rope_kv_kernel(const float* __restrict__ qk, const float* __restrict__ v, float* __restrict__ q,
                                   float* __restrict__ kc, float* __restrict__ vc, const float* __restrict__ rope_cs,
-                                  int pos0, int D, int KV, int hd) {
-  const int r = blockIdx.y, pos = pos0 + r, half = hd >> 1;
+                                  int pos0, const int* __restrict__ row_pos, size_t slot_stride, int D, int KV,
+                                  int hd) {
+  const int r = blockIdx.y, half = hd >> 1;
+  const int pos = row_pos ? row_pos[r] : pos0 + r;
+  if (row_pos) {
+    kc += (size_t)r * slot_stride;
+    vc += (size_t)r * slot_stride;
+  }
   const int n_pairs = (D + KV) >> 1;
   const float* row = qk + (size_t)r * (D + KV);
   for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n_pairs + KV; p += blockDim.x * gridDim.x) {
@@ -216,9 +339,39 @@ __global__ void pf_rope_kv_kernel(const float* __restrict__ qk, const float* __r
 }
 
 cudaError_t launch_pf_rope_kv(const float* qk, const float* v, float* q, float* kc, float* vc, const float* rope_cs,
-                              int M, int pos0, int D, int KV, int hd, cudaStream_t s) {
+                              int M, int pos0, const int* row_pos, size_t slot_stride, int D, int KV, int hd,
+                              cudaStream_t s) {
   const int n = (D + KV) / 2 + KV;
-  pf_rope_kv_kernel<<<dim3((n + 255) / 256, M), 256, 0, s>>>(qk, v, q, kc, vc, rope_cs, pos0, D, KV, hd);
+  pf_rope_kv_kernel<<<dim3((n + 255) / 256, M), 256, 0, s>>>(qk, v, q, kc, vc, rope_cs, pos0, row_pos, slot_stride, D,
+                                                             KV, hd);
+  return cudaGetLastError();
+}
+
+// out[r] = index of the largest of logits[r][0..V) (greedy sample_token,
+// src/sample.c:28-32: the first maximum wins). One CTA per row.
+__global__ void __launch_bounds__(256) pf_argmax_kernel(int* __restrict__ out, const float* __restrict__ logits, int V) {
+  __shared__ unsigned long long best[8];
+  const float* row = logits + (size_t)blockIdx.x * V;
+  unsigned long long k = 0ull;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const unsigned long long kk = argmax_key(row[i], i);
+    k = kk > k ? kk : k;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, o);
+    k = other > k ? other : k;
+  }
+  if ((threadIdx.x & 31) == 0) best[threadIdx.x >> 5] = k;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); w++) k = best[w] > k ? best[w] : k;
+    out[blockIdx.x] = argmax_key_index(k);
+  }
+}
+
+cudaError_t launch_pf_argmax(int* out, const float* logits, int M, int V, cudaStream_t s) {
+  pf_argmax_kernel<<<M, 256, 0, s>>>(out, logits, V);
   return cudaGetLastError();
 }
 

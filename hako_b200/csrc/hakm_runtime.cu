@@ -199,6 +199,9 @@ struct hakmc_ctx {
         *pf_gu = nullptr, *pf_h = nullptr, *pf_tmp = nullptr, *pf_xs = nullptr, *pf_part = nullptr;
   int8_t* pf_xq = nullptr;
   size_t pf_part_bytes = 0;
+  float* pf_part6 = nullptr;  // Q6_K K-split partials, pf_part6_floats
+  size_t pf_part6_floats = 0;
+  int* row_io = nullptr;  // batched decode: [max_batch] tokens, positions, picks
 };
 
 static int dalloc(hakmc_ctx* c, void** p, size_t n) {
@@ -1134,7 +1137,9 @@ static int pf_ensure(hakmc_ctx* c, int rows) {
 // through pf_tmp, then one add (the reference's order: product, then +=).
 static cudaError_t pf_matmul(hakmc_ctx* c, float* out, const DevMat& W, const float* xn, const int8_t* xq,
                              const float* xs, const float* bias, int M, bool accumulate) {
-  if (W.type == W_Q6K) return launch_pf_q6k_gemm(out, W.w, xn, bias, W.rows, W.cols, M, accumulate, c->stream);
+  if (W.type == W_Q6K)
+    return launch_pf_q6k_gemm(out, W.w, xn, bias, W.rows, W.cols, M, accumulate, c->pf_part6, c->pf_part6_floats,
+                              c->pf_tmp, c->stream);
   float* dst = accumulate ? c->pf_tmp : out;
   cudaError_t e = launch_q4k_mma(dst, W.w, xq, xs, bias, W.rows, W.cols, M, c->pf_part, c->err_flag, c->num_sms,
                                  c->stream);
@@ -1142,13 +1147,26 @@ static cudaError_t pf_matmul(hakmc_ctx* c, float* out, const DevMat& W, const fl
   return launch_pf_add(out, c->pf_tmp, (size_t)M * W.rows, c->stream);
 }
 
-// Tensor-core split partials for every Q4_K matmul of a chunk of M rows.
+// Split partials for every matmul of a chunk of M rows: tensor-core (Q4_K)
+// and fp32-tile (Q6_K) ones.
 static int pf_ensure_part(hakmc_ctx* c, int M) {
-  size_t need = 0;
+  size_t need = 0, need6 = 0;
+  auto add = [&](const DevMat& W) {
+    if (W.type == W_Q4K) need = std::max(need, q4k_mma_scratch_bytes(W.rows, W.cols, M, c->num_sms));
+    else need6 = std::max(need6, pf_q6k_part_floats(W.rows, W.cols, M));
+  };
   for (int l = 0; l < c->run_layers; l++) {
     const DevLayer& y = c->layers[l];
-    for (const DevMat* W : {&y.wqk, &y.wv, &y.wo, &y.wgu, &y.down})
-      if (W->type == W_Q4K) need = std::max(need, q4k_mma_scratch_bytes(W->rows, W->cols, M, c->num_sms));
+    for (const DevMat* W : {&y.wqk, &y.wv, &y.wo, &y.wgu, &y.down}) add(*W);
+  }
+  add(c->lm_head);
+  if (need6 > c->pf_part6_floats) {
+    dfree(c, c->pf_part6);
+    c->pf_part6 = nullptr;
+    c->pf_part6_floats = 0;
+    const int r = dalloc(c, (void**)&c->pf_part6, need6 * 4);
+    if (r) return r;
+    c->pf_part6_floats = need6;
   }
   if (need <= c->pf_part_bytes) return 0;
   dfree(c, c->pf_part);
@@ -1176,7 +1194,7 @@ static cudaError_t pf_chunk(hakmc_ctx* c, const int* tokens_dev, int M, int pos0
     if ((e = launch_pf_norm_quant(c->pf_x, y.attn_norm, M, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
     if ((e = pf_matmul(c, c->pf_qk, y.wqk, c->pf_xn, c->pf_xq, c->pf_xs, y.bqk, M, false))) break;
     if ((e = pf_matmul(c, c->pf_v, y.wv, c->pf_xn, c->pf_xq, c->pf_xs, y.bv, M, false))) break;
-    if ((e = launch_pf_rope_kv(c->pf_qk, c->pf_v, c->pf_q, kc, vc, c->rope_cs, M, pos0, D, KV, c->hd, s))) break;
+    if ((e = launch_pf_rope_kv(c->pf_qk, c->pf_v, c->pf_q, kc, vc, c->rope_cs, M, pos0, nullptr, 0, D, KV, c->hd, s))) break;
     if ((e = launch_pf_attention(c->pf_att, c->pf_q, kc, vc, M, pos0, c->H, c->KVH, c->hd, scale, s))) break;
     if (y.wo.type == W_Q4K && (e = launch_quantize_q8(c->pf_att, M * D, c->pf_xq, c->pf_xs, s))) break;
     if ((e = pf_matmul(c, c->pf_x, y.wo, c->pf_att, c->pf_xq, c->pf_xs, nullptr, M, true))) break;
@@ -1421,41 +1439,90 @@ extern "C" int hakmc_trace_step(hakmc_ctx* c, unsigned long long* stamps, int ma
   return c->num_sms;
 }
 
+// Batched decode: one pass of the layers in which row r is sequence r (input
+// tokens[r] at position pos[r], cache slot r), so every weight byte read
+// serves all n rows (the kernels of the batched prompt path; attention reads
+// each row's own slot up to its position). Then every row's final norm,
+// lm_head and greedy pick. Leaves the residual rows in xb[0..n), the logits
+// in logits[0..n).
+static int batch_decode(hakmc_ctx* c, const int* tokens, const int* pos, int n, float* logits, int* argmax) {
+  int r = pf_ensure(c, n);
+  if (!r) r = pf_ensure_part(c, n);
+  if (!r && !c->row_io) r = dalloc(c, (void**)&c->row_io, (size_t)3 * c->max_batch * 4);
+  if (r) return r;
+  const int D = c->D, KV = c->KV, F = c->F, B = c->max_batch;
+  int* tok_dev = c->row_io;
+  int* pos_dev = c->row_io + B;
+  int* pick_dev = c->row_io + 2 * B;
+  cudaStream_t s = c->stream;
+  CK(cudaMemcpyAsync(tok_dev, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(pos_dev, pos, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+  int max_pos = 0;
+  for (int i = 0; i < n; i++) max_pos = std::max(max_pos, pos[i]);
+  const size_t lstride = (size_t)c->max_seq * KV, slot = (size_t)c->L * lstride;
+  AttnParams at = {};
+  at.n_heads = c->H;
+  at.n_kv = c->KVH;
+  at.head_dim = c->hd;
+  at.scale = 1.0f / sqrtf((float)c->hd);
+  at.n_split = max_pos / ATTN_CHUNK + 1;
+  at.part = c->attn_part;
+  at.counters = c->attn_counters;
+  CK(cudaEventRecord(c->ev0, s));
+  cudaError_t e = launch_pf_embed(c->pf_x, c->tok_embd.w, tok_dev, n, D, s);
+  for (int l = 0; l < c->run_layers && e == cudaSuccess; l++) {
+    const DevLayer& y = c->layers[l];
+    float* kc = c->k_cache + (size_t)l * lstride;
+    float* vc = c->v_cache + (size_t)l * lstride;
+    if ((e = launch_pf_norm_quant(c->pf_x, y.attn_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
+    if ((e = pf_matmul(c, c->pf_qk, y.wqk, c->pf_xn, c->pf_xq, c->pf_xs, y.bqk, n, false))) break;
+    if ((e = pf_matmul(c, c->pf_v, y.wv, c->pf_xn, c->pf_xq, c->pf_xs, y.bv, n, false))) break;
+    if ((e = launch_pf_rope_kv(c->pf_qk, c->pf_v, c->pf_q, kc, vc, c->rope_cs, n, 0, pos_dev, slot, D, KV, c->hd, s)))
+      break;
+    at.q = c->pf_q;
+    at.k_cache = kc;
+    at.v_cache = vc;
+    at.out = c->pf_att;
+    if ((e = launch_attention_rows(at, pos_dev, n, slot, c->attn_part_floats, s))) break;
+    if (y.wo.type == W_Q4K && (e = launch_quantize_q8(c->pf_att, n * D, c->pf_xq, c->pf_xs, s))) break;
+    if ((e = pf_matmul(c, c->pf_x, y.wo, c->pf_att, c->pf_xq, c->pf_xs, nullptr, n, true))) break;
+    if ((e = launch_pf_norm_quant(c->pf_x, y.ffn_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
+    if ((e = pf_matmul(c, c->pf_gu, y.wgu, c->pf_xn, c->pf_xq, c->pf_xs, nullptr, n, false))) break;
+    if ((e = launch_pf_swiglu(c->pf_h, c->pf_gu, n, F, s))) break;
+    if (y.down.type == W_Q4K && (e = launch_quantize_q8(c->pf_h, n * F, c->pf_xq, c->pf_xs, s))) break;
+    e = pf_matmul(c, c->pf_x, y.down, c->pf_h, c->pf_xq, c->pf_xs, nullptr, n, true);
+  }
+  // final norm, lm_head, greedy pick per row (src/model.c:159-164, src/sample.c:28-32)
+  if (e == cudaSuccess) e = launch_pf_norm_quant(c->pf_x, c->out_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s);
+  if (e == cudaSuccess) e = pf_matmul(c, c->logits, c->lm_head, c->pf_xn, c->pf_xq, c->pf_xs, nullptr, n, false);
+  if (e == cudaSuccess) e = launch_pf_argmax(pick_dev, c->logits, n, c->V, s);
+  CK(e);
+  CK(cudaEventRecord(c->ev1, s));
+  CK(cudaMemcpyAsync(c->xb, c->pf_x, (size_t)n * D * 4, cudaMemcpyDeviceToDevice, s));
+  if (argmax) CK(cudaMemcpyAsync(argmax, pick_dev, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+  if (logits) CK(cudaMemcpyAsync(logits, c->logits, (size_t)n * c->V * 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  CK(cudaEventElapsedTime(&c->last_ms, c->ev0, c->ev1));
+  return check_flag(c);
+}
+
 extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* pos, int n_seq,
                                    float* logits, int* argmax) {
   if (!c || !tokens || !pos || n_seq <= 0 || n_seq > c->max_batch) { set_err("bad batch"); return HAKMC_EINVAL; }
-  if (!c->use_step) { set_err("forward_batch runs on the step kernel (HAKMC_STEP=0 is set)"); return HAKMC_EINVAL; }
   for (int i = 0; i < n_seq; i++) {
     if (tokens[i] < 0 || tokens[i] >= c->V) { set_err("token %d out of range", tokens[i]); return HAKMC_EINVAL; }
     if (pos[i] < 0 || pos[i] >= c->max_seq) { set_err("position %d beyond max_seq %d", pos[i], c->max_seq); return HAKMC_ERANGE; }
   }
   CK(cudaSetDevice(c->device));
+  // two or more sequences on one GPU: one batched pass (weights read once)
+  if (n_seq >= 2 && c->tp_world == 1) return batch_decode(c, tokens, pos, n_seq, logits, argmax);
+  if (!c->use_step) { set_err("forward_batch runs on the step kernel (HAKMC_STEP=0 is set)"); return HAKMC_EINVAL; }
   // sequence 0 is also the single-sequence API's: its position and last pick
   // (the input hakmc_decode continues from) are restored afterwards
   const int saved_pos = c->pos;
   CK(cudaMemcpyAsync(c->token_dev + 2 * STEP_SEQ_MAX, c->token_dev, 4, cudaMemcpyDeviceToDevice, c->stream));
   int r = 0;
-  int i = 0;
-  // the first sequences share one launch (one GPU, step kernel, cache slots
-  // 0..g-1): as many as the context and the shared-memory plan allow
-  // (at most STEP_GROUP_MAX: four sequences per launch on the 3B shapes, a
-  // virtual grid of 37 CTAs, stopped with an illegal-instruction error whose
-  // cause reading has not found; three and two run clean)
-  int g = c->tp_world == 1 ? std::min(std::min(n_seq, c->max_batch), STEP_GROUP_MAX) : 1;
-  while (g > 1 && ensure_program_n(c, g) != 0) g--;
-  if (g > 1) {
-    r = run_group(c, g, tokens, pos);
-    if (!r) {
-      CK(cudaMemcpyAsync(&c->h_pinned[12], c->token_dev, 4 * g, cudaMemcpyDeviceToHost, c->stream));
-      if (logits) CK(cudaMemcpyAsync(logits, c->logits, (size_t)g * c->V * 4, cudaMemcpyDeviceToHost, c->stream));
-      CK(cudaStreamSynchronize(c->stream));
-      r = check_flag(c);
-      if (!r && argmax)
-        for (int q = 0; q < g; q++) argmax[q] = c->h_pinned[12 + q];
-      i = g;
-    }
-  }
-  for (; i < n_seq && !r; i++) {
+  for (int i = 0; i < n_seq && !r; i++) {
     c->pos = pos[i];
     c->h_pinned[0] = tokens[i];
     CK(cudaMemcpyAsync(c->token_dev, &c->h_pinned[0], 4, cudaMemcpyHostToDevice, c->stream));
