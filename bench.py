@@ -320,13 +320,111 @@ def config_block(args, world):
             "l2": "weights stream from HBM every step (2.03 GB > 126 MB L2)"}
 
 
+def run_prefill(args):
+    """Config 4a: a seeded 2048-id prompt through hakmc_prefill_batched (each
+    call restarts the sequence, so every step is the whole prompt)."""
+    from hako_b200 import HakmCtx, synth
+    n = 2048
+    cfg = synth.PRESETS[args.model]
+    prompt = np.random.default_rng(41).integers(0, 151643, n).tolist()
+    ctx = HakmCtx(synth.cached_model(cfg), max_seq=n + 8)
+    for _ in range(args.warmup):
+        ctx.reset()
+        ctx.prefill_batched(prompt, want_logits=False)
+    dev = []
+    with ClockSampler(0) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            ctx.reset()
+            ctx.prefill_batched(prompt, want_logits=True)  # ids in, last logits out
+            dev.append(float(ctx.last_device_ms))
+        wall = time.perf_counter() - t0
+    # per-position prompt feed (the reference's loop, one launch) on a 256-id slice
+    ctx.reset()
+    ctx.prefill(prompt[:256], want_logits=False)
+    per_pos = 256 / (ctx.last_device_ms / 1e3)
+    ctx.close()
+    ms = sum(dev) / len(dev)
+    line = {"metric": "prefill tok/s (2048-id prompt)", "value": n / (ms / 1e3), "unit": "tok/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int4 (tensor cores), fp32 x int6, fp32 attention",
+            "data": "synthetic (seeded random-init weights, seeded prompt ids)",
+            "config": {"workload": f"config 4a: Qwen2 {args.model.upper()}-shaped, prefill of a 2048-id prompt "
+                                   "(positions batched through each layer, causal attention)",
+                       "model": f"qwen2-{args.model}-synthetic", "prompt_len": n, "chunk_rows": 1024},
+            "e2e": {"value": args.steps * n / wall, "unit": "tok/s", "h2d_bytes_per_step": 4 * n,
+                    "d2h_bytes_per_step": 4 * cfg.vocab},
+            "per_position_prefill_tok_s": per_pos, "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_batch(args):
+    """Config 4b: 64 independent sequences, each with a 4096-position KV cache
+    of seeded N(0, 1) values, decoded together (hakmc_forward_batch, one row
+    per sequence); a step = one new token for every sequence. N > 1: each GPU
+    runs its own 64 sequences (replicas, no collective on the data path)."""
+    import torch
+    world, rank, local, pg = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    from hako_b200 import HakmCtx, synth
+    n_seq, ctx_len = 64, 4096
+    cfg = synth.PRESETS[args.model]
+    ctx = HakmCtx(synth.cached_model(cfg), max_seq=ctx_len + args.warmup + args.steps + 1, max_batch=n_seq,
+                  device=local)
+    for i in range(n_seq):
+        ctx.fill_kv_normal(ctx_len, seq=i, seed=1000 * rank + i)
+    toks = np.random.default_rng(5 + rank).integers(0, 151643, n_seq).tolist()
+    pos = ctx_len
+    for _ in range(args.warmup):
+        _, am = ctx.forward_batch(toks, [pos] * n_seq)
+        toks = [int(a) for a in am]
+        pos += 1
+    barrier(pg, device)
+    dev = 0.0
+    with ClockSampler(local) as clk:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            _, am = ctx.forward_batch(toks, [pos] * n_seq)  # ids in, picks out
+            toks = [int(a) for a in am]
+            pos += 1
+            dev += float(ctx.last_device_ms)
+        barrier(pg, device)
+        wall = time.perf_counter() - t0
+    ctx.close()
+    max_ms = reduce_max(pg, dev, device)
+    e2e_s = reduce_max(pg, wall, device)
+    line = {"metric": "batched decode tok/s (64 sequences, 4096-position caches)",
+            "value": world * n_seq * args.steps / (max_ms / 1e3), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int4 (tensor cores), fp32 x int6, fp32 attention",
+            "data": "synthetic (seeded random-init weights, seeded N(0,1) K/V caches, seeded first ids)",
+            "config": {"workload": f"config 4b: Qwen2 {args.model.upper()}-shaped, {n_seq} sequences x "
+                                   f"{ctx_len}-position caches, one new token each per step",
+                       "model": f"qwen2-{args.model}-synthetic", "global_batch": world * n_seq,
+                       "seq_len": ctx_len, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "l2": f"K/V read per step {2 * cfg.n_layers * cfg.kv_dim * 4 * ctx_len * n_seq / 1e9:.1f} GB > L2"},
+            "e2e": {"value": world * n_seq * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8 * n_seq,
+                    "d2h_bytes_per_step": 4 * n_seq},
+            "clocks": clk.summary()}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        pg.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--model", default="3b", choices=["3b", "7b"])
+    ap.add_argument("--model", default=None, choices=["3b", "7b"],
+                    help="default: 3b for decode, 7b for the prefill and batch workloads")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "batch"],
+                    help="decode: batch-1 greedy decode (the headline); prefill: config 4a; batch: config 4b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv-sweep", action="store_true")
     ap.add_argument("--step-profile", action="store_true",
@@ -337,6 +435,12 @@ def main():
                          "(a small case for a profiler), print nothing else")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.model is None:
+        args.model = "3b" if args.workload == "decode" else "7b"
+    if args.impl == "ours" and args.workload == "prefill":
+        return run_prefill(args)
+    if args.impl == "ours" and args.workload == "batch":
+        return run_batch(args)
     if args.gemv_shape:
         return gemv_one(*(int(v) for v in args.gemv_shape.split("x")))
     if args.step_profile:

@@ -22,6 +22,7 @@ SIGNATURES = {
     "hakmc_free": (None, [_vp]),
     "hakmc_prefill": (_i, [_vp, _vp, _i, _vp, _vp]),
     "hakmc_prefill_batched": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
+    "hakmc_fill_kv_normal": (_i, [_vp, _i, _i, C.c_ulonglong]),
     "hakmc_tp_handle_bytes": (C.c_size_t, []),
     "hakmc_tp_export": (_i, [_vp, _vp]),
     "hakmc_tp_connect": (_i, [_vp, _i, _i, _vp]),

@@ -151,6 +151,7 @@ cudaError_t launch_pf_rope_kv(const float* qk, const float* v, float* q, float* 
                               int M, int pos0, const int* row_pos, size_t slot_stride, int D, int KV, int hd,
                               cudaStream_t s);
 cudaError_t launch_pf_argmax(int* out, const float* logits, int M, int V, cudaStream_t s);
+cudaError_t launch_pf_fill_normal(float* dst, size_t ystride, size_t n, int blocks_y, uint64_t seed, cudaStream_t s);
 cudaError_t launch_pf_attention(float* out, const float* q, const float* kc, const float* vc, int M, int pos0, int H,
                                 int KVH, int hd, float scale, cudaStream_t s);
 cudaError_t launch_pf_swiglu(float* h, const float* gu, int M, int F, cudaStream_t s);

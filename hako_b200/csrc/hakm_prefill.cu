@@ -90,7 +90,7 @@ cudaError_t launch_pf_norm_quant(const float* x, const float* w, int M, int D, f
 // 11-bit d times an 8-bit scale times a 6-bit code), so only the order of
 // the k sum differs from the reference's: here one fma chain per output in
 // k order.
-// CTA tile 128 weight rows x BM activation rows (128, or 64 for short
+// CTA tile 128 weight rows x BM activation rows (128, 64, or 16 for short
 // batches), k tiles of 32 (two 16-element scale groups); thread tile 8 weight
 // rows x BM/16 activation rows, read as float4 pairs 64 apart (conflict-free
 // shared loads). Double-buffered: the next k tile's raw weight bytes and
@@ -105,12 +105,12 @@ struct G6Tile {
 };
 
 template <int BM>
-__global__ void __launch_bounds__(256, BM == 128 ? 2 : 3) pf_q6k_gemm_kernel(float* __restrict__ out, const uint8_t* __restrict__ w,
+__global__ void __launch_bounds__(256, BM == 128 ? 2 : BM == 64 ? 3 : 4) pf_q6k_gemm_kernel(float* __restrict__ out, const uint8_t* __restrict__ w,
                                                           const float* __restrict__ x, const float* __restrict__ bias,
                                                           int n_out, int K, int M, int accumulate, int kt_per) {
-  constexpr int TM = BM / 16;                // activation rows per thread
-  constexpr int XV = BM * G6_BK / 256 / 4;   // float4 activation loads per thread and tile
-  constexpr int XPR = G6_BK / (4 * XV);      // threads per activation row
+  constexpr int TM = BM / 16;                // activation rows per thread (1, 4 or 8)
+  constexpr int XV = BM * G6_BK / 256 / 2;   // float2 activation loads per thread and tile
+  constexpr int XPR = G6_BK / (2 * XV);      // threads per activation row
   extern __shared__ __align__(16) float g6_smem[];
   G6Tile<BM>& S = *reinterpret_cast<G6Tile<BM>*>(g6_smem);
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -122,13 +122,13 @@ __global__ void __launch_bounds__(256, BM == 128 ? 2 : 3) pf_q6k_gemm_kernel(flo
   // dequantization: weight row lr, 16 values at k0 + 16 * hf (one scale group)
   const int lr = tid >> 1, hf = tid & 1;
   const uint8_t* wrow = w + (size_t)min(n0 + lr, n_out - 1) * rowB;
-  // activations: row xm, 4 * XV values at k0 + xk
-  const int xm = tid / XPR, xk = (tid % XPR) * 4 * XV;
+  // activations: row xm, 2 * XV values at k0 + xk
+  const int xm = tid / XPR, xk = (tid % XPR) * 2 * XV;
   const float* xrow = x + (size_t)min(m0 + xm, M - 1) * K;
 
   uint4 rlo, rhi;
   float rds;
-  float4 rx[XV];
+  float2 rx[XV];
   auto load = [&](int k0) {
     const int kk = k0 + 16 * hf;
     const int b = kk / QK, i0 = kk % QK;
@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(256, BM == 128 ? 2 : 3) pf_q6k_gemm_kernel(flo
     rlo = *reinterpret_cast<const uint4*>(body + 64 * nh + 32 * (qd & 1) + l0);
     rhi = *reinterpret_cast<const uint4*>(body + 128 + 32 * nh + l0);
 #pragma unroll
-    for (int v = 0; v < XV; v++) rx[v] = *reinterpret_cast<const float4*>(xrow + k0 + xk + 4 * v);
+    for (int v = 0; v < XV; v++) rx[v] = *reinterpret_cast<const float2*>(xrow + k0 + xk + 2 * v);
   };
   auto store = [&](int buf, int k0) {
     const int qd = (((k0 + 16 * hf) % QK) >> 5) & 3;
@@ -156,10 +156,8 @@ __global__ void __launch_bounds__(256, BM == 128 ? 2 : 3) pf_q6k_gemm_kernel(flo
     }
 #pragma unroll
     for (int v = 0; v < XV; v++) {
-      S.x[buf][xk + 4 * v + 0][xm] = rx[v].x;
-      S.x[buf][xk + 4 * v + 1][xm] = rx[v].y;
-      S.x[buf][xk + 4 * v + 2][xm] = rx[v].z;
-      S.x[buf][xk + 4 * v + 3][xm] = rx[v].w;
+      S.x[buf][xk + 2 * v + 0][xm] = rx[v].x;
+      S.x[buf][xk + 2 * v + 1][xm] = rx[v].y;
     }
   };
 
@@ -180,6 +178,7 @@ __global__ void __launch_bounds__(256, BM == 128 ? 2 : 3) pf_q6k_gemm_kernel(flo
       const float4 w1 = *reinterpret_cast<const float4*>(&S.w[buf][kk][64 + tx * 4]);
       const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
       float xa[TM];
+      if constexpr (TM == 1) xa[0] = S.x[buf][kk][ty];
 #pragma unroll
       for (int h = 0; h < TM / 4; h++) {
         const float4 xv = *reinterpret_cast<const float4*>(&S.x[buf][kk][64 * h + ty * 4]);
@@ -199,7 +198,7 @@ __global__ void __launch_bounds__(256, BM == 128 ? 2 : 3) pf_q6k_gemm_kernel(flo
   if (split) out += (size_t)blockIdx.z * M * n_out;
 #pragma unroll
   for (int i = 0; i < TM; i++) {
-    const int m = m0 + 64 * (i >> 2) + ty * 4 + (i & 3);
+    const int m = TM == 1 ? m0 + ty : m0 + 64 * (i >> 2) + ty * 4 + (i & 3);
     if (m >= M) continue;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
@@ -251,9 +250,9 @@ G6Plan g6_plan(int n_out, int K, int M, int sms) {
   const long t128 = (long)p.tn * ((M + 127) / 128), t64 = (long)p.tn * ((M + 63) / 64);
   const double c128 = (double)((t128 + 2L * sms - 1) / (2L * sms)) * 128.0;
   const double c64 = (double)((t64 + 3L * sms - 1) / (3L * sms)) * 64.0 * 1.15;
-  p.bm = (M > 64 && c128 <= c64) ? 128 : 64;
+  p.bm = M <= 16 ? 16 : (M > 64 && c128 <= c64) ? 128 : 64;
   p.tm = (M + p.bm - 1) / p.bm;
-  const long tiles = (long)p.tn * p.tm, slots = (p.bm == 128 ? 2L : 3L) * sms;
+  const long tiles = (long)p.tn * p.tm, slots = (p.bm == 128 ? 2L : p.bm == 64 ? 3L : 4L) * sms;
   const int nk = K / G6_BK;
   int split = tiles < slots ? (int)std::min<long>(slots / tiles, nk / 8) : 1;
   split = std::max(split, 1);
@@ -286,8 +285,9 @@ cudaError_t launch_pf_q6k_gemm(float* out, const uint8_t* w, const float* x, con
   }
   const dim3 grid((unsigned)p.tn, (unsigned)p.tm, (unsigned)p.split);
   float* dst = p.split > 1 ? part : out;
-  cudaError_t e = p.bm == 128 ? launch_g6<128>(grid, dst, w, x, bias, n_out, K, M, accumulate, p.kt_per, s)
-                              : launch_g6<64>(grid, dst, w, x, bias, n_out, K, M, accumulate, p.kt_per, s);
+  cudaError_t e = p.bm == 128  ? launch_g6<128>(grid, dst, w, x, bias, n_out, K, M, accumulate, p.kt_per, s)
+                  : p.bm == 64 ? launch_g6<64>(grid, dst, w, x, bias, n_out, K, M, accumulate, p.kt_per, s)
+                               : launch_g6<16>(grid, dst, w, x, bias, n_out, K, M, accumulate, p.kt_per, s);
   if (e != cudaSuccess || p.split == 1) return e;
   e = launch_chunk_sum(accumulate ? tmp : out, part, bias, n_out, M, p.split, sms, s);
   if (e != cudaSuccess || !accumulate) return e;
@@ -544,6 +544,33 @@ __global__ void pf_add_kernel(float* __restrict__ x, const float* __restrict__ o
 
 cudaError_t launch_pf_add(float* x, const float* o, size_t n, cudaStream_t s) {
   pf_add_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 148 * 16), 256, 0, s>>>(x, o, n);
+  return cudaGetLastError();
+}
+
+// Seeded N(0, 1) fp32 values (a measurement workload's synthetic KV cache):
+// element i of block y gets a Box-Muller value from two uniforms taken from a
+// splitmix64 hash of (seed, y, i). dst + y * ystride, n per block.
+__device__ __forceinline__ uint64_t pf_mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void pf_fill_normal_kernel(float* dst, size_t ystride, size_t n, uint64_t seed) {
+  float* d = dst + blockIdx.y * ystride;
+  const uint64_t base = pf_mix64(seed ^ ((uint64_t)blockIdx.y << 40));
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)blockDim.x * gridDim.x) {
+    const uint64_t h = pf_mix64(base + i);
+    const float u1 = ((float)(uint32_t)(h >> 40) + 1.0f) * (1.0f / 16777217.0f);  // (0, 1]
+    const float u2 = (float)(uint32_t)(h & 0xFFFFFFu) * (1.0f / 16777216.0f);      // [0, 1)
+    d[i] = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+  }
+}
+
+cudaError_t launch_pf_fill_normal(float* dst, size_t ystride, size_t n, int blocks_y, uint64_t seed, cudaStream_t s) {
+  const unsigned gx = (unsigned)std::min<size_t>((n + 255) / 256, 4096);
+  pf_fill_normal_kernel<<<dim3(gx, blocks_y), 256, 0, s>>>(dst, ystride, n, seed);
   return cudaGetLastError();
 }
 

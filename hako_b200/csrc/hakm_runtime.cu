@@ -1584,6 +1584,22 @@ extern "C" int hakmc_fill_kv(hakmc_ctx* c, int seq, const float* k, const float*
   return 0;
 }
 
+extern "C" int hakmc_fill_kv_normal(hakmc_ctx* c, int seq, int n_pos, unsigned long long seed) {
+  if (!c || seq < 0 || seq >= c->max_batch || n_pos < 0 || n_pos > c->max_seq) {
+    set_err("bad fill_kv_normal arguments");
+    return HAKMC_EINVAL;
+  }
+  CK(cudaSetDevice(c->device));
+  const size_t lstride = (size_t)c->max_seq * c->KV, off = (size_t)seq * c->L * lstride;
+  if (n_pos > 0) {
+    CK(launch_pf_fill_normal(c->k_cache + off, lstride, (size_t)n_pos * c->KV, c->L, seed * 2 + 1, c->stream));
+    CK(launch_pf_fill_normal(c->v_cache + off, lstride, (size_t)n_pos * c->KV, c->L, seed * 2 + 2, c->stream));
+  }
+  CK(cudaStreamSynchronize(c->stream));
+  if (seq == 0) return hakmc_set_pos(c, n_pos);
+  return 0;
+}
+
 // ------------------------------------------------------------ kernel-level API
 
 namespace {

@@ -148,6 +148,10 @@ class HakmCtx:
         check(lib.hakmc_fill_kv(self._h, seq, C.c_void_p(k.ctypes.data), C.c_void_p(v.ctypes.data),
                                 n_pos), "fill_kv")
 
+    def fill_kv_normal(self, n_pos: int, seq: int = 0, seed: int = 0):
+        """Seeded N(0, 1) K/V for positions [0, n_pos) of slot `seq`, on the device."""
+        check(lib.hakmc_fill_kv_normal(self._h, seq, n_pos, seed), "fill_kv_normal")
+
     def forward_batch(self, tokens, pos, want_logits: bool = False):
         t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
         p = np.ascontiguousarray(np.asarray(pos, dtype=np.int32))

@@ -105,12 +105,14 @@ int hakmc_decode(hakmc_ctx *c, int n_steps, int *out_tokens);
  * max_batch), sequence i at position pos[i] with input tokens[i] ([host]),
  * using KV-cache slot i (slot 0 is also the single-sequence calls' cache;
  * their position and last pick are left as they were). The reference
- * decodes one sequence at a time; each row of this call equals hakm_forward
- * on a context holding that sequence's cache. Sequences 0..2 share one
- * step-kernel launch, each on a third (two: half) of the SMs (one GPU,
- * max_batch >= 2): their rows agree with single-sequence runs to fp32
- * rounding (rel 1e-6); further sequences run one launch each, bit for bit.
- * argmax [host] gets n_seq ids;
+ * decodes one sequence at a time; each row of this call is hakm_forward on
+ * a context holding that sequence's cache. Two or more sequences on one GPU
+ * go through each layer together as the rows of one pass (the kernels of
+ * hakmc_prefill_batched; attention reads each row's own cache slot up to its
+ * position), so each weight byte is read once per call: rows agree with
+ * single-sequence runs to fp32 rounding plus the int8 flips it can move. One
+ * sequence (or tensor parallelism) runs the step kernel per sequence, bit
+ * for bit. argmax [host] gets n_seq ids;
  * logits [host] (may be NULL) n_seq*vocab floats. 0, HAKMC_ERANGE for a
  * position beyond max_seq, or another negative code. */
 int hakmc_forward_batch(hakmc_ctx *c, const int *tokens, const int *pos,
@@ -154,6 +156,12 @@ int hakmc_debug_read(hakmc_ctx *c, int which, float *out);
  * and set that sequence's position to n_pos. Mirrors pre-filling
  * hakm_ctx.k_cache / v_cache / pos (src/model.h:20-21). */
 int hakmc_fill_kv(hakmc_ctx *c, int seq, const float *k, const float *v, int n_pos);
+
+/* Fill the KV cache of sequence `seq` for positions [0, n_pos) of every
+ * layer with seeded N(0, 1) fp32 values on the device (the synthetic cache
+ * of a long-context measurement workload), and for seq 0 set the position
+ * to n_pos. Measurement hook; no counterpart in the reference. */
+int hakmc_fill_kv_normal(hakmc_ctx *c, int seq, int n_pos, unsigned long long seed);
 
 /* Average device time in ms of one launch of decode-step phase `phase`
  * (0 qkv, 1 attention, 2 attn-output, 3 ffn gate/up, 4 ffn down, 5 lm_head),
