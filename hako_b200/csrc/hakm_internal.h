@@ -223,14 +223,6 @@ struct alignas(16) PhaseDesc {  // copied to shared memory as 16-byte words
   int epi_rec_off;
 };
 
-constexpr int STEP_SEQ_MAX = 4;  // sequences one step-kernel launch can address
-// Sequences forward_batch puts in one step-kernel launch. 1: multi-sequence
-// launches are off. With two or three sequences per launch (7B and 3B shapes)
-// a call now and then stopped with an illegal-instruction error after many
-// clean ones; a build whose step kernel checked every bulk copy (size,
-// alignment, slot bounds), its shared-memory carve and every partial-sum
-// range found nothing out of bounds, so the cause is not known.
-constexpr int STEP_GROUP_MAX = 1;
 
 struct StepArgs {
   const PhaseDesc* prog;   // device array, n_phases entries (one decode step)
@@ -242,13 +234,6 @@ struct StepArgs {
   int* token_dev;          // in: input of step 0 when n_forced == 0; out: last pick
   int* pos_dev;            // out: pos0 + n_steps
   long long kv_off;        // elements from the K/V cache pointers to this launch's sequence
-  // several sequences per launch (n_seq > 1, one GPU): sequence h runs on
-  // CTAs [h * grid / n_seq, (h + 1) * grid / n_seq) with program
-  // prog + h * n_phases, exchange words xb_ll + h * ll_stride, counters
-  // bar + 8h, keys + 4h, token_dev[h], pos_dev[h], forced + h * n_forced
-  int n_seq;
-  int seq_pos0[STEP_SEQ_MAX];
-  long long ll_stride;
   int* token_log;          // pick of step j at token_log[j - log_base] (may be null)
   int token_log_cap;
   int log_base;

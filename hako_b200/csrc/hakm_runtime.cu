@@ -121,6 +121,12 @@ size_t row_bytes(uint32_t type, int n_in) {
 
 // ------------------------------------------------------------ context
 
+// token_dev word where forward_batch keeps the single-sequence API's last
+// pick while it runs other sequences through the step kernel
+constexpr int TOKEN_SAVE = 8;
+// forward_batch: batches of at least this many sequences take the batched pass
+constexpr int BATCH_ROWS_MIN = 8;
+
 struct DevMat {         // one weight matrix on the device (layout: hakm_internal.h)
   int type = 0, rows = 0, cols = 0;
   uint8_t* w = nullptr;
@@ -165,15 +171,6 @@ struct hakmc_ctx {
   SegRange* ranges_dev = nullptr;  // [phase][cta][segment] rows of the step program
   size_t ranges_cap = 0;
   StepArgs step = {};
-  // forward_batch: n (2..STEP_SEQ_MAX) sequences per launch, each on 1/n of
-  // the SMs with its own program (exchange vectors, cache slot, logits,
-  // counters); indexed by n
-  PhaseDesc* progn_dev[STEP_SEQ_MAX + 1] = {};
-  int progn_cap[STEP_SEQ_MAX + 1] = {}, progn_layers[STEP_SEQ_MAX + 1] = {-1, -1, -1, -1, -1};
-  SegRange* rangesn_dev[STEP_SEQ_MAX + 1] = {};
-  size_t rangesn_cap[STEP_SEQ_MAX + 1] = {};
-  StepArgs stepn[STEP_SEQ_MAX + 1] = {};
-  int* seq_tokens_dev = nullptr;  // input tokens of a multi-sequence launch
   size_t attn_part_floats = 0;    // attention scratch of one sequence
   unsigned int* step_bar = nullptr;
   unsigned int* step_tickets = nullptr;
@@ -575,105 +572,8 @@ static int ensure_program(hakmc_ctx* c) {
   a.n_layers = c->run_layers;
   a.skip_last = 1;  // the program ends with lm_head
   a.head_dim = c->hd;
-  a.n_seq = 1;
   c->step = a;
   c->prog_layers = c->run_layers;
-  return 0;
-}
-
-// The programs of sequences 0..n-1 for an n-sequence launch: each runs on
-// 1/n of the SMs (the shared-memory plan and row table are those of that
-// virtual grid), with its own exchange vectors, cache slot, logits and
-// counters. HAKMC_EINVAL when the shapes do not fit that grid's plan.
-static int ensure_program_n(hakmc_ctx* c, int n) {
-  if (c->progn_layers[n] == c->run_layers) return 0;
-  const int vgrid = c->num_sms / n;
-  std::vector<PhaseDesc> all, pr;
-  StepArgs a = {};
-  for (int q = 0; q < n; q++) {
-    build_program(c, q, pr);
-    StepArgs aq = {};
-    if (!plan_step(pr.data(), (int)pr.size(), vgrid, aq)) {
-      set_err("step kernel: shapes do not fit its shared-memory plan at %d CTAs", vgrid);
-      return HAKMC_EINVAL;
-    }
-    if (q == 0) a = aq;
-    all.insert(all.end(), pr.begin(), pr.end());
-  }
-  const int n_phases = (int)pr.size();
-  if ((int)all.size() > c->progn_cap[n]) {
-    void* p = nullptr;
-    const int r = dalloc(c, &p, all.size() * sizeof(PhaseDesc));
-    if (r) return r;
-    c->progn_dev[n] = (PhaseDesc*)p;
-    c->progn_cap[n] = (int)all.size();
-  }
-  CK(cudaMemcpy(c->progn_dev[n], all.data(), all.size() * sizeof(PhaseDesc), cudaMemcpyHostToDevice));
-  {
-    std::vector<SegRange> tab((size_t)n_phases * vgrid * MAX_SEGS);
-    step_ranges(all.data(), n_phases, vgrid, 0, vgrid, tab.data());
-    if (tab.size() > c->rangesn_cap[n]) {
-      void* p = nullptr;
-      const int r = dalloc(c, &p, tab.size() * sizeof(SegRange));
-      if (r) return r;
-      c->rangesn_dev[n] = (SegRange*)p;
-      c->rangesn_cap[n] = tab.size();
-    }
-    CK(cudaMemcpy(c->rangesn_dev[n], tab.data(), tab.size() * sizeof(SegRange), cudaMemcpyHostToDevice));
-  }
-  a.prog = c->progn_dev[n];
-  a.ranges = c->rangesn_dev[n];
-  a.n_phases = n_phases;
-  a.token_dev = c->token_dev;  // [sequence]
-  a.pos_dev = c->pos_dev;      // [sequence]
-  a.token_log = nullptr;
-  a.keys = c->step_keys;
-  a.bar = c->step_bar;
-  a.tickets = c->step_tickets;
-  a.err_flag = c->err_flag;
-  a.tok_embd = c->tok_embd.w;
-  a.xb_ll = c->xb_ll;
-  a.ll_stride = (long long)c->ll_words;
-  a.xb_plain = c->xb;
-  a.D = c->D;
-  a.n_layers = c->run_layers;
-  a.skip_last = 1;
-  a.head_dim = c->hd;
-  a.n_seq = n;
-  c->stepn[n] = a;
-  c->progn_layers[n] = c->run_layers;
-  return 0;
-}
-
-// One decode step of sequences 0..n-1 (cache slots 0..n-1) at positions
-// pos[i] with input tokens tokens[i], in one launch; the picks land in
-// token_dev[0..n-1], the logits in logits + i * vocab.
-static int run_group(hakmc_ctx* c, int n, const int* tokens, const int* pos) {
-  int r = ensure_program_n(c, n);
-  if (r) return r;
-  StepArgs a = c->stepn[n];
-  a.n_steps = 1;
-  a.n_forced = 1;
-  a.forced = c->seq_tokens_dev;
-  for (int q = 0; q < n; q++) a.seq_pos0[q] = pos[q];
-  a.pos0 = pos[0];
-  a.log_base = 0;
-  const uint64_t span = (uint64_t)(a.n_phases + 1);
-  if ((uint64_t)c->tag_base + span >= 0xFFFFFFF0ull) {
-    CK(cudaMemsetAsync(c->xb_ll, 0, c->ll_words * 8 * STEP_SEQ_MAX, c->stream));
-    c->tag_base = 1;
-  }
-  a.tp_rank = 0;
-  a.tp_world = 1;
-  a.tag_base = c->tag_base;
-  c->tag_base += (uint32_t)span;
-  for (int q = 0; q < n; q++) c->h_pinned[8 + q] = tokens[q];
-  CK(cudaMemcpyAsync(c->seq_tokens_dev, &c->h_pinned[8], 4 * n, cudaMemcpyHostToDevice, c->stream));
-  CK(cudaMemsetAsync(c->step_bar, 0, 32 * STEP_SEQ_MAX, c->stream));
-  CK(cudaMemsetAsync(c->step_tickets, 0, 64 * 4 * STEP_SEQ_MAX, c->stream));
-  CK(cudaMemsetAsync(c->step_keys, 0, 32 * STEP_SEQ_MAX, c->stream));
-  CK(launch_step(a, n * (c->num_sms / n), c->stream));
-  c->step_ran = true;
   return 0;
 }
 
@@ -702,7 +602,7 @@ static int run_steps(hakmc_ctx* c, int n_steps, int n_forced, const int* forced_
     // peers write into these words without a host round trip: clearing them
     // under tensor parallelism could erase a peer's early write
     if (c->tp_world > 1) { set_err("tag space of the tensor-parallel group used up: recreate the contexts"); return HAKMC_ERANGE; }
-    CK(cudaMemsetAsync(c->xb_ll, 0, c->ll_words * 8 * STEP_SEQ_MAX, c->stream));
+    CK(cudaMemsetAsync(c->xb_ll, 0, c->ll_words * 8, c->stream));
     c->tag_base = 1;
   }
   a.tp_rank = c->tp_rank;
@@ -876,11 +776,11 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
     return HAKMC_EINVAL;
   }
   c->attn_part_floats = attention_scratch_floats(c->KVH, max_split, c->H / c->KVH, c->hd);
-  if ((r = dalloc(c, (void**)&c->attn_part, c->attn_part_floats * 4 * std::max(B, STEP_SEQ_MAX)))) return r;
+  if ((r = dalloc(c, (void**)&c->attn_part, c->attn_part_floats * 4 * B))) return r;
   if ((r = dalloc(c, (void**)&c->attn_counters, 64 * 4 * B))) return r;
   CK(cudaMemset(c->attn_counters, 0, 64 * 4 * B));
-  // [sequence] plus a save slot (forward_batch) past the STEP_SEQ_MAX sequences
-  if ((r = dalloc(c, (void**)&c->token_dev, 4 * std::max(4 * B, 2 * STEP_SEQ_MAX + 1)))) return r;
+  // [sequence] plus a save slot (forward_batch, TOKEN_SAVE)
+  if ((r = dalloc(c, (void**)&c->token_dev, 4 * std::max(4 * B, TOKEN_SAVE + 1)))) return r;
   if ((r = dalloc(c, (void**)&c->pos_dev, 16 * B))) return r;
   if ((r = dalloc(c, (void**)&c->step_dev, 16))) return r;
   c->token_log_cap = c->max_seq + 8;
@@ -888,24 +788,21 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
   if ((r = dalloc(c, (void**)&c->argmax_key, 8 * B))) return r;
   if ((r = dalloc(c, (void**)&c->done_counter, 4 * B))) return r;
   if ((r = dalloc(c, (void**)&c->err_flag, 16))) return r;
-  // per sequence of a launch: bar 8 words, keys 4, tickets 64 (the kernel's strides)
-  if ((r = dalloc(c, (void**)&c->step_bar, 32 * STEP_SEQ_MAX))) return r;
-  if ((r = dalloc(c, (void**)&c->step_keys, 32 * STEP_SEQ_MAX))) return r;
-  if ((r = dalloc(c, (void**)&c->step_tickets, 64 * 4 * STEP_SEQ_MAX))) return r;
-  if ((r = dalloc(c, (void**)&c->seq_tokens_dev, 4 * STEP_SEQ_MAX))) return r;
+  if ((r = dalloc(c, (void**)&c->step_bar, 32))) return r;
+  if ((r = dalloc(c, (void**)&c->step_keys, 32))) return r;
+  if ((r = dalloc(c, (void**)&c->step_tickets, 64 * 4))) return r;
   if ((r = dalloc(c, (void**)&c->step_xbar, 16))) return r;
   CK(cudaMemset(c->step_xbar, 0, 16));
-  CK(cudaMemset(c->step_bar, 0, 32 * STEP_SEQ_MAX));
-  CK(cudaMemset(c->step_keys, 0, 32 * STEP_SEQ_MAX));
-  CK(cudaMemset(c->step_tickets, 0, 64 * 4 * STEP_SEQ_MAX));
+  CK(cudaMemset(c->step_bar, 0, 32));
+  CK(cudaMemset(c->step_keys, 0, 32));
+  CK(cudaMemset(c->step_tickets, 0, 64 * 4));
   {
     // exchange vectors, 16-byte aligned pieces of one allocation
     auto up2 = [](size_t n) { return (n + 1) & ~(size_t)1; };
     const size_t nD = up2(c->D), nKV = up2(c->KV), nF = up2(c->F);
     c->ll_words = 2 * nD + nD + 2 * nKV + nD + nF;
-    // one copy per sequence of a multi-sequence launch, ll_words apart
-    if ((r = dalloc(c, (void**)&c->xb_ll, c->ll_words * 8 * STEP_SEQ_MAX))) return r;
-    CK(cudaMemset(c->xb_ll, 0, c->ll_words * 8 * STEP_SEQ_MAX));
+    if ((r = dalloc(c, (void**)&c->xb_ll, c->ll_words * 8))) return r;
+    CK(cudaMemset(c->xb_ll, 0, c->ll_words * 8));
     c->q_ll = c->xb_ll + 2 * nD;
     c->k_ll = c->q_ll + nD;
     c->v_ll = c->k_ll + nKV;
@@ -1514,13 +1411,16 @@ extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* p
     if (pos[i] < 0 || pos[i] >= c->max_seq) { set_err("position %d beyond max_seq %d", pos[i], c->max_seq); return HAKMC_ERANGE; }
   }
   CK(cudaSetDevice(c->device));
-  // two or more sequences on one GPU: one batched pass (weights read once)
-  if (n_seq >= 2 && c->tp_world == 1) return batch_decode(c, tokens, pos, n_seq, logits, argmax);
+  // BATCH_ROWS_MIN or more sequences on one GPU: one batched pass (weights
+  // read once). Fewer run the step kernel per sequence: the batched pass
+  // costs ~8 ms on the 3B shapes whatever the batch up to 16 (about 470
+  // launches of short kernels), the step kernel 1.4 ms per sequence.
+  if (n_seq >= BATCH_ROWS_MIN && c->tp_world == 1) return batch_decode(c, tokens, pos, n_seq, logits, argmax);
   if (!c->use_step) { set_err("forward_batch runs on the step kernel (HAKMC_STEP=0 is set)"); return HAKMC_EINVAL; }
   // sequence 0 is also the single-sequence API's: its position and last pick
   // (the input hakmc_decode continues from) are restored afterwards
   const int saved_pos = c->pos;
-  CK(cudaMemcpyAsync(c->token_dev + 2 * STEP_SEQ_MAX, c->token_dev, 4, cudaMemcpyDeviceToDevice, c->stream));
+  CK(cudaMemcpyAsync(c->token_dev + TOKEN_SAVE, c->token_dev, 4, cudaMemcpyDeviceToDevice, c->stream));
   int r = 0;
   for (int i = 0; i < n_seq && !r; i++) {
     c->pos = pos[i];
@@ -1539,7 +1439,7 @@ extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* p
   c->pos = saved_pos;
   c->h_pinned[2] = saved_pos;
   CK(cudaMemcpyAsync(c->pos_dev, &c->h_pinned[2], 4, cudaMemcpyHostToDevice, c->stream));
-  CK(cudaMemcpyAsync(c->token_dev, c->token_dev + 2 * STEP_SEQ_MAX, 4, cudaMemcpyDeviceToDevice, c->stream));
+  CK(cudaMemcpyAsync(c->token_dev, c->token_dev + TOKEN_SAVE, 4, cudaMemcpyDeviceToDevice, c->stream));
   CK(cudaStreamSynchronize(c->stream));
   return r;
 }

@@ -446,16 +446,7 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
   return ok;
 }
 
-// Sequence views (MS: several sequences per launch, each on its own
-// n-th of the grid with its own program, exchange vectors, counters and
-// cache slot; the program of sequence h follows that of h - 1).
-#define SEQ_PROG (A.prog + (MS ? (size_t)half * A.n_phases : 0))
-#define SEQ_BAR (A.bar + (MS ? half * 8 : 0))
-#define SEQ_KEYS (A.keys + (MS ? half * 4 : 0))
-#define SEQ_TOKEN (A.token_dev + (MS ? half : 0))
-#define SEQ_POS0 (MS ? A.seq_pos0[half] : A.pos0)
-
-template <int HD, bool TP, bool MS>
+template <int HD, bool TP>
 __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant__ StepArgs A) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -466,9 +457,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
   float* part = reinterpret_cast<float*>(region + A.region_bytes);
   float* red = part + A.part_floats;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const unsigned grid = MS ? gridDim.x / (unsigned)A.n_seq : gridDim.x;  // CTAs of one sequence
-  const unsigned half = MS ? blockIdx.x / grid : 0u;                      // this CTA's sequence
-  const unsigned vcta = MS ? blockIdx.x - half * grid : blockIdx.x;       // CTA index within it
+  const unsigned grid = gridDim.x, vcta = blockIdx.x;
   const int NP = A.n_phases + 1;  // tags per step: embedding + program
 
   if (threadIdx.x == 0) {
@@ -488,7 +477,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
     bool ok = true;
     for (int step = 0; step < A.n_steps && ok; step++) {
       for (int ph = 0; ph < A.n_phases && ok; ph++) {
-        const PhaseDesc& D = SEQ_PROG[ph];
+        const PhaseDesc& D = A.prog[ph];
         if (D.kind != PK_GEMV || !phase_runs(A, ph, step)) continue;
         const SegRange* rtab = A.ranges + ((size_t)ph * grid + vcta) * MAX_SEGS;
         for (int s = 0; s < D.g.n_seg && ok; s++) {
@@ -550,12 +539,12 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
   auto tag_of = [&](int step, int idx) -> uint32_t { return A.tag_base + (uint32_t)(step * NP + idx); };
 
   for (int step = 0; step < A.n_steps; step++) {
-    const int pos = SEQ_POS0 + step;
+    const int pos = A.pos0 + step;
     // ---- step barrier: the previous step's pick and K/V rows are complete
     // (with tensor parallelism: on every GPU, through the cross-GPU counter)
     if (step > 0) {
       if (t == 0)
-        s_ok = A.tp_world == 1 ? grid_wait(SEQ_BAR, (unsigned)step * grid, err)
+        s_ok = A.tp_world == 1 ? grid_wait(A.bar, (unsigned)step * grid, err)
                                : grid_wait(A.xbar, (A.xbar_base + (unsigned)step) * (unsigned)A.tp_world, err);
       consumers_sync();
       if (!s_ok) bad = true;
@@ -565,16 +554,16 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
     // ---- embedding of this step's input token (deq_row, src/nn.c:55-59)
     {
       int token;
-      if (step < A.n_forced) token = A.forced[(MS ? half * A.n_forced : 0) + step];
-      else if (step == 0) token = __ldcg(SEQ_TOKEN);
-      else token = key_pick(SEQ_KEYS + (step - 1) % 3);
+      if (step < A.n_forced) token = A.forced[step];
+      else if (step == 0) token = __ldcg(A.token_dev);
+      else token = key_pick(A.keys + (step - 1) % 3);
       if (vcta == 0 && t == 0) {
         const int j = step - 1 - A.log_base;
-        if (half == 0 && step >= 1 && A.token_log && j >= 0 && j < A.token_log_cap)
-          A.token_log[j] = key_pick(SEQ_KEYS + (step - 1) % 3);
+        if (step >= 1 && A.token_log && j >= 0 && j < A.token_log_cap)
+          A.token_log[j] = key_pick(A.keys + (step - 1) % 3);
         // keys[(step + 1) % 3]: last read at the start of step - 1, first
         // written in step + 1, after a barrier this CTA arrives at later
-        SEQ_KEYS[(step + 1) % 3] = 0ull;
+        A.keys[(step + 1) % 3] = 0ull;
       }
       const int nbD = A.D / QK;
       const uint8_t* row = A.tok_embd + (size_t)token * dev_row_bytes(W_Q6K, nbD);
@@ -583,7 +572,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
       const int e1 = min(A.D, (gc + 1) * per);
       const uint32_t tg = tag_of(step, 0);
       for (int e = gc * per + t; e < e1; e += nt)
-        put_all<TP>(A, A.xb_ll + (MS ? half * A.ll_stride : 0) + e, ll_word(q6k_dequant_packed(row, nbD, e), tg));
+        put_all<TP>(A, A.xb_ll + e, ll_word(q6k_dequant_packed(row, nbD, e), tg));
     }
     stamp(3);
     kph++;
@@ -592,7 +581,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
       if (!phase_runs(A, ph, step)) continue;
       const int b = e % 3;
       if (s_didx[b] != ph) {  // not staged ahead (first phase, or after a skipped one)
-        stage_desc(&s_desc[b], &SEQ_PROG[ph], t);
+        stage_desc(&s_desc[b], &A.prog[ph], t);
         stage_ranges(s_sr[b], A.ranges, ph, t, grid, vcta);
         if (t == 0) s_didx[b] = ph;
         consumers_sync();
@@ -601,7 +590,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         int nx = ph + 1;
         if (nx >= A.n_phases || !phase_runs(A, nx, step)) nx = 0;
         const int nb = (e + 1) % 3;
-        stage_desc(&s_desc[nb], &SEQ_PROG[nx], t);
+        stage_desc(&s_desc[nb], &A.prog[nx], t);
         stage_ranges(s_sr[nb], A.ranges, nx, t, grid, vcta);
         if (t == 0) s_didx[nb] = nx;
       }
@@ -658,7 +647,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         }
         const Act X = carve_act(region, K, P.need_q8, P.need_q6);
         float* plain =
-            (P.seg[0].epi == EPI_ARGMAX && vcta == 0) ? A.xb_plain + (MS ? half * (unsigned)A.D : 0) : nullptr;
+            (P.seg[0].epi == EPI_ARGMAX && vcta == 0) ? A.xb_plain : nullptr;
         bad |= !build_activation_ll(P, D.x_ll, tag_of(step, D.x_src), wpre, X, red, err, plain);
         if (consumers_sync_or(bad)) goto fail;
         stamp(1);
@@ -708,7 +697,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         stamp(2);
         for (int s = 0; s < n_rec; s++) epi_apply<TP>(A, D, s, recs[s], part, pos, tag);
         bad |= !ok_pre;
-        bad |= !epilogue_ll<TP>(A, D, sr, part, pos, P.argmax_key ? SEQ_KEYS + step % 3 : nullptr, tag, res_tag, res, pre,
+        bad |= !epilogue_ll<TP>(A, D, sr, part, pos, P.argmax_key ? A.keys + step % 3 : nullptr, tag, res_tag, res, pre,
                                 err, n_rec);
         // the next phase's activation may be built over these records
         if (n_rec) consumers_sync();
@@ -749,10 +738,10 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
     // ---- end of step: every CTA's pick and cache rows are in
     if (consumers_sync_or(bad)) goto fail;
     if (t == 0) {
-      grid_arrive(SEQ_BAR);
+      grid_arrive(A.bar);
       if (A.tp_world > 1 && vcta == 0) {
         // this GPU's CTAs are done: signal every GPU's cross-GPU counter
-        if (grid_wait(SEQ_BAR, (unsigned)(step + 1) * grid, err)) {
+        if (grid_wait(A.bar, (unsigned)(step + 1) * grid, err)) {
           for (int r = 0; r < A.tp_world; r++)
             asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(on_rank(A, A.xbar, XR_XBAR, r)) : "memory");
         } else {
@@ -764,14 +753,14 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
   // the last step's pick: next input token, token log, position
   if (vcta == 0 && t == 0) {
     const bool done = A.tp_world == 1
-                          ? grid_wait(SEQ_BAR, (unsigned)A.n_steps * grid, err)
+                          ? grid_wait(A.bar, (unsigned)A.n_steps * grid, err)
                           : grid_wait(A.xbar, (A.xbar_base + (unsigned)A.n_steps) * (unsigned)A.tp_world, err);
     if (done) {
-      const int tok = key_pick(SEQ_KEYS + (A.n_steps - 1) % 3);
-      *SEQ_TOKEN = tok;
+      const int tok = key_pick(A.keys + (A.n_steps - 1) % 3);
+      *A.token_dev = tok;
       const int j = A.n_steps - 1 - A.log_base;
-      if (half == 0 && A.token_log && j >= 0 && j < A.token_log_cap) A.token_log[j] = tok;
-      A.pos_dev[MS ? half : 0] = SEQ_POS0 + A.n_steps;
+      if (A.token_log && j >= 0 && j < A.token_log_cap) A.token_log[j] = tok;
+      *A.pos_dev = A.pos0 + A.n_steps;
     } else {
       atomicExch(A.err_flag, 1);
     }
@@ -894,13 +883,13 @@ bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
   return step_smem_bytes(a) <= (size_t)STEP_SMEM_MAX;
 }
 
-template <int HD, bool TP, bool MS>
+template <int HD, bool TP>
 static cudaError_t launch_step_hd(const StepArgs& a, int grid, cudaStream_t s) {
   static unsigned done = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 32 && !(done & (1u << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(step_kernel<HD, TP, MS>, cudaFuncAttributeMaxDynamicSharedMemorySize, STEP_SMEM_MAX);
+    cudaError_t e = cudaFuncSetAttribute(step_kernel<HD, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, STEP_SMEM_MAX);
     if (e != cudaSuccess) return e;
     done |= 1u << dev;
   }
@@ -914,18 +903,13 @@ static cudaError_t launch_step_hd(const StepArgs& a, int grid, cudaStream_t s) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, step_kernel<HD, TP, MS>, a);
+  return cudaLaunchKernelEx(&cfg, step_kernel<HD, TP>, a);
 }
 
 cudaError_t launch_step(const StepArgs& a, int grid, cudaStream_t s) {
-  const bool tp = a.tp_world > 1, ms = a.n_seq > 1;
-  if (tp && ms) return cudaErrorInvalidValue;  // several sequences per launch: one GPU only
-  if (a.head_dim == 128)
-    return tp ? launch_step_hd<128, true, false>(a, grid, s)
-              : ms ? launch_step_hd<128, false, true>(a, grid, s) : launch_step_hd<128, false, false>(a, grid, s);
-  if (a.head_dim == 64)
-    return tp ? launch_step_hd<64, true, false>(a, grid, s)
-              : ms ? launch_step_hd<64, false, true>(a, grid, s) : launch_step_hd<64, false, false>(a, grid, s);
+  const bool tp = a.tp_world > 1;
+  if (a.head_dim == 128) return tp ? launch_step_hd<128, true>(a, grid, s) : launch_step_hd<128, false>(a, grid, s);
+  if (a.head_dim == 64) return tp ? launch_step_hd<64, true>(a, grid, s) : launch_step_hd<64, false>(a, grid, s);
   return cudaErrorInvalidValue;
 }
 

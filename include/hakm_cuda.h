@@ -106,13 +106,13 @@ int hakmc_decode(hakmc_ctx *c, int n_steps, int *out_tokens);
  * using KV-cache slot i (slot 0 is also the single-sequence calls' cache;
  * their position and last pick are left as they were). The reference
  * decodes one sequence at a time; each row of this call is hakm_forward on
- * a context holding that sequence's cache. Two or more sequences on one GPU
+ * a context holding that sequence's cache. Eight or more sequences on one GPU
  * go through each layer together as the rows of one pass (the kernels of
  * hakmc_prefill_batched; attention reads each row's own cache slot up to its
  * position), so each weight byte is read once per call: rows agree with
- * single-sequence runs to fp32 rounding plus the int8 flips it can move. One
- * sequence (or tensor parallelism) runs the step kernel per sequence, bit
- * for bit. argmax [host] gets n_seq ids;
+ * single-sequence runs to fp32 rounding plus the int8 flips it can move.
+ * Fewer sequences (or tensor parallelism) run the step kernel per sequence,
+ * bit for bit. argmax [host] gets n_seq ids;
  * logits [host] (may be NULL) n_seq*vocab floats. 0, HAKMC_ERANGE for a
  * position beyond max_seq, or another negative code. */
 int hakmc_forward_batch(hakmc_ctx *c, const int *tokens, const int *pos,

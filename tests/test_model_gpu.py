@@ -305,11 +305,12 @@ def test_forward_batch_rows_equal_single_sequence_contexts(cuda, small_path, lay
     logits agree with single-sequence runs to fp32 rounding plus the int8
     flips it can move downstream (all layers: the reference-comparison bound;
     one layer: tighter), picks agree unless the two best logits are within
-    that noise. Five sequences with different prompts, fed and then decoded
-    greedily in lockstep; two of them start later, idle rows write a spare
-    position."""
-    prompts = [[11, 22, 33, 44], [500, 600, 700, 800], [3000, 17, 42, 9], [7, 8, 9, 10], [1234, 99, 5, 66]]
-    n_seq, n_gen, start = 5, 6, [0, 0, 2, 0, 1]
+    that noise. Nine sequences (a batch that takes the batched pass) with
+    different prompts, fed and then decoded greedily in lockstep; three of
+    them start later, idle rows write a spare position."""
+    prompts = [[11, 22, 33, 44], [500, 600, 700, 800], [3000, 17, 42, 9], [7, 8, 9, 10], [1234, 99, 5, 66],
+               [1, 2, 3, 4], [4095, 4094, 100, 200], [31, 62, 93, 124], [2048, 1024, 512, 256]]
+    n_seq, n_gen, start = 9, 6, [0, 0, 2, 0, 1, 0, 3, 0, 0]
     batch = HakmCtx(small_path, max_seq=64, max_batch=n_seq)
     singles = [HakmCtx(small_path, max_seq=64) for _ in prompts]
     if layers:
@@ -344,14 +345,26 @@ def test_forward_batch_rows_equal_single_sequence_contexts(cuda, small_path, lay
             s.close()
 
 
-def test_forward_batch_single_sequence_is_forward(cuda, small_path):
-    """One sequence per call takes the step kernel, as hakm_forward: bit for bit."""
-    with HakmCtx(small_path, max_seq=64, max_batch=2) as a, HakmCtx(small_path, max_seq=64) as b:
-        for p, t in enumerate([11, 22, 33, 44, 55]):
-            la, ama = a.forward_batch([t], [p], want_logits=True)
-            lb, amb = b.forward(t)
-            assert np.array_equal(la[0].view(np.uint32), lb.view(np.uint32)), p
+def test_forward_batch_small_batches_are_forward(cuda, small_path):
+    """Batches below the batched pass's size take the step kernel per
+    sequence, as hakm_forward: bit for bit (three sequences, then one)."""
+    with HakmCtx(small_path, max_seq=64, max_batch=3) as a:
+        singles = [HakmCtx(small_path, max_seq=64) for _ in range(3)]
+        try:
+            for p in range(5):
+                toks = [11 * (p + 1) + 7 * i for i in range(3)]
+                la, ama = a.forward_batch(toks, [p] * 3, want_logits=True)
+                for i in range(3):
+                    lb, amb = singles[i].forward(toks[i])
+                    assert np.array_equal(la[i].view(np.uint32), lb.view(np.uint32)), (p, i)
+                    assert ama[i] == amb
+            la, ama = a.forward_batch([5], [5], want_logits=True)  # slot 0 alone
+            lb, amb = singles[0].forward(5)
+            assert np.array_equal(la[0].view(np.uint32), lb.view(np.uint32))
             assert ama[0] == amb
+        finally:
+            for x in singles:
+                x.close()
 
 
 def test_forward_batch_rejects_bad_input(cuda, tiny_path):
