@@ -241,9 +241,9 @@ struct G6Plan {
 };
 
 // Tile height and K split: the height that wastes least of the last wave (2
-// CTAs of 128 or 3 of 64 per SM; a 64-row tile does ~15% less work per
-// instruction); when the tiles fill less than one wave (short batches), the
-// k tiles are split over CTAs (at least 8 per CTA).
+// CTAs of 128, 3 of 64 or 4 of 16 per SM; a 64-row tile does ~15% less work
+// per instruction), then the k tiles split over CTAs (at least 8 per CTA)
+// until the last wave is nearly full.
 G6Plan g6_plan(int n_out, int K, int M, int sms) {
   G6Plan p;
   p.tn = (n_out + G6_BN - 1) / G6_BN;
@@ -254,8 +254,18 @@ G6Plan g6_plan(int n_out, int K, int M, int sms) {
   p.tm = (M + p.bm - 1) / p.bm;
   const long tiles = (long)p.tn * p.tm, slots = (p.bm == 128 ? 2L : p.bm == 64 ? 3L : 4L) * sms;
   const int nk = K / G6_BK;
-  int split = tiles < slots ? (int)std::min<long>(slots / tiles, nk / 8) : 1;
-  split = std::max(split, 1);
+  // the smallest split (at least 8 k tiles per CTA) whose CTAs fill their
+  // last wave to 90%; else the best-filling one (a last wave of 224 tiles
+  // on 296 slots left a quarter of the SMs idle: measured)
+  const int max_split = std::max(1, std::min(nk / 8, 32));
+  int split = 1;
+  double best = 0.0;
+  for (int sp = 1; sp <= max_split; sp++) {
+    const long ctas = tiles * sp, waves = (ctas + slots - 1) / slots;
+    const double fill = (double)ctas / (double)(waves * slots);
+    if (fill > best + 1e-9) { best = fill; split = sp; }
+    if (fill >= 0.9) break;
+  }
   p.kt_per = (nk + split - 1) / split;
   p.split = (nk + p.kt_per - 1) / p.kt_per;
   return p;
