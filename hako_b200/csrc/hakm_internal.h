@@ -154,6 +154,12 @@ cudaError_t launch_pf_argmax(int* out, const float* logits, int M, int V, cudaSt
 cudaError_t launch_pf_fill_normal(float* dst, size_t ystride, size_t n, int blocks_y, uint64_t seed, cudaStream_t s);
 cudaError_t launch_pf_attention(float* out, const float* q, const float* kc, const float* vc, int M, int pos0, int H,
                                 int KVH, int hd, float scale, cudaStream_t s);
+// Batched decode rows (row r: sequence r at row_pos[r], its cache slot_stride
+// floats on), positions split over CTAs; part: pf_decode_attention_part_floats.
+cudaError_t launch_pf_decode_attention(float* out, const float* q, const float* kc, const float* vc, int rows,
+                                       const int* row_pos, int max_pos, size_t slot_stride, int H, int KVH, int hd,
+                                       float scale, float* part, size_t part_floats, int sms, cudaStream_t s);
+size_t pf_decode_attention_part_floats(int rows, int H, int KVH, int hd, int max_pos, int sms);
 cudaError_t launch_pf_swiglu(float* h, const float* gu, int M, int F, cudaStream_t s);
 cudaError_t launch_pf_add(float* x, const float* o, size_t n, cudaStream_t s);
 
@@ -172,9 +178,6 @@ struct AttnParams {
 };
 constexpr int ATTN_CHUNK = 32;   // positions per attention work item
 cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl);
-// One query row per sequence, n_rows sequences (grid z); see hakm_kernels.cu.
-cudaError_t launch_attention_rows(const AttnParams& a, const int* row_pos, int n_rows, size_t kv_stride,
-                                  size_t part_stride, cudaStream_t s);
 // hakmc_attention_noalloc: scratch in a static device array, no allocation
 cudaError_t attention_noalloc(float* out, const float* q, const float* kc, const float* vc, int pos, int n_heads,
                               int n_kv, int head_dim, cudaStream_t stream);

@@ -247,55 +247,6 @@ cudaError_t launch_attention(const AttnParams& a0, cudaStream_t s, bool pdl) {
   return cudaErrorInvalidValue;
 }
 
-// Attention of several sequences' single query rows in one launch (batched
-// decode): row r (grid z) is sequence r at position row_pos[r], its q and
-// output at r * n_heads * HD, its cache slot kv_stride floats after row
-// r - 1's, its split partials part_stride floats and its tickets 64 words
-// apart. n_split covers the longest row; chunks past a row's position add
-// nothing (attn_item). Per row the arithmetic of the one-sequence launch.
-template <int HD>
-__global__ void __launch_bounds__(256) attention_rows_kernel(const AttnParams a0, const int* row_pos, size_t kv_stride,
-                                                             size_t part_stride) {
-  extern __shared__ __align__(16) float sm[];
-  const int r = blockIdx.z;
-  AttnParams a = a0;
-  const size_t qo = (size_t)r * a.n_heads * HD;
-  a.q += qo;
-  a.out += qo;
-  a.k_cache += (size_t)r * kv_stride;
-  a.v_cache += (size_t)r * kv_stride;
-  a.part += (size_t)r * part_stride;
-  a.counters += 64 * r;
-  attn_item<HD, false>(a, blockIdx.x, blockIdx.y, row_pos[r], sm, threadIdx.x, blockDim.x, BlockSync());
-}
-
-template <int HD>
-static cudaError_t launch_attn_rows(const AttnParams& a, const int* row_pos, int n_rows, size_t kv_stride,
-                                    size_t part_stride, cudaStream_t s) {
-  const size_t smem = attn_smem_bytes(HD);
-  static unsigned done = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 32 && !(done & (1u << dev))) {
-    cudaError_t e =
-        cudaFuncSetAttribute(attention_rows_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    done |= 1u << dev;
-  }
-  attention_rows_kernel<HD><<<dim3(a.n_kv, a.n_split, n_rows), 256, smem, s>>>(a, row_pos, kv_stride, part_stride);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_attention_rows(const AttnParams& a0, const int* row_pos, int n_rows, size_t kv_stride,
-                                  size_t part_stride, cudaStream_t s) {
-  if (a0.n_heads % a0.n_kv || a0.n_heads / a0.n_kv > 8 || a0.n_kv > 64 || n_rows <= 0) return cudaErrorInvalidValue;
-  AttnParams a = a0;
-  a.head_group = a.n_heads / a.n_kv;
-  if (a.head_dim == 128) return launch_attn_rows<128>(a, row_pos, n_rows, kv_stride, part_stride, s);
-  if (a.head_dim == 64) return launch_attn_rows<64>(a, row_pos, n_rows, kv_stride, part_stride, s);
-  return cudaErrorInvalidValue;
-}
-
 // ------------------------------------------------------------ allocation-free attention
 
 // Scratch of hakmc_attention_noalloc: split partials, per-kv-head tickets and

@@ -528,6 +528,233 @@ cudaError_t launch_pf_attention(float* out, const float* q, const float* kc, con
   return cudaErrorInvalidValue;
 }
 
+// ---------------------------------------------------------------- decode rows
+//
+// Attention of batched decode rows (one query position per row): row r is
+// sequence r at position row_pos[r], its cache slot_stride floats after row
+// r - 1's (src/model.c:122-142 per row). Flash-decoding: CTA = (position
+// split, kv head, row); the kv head's G <= 8 query heads share every K/V
+// tile of 32 positions, which cp.async brings into a double buffer while
+// the previous tile is used. All 8 warps work on every tile: for the scores
+// warp w sums dimensions [w * HD/8, (w + 1) * HD/8) of every (head,
+// position) pair (lane = position), the partial sums meet in shared memory,
+// warp v finishes head v's scores and its online softmax, and for the
+// weighted sum thread (v, lane) owns head v's dimensions 4 lane..4 lane + 3
+// (HD 128; HD 64: two halves of the tile). Each CTA leaves (max, sum,
+// unnormalised output) per head; da_merge_kernel combines the splits in
+// order.
+constexpr int DA_TILE = 32, DA_MAXG = 8;
+
+template <int HD>
+struct DaSmem {
+  float k[2][DA_TILE][HD + 4];
+  float v[2][DA_TILE][HD];
+  float q[DA_MAXG][HD];
+  float part[8][DA_MAXG][DA_TILE];  // [warp][head][position] partial dots
+  float p[DA_MAXG][DA_TILE];        // probabilities of the tile
+  float alpha[DA_MAXG];             // rescale of the running output
+};
+
+struct DaArgs {
+  float* part;  // [rows][H][splits][HD + 2]
+  const float* q;
+  const float* kc;
+  const float* vc;
+  const int* row_pos;
+  size_t slot_stride;
+  int H, KVH, tiles_per_split;
+  float scale;
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  const int n = valid ? 16 : 0;  // 0: zero-fill, nothing read
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) da_rows_kernel(const DaArgs a) {
+  constexpr int DW = HD / 8;   // dimensions per warp in the score pass
+  constexpr int NV = HD / 4;   // float4 per K or V row
+  constexpr int VW = HD / 32;  // dimensions per lane in the weighted sum
+  extern __shared__ __align__(16) float da_raw[];
+  DaSmem<HD>& S = *reinterpret_cast<DaSmem<HD>*>(da_raw);
+  const int G = a.H / a.KVH, g = blockIdx.y, r = blockIdx.z;
+  const int KV = a.KVH * HD;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int pos = a.row_pos[r];
+  const float* kc = a.kc + (size_t)r * a.slot_stride + g * HD;
+  const float* vc = a.vc + (size_t)r * a.slot_stride + g * HD;
+  const int t_begin = blockIdx.x * a.tiles_per_split * DA_TILE;
+  const int t_end = min(pos + 1, t_begin + a.tiles_per_split * DA_TILE);
+  const int n_tiles = t_end > t_begin ? (t_end - t_begin + DA_TILE - 1) / DA_TILE : 0;
+  for (int i = tid; i < G * HD; i += 256)
+    S.q[i / HD][i % HD] = a.q[(size_t)r * a.H * HD + (size_t)(g * G) * HD + i];
+  auto issue = [&](int tile, int buf) {
+    const int t0 = t_begin + tile * DA_TILE;
+    for (int i = tid; i < DA_TILE * NV; i += 256) {
+      const int j = i / NV, c4 = (i % NV) * 4, p = t0 + j;
+      const bool ok = p < t_end;
+      const size_t off = (size_t)(ok ? p : t_begin) * KV + c4;
+      cp_async16(&S.k[buf][j][c4], kc + off, ok);
+      cp_async16(&S.v[buf][j][c4], vc + off, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float acc[VW];  // head `warp`, dimensions VW * lane ..
+#pragma unroll
+  for (int e = 0; e < VW; e++) acc[e] = 0.f;
+  float m = -CUDART_INF_F, l = 0.f;  // head `warp`'s running max and sum (warps < G)
+  if (n_tiles > 0) issue(0, 0);
+  for (int it = 0; it < n_tiles; it++) {
+    const int buf = it & 1, t0 = t_begin + it * DA_TILE;
+    if (it + 1 < n_tiles) {
+      issue(it + 1, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();  // tile `it` in shared memory for every thread (and q, the first time)
+    {
+      float sacc[DA_MAXG];
+#pragma unroll
+      for (int v = 0; v < DA_MAXG; v++) sacc[v] = 0.f;
+#pragma unroll
+      for (int d4 = 0; d4 < DW; d4 += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(&S.k[buf][lane][warp * DW + d4]);
+#pragma unroll
+        for (int v = 0; v < DA_MAXG; v++) {
+          if (v < G) {
+            const float4 q4 = *reinterpret_cast<const float4*>(&S.q[v][warp * DW + d4]);
+            sacc[v] = __fmaf_rn(q4.x, k4.x, sacc[v]);
+            sacc[v] = __fmaf_rn(q4.y, k4.y, sacc[v]);
+            sacc[v] = __fmaf_rn(q4.z, k4.z, sacc[v]);
+            sacc[v] = __fmaf_rn(q4.w, k4.w, sacc[v]);
+          }
+        }
+      }
+#pragma unroll
+      for (int v = 0; v < DA_MAXG; v++)
+        if (v < G) S.part[warp][v][lane] = sacc[v];
+    }
+    __syncthreads();
+    if (warp < G) {
+      float sc = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; w++) sc += S.part[w][warp][lane];
+      const bool ok = t0 + lane < t_end;
+      sc = ok ? sc * a.scale : -CUDART_INF_F;
+      const float mnew = fmaxf(m, warp_max(sc));  // the tile holds >= 1 position: finite
+      const float al = expf(m - mnew);
+      const float p = ok ? expf(sc - mnew) : 0.f;
+      l = l * al + warp_sum(p);
+      m = mnew;
+      S.p[warp][lane] = p;
+#pragma unroll
+      for (int e = 0; e < VW; e++) acc[e] *= al;
+    }
+    __syncthreads();
+    if (warp < G) {
+#pragma unroll 8
+      for (int j = 0; j < DA_TILE; j++) {
+        const float pj = S.p[warp][j];
+        if constexpr (VW == 4) {
+          const float4 v4 = *reinterpret_cast<const float4*>(&S.v[buf][j][4 * lane]);
+          acc[0] = __fmaf_rn(pj, v4.x, acc[0]); acc[1] = __fmaf_rn(pj, v4.y, acc[1]);
+          acc[2] = __fmaf_rn(pj, v4.z, acc[2]); acc[3] = __fmaf_rn(pj, v4.w, acc[3]);
+        } else {
+          const float2 v2 = *reinterpret_cast<const float2*>(&S.v[buf][j][2 * lane]);
+          acc[0] = __fmaf_rn(pj, v2.x, acc[0]); acc[1] = __fmaf_rn(pj, v2.y, acc[1]);
+        }
+      }
+    }
+    __syncthreads();  // buffer `buf` is refilled by the next issue
+  }
+  // partials: [row][head][split][max, sum, out]
+  if (warp < G) {
+    float* pp = a.part + (((size_t)r * a.H + g * G + warp) * gridDim.x + blockIdx.x) * (HD + 2);
+    if (lane == 0) { pp[0] = m; pp[1] = l; }
+#pragma unroll
+    for (int e = 0; e < VW; e++) pp[2 + VW * lane + e] = acc[e];
+  }
+}
+
+// out[row][head] from the splits' partials, in split order: one warp per
+// (row, head).
+template <int HD>
+__global__ void __launch_bounds__(256) da_merge_kernel(float* __restrict__ out, const float* __restrict__ part,
+                                                       int rows, int H, int n_split) {
+  constexpr int VW = HD / 32;
+  const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (w >= rows * H) return;
+  const float* pp = part + (size_t)w * n_split * (HD + 2);
+  float m = -CUDART_INF_F;
+  for (int sp = 0; sp < n_split; sp++) m = fmaxf(m, pp[(size_t)sp * (HD + 2)]);
+  float l = 0.f, acc[VW];
+#pragma unroll
+  for (int e = 0; e < VW; e++) acc[e] = 0.f;
+  for (int sp = 0; sp < n_split; sp++) {
+    const float* ps = pp + (size_t)sp * (HD + 2);
+    if (ps[1] == 0.f) continue;  // a split with no position of this row
+    const float f = expf(ps[0] - m);
+    l = __fmaf_rn(ps[1], f, l);
+#pragma unroll
+    for (int e = 0; e < VW; e++) acc[e] = __fmaf_rn(ps[2 + VW * lane + e], f, acc[e]);
+  }
+  float* o = out + (size_t)w * HD;  // rows' outputs are [row][H][HD]
+  const float inv = 1.0f / l;
+#pragma unroll
+  for (int e = 0; e < VW; e++) o[VW * lane + e] = acc[e] * inv;
+}
+
+namespace {
+// Position splits: about two waves of 2 CTAs per SM.
+int da_splits(int rows, int KVH, int max_pos, int sms, int* tiles_per) {
+  const int n_tiles = max_pos / DA_TILE + 1;
+  int split = (4 * sms + rows * KVH - 1) / (rows * KVH);
+  split = std::max(1, std::min(split, n_tiles));
+  *tiles_per = (n_tiles + split - 1) / split;
+  return (n_tiles + *tiles_per - 1) / *tiles_per;
+}
+
+template <int HD>
+cudaError_t launch_da_hd(dim3 grid, const DaArgs& a, float* out, int rows, cudaStream_t s) {
+  static unsigned done = 0;  // attribute set, per device
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 32 && !(done & (1u << dev))) {
+    e = cudaFuncSetAttribute(da_rows_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(DaSmem<HD>));
+    if (e != cudaSuccess) return e;
+    done |= 1u << dev;
+  }
+  da_rows_kernel<HD><<<grid, 256, sizeof(DaSmem<HD>), s>>>(a);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  da_merge_kernel<HD><<<(rows * a.H + 7) / 8, 256, 0, s>>>(out, a.part, rows, a.H, (int)grid.x);
+  return cudaGetLastError();
+}
+}  // namespace
+
+size_t pf_decode_attention_part_floats(int rows, int H, int KVH, int hd, int max_pos, int sms) {
+  int per = 0;
+  return (size_t)rows * H * da_splits(rows, KVH, max_pos, sms, &per) * (hd + 2);
+}
+
+cudaError_t launch_pf_decode_attention(float* out, const float* q, const float* kc, const float* vc, int rows,
+                                       const int* row_pos, int max_pos, size_t slot_stride, int H, int KVH, int hd,
+                                       float scale, float* part, size_t part_floats, int sms, cudaStream_t s) {
+  if (H % KVH || H / KVH > DA_MAXG || rows <= 0 || !row_pos || !part) return cudaErrorInvalidValue;
+  int per = 0;
+  const int split = da_splits(rows, KVH, max_pos, sms, &per);
+  if (part_floats < (size_t)rows * H * split * (hd + 2)) return cudaErrorInvalidValue;
+  const DaArgs a = {part, q, kc, vc, row_pos, slot_stride, H, KVH, per, scale};
+  const dim3 grid(split, KVH, rows);
+  if (hd == 128) return launch_da_hd<128>(grid, a, out, rows, s);
+  if (hd == 64) return launch_da_hd<64>(grid, a, out, rows, s);
+  return cudaErrorInvalidValue;
+}
+
 // ---------------------------------------------------------------- FFN, residual
 //
 // gu: [M][2F], gate and up rows interleaved (device row 2i = gate row i,

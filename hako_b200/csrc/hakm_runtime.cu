@@ -199,6 +199,8 @@ struct hakmc_ctx {
   float* pf_part6 = nullptr;  // Q6_K K-split partials, pf_part6_floats
   size_t pf_part6_floats = 0;
   int* row_io = nullptr;  // batched decode: [max_batch] tokens, positions, picks
+  float* pf_apart = nullptr;  // batched decode: attention split partials, pf_apart_floats
+  size_t pf_apart_floats = 0;
 };
 
 static int dalloc(hakmc_ctx* c, void** p, size_t n) {
@@ -1357,14 +1359,15 @@ static int batch_decode(hakmc_ctx* c, const int* tokens, const int* pos, int n, 
   int max_pos = 0;
   for (int i = 0; i < n; i++) max_pos = std::max(max_pos, pos[i]);
   const size_t lstride = (size_t)c->max_seq * KV, slot = (size_t)c->L * lstride;
-  AttnParams at = {};
-  at.n_heads = c->H;
-  at.n_kv = c->KVH;
-  at.head_dim = c->hd;
-  at.scale = 1.0f / sqrtf((float)c->hd);
-  at.n_split = max_pos / ATTN_CHUNK + 1;
-  at.part = c->attn_part;
-  at.counters = c->attn_counters;
+  const float scale = 1.0f / sqrtf((float)c->hd);
+  const size_t apart = pf_decode_attention_part_floats(n, c->H, c->KVH, c->hd, max_pos, c->num_sms);
+  if (apart > c->pf_apart_floats) {
+    dfree(c, c->pf_apart);
+    c->pf_apart = nullptr;
+    c->pf_apart_floats = 0;
+    if ((r = dalloc(c, (void**)&c->pf_apart, apart * 4))) return r;
+    c->pf_apart_floats = apart;
+  }
   CK(cudaEventRecord(c->ev0, s));
   cudaError_t e = launch_pf_embed(c->pf_x, c->tok_embd.w, tok_dev, n, D, s);
   for (int l = 0; l < c->run_layers && e == cudaSuccess; l++) {
@@ -1376,11 +1379,9 @@ static int batch_decode(hakmc_ctx* c, const int* tokens, const int* pos, int n, 
     if ((e = pf_matmul(c, c->pf_v, y.wv, c->pf_xn, c->pf_xq, c->pf_xs, y.bv, n, false))) break;
     if ((e = launch_pf_rope_kv(c->pf_qk, c->pf_v, c->pf_q, kc, vc, c->rope_cs, n, 0, pos_dev, slot, D, KV, c->hd, s)))
       break;
-    at.q = c->pf_q;
-    at.k_cache = kc;
-    at.v_cache = vc;
-    at.out = c->pf_att;
-    if ((e = launch_attention_rows(at, pos_dev, n, slot, c->attn_part_floats, s))) break;
+    if ((e = launch_pf_decode_attention(c->pf_att, c->pf_q, kc, vc, n, pos_dev, max_pos, slot, c->H, c->KVH, c->hd,
+                                        scale, c->pf_apart, c->pf_apart_floats, c->num_sms, s)))
+      break;
     if (y.wo.type == W_Q4K && (e = launch_quantize_q8(c->pf_att, n * D, c->pf_xq, c->pf_xs, s))) break;
     if ((e = pf_matmul(c, c->pf_x, y.wo, c->pf_att, c->pf_xq, c->pf_xs, nullptr, n, true))) break;
     if ((e = launch_pf_norm_quant(c->pf_x, y.ffn_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
@@ -1415,7 +1416,9 @@ extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* p
   // read once). Fewer run the step kernel per sequence: the batched pass
   // costs ~8 ms on the 3B shapes whatever the batch up to 16 (about 470
   // launches of short kernels), the step kernel 1.4 ms per sequence.
-  if (n_seq >= BATCH_ROWS_MIN && c->tp_world == 1) return batch_decode(c, tokens, pos, n_seq, logits, argmax);
+  // (its attention takes up to 8 query heads per kv head)
+  if (n_seq >= BATCH_ROWS_MIN && c->tp_world == 1 && c->H / c->KVH <= 8)
+    return batch_decode(c, tokens, pos, n_seq, logits, argmax);
   if (!c->use_step) { set_err("forward_batch runs on the step kernel (HAKMC_STEP=0 is set)"); return HAKMC_EINVAL; }
   // sequence 0 is also the single-sequence API's: its position and last pick
   // (the input hakmc_decode continues from) are restored afterwards

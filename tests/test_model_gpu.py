@@ -345,6 +345,27 @@ def test_forward_batch_rows_equal_single_sequence_contexts(cuda, small_path, lay
             s.close()
 
 
+def test_forward_batch_long_caches(cuda, small_path):
+    """Batched decode over long caches (positions split over many CTAs, the
+    splits merged in order): nine sequences whose caches hold 700 seeded
+    N(0,1) positions (each its own seed), one step each at positions
+    700..708, against single-sequence contexts filled with the same values."""
+    n_seq = 9
+    pos = [700 + i for i in range(n_seq)]
+    toks = [(131 * i + 7) % 4000 for i in range(n_seq)]
+    with HakmCtx(small_path, max_seq=1024, max_batch=n_seq) as batch:
+        for i in range(n_seq):
+            batch.fill_kv_normal(pos[i], seq=i, seed=50 + i)
+        logits, am = batch.forward_batch(toks, pos, want_logits=True)
+    for i in range(n_seq):
+        with HakmCtx(small_path, max_seq=1024) as one:
+            one.fill_kv_normal(pos[i], seq=0, seed=50 + i)
+            assert one.pos == pos[i]
+            ref, ref_am = one.forward(toks[i])
+        assert rel_l2(logits[i], ref) < 2e-2, (i, rel_l2(logits[i], ref))
+        assert _margin_ok(ref, int(am[i]), ref_am), i
+
+
 def test_forward_batch_small_batches_are_forward(cuda, small_path):
     """Batches below the batched pass's size take the step kernel per
     sequence, as hakm_forward: bit for bit (three sequences, then one)."""
