@@ -93,24 +93,38 @@ cudaError_t launch_pf_norm_quant(const float* x, const float* w, int M, int D, f
 // CTA tile 128 weight rows x BM activation rows (128, 64, or 16 for short
 // batches), k tiles of 32 (two 16-element scale groups); thread tile 8 weight
 // rows x BM/16 activation rows, read as float4 pairs 64 apart (conflict-free
-// shared loads). Double-buffered: the next k tile's raw weight bytes and
-// activations are loaded into registers while the current one is
-// multiplied, then dequantized into the other buffer; one barrier per tile.
+// shared loads). Double-buffered: the next k tile's raw weight bytes are
+// loaded into registers and its activations copied asynchronously into a
+// staging tile while the current one is multiplied, then both go
+// (dequantized, transposed) into the other buffer; one barrier per tile.
 constexpr int G6_BN = 128, G6_BK = 32;
 
 template <int BM>
 struct G6Tile {
   float w[2][G6_BK][G6_BN];
   float x[2][G6_BK][BM + 4];
+  float xs[BM][G6_BK + 4];  // the next activation tile as copied, [row][k]
 };
+
+// Asynchronous global -> shared copy of BYTES (8 or 16) bytes.
+template <int BYTES>
+__device__ __forceinline__ void g6_cp_async(void* dst, const void* src) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  if constexpr (BYTES == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], %2;" ::"r"(d), "l"(src), "n"(BYTES) : "memory");
+}
 
 template <int BM>
 __global__ void __launch_bounds__(256, BM == 128 ? 2 : BM == 64 ? 3 : 4) pf_q6k_gemm_kernel(float* __restrict__ out, const uint8_t* __restrict__ w,
                                                           const float* __restrict__ x, const float* __restrict__ bias,
                                                           int n_out, int K, int M, int accumulate, int kt_per) {
   constexpr int TM = BM / 16;                // activation rows per thread (1, 4 or 8)
-  constexpr int XV = BM * G6_BK / 256 / 2;   // float2 activation loads per thread and tile
-  constexpr int XPR = G6_BK / (2 * XV);      // threads per activation row
+  constexpr int XE = BM * G6_BK / 256;       // activation values per thread and tile (16, 8 or 2)
+  constexpr int XPR = G6_BK / XE;            // threads per activation row
+  constexpr int CB = XE >= 4 ? 16 : 4 * XE;  // bytes per asynchronous copy
+  constexpr int NCP = 4 * XE / CB;           // copies per thread and tile
   extern __shared__ __align__(16) float g6_smem[];
   G6Tile<BM>& S = *reinterpret_cast<G6Tile<BM>*>(g6_smem);
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
@@ -122,13 +136,14 @@ __global__ void __launch_bounds__(256, BM == 128 ? 2 : BM == 64 ? 3 : 4) pf_q6k_
   // dequantization: weight row lr, 16 values at k0 + 16 * hf (one scale group)
   const int lr = tid >> 1, hf = tid & 1;
   const uint8_t* wrow = w + (size_t)min(n0 + lr, n_out - 1) * rowB;
-  // activations: row xm, 2 * XV values at k0 + xk
-  const int xm = tid / XPR, xk = (tid % XPR) * 2 * XV;
+  // activations: row xm, XE values at k0 + xk, copied by cp.async into xs
+  // (no registers held across the multiply), then transposed by the same
+  // thread (its own copies: no barrier) into x[buf]
+  const int xm = tid / XPR, xk = (tid % XPR) * XE;
   const float* xrow = x + (size_t)min(m0 + xm, M - 1) * K;
 
   uint4 rlo, rhi;
   float rds;
-  float2 rx[XV];
   auto load = [&](int k0) {
     const int kk = k0 + 16 * hf;
     const int b = kk / QK, i0 = kk % QK;
@@ -142,7 +157,8 @@ __global__ void __launch_bounds__(256, BM == 128 ? 2 : BM == 64 ? 3 : 4) pf_q6k_
     rlo = *reinterpret_cast<const uint4*>(body + 64 * nh + 32 * (qd & 1) + l0);
     rhi = *reinterpret_cast<const uint4*>(body + 128 + 32 * nh + l0);
 #pragma unroll
-    for (int v = 0; v < XV; v++) rx[v] = *reinterpret_cast<const float2*>(xrow + k0 + xk + 2 * v);
+    for (int c = 0; c < NCP; c++) g6_cp_async<CB>(&S.xs[xm][xk + c * CB / 4], xrow + k0 + xk + c * CB / 4);
+    asm volatile("cp.async.commit_group;" ::: "memory");
   };
   auto store = [&](int buf, int k0) {
     const int qd = (((k0 + 16 * hf) % QK) >> 5) & 3;
@@ -154,11 +170,9 @@ __global__ void __launch_bounds__(256, BM == 128 ? 2 : BM == 64 ? 3 : 4) pf_q6k_
       const int q = (nib | (int)(((hb >> (2 * qd)) & 3u) << 4)) - 32;
       S.w[buf][16 * hf + e][lr] = __fmul_rn(rds, (float)q);
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 #pragma unroll
-    for (int v = 0; v < XV; v++) {
-      S.x[buf][xk + 2 * v + 0][xm] = rx[v].x;
-      S.x[buf][xk + 2 * v + 1][xm] = rx[v].y;
-    }
+    for (int e = 0; e < XE; e++) S.x[buf][xk + e][xm] = S.xs[xm][xk + e];
   };
 
   float acc[TM][8];
