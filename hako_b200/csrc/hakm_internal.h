@@ -160,6 +160,8 @@ cudaError_t launch_pf_decode_attention(float* out, const float* q, const float* 
                                        const int* row_pos, int max_pos, size_t slot_stride, int H, int KVH, int hd,
                                        float scale, float* part, size_t part_floats, int sms, cudaStream_t s);
 size_t pf_decode_attention_part_floats(int rows, int H, int KVH, int hd, int max_pos, int sms);
+// its position splits (the return) and tiles per split for max_pos
+int pf_decode_attention_plan(int rows, int KVH, int max_pos, int sms, int* tiles_per);
 cudaError_t launch_pf_swiglu(float* h, const float* gu, int M, int F, cudaStream_t s);
 cudaError_t launch_pf_add(float* x, const float* o, size_t n, cudaStream_t s);
 

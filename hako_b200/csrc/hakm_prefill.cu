@@ -750,6 +750,10 @@ cudaError_t launch_da_hd(dim3 grid, const DaArgs& a, float* out, int rows, cudaS
 }
 }  // namespace
 
+int pf_decode_attention_plan(int rows, int KVH, int max_pos, int sms, int* tiles_per) {
+  return da_splits(rows, KVH, max_pos, sms, tiles_per);
+}
+
 size_t pf_decode_attention_part_floats(int rows, int H, int KVH, int hd, int max_pos, int sms) {
   int per = 0;
   return (size_t)rows * H * da_splits(rows, KVH, max_pos, sms, &per) * (hd + 2);

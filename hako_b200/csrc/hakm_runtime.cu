@@ -201,6 +201,9 @@ struct hakmc_ctx {
   int* row_io = nullptr;  // batched decode: [max_batch] tokens, positions, picks
   float* pf_apart = nullptr;  // batched decode: attention split partials, pf_apart_floats
   size_t pf_apart_floats = 0;
+  // batched decode: one captured graph per (rows, layers, attention splits);
+  // dropped whenever a buffer it names is reallocated
+  std::map<uint64_t, cudaGraphExec_t> bgraphs;
 };
 
 static int dalloc(hakmc_ctx* c, void** p, size_t n) {
@@ -213,9 +216,15 @@ static int dalloc(hakmc_ctx* c, void** p, size_t n) {
   return 0;
 }
 
+static void drop_bgraphs(hakmc_ctx* c) {
+  for (auto& kv : c->bgraphs) cudaGraphExecDestroy(kv.second);
+  c->bgraphs.clear();
+}
+
 // Free one dalloc'd buffer before the context goes (a buffer being regrown).
 static void dfree(hakmc_ctx* c, void* p) {
   if (!p) return;
+  drop_bgraphs(c);  // a captured batched-decode graph may name this buffer
   for (size_t i = 0; i < c->allocs.size(); i++)
     if (c->allocs[i] == p) {
       cudaFree(p);
@@ -648,6 +657,7 @@ extern "C" void hakmc_destroy(hakmc_ctx* c) {
     if (c->peer_ipc[rr])
       for (int x = 0; x < XR_COUNT; x++)
         if (c->peer_ptr[rr][x]) cudaIpcCloseMemHandle(c->peer_ptr[rr][x]);
+  drop_bgraphs(c);
   for (void* p : c->allocs) cudaFree(p);
   if (c->h_pinned) cudaFreeHost(c->h_pinned);
   if (c->logits_pinned) cudaFreeHost(c->logits_pinned);
@@ -1368,33 +1378,64 @@ static int batch_decode(hakmc_ctx* c, const int* tokens, const int* pos, int n, 
     if ((r = dalloc(c, (void**)&c->pf_apart, apart * 4))) return r;
     c->pf_apart_floats = apart;
   }
-  CK(cudaEventRecord(c->ev0, s));
-  cudaError_t e = launch_pf_embed(c->pf_x, c->tok_embd.w, tok_dev, n, D, s);
-  for (int l = 0; l < c->run_layers && e == cudaSuccess; l++) {
-    const DevLayer& y = c->layers[l];
-    float* kc = c->k_cache + (size_t)l * lstride;
-    float* vc = c->v_cache + (size_t)l * lstride;
-    if ((e = launch_pf_norm_quant(c->pf_x, y.attn_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
-    if ((e = pf_matmul(c, c->pf_qk, y.wqk, c->pf_xn, c->pf_xq, c->pf_xs, y.bqk, n, false))) break;
-    if ((e = pf_matmul(c, c->pf_v, y.wv, c->pf_xn, c->pf_xq, c->pf_xs, y.bv, n, false))) break;
-    if ((e = launch_pf_rope_kv(c->pf_qk, c->pf_v, c->pf_q, kc, vc, c->rope_cs, n, 0, pos_dev, slot, D, KV, c->hd, s)))
-      break;
-    if ((e = launch_pf_decode_attention(c->pf_att, c->pf_q, kc, vc, n, pos_dev, max_pos, slot, c->H, c->KVH, c->hd,
-                                        scale, c->pf_apart, c->pf_apart_floats, c->num_sms, s)))
-      break;
-    if (y.wo.type == W_Q4K && (e = launch_quantize_q8(c->pf_att, n * D, c->pf_xq, c->pf_xs, s))) break;
-    if ((e = pf_matmul(c, c->pf_x, y.wo, c->pf_att, c->pf_xq, c->pf_xs, nullptr, n, true))) break;
-    if ((e = launch_pf_norm_quant(c->pf_x, y.ffn_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
-    if ((e = pf_matmul(c, c->pf_gu, y.wgu, c->pf_xn, c->pf_xq, c->pf_xs, nullptr, n, false))) break;
-    if ((e = launch_pf_swiglu(c->pf_h, c->pf_gu, n, F, s))) break;
-    if (y.down.type == W_Q4K && (e = launch_quantize_q8(c->pf_h, n * F, c->pf_xq, c->pf_xs, s))) break;
-    e = pf_matmul(c, c->pf_x, y.down, c->pf_h, c->pf_xq, c->pf_xs, nullptr, n, true);
+  // the kernels of the step, captured once per (rows, layers, attention
+  // splits) into a graph: ~370 launches of short kernels per step
+  int tiles_per = 0;
+  const int n_split = pf_decode_attention_plan(n, c->KVH, max_pos, c->num_sms, &tiles_per);
+  const uint64_t key = ((uint64_t)n << 48) | ((uint64_t)c->run_layers << 40) | ((uint64_t)n_split << 24) |
+                       (uint64_t)tiles_per;
+  auto enqueue = [&]() -> cudaError_t {
+    cudaError_t e = launch_pf_embed(c->pf_x, c->tok_embd.w, tok_dev, n, D, s);
+    for (int l = 0; l < c->run_layers && e == cudaSuccess; l++) {
+      const DevLayer& y = c->layers[l];
+      float* kc = c->k_cache + (size_t)l * lstride;
+      float* vc = c->v_cache + (size_t)l * lstride;
+      if ((e = launch_pf_norm_quant(c->pf_x, y.attn_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
+      if ((e = pf_matmul(c, c->pf_qk, y.wqk, c->pf_xn, c->pf_xq, c->pf_xs, y.bqk, n, false))) break;
+      if ((e = pf_matmul(c, c->pf_v, y.wv, c->pf_xn, c->pf_xq, c->pf_xs, y.bv, n, false))) break;
+      if ((e = launch_pf_rope_kv(c->pf_qk, c->pf_v, c->pf_q, kc, vc, c->rope_cs, n, 0, pos_dev, slot, D, KV, c->hd, s)))
+        break;
+      if ((e = launch_pf_decode_attention(c->pf_att, c->pf_q, kc, vc, n, pos_dev, max_pos, slot, c->H, c->KVH, c->hd,
+                                          scale, c->pf_apart, c->pf_apart_floats, c->num_sms, s)))
+        break;
+      if (y.wo.type == W_Q4K && (e = launch_quantize_q8(c->pf_att, n * D, c->pf_xq, c->pf_xs, s))) break;
+      if ((e = pf_matmul(c, c->pf_x, y.wo, c->pf_att, c->pf_xq, c->pf_xs, nullptr, n, true))) break;
+      if ((e = launch_pf_norm_quant(c->pf_x, y.ffn_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
+      if ((e = pf_matmul(c, c->pf_gu, y.wgu, c->pf_xn, c->pf_xq, c->pf_xs, nullptr, n, false))) break;
+      if ((e = launch_pf_swiglu(c->pf_h, c->pf_gu, n, F, s))) break;
+      if (y.down.type == W_Q4K && (e = launch_quantize_q8(c->pf_h, n * F, c->pf_xq, c->pf_xs, s))) break;
+      e = pf_matmul(c, c->pf_x, y.down, c->pf_h, c->pf_xq, c->pf_xs, nullptr, n, true);
+    }
+    // final norm, lm_head, greedy pick per row (src/model.c:159-164, src/sample.c:28-32)
+    if (e == cudaSuccess) e = launch_pf_norm_quant(c->pf_x, c->out_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s);
+    if (e == cudaSuccess) e = pf_matmul(c, c->logits, c->lm_head, c->pf_xn, c->pf_xq, c->pf_xs, nullptr, n, false);
+    if (e == cudaSuccess) e = launch_pf_argmax(pick_dev, c->logits, n, c->V, s);
+    return e;
+  };
+  cudaGraphExec_t ge = nullptr;
+  auto it = c->bgraphs.find(key);
+  if (it != c->bgraphs.end()) {
+    ge = it->second;
+  } else {
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+      const cudaError_t e1 = enqueue();
+      e = cudaStreamEndCapture(s, &g);
+      if (e1 != cudaSuccess) e = e1;
+    }
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&ge, g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (e == cudaSuccess) {
+      c->bgraphs[key] = ge;
+    } else {
+      ge = nullptr;  // not capturable here: launch the kernels directly
+      cudaGetLastError();
+    }
   }
-  // final norm, lm_head, greedy pick per row (src/model.c:159-164, src/sample.c:28-32)
-  if (e == cudaSuccess) e = launch_pf_norm_quant(c->pf_x, c->out_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s);
-  if (e == cudaSuccess) e = pf_matmul(c, c->logits, c->lm_head, c->pf_xn, c->pf_xq, c->pf_xs, nullptr, n, false);
-  if (e == cudaSuccess) e = launch_pf_argmax(pick_dev, c->logits, n, c->V, s);
-  CK(e);
+  CK(cudaEventRecord(c->ev0, s));
+  if (ge) CK(cudaGraphLaunch(ge, s));
+  else CK(enqueue());
   CK(cudaEventRecord(c->ev1, s));
   CK(cudaMemcpyAsync(c->xb, c->pf_x, (size_t)n * D * 4, cudaMemcpyDeviceToDevice, s));
   if (argmax) CK(cudaMemcpyAsync(argmax, pick_dev, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
@@ -1425,15 +1466,22 @@ extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* p
   const int saved_pos = c->pos;
   CK(cudaMemcpyAsync(c->token_dev + TOKEN_SAVE, c->token_dev, 4, cudaMemcpyDeviceToDevice, c->stream));
   int r = 0;
+  float dev_ms = 0.f;  // the step launches' device time, summed
   for (int i = 0; i < n_seq && !r; i++) {
     c->pos = pos[i];
     c->h_pinned[0] = tokens[i];
     CK(cudaMemcpyAsync(c->token_dev, &c->h_pinned[0], 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaEventRecord(c->ev0, c->stream));
     r = run_steps(c, 1, 1, c->token_dev, 0, nullptr, 0, i);
     if (r) break;
+    CK(cudaEventRecord(c->ev1, c->stream));
     CK(cudaMemcpyAsync(&c->h_pinned[1], c->token_dev, 4, cudaMemcpyDeviceToHost, c->stream));
     if (logits) CK(cudaMemcpyAsync(c->logits_pinned, c->logits, (size_t)c->V * 4, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, c->ev0, c->ev1));
+    dev_ms += ms;
+    c->last_ms = dev_ms;
     r = check_flag(c);
     if (r) break;
     if (argmax) argmax[i] = c->h_pinned[1];
