@@ -16,6 +16,7 @@
 #include "hakm_internal.h"
 
 #include <algorithm>
+#include <array>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -198,6 +199,12 @@ struct hakmc_ctx {
   size_t pf_part_bytes = 0;
   float* pf_part6 = nullptr;  // Q6_K K-split partials, pf_part6_floats
   size_t pf_part6_floats = 0;
+  // dp4a batched Q4_K (short batches): one zeroed scratch region (partials,
+  // then tickets) per matrix shape, at pf_bscr + offset
+  void* pf_bscr = nullptr;
+  size_t pf_bscr_bytes = 0;
+  int pf_bscr_rows = 0;  // the batch the regions were sized for
+  std::vector<std::array<long long, 3>> pf_bscr_regions;  // {rows, cols, byte offset}
   int* row_io = nullptr;  // batched decode: [max_batch] tokens, positions, picks
   float* pf_apart = nullptr;  // batched decode: attention split partials, pf_apart_floats
   size_t pf_apart_floats = 0;
@@ -1041,8 +1048,12 @@ static int pf_ensure(hakmc_ctx* c, int rows) {
   return 0;
 }
 
+static bool use_tensor_cores(int n_out, int n_in, int n_batch);
+
 // out[M][W.rows] (+)= W x (+ bias) for the chunk's rows: Q4_K on the q8
-// codes (xq, xs), Q6_K on the fp32 rows xn. Accumulating Q4_K products go
+// codes (xq, xs) — the dp4a kernel for short batches of small matrices,
+// as hakmc_gemv_q4k_q8_batch routes them, else the tensor cores — and Q6_K
+// on the fp32 rows xn. Accumulating Q4_K products go
 // through pf_tmp, then one add (the reference's order: product, then +=).
 static cudaError_t pf_matmul(hakmc_ctx* c, float* out, const DevMat& W, const float* xn, const int8_t* xq,
                              const float* xs, const float* bias, int M, bool accumulate) {
@@ -1050,8 +1061,14 @@ static cudaError_t pf_matmul(hakmc_ctx* c, float* out, const DevMat& W, const fl
     return launch_pf_q6k_gemm(out, W.w, xn, bias, W.rows, W.cols, M, accumulate, c->pf_part6, c->pf_part6_floats,
                               c->pf_tmp, c->stream);
   float* dst = accumulate ? c->pf_tmp : out;
-  cudaError_t e = launch_q4k_mma(dst, W.w, xq, xs, bias, W.rows, W.cols, M, c->pf_part, c->err_flag, c->num_sms,
-                                 c->stream);
+  void* bscr = nullptr;  // this shape's dp4a region (sized for M rows)
+  if (!use_tensor_cores(W.rows, W.cols, M) && c->pf_bscr && c->pf_bscr_rows == M)
+    for (const auto& rg : c->pf_bscr_regions)
+      if (rg[0] == W.rows && rg[1] == W.cols) bscr = (char*)c->pf_bscr + rg[2];
+  cudaError_t e = bscr ? launch_q4k_batch(dst, W.w, xq, xs, bias, W.rows, W.cols, M, bscr, c->err_flag,
+                                          c->num_sms, c->stream)
+                       : launch_q4k_mma(dst, W.w, xq, xs, bias, W.rows, W.cols, M, c->pf_part, c->err_flag,
+                                        c->num_sms, c->stream);
   if (e != cudaSuccess || !accumulate) return e;
   return launch_pf_add(out, c->pf_tmp, (size_t)M * W.rows, c->stream);
 }
@@ -1060,15 +1077,42 @@ static cudaError_t pf_matmul(hakmc_ctx* c, float* out, const DevMat& W, const fl
 // and fp32-tile (Q6_K) ones.
 static int pf_ensure_part(hakmc_ctx* c, int M) {
   size_t need = 0, need6 = 0;
+  std::vector<std::array<long long, 3>> regions;
+  size_t needb = 0;
   auto add = [&](const DevMat& W) {
-    if (W.type == W_Q4K) need = std::max(need, q4k_mma_scratch_bytes(W.rows, W.cols, M, c->num_sms));
-    else need6 = std::max(need6, pf_q6k_part_floats(W.rows, W.cols, M));
+    if (W.type != W_Q4K) {
+      need6 = std::max(need6, pf_q6k_part_floats(W.rows, W.cols, M));
+    } else if (use_tensor_cores(W.rows, W.cols, M)) {
+      need = std::max(need, q4k_mma_scratch_bytes(W.rows, W.cols, M, c->num_sms));
+    } else {
+      for (const auto& rg : regions)
+        if (rg[0] == W.rows && rg[1] == W.cols) return;
+      regions.push_back({W.rows, W.cols, (long long)needb});
+      needb += (q4k_batch_scratch_bytes(W.rows, W.cols, M, c->num_sms) + 255) & ~(size_t)255;
+    }
   };
   for (int l = 0; l < c->run_layers; l++) {
     const DevLayer& y = c->layers[l];
     for (const DevMat* W : {&y.wqk, &y.wv, &y.wo, &y.wgu, &y.down}) add(*W);
   }
   add(c->lm_head);
+  // the dp4a regions are laid out for this M (a later call with another M
+  // re-lays them; the batched pass sizes them for its row count only)
+  if (needb && (c->pf_bscr_rows != M || needb > c->pf_bscr_bytes)) {
+    if (needb > c->pf_bscr_bytes) {
+      dfree(c, c->pf_bscr);
+      c->pf_bscr = nullptr;
+      c->pf_bscr_bytes = 0;
+      const int r = dalloc(c, &c->pf_bscr, needb);
+      if (r) return r;
+      c->pf_bscr_bytes = needb;
+    } else {
+      drop_bgraphs(c);  // graphs captured for the old layout
+    }
+    CK(cudaMemset(c->pf_bscr, 0, c->pf_bscr_bytes));  // tickets start at zero (each launch leaves them so)
+    c->pf_bscr_rows = M;
+    c->pf_bscr_regions = regions;
+  }
   if (need6 > c->pf_part6_floats) {
     dfree(c, c->pf_part6);
     c->pf_part6 = nullptr;
