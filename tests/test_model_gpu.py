@@ -366,6 +366,32 @@ def test_forward_batch_long_caches(cuda, small_path):
         assert _margin_ok(ref, int(am[i]), ref_am), i
 
 
+def test_forward_batch_repeated_calls(cuda, small_path):
+    """Two hundred consecutive batched steps of twelve sequences (the cached
+    graph replayed, positions past several attention tiles): every call
+    succeeds, picks are the logits' argmax, and a replay of the same calls
+    on a fresh context gives the same bits (deterministic)."""
+    n_seq, n_steps = 12, 200
+
+    def run():
+        out = []
+        with HakmCtx(small_path, max_seq=256, max_batch=n_seq) as ctx:
+            toks = [(37 * i + 3) % 4000 for i in range(n_seq)]
+            for p in range(n_steps):
+                logits, am = ctx.forward_batch(toks, [p] * n_seq, want_logits=(p % 50 == 49))
+                if logits is not None:
+                    assert all(int(am[i]) == int(np.argmax(logits[i])) for i in range(n_seq))
+                    out.append(logits.copy())
+                toks = [int(a) for a in am]
+        return out, toks
+
+    a, ta = run()
+    b, tb = run()
+    assert ta == tb
+    for x, y in zip(a, b):
+        assert np.array_equal(x.view(np.uint32), y.view(np.uint32))
+
+
 def test_forward_batch_small_batches_are_forward(cuda, small_path):
     """Batches below the batched pass's size take the step kernel per
     sequence, as hakm_forward: bit for bit (three sequences, then one)."""
