@@ -354,7 +354,7 @@ enum { PH_QKV = 0, PH_ATTN = 1, PH_WO = 2, PH_FFN = 3, PH_DOWN = 4, PH_LMHEAD = 
 static PhaseDesc make_phase(hakmc_ctx* c, int l, int ph, int n_split, bool timing, int seq = 0) {
   const size_t lstride = (size_t)c->max_seq * c->KV;
   DevLayer& y = c->layers[l < c->L ? l : 0];
-  // cache slot `seq` (the step program of a multi-sequence launch)
+  // cache slot `seq`
   float* kc = c->k_cache + ((size_t)seq * c->L + l) * lstride;
   float* vc = c->v_cache + ((size_t)seq * c->L + l) * lstride;
   PhaseDesc d = {};
