@@ -19,6 +19,9 @@ every step streams them from HBM.
   position, over the launch's device time.
 - cpu_baseline: the reference engine's own compiled decode (oracle/_ref) on
   this host's cores, on a bounded sample of the same workload.
+- prefill / batched_decode (one GPU; --no-next-rows skips them): short samples
+  of configs 4a and 4b on the 7B shapes, whose full lines come from
+  --workload prefill and --workload batch.
 
 N > 1 (torchrun): one tensor-parallel group over the N GPUs (hakmc_tp_*):
 every GEMV phase's rows split over all GPUs' CTAs, outputs all-gathered by
@@ -320,7 +323,7 @@ def config_block(args, world):
             "l2": "weights stream from HBM every step (2.03 GB > 126 MB L2)"}
 
 
-def run_prefill(args):
+def run_prefill(args, emit: bool = True):
     """Config 4a: a seeded 2048-id prompt through hakmc_prefill_batched (each
     call restarts the sequence, so every step is the whole prompt)."""
     from hako_b200 import HakmCtx, synth
@@ -355,11 +358,13 @@ def run_prefill(args):
             "e2e": {"value": args.steps * n / wall, "unit": "tok/s", "h2d_bytes_per_step": 4 * n,
                     "d2h_bytes_per_step": 4 * cfg.vocab},
             "per_position_prefill_tok_s": per_pos, "clocks": clk.summary()}
+    if not emit:
+        return line
     print(json.dumps(line), flush=True)
     return 0
 
 
-def run_batch(args):
+def run_batch(args, emit: bool = True):
     """Config 4b: 64 independent sequences, each with a 4096-position KV cache
     of seeded N(0, 1) values, decoded together (hakmc_forward_batch, one row
     per sequence); a step = one new token for every sequence. N > 1: each GPU
@@ -408,11 +413,29 @@ def run_batch(args):
             "e2e": {"value": world * n_seq * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8 * n_seq,
                     "d2h_bytes_per_step": 4 * n_seq},
             "clocks": clk.summary()}
+    if not emit:
+        return line
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.destroy_process_group()
     return 0
+
+
+def prefill_summary(steps: int, warmup: int, model: str = "7b"):
+    """Config 4a in brief for the decode line: run_prefill's measurement."""
+    ns = argparse.Namespace(model=model, steps=steps, warmup=warmup)
+    d = run_prefill(ns, emit=False)
+    return {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "steps", "per_position_prefill_tok_s")} | \
+        {"workload": d["config"]["workload"], "e2e_tok_s": d["e2e"]["value"]}
+
+
+def batch_summary(steps: int, warmup: int, model: str = "7b"):
+    """Config 4b in brief for the decode line (one GPU): run_batch's measurement."""
+    ns = argparse.Namespace(model=model, steps=steps, warmup=warmup, gpus=1)
+    d = run_batch(ns, emit=False)
+    return {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "steps")} | \
+        {"workload": d["config"]["workload"], "e2e_tok_s": d["e2e"]["value"]}
 
 
 def main():
@@ -427,6 +450,8 @@ def main():
                     help="decode: batch-1 greedy decode (the headline); prefill: config 4a; batch: config 4b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemv-sweep", action="store_true")
+    ap.add_argument("--no-next-rows", action="store_true",
+                    help="skip the short config 4a / 4b samples added to the decode line")
     ap.add_argument("--step-profile", action="store_true",
                     help="only a 4-id prompt, 2 generated ids, then two one-step hakmc_decode launches "
                          "(the last is the one a profiler captures: -k step_kernel -s 2 -c 1)")
@@ -531,6 +556,10 @@ def main():
     ctx.close()
     if rank == 0 and world == 1 and not args.no_gemv_sweep:
         line["gemv_sweep"] = gemv_sweep(device, pk["hbm_gbs"])
+    if rank == 0 and world == 1 and not args.no_next_rows:
+        # the survey's next rows, short samples (their own lines: --workload prefill / batch)
+        line["prefill"] = prefill_summary(steps=2, warmup=2)
+        line["batched_decode"] = batch_summary(steps=8, warmup=3)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if pg is not None:
