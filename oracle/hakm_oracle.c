@@ -2,12 +2,14 @@
  * hakm_oracle.c — CPU restatement of hako's quantized decode path.
  *
  * TEST INFRASTRUCTURE ONLY (see hakm_oracle.h). Written for clarity, not
- * speed: plain scalar C, strict IEEE (built without -ffast-math and with
- * -ffp-contract=off), single thread. Each function cites the reference
- * file:line whose behaviour it restates.
+ * speed: plain scalar C, single thread, built without -ffast-math and with
+ * -ffp-contract=off, so every rounding below is the one written: fused
+ * multiply-adds appear as fmaf() exactly where the reference's own build
+ * fuses them. Each function cites the reference file:line it restates.
  */
 #include "hakm_oracle.h"
 
+#include <immintrin.h>
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -150,7 +152,7 @@ void orc_quantize_q8_32(const float *x, int n, int8_t *xq, float *xs) {
 	}
 }
 
-/* src/quant.c:163-267 (scalar branch 260-266 is the plain statement). */
+/* src/quant.c:163-229 (the scalar branch, quant.c:214-221, is the plain statement). */
 void orc_q4k_subsums(const void *row, int n_in, const int8_t *xq,
                      int32_t *iqx, int32_t *ix) {
 	const uint8_t *b = (const uint8_t *)row;
@@ -171,7 +173,166 @@ void orc_q4k_subsums(const void *row, int n_in, const int8_t *xq,
 	}
 }
 
-/* src/quant.c:268-271: acc += xs * (d*s*iqx - dmin*m*ix), sub-blocks in order. */
+/* ------------------------------------------------- as-built fp32 orders
+ *
+ * The reference is built with -O3 -ffast-math -march=x86-64-v3 (its
+ * Makefile:8 flags, ARCH pinned by oracle/Makefile). gcc then fixes every
+ * floating-point rounding of the path: which products are fused (FMA), how
+ * the reductions are split over the 8 lanes of a 256-bit vector and folded,
+ * which libm / libmvec variant each exp/pow/cos/sin goes through, and that
+ * 1/sqrtf becomes rsqrtss plus one Newton step. The functions below restate
+ * those roundings one by one; tests/test_oracle.py pins each against the
+ * reference's own build (bit for bit), and the CUDA kernels follow the same
+ * steps. */
+
+static inline uint32_t fbits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float bitsf(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+static inline double bitsd(uint64_t u) { double d; memcpy(&d, &u, 8); return d; }
+static inline uint64_t dbits(double d) { uint64_t u; memcpy(&u, &d, 8); return u; }
+
+/* 8-lane reduction fold of a 256-bit accumulator (the vextractf128 / movhlps
+ * / shufps sequence gcc emits): ((a1+a5)+(a3+a7)) + ((a0+a4)+(a2+a6)). */
+static float fold8(const float a[8]) {
+	float s0 = a[0] + a[4], s1 = a[1] + a[5], s2 = a[2] + a[6], s3 = a[3] + a[7];
+	return (s0 + s2) + (s1 + s3);
+}
+static float fold4(const float u[4]) { return (u[0] + u[2]) + (u[1] + u[3]); }
+
+/* Σ a[i]·b[i] as gcc vectorizes `acc += a[i] * b[i]` under -ffast-math
+ * (src/nn.c:15 with a == b, src/nn.c:92, src/model.c:130): lane i%8 of the
+ * main loop accumulates the ROUNDED products (vmulps then vaddps, no FMA);
+ * the lanes fold to 4 (lo + hi); a remainder of 4..7 takes one 4-wide FMA
+ * step on those 4 lanes before they fold; the last 0..3 elements are scalar
+ * FMAs. n < 8 starts from the 4-wide step with zero lanes. */
+float orc_dot_f32(const float *a, const float *b, int n) {
+	float acc8[8] = {0, 0, 0, 0, 0, 0, 0, 0}, c4[4] = {0, 0, 0, 0}, sum = 0.0f;
+	int i = 0;
+	if (n >= 8) {
+		for (; i + 8 <= n; i += 8)
+			for (int l = 0; l < 8; l++) acc8[l] = acc8[l] + a[i + l] * b[i + l];
+		for (int l = 0; l < 4; l++) c4[l] = acc8[l] + acc8[l + 4];
+		sum = fold8(acc8);
+	}
+	if (n - i >= 4) {
+		for (int l = 0; l < 4; l++) c4[l] = fmaf(a[i + l], b[i + l], c4[l]);
+		sum = fold4(c4);
+		i += 4;
+	}
+	for (; i < n; i++) sum = fmaf(a[i], b[i], sum);
+	return sum;
+}
+
+/* rsqrtss, the approximate reciprocal square root gcc emits for 1/sqrtf under
+ * -ffast-math. Its result is fixed by the exponent's parity and the top 10
+ * mantissa bits; the 2048 results for [1, 4) are measured once from this
+ * host's instruction (orc_rsqrt_table) and the exponent is scaled by two per
+ * step of four. Positive normal inputs only (the reference's arguments). */
+static uint32_t RSQ[2048];
+static int rsq_ready;
+void orc_rsqrt_table(uint32_t *out) {
+	for (int par = 0; par < 2; par++)
+		for (int m = 0; m < 1024; m++) {
+			float x = bitsf(((uint32_t)(127 + par) << 23) | ((uint32_t)m << 13));
+			out[par * 1024 + m] = fbits(_mm_cvtss_f32(_mm_rsqrt_ss(_mm_set_ss(x))));
+		}
+}
+float orc_rsqrt_approx(float v) {
+	if (!rsq_ready) { orc_rsqrt_table(RSQ); rsq_ready = 1; }
+	uint32_t u = fbits(v);
+	int E = (int)(u >> 23) - 127, par = E & 1, k = (E - par) / 2;
+	uint32_t r = RSQ[par * 1024 + ((u >> 13) & 1023)];
+	return bitsf(r - ((uint32_t)k << 23));
+}
+/* 1/sqrtf(v) as built: r = rsqrtss(v); (-0.5 r) * fma(r, v r, -3). */
+float orc_rsqrt_nr(float v) {
+	float r = orc_rsqrt_approx(v);
+	float t = fmaf(r, v * r, -3.0f);
+	return (r * -0.5f) * t;
+}
+
+/* glibc's scalar expf (the FMA-built variant the host selects): the
+ * published exp2f table method, 2^(k/32) from a 32-entry table of doubles,
+ * a cubic in double, one rounding to float at the end. The table entries are
+ * 2^(i/32) rounded to double, stored minus i << 47 (the exponent bits that
+ * the index adds back). */
+static const double EXP_INVLN2N = 0x1.71547652b82fep+0 * 32, EXP_SHIFT = 0x1.8p+52;
+static const double EXP_C0 = 0x1.c6af84b912394p-5 / 32 / 32 / 32, EXP_C1 = 0x1.ebfce50fac4f3p-3 / 32 / 32,
+                    EXP_C2 = 0x1.62e42ff0c52d6p-1 / 32;
+static uint64_t EXP_T[32];
+static int exp_ready;
+static void exp_table(void) {
+	/* 2^(i/32) correctly rounded: long double (64-bit mantissa) exp2l,
+	 * rounded once more to double, agrees with the exact value here. */
+	for (int i = 0; i < 32; i++) EXP_T[i] = dbits((double)exp2l((long double)i / 32.0L)) - ((uint64_t)i << 47);
+	exp_ready = 1;
+}
+void orc_exp_table(uint64_t *out) {
+	if (!exp_ready) exp_table();
+	memcpy(out, EXP_T, sizeof EXP_T);
+}
+float orc_expf(float x) {
+	if (!exp_ready) exp_table();
+	uint32_t ax = fbits(x) & 0x7FFFFFFFu;
+	if (ax >= 0x42B00000u) {                  /* |x| >= 88, inf, nan */
+		if (fbits(x) == 0xFF800000u) return 0.0f;
+		if (ax >= 0x7F800000u) return x + x;
+		if (x > 0x1.62e42ep6f) return bitsf(0x7F800000u);
+		if (x < -0x1.9fe368p6f) return 0.0f;
+	}
+	double xd = (double)x, z = EXP_INVLN2N * xd;
+	double kd = z + EXP_SHIFT;
+	uint64_t ki = dbits(kd);
+	kd -= EXP_SHIFT;
+	double r = fma(EXP_INVLN2N, xd, -kd);
+	uint64_t t = EXP_T[ki % 32] + (ki << 47);
+	double s = bitsd(t);
+	double zz = fma(EXP_C0, r, EXP_C1), r2 = r * r, y = fma(EXP_C2, r, 1.0);
+	y = fma(zz, r2, y);
+	return (float)(y * s);
+}
+
+/* libmvec's vector expf (the 8-wide AVX2 and the 4-wide SSE4 entry points
+ * that -ffast-math vectorization calls): n = rint(x/ln2) by the 1.5*2^23
+ * shifter, r = x - n*ln2 in two parts, a degree-5 polynomial for e^r, times
+ * 2^n built in the exponent field. The AVX2 form fuses each step (FMA); the
+ * SSE4 form rounds every product and sum. Lanes with |x| > 87.3365 go to
+ * the scalar expf. */
+#define VX_INVLN2 0x3fb8aa3bu
+#define VX_SHIFT 0x4b400000u
+#define VX_LN2HI 0x3f317200u
+#define VX_LN2LO 0x35bfbe8eu
+#define VX_DOM 0x42aeac4fu
+static const uint32_t VX_P[6] = {0x3f800000u, 0x3f7ffffeu, 0x3effff34u, 0x3e2aacacu, 0x3d2b8392u, 0x3c07d9feu};
+float orc_expf_v8(float x) {
+	if ((fbits(x) & 0x7FFFFFFFu) > VX_DOM) return orc_expf(x);
+	float m = fmaf(x, bitsf(VX_INVLN2), bitsf(VX_SHIFT));
+	float n = m - bitsf(VX_SHIFT);
+	float r = fmaf(-n, bitsf(VX_LN2HI), x);
+	r = fmaf(-n, bitsf(VX_LN2LO), r);
+	float p = fmaf(bitsf(VX_P[5]), r, bitsf(VX_P[4]));
+	for (int k = 3; k >= 0; k--) p = fmaf(p, r, bitsf(VX_P[k]));
+	return p * bitsf((fbits(m) + 127u) << 23);
+}
+float orc_expf_v4(float x) {
+	if ((fbits(x) & 0x7FFFFFFFu) > VX_DOM) return orc_expf(x);
+	float m = x * bitsf(VX_INVLN2);
+	m = m + bitsf(VX_SHIFT);
+	float n = m - bitsf(VX_SHIFT);
+	float t = n * bitsf(VX_LN2HI);
+	float r = x - t;
+	t = n * bitsf(VX_LN2LO);
+	r = r - t;
+	float p = bitsf(VX_P[5]) * r;
+	for (int k = 4; k >= 0; k--) { p = p + bitsf(VX_P[k]); if (k) p = p * r; }
+	return p * bitsf((fbits(m) + 127u) << 23);
+}
+
+/* src/quant.c:150-232 (AVX2 branch, quant.c:193-213), as built: per pair of
+ * sub-blocks (A = 2g, B = 2g+1) of a super-block
+ *   tA = fma(sA, d*iqxA, -(mA*(dmin*ixA)))       (gcc reassociates d*s*iqx)
+ *   uA = tA * xsA
+ *   acc = acc + fma(tB, xsB, uA)                 (tB likewise)
+ * i.e. one rounded add into the running sum per 64 weights, in order. */
 float orc_q4k_dot(const void *row, int n_in, const int8_t *xq, const float *xs) {
 	const uint8_t *b = (const uint8_t *)row;
 	int nsb = n_in / 32;
@@ -180,63 +341,135 @@ float orc_q4k_dot(const void *row, int n_in, const int8_t *xq, const float *xs) 
 	float acc = 0.0f;
 	for (int i = 0; i < n_in / ORC_QK; i++, b += 144) {
 		float d = orc_f16_to_f32(rd16(b)), dmin = orc_f16_to_f32(rd16(b + 2));
-		for (int sb = 0; sb < 8; sb++) {
-			int s, m;
-			orc_scale_min_k4(sb, b + 4, &s, &m);
-			int k = 8 * i + sb;
-			acc += xs[k] * (d * (float)s * (float)iqx[k] - dmin * (float)m * (float)ix[k]);
+		for (int g = 0; g < 4; g++) {
+			int sa, ma, sb_, mb, ka = 8 * i + 2 * g, kb = ka + 1;
+			orc_scale_min_k4(2 * g, b + 4, &sa, &ma);
+			orc_scale_min_k4(2 * g + 1, b + 4, &sb_, &mb);
+			float tA = fmaf((float)sa, d * (float)iqx[ka], -((float)ma * (dmin * (float)ix[ka])));
+			float tB = fmaf((float)sb_, d * (float)iqx[kb], -((float)mb * (dmin * (float)ix[kb])));
+			float uA = tA * xs[ka];
+			acc = acc + fmaf(tB, xs[kb], uA);
 		}
 	}
 	free(iqx); free(ix);
 	return acc;
 }
 
-/* src/nn.c:113-123: dequantize the whole row, then accumulate w[i]*x[i] in order. */
+/* src/nn.c:84-95: dequantize the row (exact: d*sc*q has at most 24
+ * significant bits), then the vectorized float dot. */
 float orc_q6k_dot(const void *row, int n_in, const float *x) {
 	float *w = malloc(sizeof(float) * (size_t)n_in);
 	orc_dequant_q6k(row, w, n_in);
-	float acc = 0.0f;
-	for (int i = 0; i < n_in; i++) acc += w[i] * x[i];
+	float acc = orc_dot_f32(w, x, n_in);
 	free(w);
 	return acc;
 }
 
 /* ------------------------------------------------------------- nn ops */
 
-/* src/nn.c:13-18 */
+/* src/nn.c:13-18 as built: Σx² by orc_dot_f32; v = ss/n + eps (one IEEE
+ * division, one add); scale = the rsqrtss Newton step; y = (x*w)*scale. */
 void orc_rmsnorm(float *y, const float *x, const float *w, int n, float eps) {
-	float ss = 0.0f;
-	for (int i = 0; i < n; i++) ss += x[i] * x[i];
-	float r = 1.0f / sqrtf(ss / (float)n + eps);
-	for (int i = 0; i < n; i++) y[i] = x[i] * r * w[i];
+	float ss = orc_dot_f32(x, x, n);
+	float v = ss / (float)n + eps;
+	float scale = orc_rsqrt_nr(v);
+	for (int i = 0; i < n; i++) y[i] = (x[i] * w[i]) * scale;
 }
 
-/* src/nn.c:20-27 */
+/* src/nn.c:20-27 as built. exp(x - max) of element i goes through the 8-wide
+ * libmvec expf for the first 8*floor(n/8) elements, the 4-wide one for the
+ * next 4 when at least 4 remain, the scalar expf for the last 0..3; the sum
+ * follows the same split (8 lanes, folded to 4, one 4-lane step, folded,
+ * then scalar adds); then one reciprocal and a multiply. */
 void orc_softmax(float *x, int n) {
 	float mx = x[0];
 	for (int i = 1; i < n; i++) mx = x[i] > mx ? x[i] : mx;
-	float sum = 0.0f;
-	for (int i = 0; i < n; i++) { x[i] = expf(x[i] - mx); sum += x[i]; }
+	float acc8[8] = {0, 0, 0, 0, 0, 0, 0, 0}, c4[4] = {0, 0, 0, 0}, sum = 0.0f;
+	int i = 0;
+	if (n >= 8) {
+		for (; i + 8 <= n; i += 8)
+			for (int l = 0; l < 8; l++) {
+				x[i + l] = orc_expf_v8(x[i + l] - mx);
+				acc8[l] = acc8[l] + x[i + l];
+			}
+		for (int l = 0; l < 4; l++) c4[l] = acc8[l] + acc8[l + 4];
+		sum = fold8(acc8);
+	}
+	if (n - i >= 4) {
+		for (int l = 0; l < 4; l++) {
+			x[i + l] = orc_expf_v4(x[i + l] - mx);
+			c4[l] = x[i + l] + c4[l];
+		}
+		sum = fold4(c4);
+		i += 4;
+	}
+	for (; i < n; i++) {
+		x[i] = orc_expf(x[i] - mx);
+		sum = sum + x[i];
+	}
 	float inv = 1.0f / sum;
-	for (int i = 0; i < n; i++) x[i] *= inv;
+	for (int k = 0; k < n; k++) x[k] *= inv;
 }
 
-/* src/nn.c:29 */
-float orc_silu(float x) { return x / (1.0f + expf(-x)); }
+/* src/nn.c:29: x / (1 + expf(-x)) with the scalar expf (silu_f is called
+ * per element from src/model.c:154, not vectorized). */
+float orc_silu(float x) { return x / (1.0f + orc_expf(-x)); }
 
-/* src/nn.c:32-42: pairs (i, i + hd/2), freq = theta^(-2i/hd), angle pos*freq. */
+/* src/nn.c:32-42 as built. The loop over pairs is vectorized 8 wide:
+ * freq = powf(theta, 2i * (-1/hd)) and cos/sin of pos*freq through the
+ * libmvec vector functions (4-wide ones for a 4-pair remainder, scalar libm
+ * for the last 0..3 pairs, and for all pairs when there are fewer than 8);
+ * then a' = fma(a, c, -(b*s)), b' = fma(a, s, b*c).
+ * orc_rope_table gives the (cos, sin) pairs of one position; both are test
+ * helpers that call the host's libm/libmvec, as the reference does. */
+__m256 _ZGVdN8vv_powf(__m256, __m256);
+__m256 _ZGVdN8v_cosf(__m256);
+__m256 _ZGVdN8v_sinf(__m256);
+__m128 _ZGVbN4vv_powf(__m128, __m128);
+__m128 _ZGVbN4v_cosf(__m128);
+__m128 _ZGVbN4v_sinf(__m128);
+void orc_rope_table(float *cs, int head_dim, int pos, float theta) {
+	int half = head_dim / 2, i = 0;
+	float nhd = -1.0f / (float)head_dim, fp = (float)pos;
+	/* below 8 pairs the two halves of vec overlap within one vector, and
+	 * gcc's alias check sends the whole loop down the scalar path */
+	if (half < 8) goto scalar;
+	for (; i + 8 <= half; i += 8) {
+		float e[8], c[8], s[8];
+		for (int l = 0; l < 8; l++) e[l] = (float)(2 * (i + l)) * nhd;
+		__m256 fr = _ZGVdN8vv_powf(_mm256_set1_ps(theta), _mm256_loadu_ps(e));
+		__m256 ang = _mm256_mul_ps(fr, _mm256_set1_ps(fp));
+		_mm256_storeu_ps(c, _ZGVdN8v_cosf(ang));
+		_mm256_storeu_ps(s, _ZGVdN8v_sinf(ang));
+		for (int l = 0; l < 8; l++) { cs[2 * (i + l)] = c[l]; cs[2 * (i + l) + 1] = s[l]; }
+	}
+	if (half - i >= 4) {
+		float e[4], c[4], s[4];
+		for (int l = 0; l < 4; l++) e[l] = (float)(2 * (i + l)) * nhd;
+		__m128 fr = _ZGVbN4vv_powf(_mm_set1_ps(theta), _mm_loadu_ps(e));
+		__m128 ang = _mm_mul_ps(fr, _mm_set1_ps(fp));
+		_mm_storeu_ps(c, _ZGVbN4v_cosf(ang));
+		_mm_storeu_ps(s, _ZGVbN4v_sinf(ang));
+		for (int l = 0; l < 4; l++) { cs[2 * (i + l)] = c[l]; cs[2 * (i + l) + 1] = s[l]; }
+		i += 4;
+	}
+scalar:
+	for (; i < half; i++) {
+		float ang = fp * powf(theta, (float)(2 * i) * nhd);
+		cs[2 * i] = cosf(ang);
+		cs[2 * i + 1] = sinf(ang);
+	}
+}
 void orc_rope_neox(float *vec, int head_dim, int pos, float theta) {
 	int half = head_dim / 2;
+	float *cs = malloc(sizeof(float) * 2 * (size_t)half);
+	orc_rope_table(cs, head_dim, pos, theta);
 	for (int i = 0; i < half; i++) {
-		float freq = powf(theta, -((float)(2 * i) / (float)head_dim));
-		float ang = (float)pos * freq;
-		float c = cosf(ang), s = sinf(ang);
-		float a = vec[i], b = vec[i + half];
-		/* the roundings of the reference as built (-ffast-math with FMA):
-		 * the b products rounded on their own, the a products fused */
+		float c = cs[2 * i], s = cs[2 * i + 1], a = vec[i], b = vec[i + half];
 		vec[i] = fmaf(a, c, -(b * s));
 		vec[i + half] = fmaf(a, s, b * c);
 	}
+	free(cs);
 }
 
 /* MLF2 tensor types (include/mlf2.h:44-49). */
@@ -283,8 +516,7 @@ int orc_matmul(float *out, const float *x, int type, const void *w,
 	float *tmp = malloc(sizeof(float) * (size_t)n_in);
 	for (int r = 0; r < n_out; r++) {
 		orc_dequant_row(type, base + (size_t)r * rb, tmp, n_in);
-		float acc = 0.0f;
-		for (int i = 0; i < n_in; i++) acc += tmp[i] * x[i];
+		float acc = orc_dot_f32(tmp, x, n_in);
 		out[r] = bias ? acc + bias[r] : acc;
 	}
 	free(tmp);
@@ -405,7 +637,7 @@ const float *orc_forward(orc_model *m, int token) {
 	int D = m->D, H = m->H, KVH = m->KVH, hd = m->hd, KV = KVH * hd, F = m->F, pos = m->pos;
 	if (pos >= m->max_seq || token < 0 || token >= m->V) return NULL;
 	int group = H / KVH;
-	float scale = 1.0f / sqrtf((float)hd);
+	float scale = orc_rsqrt_nr((float)hd);   /* 1.0f / sqrtf(hd) as built */
 	orc_dequant_row(m->tok_embd.type,
 	                m->tok_embd.data + (size_t)token * orc_row_bytes(m->tok_embd.type, D), m->xb, D);
 	for (int l = 0; l < m->run_layers; l++) {
@@ -425,15 +657,13 @@ const float *orc_forward(orc_model *m, int token) {
 			const float *qh = m->q + h * hd;
 			for (int s = 0; s <= pos; s++) {
 				const float *ks = kc + (size_t)s * KV + kh * hd;
-				float dot = 0.0f;
-				for (int d = 0; d < hd; d++) dot += qh[d] * ks[d];
-				m->scores[s] = dot * scale;
+				m->scores[s] = orc_dot_f32(qh, ks, hd) * scale;
 			}
 			orc_softmax(m->scores, pos + 1);
 			float *o = m->att + h * hd;
 			for (int s = 0; s <= pos; s++) {
 				const float *vs = vc + (size_t)s * KV + kh * hd;
-				for (int d = 0; d < hd; d++) o[d] += m->scores[s] * vs[d];
+				for (int d = 0; d < hd; d++) o[d] = fmaf(m->scores[s], vs[d], o[d]);
 			}
 		}
 		orc_matmul(m->xn, m->att, y->wo.type, y->wo.data, NULL, D, D);
@@ -458,4 +688,30 @@ int orc_argmax(const float *logits, int n) {
 	int best = 0;
 	for (int i = 1; i < n; i++) if (logits[i] > logits[best]) best = i;
 	return best;
+}
+
+/* ------------------------------------------------- pins of the libm steps */
+
+/* Counts inputs in [lo, hi] (float bit patterns, every step-th) where the
+ * restatements above differ from what the host's libm / libmvec / rsqrtss
+ * return: out[0] scalar expf, out[1] 8-wide expf, out[2] 4-wide expf,
+ * out[3] rsqrtss (positive normal inputs only). */
+__m256 _ZGVdN8v_expf(__m256);
+__m128 _ZGVbN4v_expf(__m128);
+void orc_check_libm(uint32_t lo, uint32_t hi, uint32_t step, long long *out) {
+	out[0] = out[1] = out[2] = out[3] = 0;
+	for (uint64_t u = lo; u <= hi; u += step) {
+		float x = bitsf((uint32_t)u);
+		float e8[8], e4[4];
+		_mm256_storeu_ps(e8, _ZGVdN8v_expf(_mm256_set1_ps(x)));
+		_mm_storeu_ps(e4, _ZGVbN4v_expf(_mm_set1_ps(x)));
+		if (!isnan(x)) {
+			out[0] += fbits(expf(x)) != fbits(orc_expf(x));
+			out[1] += fbits(e8[0]) != fbits(orc_expf_v8(x));
+			out[2] += fbits(e4[0]) != fbits(orc_expf_v4(x));
+		}
+		uint32_t a = (uint32_t)u;
+		if (a >= 0x00800000u && a < 0x7F800000u)
+			out[3] += fbits(_mm_cvtss_f32(_mm_rsqrt_ss(_mm_set_ss(x)))) != fbits(orc_rsqrt_approx(x));
+	}
 }

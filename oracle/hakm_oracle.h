@@ -39,13 +39,34 @@ void orc_dequant_q6k(const void *blocks, float *out, int nelem);
 void orc_quantize_q8_32(const float *x, int n, int8_t *xq, float *xs);
 
 /* Exact per-32 sub-block integer sums of one Q4_K row against xq:
- * iqx[sb] = sum(q * xq), ix[sb] = sum(xq) (src/quant.c:163-267). */
+ * iqx[sb] = sum(q * xq), ix[sb] = sum(xq) (src/quant.c:163-229). */
 void orc_q4k_subsums(const void *row, int n_in, const int8_t *xq,
                      int32_t *iqx, int32_t *ix);
-/* One Q4_K row . q8 activation (src/quant.c:150-232). */
+/* One Q4_K row . q8 activation (src/quant.c:150-232), in the as-built
+ * rounding order (one rounded add per pair of sub-blocks). */
 float orc_q4k_dot(const void *row, int n_in, const int8_t *xq, const float *xs);
-/* One Q6_K row . fp32 activation: dequantize then float dot (src/nn.c:113-123). */
+/* One Q6_K row . fp32 activation: dequantize then float dot (src/nn.c:84-95). */
 float orc_q6k_dot(const void *row, int n_in, const float *x);
+
+/* The as-built fp32 building blocks (-O3 -ffast-math -march=x86-64-v3):
+ *  orc_dot_f32      the vectorized `acc += a[i]*b[i]` (src/nn.c:15,92, src/model.c:130)
+ *  orc_rsqrt_table  rsqrtss on [1,4): 2 x 1024 results of this host's instruction
+ *  orc_rsqrt_approx rsqrtss from that table; orc_rsqrt_nr: 1.0f/sqrtf as built
+ *  orc_expf         glibc's scalar expf; orc_exp_table its 32 table words
+ *  orc_expf_v8/_v4  libmvec's 8-wide (AVX2) and 4-wide (SSE4) vector expf
+ *  orc_rope_table   (cos, sin) of one position's RoPE pairs, as rope_neox computes them */
+float orc_dot_f32(const float *a, const float *b, int n);
+void  orc_rsqrt_table(uint32_t *out);
+float orc_rsqrt_approx(float v);
+float orc_rsqrt_nr(float v);
+float orc_expf(float x);
+void  orc_exp_table(uint64_t *out);
+float orc_expf_v8(float x);
+float orc_expf_v4(float x);
+void  orc_rope_table(float *cs, int head_dim, int pos, float theta);
+/* Mismatch counts of the restated expf / vector expf / rsqrtss against the
+ * host libraries over [lo, hi] by step (out[4]); a test-side pin. */
+void  orc_check_libm(uint32_t lo, uint32_t hi, uint32_t step, long long *out);
 
 /* src/nn.c:13-18, 20-27, 29, 32-42 */
 void  orc_rmsnorm(float *y, const float *x, const float *w, int n, float eps);

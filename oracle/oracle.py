@@ -20,7 +20,8 @@ ORACLE_SO = os.path.join(HERE, "_build", "libhakm_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "libhakm_ref.so")
 REF_CLI = os.path.join(HERE, "_ref", "hakm")
 DROPIN_CLI = os.path.join(HERE, "_ref", "hakm_cuda")  # the same CLI over the CUDA drop-in
-REF_SRC = os.environ.get("HAKM_REF_SRC", "/root/reference")
+# the reference checkout: HAKM_REF_SRC, by default one beside this repository
+REF_SRC = os.environ.get("HAKM_REF_SRC", os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 _vp, _i, _f = C.c_void_p, C.c_int, C.c_float
 
