@@ -63,16 +63,49 @@ def prompt_ids(model: str):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock, power and clock-event (throttle) reasons sampled during the
+    timed region: an NVML polling thread (about one sample per millisecond,
+    so even a region of a few tens of milliseconds gets many samples), with
+    nvidia-smi as the fallback when NVML is unavailable."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits
+    BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.p = None
+        self.rows = []
+        self.nv = None
+        self.out = ""
+
+    def _poll(self):
+        nv, h = self.nv, self.h
+        while not self.stop:
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.rows.append((float(sm), int(rs)))
+            except Exception:
+                pass
+            time.sleep(0.001)
 
     def __enter__(self):
+        self.stop = False
+        try:
+            import threading
+            import pynvml as nv
+            nv.nvmlInit()
+            self.h = nv.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+            self.nv = nv
+            self.th = threading.Thread(target=self._poll, daemon=True)
+            self.th.start()
+            time.sleep(0.003)  # first samples in before the region starts
+            return self
+        except Exception:
+            self.nv = None
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                        "-lms", "100", "-i", str(self.idx)],
@@ -82,7 +115,10 @@ class ClockSampler:
         return self
 
     def __exit__(self, *a):
-        self.out = ""
+        if self.nv is not None:
+            self.stop = True
+            self.th.join(timeout=2)
+            return
         if self.p:
             self.p.terminate()
             try:
@@ -92,6 +128,13 @@ class ClockSampler:
                 self.out = ""
 
     def summary(self):
+        if self.nv is not None and self.rows:
+            sm = [r[0] for r in self.rows]
+            mx = self.max_mhz
+            reasons = sorted({n for r in self.rows for n, b in self.BITS.items() if r[1] & b})
+            loaded = [x for x in sm if x > 0.5 * mx] or sm
+            return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
+                    "samples": len(self.rows), "source": "nvml"}
         rows = [r.split(",") for r in self.out.strip().splitlines() if r.count(",") >= 8]
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
@@ -101,7 +144,7 @@ class ClockSampler:
         reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip().lower() == "active"})
         loaded = [s for s in sm if s > 0.5 * mx] or sm
         return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows)}
+                "samples": len(rows), "source": "nvidia-smi"}
 
 
 def dist_setup(n_gpus: int):
@@ -156,9 +199,11 @@ def run_reference_arm(args):
     world, rank, local, pg = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0, None
     if rank != 0:
         return 0
+    # the model file through the stand-alone writer: this process maps no
+    # library of the package, only the reference's own build (oracle/_ref)
     from hako_b200 import synth
     cfg = synth.PRESETS[args.model]
-    path = synth.cached_model(cfg)
+    path = synth.cached_model(cfg, via_exe=True)
     max_seq = len(prompt_ids(args.model)) + args.warmup + args.steps + 8
     cores = min(os.cpu_count() or 1, 16)
     os.environ["HAKM_THREADS"] = str(cores)
@@ -182,9 +227,25 @@ def run_reference_arm(args):
             "config": config_block(args, world),
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
                              "sample": f"{args.steps} greedy decode steps after a {len(prompt_ids(args.model))}-id prompt"},
-            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "libraries_mapped": repo_libraries_mapped()}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def repo_libraries_mapped():
+    """Shared libraries under this repository that this process has mapped
+    (the reference arm must show only oracle/_ref's build of the reference)."""
+    seen = set()
+    try:
+        with open("/proc/self/maps") as f:
+            for ln in f:
+                p = ln.split()[-1] if ln.strip() else ""
+                if p.startswith(ROOT) and ".so" in os.path.basename(p):
+                    seen.add(os.path.relpath(p, ROOT))
+    except OSError:
+        pass
+    return sorted(seen)
 
 
 GEMV_SHAPES = [(2048, 2048), (256, 2048), (11008, 2048), (2048, 11008), (18944, 3584), (3584, 18944)]

@@ -19,8 +19,11 @@ ROOT = os.path.dirname(HERE)
 
 CUDA_SOURCES = ["csrc/hakm_stream.cu", "csrc/hakm_step.cu", "csrc/hakm_kernels.cu", "csrc/hakm_batch.cu",
                 "csrc/hakm_mma.cu", "csrc/hakm_prefill.cu", "csrc/hakm_runtime.cu"]
-CUDA_HEADERS = ["csrc/hakm_internal.h", "csrc/hakm_device.cuh", "csrc/hakm_gemv.cuh", "csrc/hakm_attn.cuh", "csrc/hakm_tmap.h",
-                "../include/hakm_cuda.h"]
+CUDA_HEADERS = ["csrc/hakm_internal.h", "csrc/hakm_device.cuh", "csrc/hakm_exact.cuh", "csrc/hakm_gemv.cuh",
+                "csrc/hakm_attn.cuh", "csrc/hakm_ll.cuh", "csrc/hakm_tmap.h", "../include/hakm_cuda.h"]
+# host tables that carry glibc's vector libm roundings: gcc with AVX2 + FMA
+# (the vector entry points' calling convention), no contraction
+HOST_C = "csrc/hakm_hostmath.c"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -47,11 +50,14 @@ def _run(cmd: list[str]) -> None:
 
 def build_cuda(force: bool = False, verbose_ptxas: bool = False) -> str:
     out = os.path.join(LIB, "libhakm_cuda.so")
-    deps = [os.path.join(HERE, s) for s in CUDA_SOURCES + CUDA_HEADERS]
+    deps = [os.path.join(HERE, s) for s in CUDA_SOURCES + CUDA_HEADERS + [HOST_C]]
     if force or _stale(out, deps):
         os.makedirs(LIB, exist_ok=True)
+        host_o = os.path.join(LIB, "hakm_hostmath.o")
+        _run(["gcc", "-O2", "-std=c11", "-Wall", "-fPIC", "-mavx2", "-mfma", "-ffp-contract=off", "-c",
+              "-o", host_o, HOST_C])
         cmd = [_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2",
-               "-shared", "-cudart", "static", "-o", out, *CUDA_SOURCES]
+               "-shared", "-cudart", "static", "-o", out, *CUDA_SOURCES, host_o, "-lmvec", "-lm"]
         if verbose_ptxas:
             cmd.insert(1, "-Xptxas=-v")
         _run(cmd)
@@ -60,10 +66,14 @@ def build_cuda(force: bool = False, verbose_ptxas: bool = False) -> str:
 
 def build_synth(force: bool = False) -> str:
     out = os.path.join(LIB, "libhakm_synth.so")
+    exe = os.path.join(LIB, "hakm_synth")
     src = os.path.join(HERE, "synth", "mlf2_synth.c")
     if force or _stale(out, [src]):
         os.makedirs(LIB, exist_ok=True)
         _run(["gcc", "-O2", "-std=c11", "-Wall", "-fPIC", "-shared", "-o", out, src, "-lm", "-lpthread"])
+    if force or _stale(exe, [src]):
+        os.makedirs(LIB, exist_ok=True)
+        _run(["gcc", "-O2", "-std=gnu11", "-Wall", "-DSYNTH_MAIN", "-o", exe, src, "-lm", "-lpthread"])
     return out
 
 

@@ -83,11 +83,12 @@ __device__ __forceinline__ float q6k_dequant_packed(const uint8_t* row, int nb, 
   const uint16_t dh = (uint16_t)(chunk[m * Q6K_BODY + 2 * j] | (chunk[m * Q6K_BODY + 2 * j + 1] << 8));
   const float d = __half2float(__ushort_as_half(dh));
   const int nh = i >> 7, k = (i >> 5) & 3, l = i & 31;
-  const int lb = body[64 * nh + 32 * (k & 1) + l];
+  // verbatim ql[64nh + 32(k&1) + l] and qh[32nh + l], at their device places
+  const int lb = body[q6k_body_pos(64 * nh + 32 * (k & 1) + l)];
   const int nib = k < 2 ? (lb & 15) : (lb >> 4);
-  const int hb = (body[128 + 32 * nh + l] >> (2 * k)) & 3;
+  const int hb = (body[q6k_body_pos(128 + 32 * nh + l)] >> (2 * k)) & 3;
   const int q = (nib | (hb << 4)) - 32;
-  // the reference's order: (d * sc) * q (src/quant.c:104-107), two roundings
+  // d * sc * q is exact in fp32 (src/quant.c:104-107)
   return __fmul_rn(__fmul_rn(d, (float)(int8_t)body[192 + (i >> 4)]), (float)q);
 }
 

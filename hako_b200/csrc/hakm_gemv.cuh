@@ -1,13 +1,15 @@
 // hakm_gemv.cuh — device building blocks of the streaming GEMV phases, shared
 // by the per-phase kernel (hakm_stream.cu) and the persistent decode-step
 // kernel (hakm_step.cu): bulk-copy / mbarrier helpers, per-CTA row schedule,
-// the activation prologue (rmsnorm, int8 q8_32 codes, fixed-point limbs), the
-// Q4_K and Q6_K 4-row units and the fused epilogues.
+// the activation prologue (rmsnorm, int8 q8_32 codes, the fp32 activation by
+// lane class), the Q4_K and Q6_K units and the fused epilogues, all with the
+// reference's own roundings (hakm_exact.cuh).
 //
 // Activations produced by other SMs earlier in the same kernel are read with
 // L2-coherent loads (__ldcg): L1 is not coherent across SMs.
 #pragma once
 #include "hakm_device.cuh"
+#include "hakm_exact.cuh"
 
 namespace hakm {
 
@@ -24,6 +26,10 @@ constexpr int SMEM_HEADER = 256;  // full[MAX_STAGES] and empty[MAX_STAGES] mbar
 constexpr long long WAIT_LIMIT = 4000000000LL;  // ~2 s of SM clock
 constexpr int BAR_CONSUMERS = 1;
 constexpr int RMS_SLOTS = 2;  // 8-element slots per consumer thread in the rmsnorm prologue
+// Per-warp shared scratch of the units (Q4_K: 4 x 36 floats of pair values
+// being handed to the row chains; Q6_K: 4 rows x 16 (d*sc, d*sc) pairs).
+constexpr int WARP_SCRATCH_FLOATS = 160;
+constexpr int WARP_SCRATCH_BYTES = CONSUMER_WARPS * WARP_SCRATCH_FLOATS * 4;
 
 // ------------------------------------------------------------------ PTX
 
@@ -100,16 +106,19 @@ __device__ __forceinline__ void consumers_sync() {
 
 // ------------------------------------------------------------------ schedule
 
-// Limb planes of the Q6_K activation: 64 bytes of padding after every 128
-// elements (see struct Act).
-__host__ __device__ inline size_t limb_plane_bytes(int K) { return (size_t)K + (size_t)K / 2; }
-__device__ __forceinline__ int limb_pos(int e) { return e + 64 * (e >> 7); }
+// The fp32 activation "by lane class": xc[l * cls_pitch(K) + t] = x[8t + l],
+// the element order in which the reference's vectorized Q6_K dot feeds lane
+// l of its accumulator (src/nn.c:92). The pitch is padded by 4 floats so the
+// 8 classes' 16-byte reads of a warp fall in distinct banks.
+__host__ __device__ inline int cls_pitch(int K) { return K / 8 + 4; }
 
-// Shared-memory bytes of the activation for an n_in of K.
-__host__ __device__ inline size_t act_bytes(int K, bool q8, bool q6) {
+// Shared-memory bytes of the activation for an n_in of K: the int8 codes,
+// scales and code sums of q8_32 (Q4_K rows), and the fp32 activation by lane
+// class (Q6_K rows; an rmsnorm prologue also keeps its squares there).
+__host__ __device__ inline size_t act_bytes(int K, bool q8, bool f32) {
   size_t b = 0;
+  if (f32) b += (size_t)8 * cls_pitch(K) * 4;
   if (q8) b += (size_t)K + (size_t)(K / 32) * 8;
-  if (q6) b += 3 * limb_plane_bytes(K) + (size_t)(K / 16) * 8;
   return b;
 }
 
@@ -122,7 +131,7 @@ __host__ __device__ inline int stage_rows(int type, int nb) {
   const size_t rb = dev_row_bytes(type, nb);
   // long rows: up to twice the target, but two stages must fit beside the
   // activation (fp32 + int8 copies, scales) in the shared-memory budget
-  const size_t act = act_bytes(nb * QK, true, true) + 8192;
+  const size_t act = act_bytes(nb * QK, true, true) + 8192 + WARP_SCRATCH_BYTES;
   size_t target = STAGE_TARGET;
   if (phase_groups(nb) == 1) {
     const size_t two = ((size_t)PHASE_BUDGET - act) / 2;
@@ -144,12 +153,12 @@ __host__ __device__ inline int stage_rows_for(int type, int nb, int slot_bytes) 
 
 // This CTA's rows of segment s: the segment's 4-row groups split evenly over
 // the grid, each segment's split rotated by the groups before it so the
-// remainders of consecutive segments land on different CTAs.
+// remainders of consecutive segments land on different CTAs. One result per
+// row (nch = 1): a unit runs whole rows, every chunk, in order.
 // 32-bit arithmetic throughout (groups * grid < 2^31): this runs in every
 // CTA at the start of every phase, on the critical path.
 __device__ __forceinline__ void cta_ranges(const PhaseParams& p, SegRange* sr) {
   const unsigned grid = gridDim.x, cta = blockIdx.x;
-  const int nb = p.n_in / QK;
   unsigned goff = 0;
   int pbase = 0;
   for (int s = 0; s < p.n_seg; s++) {
@@ -159,55 +168,34 @@ __device__ __forceinline__ void cta_ranges(const PhaseParams& p, SegRange* sr) {
     const int g0 = (int)(idx * G / grid), g1 = (int)((idx + 1) * G / grid);
     sr[s].row0 = 4 * g0;
     sr[s].row1 = min(4 * g1, n);
-    sr[s].nch = n_chunks(nb);
+    sr[s].nch = 1;
     sr[s].part_base = pbase;
-    pbase += (sr[s].row1 - sr[s].row0) * sr[s].nch;
+    pbase += sr[s].row1 - sr[s].row0;
     goff += G;
   }
 }
 
 // ------------------------------------------------------------------ prologue
 
-static __device__ float consumers_sum(float v, float* red) {
-  const int cl = threadIdx.x - 32, lane = cl & 31, w = cl >> 5;
-  v = warp_sum(v);
-  consumers_sync();
-  if (lane == 0) red[w] = v;
-  consumers_sync();
-  float t = lane < CONSUMER_WARPS ? red[lane] : 0.f;
-  return warp_sum(t);
-}
-
 // The activation in shared memory, in the two forms the row types consume:
-//  q8    (Q4_K rows): per-32 int8 codes xq, scales xs and code sums xsum —
-//        quantize_row_q8_32 as the reference builds it (src/quant.c:127-144).
-//  limbs (Q6_K rows): each 16-element group as exact 23-bit fixed point
-//        relative to its largest element, X = rint(x * 2^(22-E)), split into
-//        bytes X = X2*2^16 + X1*2^8 + X0 (X0, X1 unsigned, X2 signed) so the
-//        fp32-activation dot of the generic path (src/nn.c:84-95) becomes
-//        three int8 dot products; lp[g] = (32 * sum(X), 2^(E-22)). Planes
-//        put 64 bytes of padding after every 128 elements, which makes the
-//        lanes' 16-byte reads bank-conflict free.
+//  q8 (Q4_K rows): per-32 int8 codes xq, scales xs and code sums xsum —
+//     quantize_row_q8_32 as the reference builds it (src/quant.c:127-144).
+//  xc (Q6_K rows): the fp32 activation by lane class (cls_pitch).
 struct Act {
   int8_t* xq;
   float* xs;
   int* xsum;
-  uint8_t* l0;
-  uint8_t* l1;
-  uint8_t* l2;
-  float2* lp;
+  float* xc;
+  int cp;  // class pitch (floats)
 };
 
-
-__device__ __forceinline__ Act carve_act(uint8_t* base, int K, bool q8, bool q6) {
+__device__ __forceinline__ Act carve_act(uint8_t* base, int K, bool q8, bool f32) {
   Act a = {};
   uint8_t* p = base;
-  if (q6) {
-    a.lp = reinterpret_cast<float2*>(p);
-    p += (size_t)(K / 16) * 8;
-    a.l0 = p; p += limb_plane_bytes(K);
-    a.l1 = p; p += limb_plane_bytes(K);
-    a.l2 = p; p += limb_plane_bytes(K);
+  a.cp = cls_pitch(K);
+  if (f32) {
+    a.xc = reinterpret_cast<float*>(p);
+    p += (size_t)8 * a.cp * 4;
   }
   if (q8) {
     a.xs = reinterpret_cast<float*>(p);
@@ -219,46 +207,25 @@ __device__ __forceinline__ Act carve_act(uint8_t* base, int K, bool q8, bool q6)
   return a;
 }
 
-// 8-element slot s (elements [8s, 8s+8)). For q8 the 4 slots of a 32-block
-// are 4 adjacent lanes, for limbs the 2 slots of a 16-group 2 adjacent lanes,
-// so block and group reductions are one or two shuffles.
+// 8-element slot s (elements [8s, 8s+8)): element 8s + i is position s of
+// class i. For q8 the 4 slots of a 32-block are 4 adjacent lanes, so the
+// block reductions are two shuffles.
 __device__ __forceinline__ void store_slot(const PhaseParams& p, int s, bool live, const float v[8], const Act& A) {
-  float amax8 = 0.f;
+  if (p.need_q6 && live) {
 #pragma unroll
-  for (int i = 0; i < 8; i++) amax8 = fmaxf(amax8, fabsf(v[i]));
-  if (p.need_q6) {
-    const float amax = fmaxf(amax8, __shfl_xor_sync(0xffffffffu, amax8, 1));
-    const uint32_t e = (__float_as_uint(amax) >> 23) & 0xFF;
-    const bool ok = e >= 22 && e < 255;  // groups below 2^-105 contribute nothing
-    const float f = ok ? __uint_as_float((275u - e) << 23) : 0.f;       // 2^(22-E)
-    const float invf = ok ? __uint_as_float((e - 21u) << 23) : 0.f;     // 2^(E-22)
-    uint32_t w0[2] = {0, 0}, w1[2] = {0, 0}, w2[2] = {0, 0};
-    int xsum16 = 0;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-      const int X = __float2int_rn(v[i] * f);  // exact scaling, |X| <= 2^22
-      xsum16 += X;
-      w0[i >> 2] |= (uint32_t)(X & 255) << (8 * (i & 3));
-      w1[i >> 2] |= (uint32_t)((X >> 8) & 255) << (8 * (i & 3));
-      w2[i >> 2] |= (uint32_t)((X >> 16) & 255) << (8 * (i & 3));
-    }
-    xsum16 += __shfl_xor_sync(0xffffffffu, xsum16, 1);
-    if (live) {
-      const int pos = limb_pos(8 * s);
-      *reinterpret_cast<uint2*>(A.l0 + pos) = make_uint2(w0[0], w0[1]);
-      *reinterpret_cast<uint2*>(A.l1 + pos) = make_uint2(w1[0], w1[1]);
-      *reinterpret_cast<uint2*>(A.l2 + pos) = make_uint2(w2[0], w2[1]);
-      if ((s & 1) == 0) A.lp[s >> 1] = make_float2(32.0f * (float)xsum16, invf);
-    }
+    for (int i = 0; i < 8; i++) A.xc[i * A.cp + s] = v[i];
   }
   if (p.need_q8) {
+    float amax8 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) amax8 = fmaxf(amax8, fabsf(v[i]));
     float amax = fmaxf(amax8, __shfl_xor_sync(0xffffffffu, amax8, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    const float sc = amax * (1.0f / 127.0f);
+    const float sc = __fmul_rn(amax, 1.0f / 127.0f);
     const float inv = q8_inv(amax, sc);
     int q[8], sum = 0;
 #pragma unroll
-    for (int i = 0; i < 8; i++) { q[i] = q8_round(v[i] * inv); sum += q[i]; }
+    for (int i = 0; i < 8; i++) { q[i] = q8_round(__fmul_rn(v[i], inv)); sum += q[i]; }
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
     if (live) {
@@ -273,9 +240,29 @@ __device__ __forceinline__ void store_slot(const PhaseParams& p, int s, bool liv
   }
 }
 
+// rmsnorm's scale (src/nn.c:14-16 as built) of the squares sq (by lane class,
+// pitch cp, K elements): lane chains l = 0..7 of sum(x*x) over t, folded,
+// then ss/K + eps and the rsqrtss Newton step. Run by one full warp; every
+// lane returns the scale.
+__device__ __forceinline__ float rms_scale(const float* sq, int cp, int K, float eps, const uint32_t* rsq) {
+  const int lane = threadIdx.x & 31, l = lane & 7, nt = K / 8;
+  float acc = 0.f;
+  if (lane < 8) {
+    const float4* row = reinterpret_cast<const float4*>(sq + l * cp);
+    for (int t = 0; t < nt / 4; t++) {
+      const float4 w = row[t];
+      acc = __fadd_rn(acc, w.x); acc = __fadd_rn(acc, w.y);
+      acc = __fadd_rn(acc, w.z); acc = __fadd_rn(acc, w.w);
+    }
+  }
+  const float ss = fold8_lanes(acc);
+  return rsqrt_nr(__fadd_rn(__fdiv_rn(ss, (float)K), eps), rsq);
+}
+
 // Activation build. ACT_RMS (K <= 8 * RMS_SLOTS * consumer threads): the
-// norm weights are already in registers (loaded before the dependency wait)
-// and one block reduction gives the rms scale.
+// norm weights are already in registers (loaded before the dependency wait);
+// the squares go to the class region, one warp takes the scale, then
+// y = (x * w) * scale (src/nn.c:17 as built).
 static __device__ void build_activation(const PhaseParams& p, const float wpre[RMS_SLOTS][8], const Act& A, float* red) {
   const int K = p.n_in, nsb = K >> 5, nslot = K >> 3;
   const int t = threadIdx.x - 32, nt = CONSUMER_WARPS * 32;
@@ -296,7 +283,6 @@ static __device__ void build_activation(const PhaseParams& p, const float wpre[R
   const float4* x4 = reinterpret_cast<const float4*>(p.x);
   if (p.act == ACT_RMS) {
     float v[RMS_SLOTS][8];
-    float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < RMS_SLOTS; j++) {
       const int s = t + j * nt;
@@ -305,21 +291,25 @@ static __device__ void build_activation(const PhaseParams& p, const float wpre[R
         v[j][0] = a.x; v[j][1] = a.y; v[j][2] = a.z; v[j][3] = a.w;
         v[j][4] = b.x; v[j][5] = b.y; v[j][6] = b.z; v[j][7] = b.w;
 #pragma unroll
-        for (int i = 0; i < 8; i++) ss += v[j][i] * v[j][i];
+        for (int i = 0; i < 8; i++) A.xc[i * A.cp + s] = __fmul_rn(v[j][i], v[j][i]);
       } else {
 #pragma unroll
         for (int i = 0; i < 8; i++) v[j][i] = 0.f;
       }
     }
-    const float tot = consumers_sum(ss, red);
-    // src/nn.c:16-17: scale = 1/sqrtf(ss/n + eps); y = x * scale * w
-    const float scale = 1.0f / sqrtf(tot / (float)K + p.eps);
+    consumers_sync();
+    if (w == 0) {
+      const float sc = rms_scale(A.xc, A.cp, K, p.eps, p.rsq);
+      if (lane == 0) red[0] = sc;
+    }
+    consumers_sync();
+    const float scale = red[0];
 #pragma unroll
     for (int j = 0; j < RMS_SLOTS; j++) {
       const int s = t + j * nt;
       if (j * nt >= nslot) break;  // uniform: no live slot for any thread
 #pragma unroll
-      for (int i = 0; i < 8; i++) v[j][i] = v[j][i] * scale * wpre[j][i];
+      for (int i = 0; i < 8; i++) v[j][i] = __fmul_rn(__fmul_rn(v[j][i], wpre[j][i]), scale);
       store_slot(p, s, s < nslot, v[j], A);
     }
   } else {
@@ -356,14 +346,13 @@ static __device__ void build_activation(const PhaseParams& p, const float wpre[R
 // Exact int -> float for |v| < 2^22 without a conversion instruction: v is
 // added to the integer image of 1.5 * 2^23 and the bias removed in float.
 __device__ __forceinline__ float i22_to_float(int v) {
-  return __int_as_float(0x4B400000 + v) - 12582912.0f;
+  return __fsub_rn(__int_as_float(0x4B400000 + v), 12582912.0f);
 }
 
 // Q4_K: lane (bl = lane/4, g = lane%4) owns qs bytes [32g, 32g+32) of block bl
-// of the chunk: low nibbles are sub-block 2g, high nibbles sub-block 2g+1
-// (src/quant.c:239-259). Per sub-block: xs * (d*s*sum(q*xq) - dmin*m*sum(xq)).
-// The lane's activation slice of one chunk (64 int8 codes, two scales, two
-// code sums) fits in registers; short rows keep it for the whole kernel.
+// of the chunk: low nibbles are sub-block 2g (A), high nibbles sub-block 2g+1
+// (B) (src/quant.c:163-229). The lane's activation slice of one chunk (64
+// int8 codes, two scales, two code sums) fits in registers.
 struct Q4X {
   int a[8], b[8];
   float xsa, xsb;
@@ -385,16 +374,21 @@ __device__ __forceinline__ Q4X q4x_load(const int8_t* xq, const float* xs, const
   return X;
 }
 
-// NR rows (4, or 2 for phases with few rows per CTA: half the latency of a
-// unit); acc[NR..3] stay 0.
+// The lane's term of each of NR rows (rows past nrows re-read row 0, result
+// unused; lanes of blocks past m give 0, unused): per pair of sub-blocks
+// (A, B) of a super-block, q4k_vec_dot as built (src/quant.c:228-231 under
+// -O3 -ffast-math with FMA):
+//   tA = fma(sA, d*iqxA, -(mA*(dmin*ixA)))     tB likewise
+//   v  = fma(tB, xsB, tA*xsA)
+// which the row's running sum then takes with one rounded add (q4k_chain).
+// The integer sums are exact dp4a results.
 template <int NR = 4>
-__device__ __forceinline__ void q4k_unit(const uint8_t* st, int rstride, int nrows, int m, const Q4X& X,
-                                         float acc[4]) {
+__device__ __forceinline__ void q4k_pairs(const uint8_t* st, int rstride, int nrows, int m, const Q4X& X,
+                                          float v[4]) {
   const int lane = threadIdx.x & 31, bl = lane >> 2, g = lane & 3;
 #pragma unroll
-  for (int r = 0; r < 4; r++) acc[r] = 0.f;
+  for (int r = 0; r < 4; r++) v[r] = 0.f;
   if (bl >= m) return;
-  // all four rows' loads first (rows past nrows re-read row 0, result unused)
   uint4 hd[NR], q0[NR], q1[NR];
 #pragma unroll
   for (int r = 0; r < NR; r++) {
@@ -405,6 +399,7 @@ __device__ __forceinline__ void q4k_unit(const uint8_t* st, int rstride, int nro
   }
   const int shf = 16 * (g & 1);  // scale bytes of j = 2g, 2g+1 within their words
   const bool low = g < 2;        // j < 4: plain 6-bit fields (src/quant.c:59-61)
+  const float fxa = i22_to_float(X.sma), fxb = i22_to_float(X.smb);
 #pragma unroll
   for (int r = 0; r < NR; r++) {
     const uint32_t qw[8] = {q0[r].x, q0[r].y, q0[r].z, q0[r].w, q1[r].x, q1[r].y, q1[r].z, q1[r].w};
@@ -423,133 +418,112 @@ __device__ __forceinline__ void q4k_unit(const uint8_t* st, int rstride, int nro
     const int ma = low ? (Z & 63) : (((W >> 4) & 15) | ((Z >> 2) & 0x30));
     const int sb = low ? (Y1 & 63) : ((W1 & 15) | ((Y1 >> 2) & 0x30));
     const int mb = low ? (Z1 & 63) : (((W1 >> 4) & 15) | ((Z1 >> 2) & 0x30));
-    // xs * (d*(s*iqx) - dmin*(m*ix)): the integer products are exact
-    // (|s*iqx| <= 63*32*15*127 < 2^22) and become floats by exponent bias
-    float a = X.xsa * (d * i22_to_float(sa * ia) - dmin * i22_to_float(ma * X.sma));
-    a += X.xsb * (d * i22_to_float(sb * ib) - dmin * i22_to_float(mb * X.smb));
-    acc[r] = r < nrows ? a : 0.f;
+    const float2 p = mul2(make_float2(d, d), make_float2(i22_to_float(ia), i22_to_float(ib)));
+    const float2 mq = mul2(make_float2(i22_to_float(ma), i22_to_float(mb)),
+                           mul2(make_float2(dmin, dmin), make_float2(fxa, fxb)));
+    const float2 tt = fma2(make_float2(i22_to_float(sa), i22_to_float(sb)), p, make_float2(-mq.x, -mq.y));
+    const float vv = __fmaf_rn(tt.y, X.xsb, __fmul_rn(tt.x, X.xsa));
+    v[r] = r < nrows ? vv : 0.f;
   }
 }
 
-// Q6_K: two passes of 4 blocks. Lane (bq = lane/8, n = half, k = quarter) of
-// block bl = 4*pass + bq owns ql[64n + 16k .. +16]: low nibbles are elements
-// 128n + 16k + i (scale group 8n + k), high nibbles 128n + 64 + 16k + i (group
-// 8n + 4 + k); their two high bits sit in qh[32n + 16(k&1) + i] at bits 0/2
-// and 4/6 — the element map of dequant_q6_K (src/quant.c:94-123).
-struct Q6L {
-  uint4 l0[2][2], l1[2][2], l2[2][2];  // [pass][lo/hi group]
-  float2 lp[2][2];
-};
-
-__device__ __forceinline__ void q6l_load(const Act& A, int c, int nb, Q6L& X) {
-  const int lane = threadIdx.x & 31, bq = lane >> 3, n = (lane >> 2) & 1, k = lane & 3;
-#pragma unroll
-  for (int pass = 0; pass < 2; pass++) {
-    const int b = min(CHUNK_BLOCKS * c + 4 * pass + bq, nb - 1);
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      const int e = 256 * b + 128 * n + 64 * h + 16 * k;  // first element of the lane's group
-      const int pos = limb_pos(e);
-      X.l0[pass][h] = *reinterpret_cast<const uint4*>(A.l0 + pos);
-      X.l1[pass][h] = *reinterpret_cast<const uint4*>(A.l1 + pos);
-      X.l2[pass][h] = *reinterpret_cast<const uint4*>(A.l2 + pos);
-      X.lp[pass][h] = A.lp[e >> 4];
-    }
-  }
-}
-
-// sum over 16 codes of q * X for one limb plane: 4 dp4a
-__device__ __forceinline__ int dot16u(const uint32_t q[4], const uint4& l) {
-  unsigned r = __dp4a(q[0], l.x, 0u);
-  r = __dp4a(q[1], l.y, r);
-  r = __dp4a(q[2], l.z, r);
-  r = __dp4a(q[3], l.w, r);
-  return (int)r;
-}
-__device__ __forceinline__ int dot16s(const uint32_t q[4], const uint4& l) {
-  int r = __dp4a((int)q[0], (int)l.x, 0);
-  r = __dp4a((int)q[1], (int)l.y, r);
-  r = __dp4a((int)q[2], (int)l.z, r);
-  r = __dp4a((int)q[3], (int)l.w, r);
-  return r;
-}
-
-// sum((q - 32) * X) of one 16-group from its three limb dot products; the
-// partial sums are exact integers below 2^22, the combine is fp32
-__device__ __forceinline__ float group_dot(const uint32_t q[4], const uint4& l0, const uint4& l1, const uint4& l2,
-                                           float xs32) {
-  const float s0 = i22_to_float(dot16u(q, l0));
-  const float s1 = i22_to_float(dot16u(q, l1));
-  const float s2 = i22_to_float(dot16s(q, l2));
-  return fmaf(s2, 65536.0f, fmaf(s1, 256.0f, s0)) - xs32;
-}
-
-template <int NR = 4>
-__device__ __forceinline__ void q6k_unit(const uint8_t* st, int rstride, int nrows, int m, const Q6L& X,
-                                         float acc[4]) {
-  const int lane = threadIdx.x & 31, bq = lane >> 3, n = (lane >> 2) & 1, k = lane & 3;
-  const int sh_lo = (k < 2) ? 0 : 2, sh_hi = (k < 2) ? 4 : 6;
-#pragma unroll
-  for (int r = 0; r < 4; r++) acc[r] = 0.f;
-#pragma unroll
-  for (int pass = 0; pass < 2; pass++) {
-    const int bl = 4 * pass + bq;
-    if (bl >= m) continue;
-    uint4 ql[NR], qh[NR];
-    uint2 sc[NR];
-    float d[NR];
-#pragma unroll
-    for (int r = 0; r < NR; r++) {  // rows past nrows re-read row 0, result unused
-      const uint8_t* chunk = st + (r < nrows ? r : 0) * rstride;
-      const uint8_t* body = chunk + bl * Q6K_BODY;
-      ql[r] = *reinterpret_cast<const uint4*>(body + 64 * n + 16 * k);
-      qh[r] = *reinterpret_cast<const uint4*>(body + 128 + 32 * n + 16 * (k & 1));
-      sc[r] = *reinterpret_cast<const uint2*>(body + 192 + 8 * n);
-      d[r] = __half2float(*reinterpret_cast<const __half*>(chunk + m * Q6K_BODY + 2 * bl));
-    }
-#pragma unroll
-    for (int r = 0; r < NR; r++) {
-      const uint32_t lw[4] = {ql[r].x, ql[r].y, ql[r].z, ql[r].w};
-      const uint32_t hw[4] = {qh[r].x, qh[r].y, qh[r].z, qh[r].w};
-      uint32_t qlo[4], qhi[4];
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        qlo[i] = (lw[i] & 0x0F0F0F0Fu) | (((hw[i] >> sh_lo) << 4) & 0x30303030u);
-        qhi[i] = ((lw[i] >> 4) & 0x0F0F0F0Fu) | (((hw[i] >> sh_hi) << 4) & 0x30303030u);
-      }
-      const float tlo = group_dot(qlo, X.l0[pass][0], X.l1[pass][0], X.l2[pass][0], X.lp[pass][0].x);
-      const float thi = group_dot(qhi, X.l0[pass][1], X.l1[pass][1], X.l2[pass][1], X.lp[pass][1].x);
-      // scales: sc[8n + k] is byte k of word 0 of this half, sc[8n + 4 + k] byte k of word 1
-      const float sl = (float)(int8_t)(sc[r].x >> (8 * k)), sh = (float)(int8_t)(sc[r].y >> (8 * k));
-      const float v = d[r] * (sl * X.lp[pass][0].y * tlo + sh * X.lp[pass][1].y * thi);
-      acc[r] += r < nrows ? v : 0.f;
-    }
-  }
-}
-
-// Sum each of 4 per-lane partials over the warp with 6 shuffles: afterwards
-// lane 8r (r < 4) holds the total of partial r.
-__device__ __forceinline__ float reduce4(const float acc[4]) {
+// Continues rows 0..3's running sums (lanes 0..3 hold them in `acc`) with
+// the pair terms of one chunk, pair 0 (lane 0) first: the terms go through
+// the warp's scratch tr (4 x 36 floats) to the row lanes.
+__device__ __forceinline__ float q4k_chain(const float v[4], int m, float acc, float* tr) {
   const int lane = threadIdx.x & 31;
-  const bool hi16 = lane & 16, hi8 = lane & 8;
-  const float k0 = hi16 ? acc[2] : acc[0], k1 = hi16 ? acc[3] : acc[1];
-  const float s0 = hi16 ? acc[0] : acc[2], s1 = hi16 ? acc[1] : acc[3];
-  const float a0 = k0 + __shfl_xor_sync(0xffffffffu, s0, 16);
-  const float a1 = k1 + __shfl_xor_sync(0xffffffffu, s1, 16);
-  float b = (hi8 ? a1 : a0) + __shfl_xor_sync(0xffffffffu, hi8 ? a0 : a1, 8);
-  b += __shfl_xor_sync(0xffffffffu, b, 4);
-  b += __shfl_xor_sync(0xffffffffu, b, 2);
-  b += __shfl_xor_sync(0xffffffffu, b, 1);
-  return b;
+  __syncwarp();
+#pragma unroll
+  for (int r = 0; r < 4; r++) tr[r * 36 + lane] = v[r];
+  __syncwarp();
+  if (lane < 4) {
+    const float4* row = reinterpret_cast<const float4*>(tr + lane * 36);
+    for (int j = 0; j < m; j++) {
+      const float4 w = row[j];
+      acc = __fadd_rn(acc, w.x); acc = __fadd_rn(acc, w.y);
+      acc = __fadd_rn(acc, w.z); acc = __fadd_rn(acc, w.w);
+    }
+  }
+  return acc;
+}
+
+// Whole Q4_K rows: st points at the unit's first row (all chunks), rows
+// rstride bytes apart. Lanes 0..nrows-1 return their row's dot product.
+template <int NR = 4>
+__device__ __forceinline__ float q4k_rows(const uint8_t* st, int rstride, int nrows, int nb, const Act& A, float* tr) {
+  float acc = 0.f;
+  const int nch = n_chunks(nb);
+  for (int c = 0; c < nch; c++) {
+    const int m = q6_chunk_blocks(nb, c);
+    const Q4X X = q4x_load(A.xq, A.xs, A.xsum, c, nb);
+    float v[4];
+    q4k_pairs<NR>(st + (size_t)c * Q4K_CHUNK, rstride, nrows, m, X, v);
+    acc = q4k_chain(v, m, acc, tr);
+  }
+  return acc;
+}
+
+// Whole Q6_K rows x the fp32 activation as the reference's generic path
+// computes them (src/nn.c:84-95 as built): lane l of the 8-lane accumulator
+// adds the rounded products w[i] * x[i] of the elements i = 8t + l one at a
+// time in increasing t; the 8 lanes fold at the end (fold8_lanes). Here
+// thread (r, l) = (lane / 8, lane % 8) runs that chain for row r over the
+// whole row, reading its class's code bytes (device body layout,
+// hakm_internal.h) and x by class (Act::xc). w = (q - 32) * (d * sc) is
+// exact in fp32 (at most 6 + 18 significant bits), as in dequant_q6_K.
+// ws: the warp's scratch (the rows' (d*sc, d*sc) pairs of the current block).
+// Lanes 8r (r < nrows) return row r's dot product.
+__device__ __forceinline__ float q6k_rows(const uint8_t* st, int rstride, int nrows, int nb, const Act& A, float* ws) {
+  const int lane = threadIdx.x & 31, r = lane >> 3, l = lane & 7;
+  const uint8_t* row = st + (size_t)(r < nrows ? r : 0) * rstride;
+  const float* xl = A.xc + l * A.cp;
+  float2* dsc = reinterpret_cast<float2*>(ws) + r * 16;
+  const float2 bias2 = make_float2(-8388640.0f, -8388640.0f);  // -(2^23 + 32)
+  float acc = 0.f;
+  for (int b = 0; b < nb; b++) {
+    const int c = b >> 3, j = b & 7, m = q6_chunk_blocks(nb, c);
+    const uint8_t* chunk = row + (size_t)c * Q6K_CHUNK;
+    const uint8_t* body = chunk + j * Q6K_BODY;
+    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(chunk + m * Q6K_BODY + 2 * j));
+    const uint32_t s2 = *reinterpret_cast<const uint16_t*>(body + 192 + 2 * l);
+    const float g0 = __fmul_rn(d, (float)(int8_t)(s2 & 255)), g1 = __fmul_rn(d, (float)(int8_t)(s2 >> 8));
+    const uint2* wp = reinterpret_cast<const uint2*>(body + 24 * l);
+    const uint2 w0 = wp[0], w1 = wp[1], w2 = wp[2];
+    __syncwarp();
+    reinterpret_cast<float4*>(dsc)[l] = make_float4(g0, g0, g1, g1);
+    __syncwarp();
+#pragma unroll
+    for (int n = 0; n < 2; n++) {
+      const uint32_t W0 = n ? w1.y : w0.x, W1 = n ? w2.x : w0.y, WH = n ? w2.y : w1.x;
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        uint32_t q;
+        if (k == 0) q = (W0 & 0x0F0F0F0Fu) | ((WH << 4) & 0x30303030u);
+        else if (k == 1) q = (W1 & 0x0F0F0F0Fu) | ((WH << 2) & 0x30303030u);
+        else if (k == 2) q = ((W0 >> 4) & 0x0F0F0F0Fu) | (WH & 0x30303030u);
+        else q = ((W1 >> 4) & 0x0F0F0F0Fu) | ((WH >> 2) & 0x30303030u);
+        const float4 x4 = *reinterpret_cast<const float4*>(xl + 32 * b + 16 * n + 4 * k);
+        const float4 ds = reinterpret_cast<const float4*>(dsc)[4 * n + k];
+        const float2 qa = add2(make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7650)),
+                                           __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7651))), bias2);
+        const float2 qb = add2(make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7652)),
+                                           __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7653))), bias2);
+        const float2 pa = mul2(mul2(qa, make_float2(ds.x, ds.y)), make_float2(x4.x, x4.y));
+        const float2 pb = mul2(mul2(qb, make_float2(ds.z, ds.w)), make_float2(x4.z, x4.w));
+        acc = __fadd_rn(acc, pa.x);
+        acc = __fadd_rn(acc, pa.y);
+        acc = __fadd_rn(acc, pb.x);
+        acc = __fadd_rn(acc, pb.y);
+      }
+    }
+  }
+  return fold8_lanes(acc);
 }
 
 // ------------------------------------------------------------------ epilogue
 
 __device__ __forceinline__ float row_total(const float* part, const SegRange& r, int row) {
-  const float* pp = part + r.part_base + (row - r.row0) * r.nch;
-  float v = pp[0];
-  for (int c = 1; c < r.nch; c++) v += pp[c];
-  return v;
+  return part[r.part_base + (row - r.row0)];
 }
 
 // key: where the argmax epilogue folds its pick (null: p.argmax_key).
@@ -567,10 +541,10 @@ static __device__ void epilogue(const PhaseParams& p, const SegRange* sr, const 
         const float a0 = row_total(part, r, dr), a1 = row_total(part, r, dr + 1);
         if (S.epi == EPI_SWIGLU) {
           // src/model.c:154 with silu_f (src/nn.c:29)
-          S.out[dr >> 1] = a0 / (1.0f + expf(-a0)) * a1;
+          S.out[dr >> 1] = swiglu_exact(a0, a1);
         } else {
-          const float x0 = S.bias ? a0 + S.bias[dr] : a0;
-          const float x1 = S.bias ? a1 + S.bias[dr + 1] : a1;
+          const float x0 = S.bias ? __fadd_rn(a0, S.bias[dr]) : a0;
+          const float x1 = S.bias ? __fadd_rn(a1, S.bias[dr + 1]) : a1;
           const bool is_k = dr >= S.split;
           const int lr = is_k ? dr - S.split : dr;
           const int hd = p.head_dim, half = hd >> 1;
@@ -593,10 +567,10 @@ static __device__ void epilogue(const PhaseParams& p, const SegRange* sr, const 
       for (int row = r.row0 + t; row < r.row1; row += nt) {
         const float v = row_total(part, r, row);
         switch (S.epi) {
-          case EPI_STORE: S.out[row] = S.bias ? v + S.bias[row] : v; break;
-          case EPI_RESID: S.out[row] = __ldcg(S.out + row) + v; break;
+          case EPI_STORE: S.out[row] = S.bias ? __fadd_rn(v, S.bias[row]) : v; break;
+          case EPI_RESID: S.out[row] = __fadd_rn(__ldcg(S.out + row), v); break;
           case EPI_V_CACHE: {
-            const float o = S.bias ? v + S.bias[row] : v;
+            const float o = S.bias ? __fadd_rn(v, S.bias[row]) : v;
             S.out[row] = o;
             S.cache[(size_t)pos * p.kv_dim + row] = o;
             break;

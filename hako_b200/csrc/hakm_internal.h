@@ -21,6 +21,17 @@ enum WType { W_Q4K = 12, W_Q6K = 14 };
 //        8 fp16 d values: 1680 bytes = 8 * 210, the verbatim byte count; a
 //        short last chunk is padded to 16 bytes. Every chunk starts 16-byte
 //        aligned, so a stage of chunks is one bulk copy per row.
+//        A body keeps the block's bytes, reordered "by lane class": the
+//        reference's Q6_K dot adds the products of element i into lane i % 8
+//        of its vectorized loop, and the device gives each such lane chain to
+//        one thread, which then needs the code bits of elements l, l+8, ...
+//        (l = i % 8). Bytes 24l .. 24l+23 hold them for class l: per half n
+//        of the block (12 bytes at 24l + 12n), W0[b] = ql[64n + 8b + l],
+//        W1[b] = ql[64n + 32 + 8b + l], WH[b] = qh[32n + 8b + l] (b = 0..3);
+//        bytes 192..207 are the 16 int8 scales, unchanged. Element
+//        i = 8(16n + 4k + b) + l is nibble (k < 2 ? low : high) of
+//        (k even ? W0 : W1)[b] with bits 2k..2k+1 of WH[b] on top, the
+//        element map of dequant_q6_K (src/quant.c:94-123).
 constexpr int CHUNK_BLOCKS = 8;
 constexpr int Q4K_CHUNK = CHUNK_BLOCKS * Q4K_BYTES;  // 1152
 constexpr int Q6K_CHUNK = CHUNK_BLOCKS * Q6K_BYTES;  // 1680
@@ -33,6 +44,18 @@ __host__ __device__ inline int q6_chunk_blocks(int nb, int c) {
 __host__ __device__ inline int chunk_bytes(int type, int nb, int c) {
   const int m = q6_chunk_blocks(nb, c);
   return type == W_Q4K ? m * Q4K_BYTES : ((m * Q6K_BYTES + 15) & ~15);
+}
+// Position in the device body of byte `src` (0..207) of a verbatim body.
+__host__ __device__ inline int q6k_body_pos(int src) {
+  if (src < 128) {  // ql
+    const int n = src >> 6, h = (src >> 5) & 1, j = src & 31;
+    return 24 * (j & 7) + 12 * n + 4 * h + (j >> 3);
+  }
+  if (src < 192) {  // qh
+    const int p = src - 128, n = p >> 5, j = p & 31;
+    return 24 * (j & 7) + 12 * n + 8 + (j >> 3);
+  }
+  return src;  // scales
 }
 __host__ __device__ inline size_t dev_row_bytes(int type, int nb) {
   if (type == W_Q4K) return (size_t)nb * Q4K_BYTES;
@@ -80,7 +103,8 @@ struct PhaseParams {
   const int8_t* xq;      // ACT_Q8 input
   const float* xs;
   int need_q8;           // some segment is Q4_K (int8 activation in the prologue)
-  int need_q6;           // some segment is Q6_K (fixed-point limbs in the prologue)
+  int need_q6;           // some segment is Q6_K (fp32 activation, by lane class, in the prologue)
+  const uint32_t* rsq;   // ACT_RMS: the rsqrtss table (2048 words, see rsqrt_est)
   int n_seg;
   Seg seg[MAX_SEGS];
   // filled by launch_phase: ring geometry and per-CTA partial-sum slots
@@ -131,7 +155,8 @@ cudaError_t launch_q4k_subsums(int32_t* iqx, int32_t* ix, const uint8_t* w, cons
                                int n_out, int n_in, cudaStream_t s);
 cudaError_t launch_q6k_pack(uint8_t* dst, const uint8_t* src, int n_rows, int n_in, cudaStream_t s);
 cudaError_t launch_dequant(float* out, const uint8_t* w, int type, int n_rows, int n_in, cudaStream_t s);
-cudaError_t launch_rmsnorm(float* y, const float* x, const float* w, int n, float eps, cudaStream_t s);
+cudaError_t launch_rmsnorm(float* y, const float* x, const float* w, int n, float eps, const uint32_t* rsq,
+                           cudaStream_t s);
 cudaError_t launch_embed_q6k(float* xb, const uint8_t* w, const int* token, int n_in, cudaStream_t s,
                              bool pdl);
 cudaError_t launch_rope(float* x, const float* rope_cs, const int* pos_dev, int n_heads, int head_dim,
@@ -172,21 +197,32 @@ struct AttnParams {
   float* out;            // [H*hd]
   const int* pos_dev;    // attend over positions 0..pos
   int n_heads, n_kv, head_dim;
-  float scale;
-  int n_split;           // grid.y; chunks of ATTN_CHUNK positions
-  float* part;           // scratch [n_heads / head_group][n_split][head_group][2 + hd]
-  unsigned int* counters;  // [n_heads / head_group], self-resetting
-  int head_group;        // query heads per work item (divides n_heads / n_kv); 0: all of them
+  float scale;           // 1.0f/sqrtf(head_dim) as the reference's build computes it
+  float* part;           // scratch: per unit, score_stride floats (scores, exps, probabilities)
+  int score_stride;      // >= positions attended (pos + 1)
 };
-constexpr int ATTN_CHUNK = 32;   // positions per attention work item
+// Attention work units: (query head, slice of ATTN_SLICE dimensions).
+constexpr int ATTN_SLICE = 32;
+__host__ __device__ inline int attn_units(int n_heads, int head_dim) { return n_heads * (head_dim / ATTN_SLICE); }
+// With tensor parallelism rank r of `world` runs units r, r + world, ...:
+// attn_units_local of them, the i-th being attn_unit_of(r, world, i).
+__host__ __device__ inline int attn_units_local(int n_units, int rank, int world) {
+  return (n_units - rank + world - 1) / world;
+}
+__host__ __device__ inline int attn_unit_of(int rank, int world, int i) { return rank + world * i; }
 cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl);
 // hakmc_attention_noalloc: scratch in a static device array, no allocation
 cudaError_t attention_noalloc(float* out, const float* q, const float* kc, const float* vc, int pos, int n_heads,
                               int n_kv, int head_dim, cudaStream_t stream);
 size_t noalloc_part_floats();
-size_t attention_scratch_floats(int n_kv, int n_split, int group, int head_dim);
-// Most ATTN_CHUNK-position splits one attention merge combines.
-int attention_max_splits(int head_dim, int group);
+// Scratch floats of launch_attention for n positions.
+size_t attention_scratch_floats(int n_heads, int head_dim, int n_pos);
+// The device's exp restatements on n inputs (variant 0 scalar, 1 8-wide, 2 4-wide).
+cudaError_t launch_exp_probe(float* out, const float* in, int n, int variant, cudaStream_t s);
+// The rsqrtss table of this host on device `dev` (made on first use).
+const uint32_t* rsqrt_table_device(int dev);
+// 1.0f/sqrtf(v) as the reference's build computes it, on the host.
+float host_rsqrt_nr(float v);
 
 // Rows of one segment that one CTA computes, and where its per-(row, chunk)
 // partial sums start in shared memory.

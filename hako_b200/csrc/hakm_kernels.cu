@@ -4,6 +4,7 @@
 // attention. The streaming GEMV phases live in hakm_stream.cu.
 #include "hakm_attn.cuh"
 #include "hakm_device.cuh"
+#include "hakm_exact.cuh"
 
 #include <mutex>
 
@@ -72,7 +73,8 @@ cudaError_t launch_q4k_subsums(int32_t* iqx, int32_t* ix, const uint8_t* w, cons
 }
 
 // Verbatim 210-byte blocks -> the chunked device layout (hakm_internal.h):
-// per 8-block chunk the 208-byte bodies, then the 8 fp16 d values. One warp
+// per 8-block chunk the 208-byte bodies (bytes reordered by lane class,
+// q6k_body_pos), then the 8 fp16 d values. One warp
 // per block; the destination is zeroed first so chunk padding is defined.
 __global__ void q6k_pack_kernel(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, int n_rows, int nb) {
   const long blk = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -82,7 +84,7 @@ __global__ void q6k_pack_kernel(uint8_t* __restrict__ dst, const uint8_t* __rest
   const int c = b / CHUNK_BLOCKS, j = b % CHUNK_BLOCKS, m = q6_chunk_blocks(nb, c);
   const uint8_t* s = src + blk * Q6K_BYTES;
   uint8_t* chunk = dst + (size_t)r * dev_row_bytes(W_Q6K, nb) + (size_t)c * Q6K_CHUNK;
-  for (int i = lane; i < Q6K_BODY; i += 32) chunk[j * Q6K_BODY + i] = s[i];
+  for (int i = lane; i < Q6K_BODY; i += 32) chunk[j * Q6K_BODY + q6k_body_pos(i)] = s[i];
   if (lane < 2) chunk[m * Q6K_BODY + 2 * j + lane] = s[Q6K_BODY + lane];
 }
 
@@ -131,17 +133,29 @@ cudaError_t launch_dequant(float* out, const uint8_t* w, int type, int n_rows, i
   return cudaGetLastError();
 }
 
-__global__ void rmsnorm_kernel(float* y, const float* x, const float* w, int n, float eps) {
-  __shared__ float red[32];
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) ss += x[i] * x[i];
-  const float tot = block_sum(ss, red);
-  const float scale = 1.0f / sqrtf(tot / (float)n + eps);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) y[i] = x[i] * scale * w[i];
+// rmsnorm (src/nn.c:13-18) as the reference's build computes it: one warp
+// takes sum(x*x) in the 8-lane vectorized order (lane l adds the rounded
+// squares of x[8t + l] in order, then the lanes fold), ss/n + eps, the
+// rsqrtss Newton step, then y = (x * w) * scale. n is a multiple of 8.
+__global__ void rmsnorm_kernel(float* y, const float* x, const float* w, int n, float eps, const uint32_t* rsq) {
+  __shared__ float s_scale;
+  if (threadIdx.x < 32) {
+    const int l = threadIdx.x & 7;
+    float acc = 0.f;
+    if (threadIdx.x < 8)
+      for (int i = l; i < n; i += 8) acc = __fadd_rn(acc, __fmul_rn(x[i], x[i]));
+    const float ss = fold8_lanes(acc);
+    if (threadIdx.x == 0) s_scale = rsqrt_nr(__fadd_rn(__fdiv_rn(ss, (float)n), eps), rsq);
+  }
+  __syncthreads();
+  const float scale = s_scale;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) y[i] = __fmul_rn(__fmul_rn(x[i], w[i]), scale);
 }
 
-cudaError_t launch_rmsnorm(float* y, const float* x, const float* w, int n, float eps, cudaStream_t s) {
-  rmsnorm_kernel<<<1, 1024, 0, s>>>(y, x, w, n, eps);
+cudaError_t launch_rmsnorm(float* y, const float* x, const float* w, int n, float eps, const uint32_t* rsq,
+                           cudaStream_t s) {
+  if (n % 8 || !rsq) return cudaErrorInvalidValue;
+  rmsnorm_kernel<<<1, 1024, 0, s>>>(y, x, w, n, eps, rsq);
   return cudaGetLastError();
 }
 
@@ -195,7 +209,7 @@ cudaError_t launch_rope(float* x, const float* rope_cs, const int* pos_dev, int 
 
 // ------------------------------------------------------------ attention
 
-// Standalone attention launch: one CTA per (kv head, chunk).
+// Standalone attention launch: one CTA per (query head, dimension slice).
 struct BlockSync {
   __device__ void operator()() const { __syncthreads(); }
 };
@@ -205,28 +219,18 @@ __global__ void __launch_bounds__(256) attention_kernel(const AttnParams a) {
   extern __shared__ __align__(16) float sm[];
   pdl_launch_dependents();
   pdl_wait();
-  attn_item<HD, false>(a, blockIdx.x, blockIdx.y, *a.pos_dev, sm, threadIdx.x, blockDim.x, BlockSync());
+  attn_item<HD, false>(a, blockIdx.x, *a.pos_dev, sm, threadIdx.x, blockDim.x, BlockSync());
 }
 
-int attention_max_splits(int head_dim, int group) { return attn_max_splits(head_dim, group); }
-
-size_t attention_scratch_floats(int n_kv, int n_split, int group, int head_dim) {
-  return (size_t)n_kv * n_split * group * (head_dim + 2);
+size_t attention_scratch_floats(int n_heads, int head_dim, int n_pos) {
+  return (size_t)attn_units(n_heads, head_dim) * (size_t)n_pos;
 }
 
 template <int HD>
 static cudaError_t launch_attn(const AttnParams& a, cudaStream_t s, bool pdl) {
   const size_t smem = attn_smem_bytes(HD);
-  static unsigned done = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 32 && !(done & (1u << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(attention_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    done |= 1u << dev;
-  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.n_kv, a.n_split);
+  cfg.gridDim = dim3(attn_units(a.n_heads, HD));
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
@@ -238,25 +242,73 @@ static cudaError_t launch_attn(const AttnParams& a, cudaStream_t s, bool pdl) {
   return cudaLaunchKernelEx(&cfg, attention_kernel<HD>, a);
 }
 
-cudaError_t launch_attention(const AttnParams& a0, cudaStream_t s, bool pdl) {
-  if (a0.n_heads % a0.n_kv || a0.n_heads / a0.n_kv > 8) return cudaErrorInvalidValue;
-  AttnParams a = a0;
-  a.head_group = a.n_heads / a.n_kv;  // one block per kv head and split
+cudaError_t launch_attention(const AttnParams& a, cudaStream_t s, bool pdl) {
+  if (a.n_kv <= 0 || a.n_heads % a.n_kv || !a.part || a.score_stride < 1) return cudaErrorInvalidValue;
   if (a.head_dim == 128) return launch_attn<128>(a, s, pdl);
   if (a.head_dim == 64) return launch_attn<64>(a, s, pdl);
   return cudaErrorInvalidValue;
 }
 
+// ------------------------------------------------------------ exp test hook
+
+__global__ void exp_probe_kernel(float* out, const float* in, int n, int variant) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float x = in[i];
+  out[i] = variant == 1 ? exp_v8(x) : variant == 2 ? exp_v4(x) : exp_scalar(x);
+}
+
+cudaError_t launch_exp_probe(float* out, const float* in, int n, int variant, cudaStream_t s) {
+  exp_probe_kernel<<<(n + 255) / 256, 256, 0, s>>>(out, in, n, variant);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ rsqrtss table
+
+extern "C" void hakm_host_rsqrt_table(uint32_t* out);
+extern "C" int hakm_host_rsqrt_table_ok(const uint32_t* tab);
+extern "C" float hakm_host_rsqrt_nr(float v);
+
+float host_rsqrt_nr(float v) { return hakm_host_rsqrt_nr(v); }
+
+// One copy per device, made on first use and kept until the process exits.
+static std::mutex g_rsq_mu;
+static uint32_t* g_rsq_dev[64];
+
+const uint32_t* rsqrt_table_device(int dev) {
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_rsq_mu);
+  if (g_rsq_dev[dev]) return g_rsq_dev[dev];
+  static uint32_t host[2048];
+  static int host_ok = -1;
+  if (host_ok < 0) {
+    hakm_host_rsqrt_table(host);
+    host_ok = hakm_host_rsqrt_table_ok(host);
+  }
+  if (!host_ok) return nullptr;
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return nullptr;
+  if (cur != dev && cudaSetDevice(dev) != cudaSuccess) return nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, sizeof host);
+  if (e == cudaSuccess) e = cudaMemcpy(p, host, sizeof host, cudaMemcpyHostToDevice);
+  if (cur != dev) cudaSetDevice(cur);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return nullptr;
+  }
+  g_rsq_dev[dev] = static_cast<uint32_t*>(p);
+  return g_rsq_dev[dev];
+}
+
 // ------------------------------------------------------------ allocation-free attention
 
-// Scratch of hakmc_attention_noalloc: split partials, per-kv-head tickets and
-// the position word, in one file-scope device array. Every GPU that loads the
-// library holds it (about 1 MiB) until the process exits.
-constexpr size_t NOALLOC_PART_FLOATS = 256 * 1024;  // 1 MiB of split partials
-constexpr int NOALLOC_TICKETS = 64;
+// Scratch of hakmc_attention_noalloc: the score rows of the attention units
+// and the position word, in one file-scope device array. Every GPU that
+// loads the library holds it (about 1 MiB) until the process exits.
+constexpr size_t NOALLOC_PART_FLOATS = 256 * 1024;  // 1 MiB of score rows
 struct NoAllocScratch {
   float part[NOALLOC_PART_FLOATS];
-  unsigned tickets[NOALLOC_TICKETS];
   int pos;
 };
 static __device__ __align__(256) NoAllocScratch g_noalloc;
@@ -268,7 +320,6 @@ static std::mutex g_noalloc_mu;
 static NoAllocScratch* g_noalloc_dev[64];
 
 __global__ void noalloc_prepare_kernel(NoAllocScratch* s, int pos) {
-  if (threadIdx.x < NOALLOC_TICKETS) s->tickets[threadIdx.x] = 0u;  // must start at zero
   if (threadIdx.x == 0) s->pos = pos;
 }
 
@@ -291,15 +342,14 @@ cudaError_t attention_noalloc(float* out, const float* q, const float* kc, const
     }
     s = g_noalloc_dev[dev];
   }
-  noalloc_prepare_kernel<<<1, NOALLOC_TICKETS, 0, stream>>>(s, pos);
+  noalloc_prepare_kernel<<<1, 32, 0, stream>>>(s, pos);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   AttnParams a = {};
   a.q = q; a.k_cache = kc; a.v_cache = vc; a.out = out; a.pos_dev = &s->pos;
-  a.n_heads = n_heads; a.n_kv = n_kv; a.head_dim = head_dim; a.scale = 1.0f / sqrtf((float)head_dim);
-  a.n_split = pos / ATTN_CHUNK + 1;
+  a.n_heads = n_heads; a.n_kv = n_kv; a.head_dim = head_dim; a.scale = host_rsqrt_nr((float)head_dim);
   a.part = s->part;
-  a.counters = s->tickets;
+  a.score_stride = pos + 1;
   return launch_attention(a, stream, false);
 }
 

@@ -153,9 +153,24 @@ __global__ void __launch_bounds__(256, BM == 128 ? 2 : BM == 64 ? 3 : 4) pf_q6k_
     const float d = half_bits_to_float((uint32_t)chunk[m * Q6K_BODY + 2 * j] |
                                        ((uint32_t)chunk[m * Q6K_BODY + 2 * j + 1] << 8));
     rds = __fmul_rn(d, (float)(int8_t)body[192 + (i0 >> 4)]);
-    const int nh = i0 >> 7, qd = (i0 >> 5) & 3, l0 = i0 & 31;
-    rlo = *reinterpret_cast<const uint4*>(body + 64 * nh + 32 * (qd & 1) + l0);
-    rhi = *reinterpret_cast<const uint4*>(body + 128 + 32 * nh + l0);
+    // the group's 16 elements i0 + e are classes e % 8 at positions 2g, 2g+1
+    // of their class (device body layout, hakm_internal.h): byte e of rlo /
+    // rhi gets element e's ql / qh byte
+    const int g = i0 >> 4, nh = g >> 3, qd = (g & 7) >> 1, b0 = 2 * (g & 1);
+    uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int l = 0; l < 8; l++) {
+      const uint8_t* cb = body + 24 * l + 12 * nh;
+      const uint32_t wl = *reinterpret_cast<const uint16_t*>(cb + 4 * (qd & 1) + b0);
+      const uint32_t wh = *reinterpret_cast<const uint16_t*>(cb + 8 + b0);
+      // element l (byte l) and element l + 8 (byte l + 8)
+      lo[l >> 2] |= (wl & 255u) << (8 * (l & 3));
+      lo[2 + (l >> 2)] |= (wl >> 8) << (8 * (l & 3));
+      hi[l >> 2] |= (wh & 255u) << (8 * (l & 3));
+      hi[2 + (l >> 2)] |= (wh >> 8) << (8 * (l & 3));
+    }
+    rlo = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    rhi = make_uint4(hi[0], hi[1], hi[2], hi[3]);
 #pragma unroll
     for (int c = 0; c < NCP; c++) g6_cp_async<CB>(&S.xs[xm][xk + c * CB / 4], xrow + k0 + xk + c * CB / 4);
     asm volatile("cp.async.commit_group;" ::: "memory");

@@ -120,6 +120,10 @@ size_t row_bytes(uint32_t type, int n_in) {
 
 }  // namespace
 
+// RoPE (cos, sin) pairs of one position as the reference's build computes
+// them (hakm_hostmath.c).
+extern "C" void hakm_host_rope_row(float* cs, int head_dim, int pos, float theta);
+
 // ------------------------------------------------------------ context
 
 // token_dev word where forward_batch keeps the single-sequence API's last
@@ -157,7 +161,8 @@ struct hakmc_ctx {
   int *token_dev, *pos_dev, *step_dev, *token_log, *prompt_dev;
   int prompt_cap = 0;
   unsigned long long* argmax_key;
-  unsigned int *done_counter, *attn_counters;
+  unsigned int* done_counter;
+  const uint32_t* rsq = nullptr;  // rsqrtss table of this host (rsqrt_table_device)
   int* err_flag = nullptr;    // set by a kernel whose bounded wait gave up
   int token_log_cap = 0;
   int* h_pinned = nullptr;    // pinned staging: [0] token in, [1] argmax out
@@ -241,8 +246,8 @@ static void dfree(hakmc_ctx* c, void* p) {
 }
 
 // Upload rows of a Q4_K / Q6_K matrix. `order[i]` is the source row of device
-// row i (identity when empty). Q6_K rows are split into 208-byte bodies and
-// an fp16 d plane (hakmc_q6k_pack layout).
+// row i (identity when empty). Q6_K rows are split into 208-byte bodies (bytes
+// reordered by lane class) and an fp16 d plane (hakmc_q6k_pack layout).
 static int upload_mat(hakmc_ctx* c, DevMat& dm, const MTensor& t, int exp_cols, int exp_rows,
                       const std::vector<int>& order, const MTensor* t2 = nullptr) {
   if (t.type != W_Q4K && t.type != W_Q6K) {
@@ -285,7 +290,7 @@ static int upload_mat(hakmc_ctx* c, DevMat& dm, const MTensor& t, int exp_cols, 
       for (int b = 0; b < nb; b++) {
         const int c = b / CHUNK_BLOCKS, j = b % CHUNK_BLOCKS, m = q6_chunk_blocks(nb, c);
         uint8_t* chunk = d + (size_t)c * Q6K_CHUNK;
-        memcpy(chunk + j * Q6K_BODY, s + (size_t)b * Q6K_BYTES, Q6K_BODY);
+        for (int i = 0; i < Q6K_BODY; i++) chunk[j * Q6K_BODY + q6k_body_pos(i)] = s[(size_t)b * Q6K_BYTES + i];
         memcpy(chunk + m * Q6K_BODY + 2 * j, s + (size_t)b * Q6K_BYTES + Q6K_BODY, 2);
       }
     }
@@ -374,8 +379,9 @@ static PhaseDesc make_phase(hakmc_ctx* c, int l, int ph, int n_split, bool timin
       d.kind = PK_ATTN;
       AttnParams& a = d.a;
       a.q = c->q; a.k_cache = kc; a.v_cache = vc; a.out = c->att; a.pos_dev = c->pos_dev;
-      a.n_heads = c->H; a.n_kv = c->KVH; a.head_dim = c->hd; a.scale = 1.0f / sqrtf((float)c->hd);
-      a.n_split = n_split; a.part = c->attn_part + (size_t)seq * c->attn_part_floats; a.counters = c->attn_counters;
+      a.n_heads = c->H; a.n_kv = c->KVH; a.head_dim = c->hd; a.scale = host_rsqrt_nr((float)c->hd);
+      // one scratch: sequences run their steps one after another
+      a.part = c->attn_part; a.score_stride = c->max_seq;
       break;
     }
     case PH_WO:
@@ -410,7 +416,9 @@ static PhaseDesc make_phase(hakmc_ctx* c, int l, int ph, int n_split, bool timin
   if (d.kind == PK_GEMV) {
     finish_params(p);
     p.err_flag = c->err_flag;
+    p.rsq = c->rsq;
   }
+  (void)n_split;
   return d;
 }
 
@@ -431,15 +439,9 @@ static cudaError_t enqueue_step(hakmc_ctx* c, int n_split) {
   return enqueue_phase(c, 0, PH_LMHEAD, n_split, false);
 }
 
-// Attention chunk count used for position `pos`, rounded up to a power of two
-// so a handful of captured graphs cover every position (chunks past pos run
-// empty and contribute nothing to the combine).
-static int n_split_for(const hakmc_ctx* c, int pos) {
-  const int need = pos / ATTN_CHUNK + 1, cap = (c->max_seq + ATTN_CHUNK - 1) / ATTN_CHUNK;
-  int k = 1;
-  while (k < need) k <<= 1;
-  return k < cap ? k : cap;
-}
+// Key of the captured per-phase step graph: the attention kernel reads the
+// position from the device, so one graph serves every position.
+static int n_split_for(const hakmc_ctx*, int) { return 1; }
 
 static int get_graph(hakmc_ctx* c, int n_split, cudaGraphExec_t* out) {
   auto it = c->graphs.find(n_split);
@@ -512,16 +514,6 @@ static void build_program(hakmc_ctx* c, int seq, std::vector<PhaseDesc>& prog) {
     PhaseDesc at = make_phase(c, l, PH_ATTN, 1, true, seq);
     at.x_ll = q_ll; at.res_ll = k_ll; at.v_ll = v_ll; at.x_src = base;
     at.out_ll[0] = att_ll; at.layer = l;
-    at.a.counters = c->step_tickets + 64 * seq;
-    {
-      // query heads per attention work item: split each kv head's group so
-      // that at least 8 items run even at one position split
-      const int G = c->H / c->KVH;
-      int nhg = G;
-      for (int d = 1; d <= G; d++)
-        if (G % d == 0 && c->KVH * d >= 8) { nhg = d; break; }
-      at.a.head_group = G / nhg;
-    }
     PhaseDesc wo = make_phase(c, l, PH_WO, 1, true, seq);
     wo.x_ll = att_ll; wo.x_src = base + 1;
     wo.res_ll = xb0; wo.res_src = xb0_src; wo.out_ll[0] = xb1;
@@ -789,15 +781,13 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
   if ((r = dalloc(c, (void**)&c->att, (size_t)B * c->D * 4))) return r;
   if ((r = dalloc(c, (void**)&c->hbuf, (size_t)B * c->F * 4))) return r;
   if ((r = dalloc(c, (void**)&c->logits, (size_t)B * c->V * 4))) return r;
-  const int max_split = (c->max_seq + ATTN_CHUNK - 1) / ATTN_CHUNK;
-  if (max_split > attention_max_splits(c->hd, c->H / c->KVH)) {
-    set_err("max_seq %d: beyond what one attention split merge combines", c->max_seq);
+  // attention score rows: one per (query head, dimension slice) unit
+  c->attn_part_floats = attention_scratch_floats(c->H, c->hd, c->max_seq);
+  if ((r = dalloc(c, (void**)&c->attn_part, c->attn_part_floats * 4))) return r;
+  if (!(c->rsq = rsqrt_table_device(c->device))) {
+    set_err("rsqrtss table: this host's estimate is not a function of exponent parity and 10 mantissa bits");
     return HAKMC_EINVAL;
   }
-  c->attn_part_floats = attention_scratch_floats(c->KVH, max_split, c->H / c->KVH, c->hd);
-  if ((r = dalloc(c, (void**)&c->attn_part, c->attn_part_floats * 4 * B))) return r;
-  if ((r = dalloc(c, (void**)&c->attn_counters, 64 * 4 * B))) return r;
-  CK(cudaMemset(c->attn_counters, 0, 64 * 4 * B));
   // [sequence] plus a save slot (forward_batch, TOKEN_SAVE)
   if ((r = dalloc(c, (void**)&c->token_dev, 4 * std::max(4 * B, TOKEN_SAVE + 1)))) return r;
   if ((r = dalloc(c, (void**)&c->pos_dev, 16 * B))) return r;
@@ -841,18 +831,12 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
   CK(cudaMemset(c->argmax_key, 0, 8 * B));
   CK(cudaMemset(c->done_counter, 0, 4 * B));
 
-  // RoPE table with the reference's formula and the host libm
-  // (src/nn.c:35-37): freq = powf(theta, -(2i/hd)), angle = pos * freq.
+  // RoPE table as the reference's build computes it (src/nn.c:35-37 through
+  // glibc's vector powf/cosf/sinf: hakm_host_rope_row)
   {
     const int half = c->hd / 2;
     std::vector<float> cs((size_t)c->max_seq * half * 2);
-    for (int p = 0; p < c->max_seq; p++)
-      for (int i = 0; i < half; i++) {
-        const float freq = powf(c->theta, -((float)(2 * i) / (float)c->hd));
-        const float ang = (float)p * freq;
-        cs[((size_t)p * half + i) * 2] = cosf(ang);
-        cs[((size_t)p * half + i) * 2 + 1] = sinf(ang);
-      }
+    for (int p = 0; p < c->max_seq; p++) hakm_host_rope_row(cs.data() + (size_t)p * half * 2, c->hd, p, c->theta);
     if ((r = dalloc(c, (void**)&c->rope_cs, cs.size() * 4))) return r;
     CK(cudaMemcpy(c->rope_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
   }
@@ -1833,6 +1817,7 @@ extern "C" int hakmc_lmhead_argmax(float* logits, int* argmax, const void* w, co
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (norm_w && !(p.rsq = rsqrt_table_device(dev))) { set_err("lmhead_argmax: no rsqrtss table"); return HAKMC_ECUDA; }
   CKL(launch_phase(p, sms, (cudaStream_t)stream, false));
   return 0;
 }
@@ -1844,32 +1829,30 @@ extern "C" int hakmc_dequant(float* out, const void* w, int type, int n_rows, in
 }
 
 extern "C" int hakmc_rmsnorm(float* y, const float* x, const float* w, int n, float eps, void* stream) {
-  if (!y || !x || !w || n <= 0) return HAKMC_EINVAL;
-  CKL(launch_rmsnorm(y, x, w, n, eps, (cudaStream_t)stream));
+  if (!y || !x || !w || n <= 0 || n % 8) return HAKMC_EINVAL;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  const uint32_t* rsq = rsqrt_table_device(dev);
+  if (!rsq) { set_err("rmsnorm: no rsqrtss table for device %d", dev); return HAKMC_ECUDA; }
+  CKL(launch_rmsnorm(y, x, w, n, eps, rsq, (cudaStream_t)stream));
   return 0;
 }
 
 extern "C" int hakmc_attention(float* out, const float* q, const float* kc, const float* vc, int pos, int n_heads,
                                int n_kv, int head_dim, void* stream) {
-  if (!out || !q || !kc || !vc || pos < 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > 8 ||
-      (head_dim != 64 && head_dim != 128) || n_kv > 64) {
+  if (!out || !q || !kc || !vc || pos < 0 || n_kv <= 0 || n_heads % n_kv || (head_dim != 64 && head_dim != 128)) {
     set_err("attention: unsupported arguments");
     return HAKMC_EINVAL;
   }
-  const int n_split = pos / ATTN_CHUNK + 1;
-  if (n_split > attention_max_splits(head_dim, n_heads / n_kv)) {
-    set_err("attention: position %d beyond what one split merge combines", pos);
-    return HAKMC_ERANGE;
-  }
   DevScratch* s;
-  int r = scratch(&s, attention_scratch_floats(n_kv, n_split, n_heads / n_kv, head_dim), 0);
+  int r = scratch(&s, attention_scratch_floats(n_heads, head_dim, pos + 1), 0);
   if (r) return r;
   cudaStream_t st = (cudaStream_t)stream;
   CKL(cudaMemcpyAsync(s->pos, &pos, 4, cudaMemcpyHostToDevice, st));
   AttnParams a = {};
   a.q = q; a.k_cache = kc; a.v_cache = vc; a.out = out; a.pos_dev = s->pos;
-  a.n_heads = n_heads; a.n_kv = n_kv; a.head_dim = head_dim; a.scale = 1.0f / sqrtf((float)head_dim);
-  a.n_split = n_split; a.part = s->part; a.counters = s->counters;
+  a.n_heads = n_heads; a.n_kv = n_kv; a.head_dim = head_dim; a.scale = host_rsqrt_nr((float)head_dim);
+  a.part = s->part; a.score_stride = pos + 1;
   CKL(launch_attention(a, st, false));
   CKL(cudaStreamSynchronize(st));
   return 0;
@@ -1877,23 +1860,47 @@ extern "C" int hakmc_attention(float* out, const float* q, const float* kc, cons
 
 extern "C" int hakmc_attention_noalloc(float* out, const float* q, const float* kc, const float* vc, int pos,
                                        int n_heads, int n_kv, int head_dim, void* stream) {
-  if (!out || !q || !kc || !vc || pos < 0 || n_kv <= 0 || n_heads % n_kv || n_heads / n_kv > 8 ||
-      (head_dim != 64 && head_dim != 128) || n_kv > 64) {
+  if (!out || !q || !kc || !vc || pos < 0 || n_kv <= 0 || n_heads % n_kv || (head_dim != 64 && head_dim != 128)) {
     set_err("attention_noalloc: unsupported arguments");
     return HAKMC_EINVAL;
   }
-  const int n_split = pos / ATTN_CHUNK + 1;
-  if (n_split > attention_max_splits(head_dim, n_heads / n_kv)) {
-    set_err("attention_noalloc: position %d beyond what one split merge combines", pos);
-    return HAKMC_ERANGE;
-  }
-  const size_t need = attention_scratch_floats(n_kv, n_split, n_heads / n_kv, head_dim);
+  const size_t need = attention_scratch_floats(n_heads, head_dim, pos + 1);
   if (need > noalloc_part_floats()) {
     set_err("attention_noalloc: %d heads x %d positions need %zu scratch floats, the fixed array holds %zu "
             "(use hakmc_attention)", n_heads, pos + 1, need, noalloc_part_floats());
     return HAKMC_ERANGE;
   }
   CKL(attention_noalloc(out, q, kc, vc, pos, n_heads, n_kv, head_dim, (cudaStream_t)stream));
+  return 0;
+}
+
+extern "C" int hakmc_plan_rows(const int* seg_rows, int n_seg, int grid, int cta, int* ranges) {
+  if (!seg_rows || !ranges || n_seg < 1 || n_seg > MAX_SEGS || grid < 1 || cta < 0 || cta >= grid) return HAKMC_EINVAL;
+  PhaseDesc d = {};
+  d.kind = PK_GEMV;
+  d.g.n_in = QK;
+  d.g.n_seg = n_seg;
+  for (int s = 0; s < n_seg; s++) {
+    if (seg_rows[s] < 1) return HAKMC_EINVAL;
+    d.g.seg[s].n_rows = seg_rows[s];
+  }
+  SegRange sr[MAX_SEGS];
+  step_ranges(&d, 1, grid, cta, 1, sr);
+  for (int s = 0; s < n_seg; s++) { ranges[2 * s] = sr[s].row0; ranges[2 * s + 1] = sr[s].row1; }
+  return 0;
+}
+
+extern "C" int hakmc_plan_attn_units(int n_heads, int head_dim, int rank, int world, int* units, int cap) {
+  if (n_heads < 1 || head_dim < ATTN_SLICE || head_dim % ATTN_SLICE || world < 1 || rank < 0 || rank >= world)
+    return HAKMC_EINVAL;
+  const int n = attn_units_local(attn_units(n_heads, head_dim), rank, world);
+  for (int i = 0; i < n && i < cap; i++) units[i] = attn_unit_of(rank, world, i);
+  return n;
+}
+
+extern "C" int hakmc_test_expf(float* out, const float* in, int n, int variant, void* stream) {
+  if (!out || !in || n < 0 || variant < 0 || variant > 2) return HAKMC_EINVAL;
+  CKL(launch_exp_probe(out, in, n, variant, (cudaStream_t)stream));
   return 0;
 }
 
@@ -1904,12 +1911,7 @@ extern "C" int hakmc_rope_neox(float* x, int n_heads, int head_dim, int pos, flo
   int r = scratch(&s, 0, (size_t)half * 2);
   if (r) return r;
   std::vector<float> cs((size_t)half * 2);
-  for (int i = 0; i < half; i++) {
-    const float freq = powf(theta, -((float)(2 * i) / (float)head_dim));
-    const float ang = (float)pos * freq;
-    cs[2 * i] = cosf(ang);
-    cs[2 * i + 1] = sinf(ang);
-  }
+  hakm_host_rope_row(cs.data(), head_dim, pos, theta);
   cudaStream_t st = (cudaStream_t)stream;
   CKL(cudaMemcpyAsync(s->rope, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice, st));
   CKL(launch_rope(x, s->rope, nullptr, n_heads, head_dim, st));

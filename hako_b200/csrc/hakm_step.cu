@@ -159,8 +159,7 @@ struct EpiPre {
 };
 
 // Per-segment stage geometry of this CTA, computed once per phase: R whole
-// rows per stage (one bulk copy), units of 4 rows x one chunk. unit -> (row
-// group, chunk) uses a multiply-shift (exact for unit < 2^16 / nch).
+// rows per stage (one bulk copy), units of ur (4, or 2) whole rows.
 struct SegGeo {
   int type, rowB, R, nch, chunkB, rn, ur;
 };
@@ -198,7 +197,6 @@ __device__ bool build_activation_ll(const PhaseParams& p, const uint64_t* x, uin
   bool ok = true;
   if (p.act == ACT_RMS) {
     float v[RMS_SLOTS][8];
-    float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < RMS_SLOTS; j++) {
       const int s = t + j * nt;
@@ -208,22 +206,28 @@ __device__ bool build_activation_ll(const PhaseParams& p, const uint64_t* x, uin
 #pragma unroll
           for (int i = 0; i < 8; i++) plain[8 * s + i] = v[j][i];
         }
+        // squares by lane class for the scale (src/nn.c:15 as built)
 #pragma unroll
-        for (int i = 0; i < 8; i++) ss += v[j][i] * v[j][i];
+        for (int i = 0; i < 8; i++) A.xc[i * A.cp + s] = __fmul_rn(v[j][i], v[j][i]);
       } else {
 #pragma unroll
         for (int i = 0; i < 8; i++) v[j][i] = 0.f;
       }
     }
-    const float tot = consumers_sum(ss, red);
-    // src/nn.c:16-17: scale = 1/sqrtf(ss/n + eps); y = x * scale * w
-    const float scale = 1.0f / sqrtf(tot / (float)K + p.eps);
+    consumers_sync();
+    if (t < 32) {
+      const float sc = rms_scale(A.xc, A.cp, K, p.eps, p.rsq);
+      if (t == 0) red[0] = sc;
+    }
+    consumers_sync();
+    const float scale = red[0];
+    // src/nn.c:17 as built: y = (x * w) * scale
 #pragma unroll
     for (int j = 0; j < RMS_SLOTS; j++) {
       const int s = t + j * nt;
       if (j * nt >= nslot) break;  // uniform: no live slot for any thread
 #pragma unroll
-      for (int i = 0; i < 8; i++) v[j][i] = v[j][i] * scale * wpre[j][i];
+      for (int i = 0; i < 8; i++) v[j][i] = __fmul_rn(__fmul_rn(v[j][i], wpre[j][i]), scale);
       store_slot(p, s, s < nslot, v[j], A);
     }
   } else {
@@ -322,10 +326,10 @@ __device__ __forceinline__ void epi_apply(const StepArgs& A, const PhaseDesc& D,
     for (int c = 1; c < nch; c++) a1 += pp[nch + c];
     if (kind == EPI_SWIGLU) {
       // src/model.c:154 with silu_f (src/nn.c:29)
-      put_all<TP>(A, D.out_ll[s] + e.o0, ll_word(a0 / (1.0f + expf(-a0)) * a1, tag));
+      put_all<TP>(A, D.out_ll[s] + e.o0, ll_word(swiglu_exact(a0, a1), tag));
       return;
     }
-    const float x0 = a0 + e.f0, x1 = a1 + e.f1;
+    const float x0 = __fadd_rn(a0, e.f0), x1 = __fadd_rn(a1, e.f1);
     // src/nn.c:38-40
     const float2 rr = rope_rotate(x0, x1, e.f2, e.f3);
     const float r0 = rr.x, r1 = rr.y;
@@ -342,7 +346,7 @@ __device__ __forceinline__ void epi_apply(const StepArgs& A, const PhaseDesc& D,
     }
     return;
   }
-  const float o = a0 + e.f0;  // residual or bias (0 when none)
+  const float o = __fadd_rn(a0, e.f0);  // residual or bias (0 when none)
   put_all<TP>(A, D.out_ll[s] + e.o0, ll_word(o, tag));
   if (kind == EPI_V_CACHE) {
     float* vc = p.seg[s].cache + A.kv_off + (size_t)pos * p.kv_dim + e.o0;
@@ -374,11 +378,11 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
         const float a0 = row_total(part, r, dr), a1 = row_total(part, r, dr + 1);
         if (S.epi == EPI_SWIGLU) {
           // src/model.c:154 with silu_f (src/nn.c:29)
-          put_all<TP>(A, out + (dr >> 1), ll_word(a0 / (1.0f + expf(-a0)) * a1, tag));
+          put_all<TP>(A, out + (dr >> 1), ll_word(swiglu_exact(a0, a1), tag));
         } else {
           const bool first = q == t;
-          const float x0 = S.bias ? a0 + (first ? pre.b0 : S.bias[dr]) : a0;
-          const float x1 = S.bias ? a1 + (first ? pre.b1 : S.bias[dr + 1]) : a1;
+          const float x0 = S.bias ? __fadd_rn(a0, first ? pre.b0 : S.bias[dr]) : a0;
+          const float x1 = S.bias ? __fadd_rn(a1, first ? pre.b1 : S.bias[dr + 1]) : a1;
           const bool is_k = dr >= S.split;
           const int lr = is_k ? dr - S.split : dr;
           const int hd = p.head_dim, half = hd >> 1;
@@ -407,11 +411,11 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
           case EPI_RESID: {
             float old = res;
             if (row != r.row0 + t) ok &= ll_get1(D.res_ll + row, res_tag, old, err);
-            put_all<TP>(A, out + row, ll_word(old + v, tag));
+            put_all<TP>(A, out + row, ll_word(__fadd_rn(old, v), tag));
             break;
           }
           case EPI_V_CACHE: {
-            const float o = S.bias ? v + (row == r.row0 + t ? pre.bv : S.bias[row]) : v;
+            const float o = S.bias ? __fadd_rn(v, row == r.row0 + t ? pre.bv : S.bias[row]) : v;
             put_all<TP>(A, out + row, ll_word(o, tag));
             float* vc = S.cache + A.kv_off + (size_t)pos * p.kv_dim + row;
             for (int rr = 0; rr < W; rr++) *on_rank(A, vc, XR_VCACHE, rr) = o;
@@ -425,7 +429,7 @@ __device__ bool epilogue_ll(const StepArgs& A, const PhaseDesc& D, const SegRang
             break;
           }
           default:
-            put_all<TP>(A, out + row, ll_word(S.bias ? v + S.bias[row] : v, tag));
+            put_all<TP>(A, out + row, ll_word(S.bias ? __fadd_rn(v, S.bias[row]) : v, tag));
             break;
         }
       }
@@ -456,6 +460,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
   uint8_t* region = ring + (size_t)S_ * SB;  // activation of a GEMV phase / attention tiles
   float* part = reinterpret_cast<float*>(region + A.region_bytes);
   float* red = part + A.part_floats;
+  float* wscr = red + 64;  // per-warp unit scratch (WARP_SCRATCH_FLOATS each)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned grid = gridDim.x, vcta = blockIdx.x;
   const int NP = A.n_phases + 1;  // tags per step: embedding + program
@@ -517,7 +522,6 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
   const int t = threadIdx.x - 32, nt = CONSUMER_WARPS * 32, cw = warp - 1;
   Ring rc;              // next stage to consume (the producer's order)
   unsigned ucount = 0;  // 4-row units seen; rotates units over the warps
-  unsigned tick = 0;    // attention split tickets handed out so far (per kv head)
   int kph = 0;          // phases run (trace index)
   bool bad = false;     // a wait of this thread gave up
   const int* err = A.err_flag;
@@ -645,7 +649,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
           if (P.n_seg > 1 && P.seg[1].epi == EPI_V_CACHE && P.seg[1].bias && sr[1].row0 + t < sr[1].row1)
             pre.bv = __ldg(P.seg[1].bias + sr[1].row0 + t);
         }
-        const Act X = carve_act(region, K, P.need_q8, P.need_q6);
+        const Act X = carve_act(region, K, P.need_q8, P.need_q6 || P.act == ACT_RMS);
         float* plain =
             (P.seg[0].epi == EPI_ARGMAX && vcta == 0) ? A.xb_plain : nullptr;
         bad |= !build_activation_ll(P, D.x_ll, tag_of(step, D.x_src), wpre, X, red, err, plain);
@@ -654,8 +658,11 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         bool failed = false;
         for (int s = 0; s < P.n_seg && !failed; s++) {
           const SegGeo G = seg_geo(D, s);
-          const int n_units_full = ((G.R + G.ur - 1) / G.ur) * G.nch;
+          // units of ur whole rows (every chunk, in order: the row sums are
+          // sequential over the row, as the reference's are)
+          const int n_units_full = (G.R + G.ur - 1) / G.ur;
           float* ps = part + sr[s].part_base;
+          float* tr = wscr + cw * WARP_SCRATCH_FLOATS;
           for (int rt = sr[s].row0; rt < sr[s].row1; rt += G.R) {
             if (!mbar_wait_or_abort(smem_addr(&full[rc.slot]), rc.par, err)) {
               failed = true;
@@ -663,28 +670,21 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
             }
             const int nr = min(G.R, sr[s].row1 - rt);
             const uint8_t* stage = ring + (size_t)rc.slot * SB;
-            // this warp's units: u = first, first + 12, ... (rotated by ucount)
+            // this warp's units: u = first, first + 11, ... (rotated by ucount)
             const int first = (int)((unsigned)(cw + CONSUMER_WARPS) - ucount % CONSUMER_WARPS) % CONSUMER_WARPS;
             for (int u = first; u < n_units_full; u += CONSUMER_WARPS) {
-              const int grp = (u * G.rn) >> 16, c = u - grp * G.nch;
-              const int t0 = G.ur * grp, nru = min(G.ur, nr - t0);
+              const int t0 = G.ur * u, nru = min(G.ur, nr - t0);
               if (nru <= 0) continue;
-              const uint8_t* st = stage + t0 * G.rowB + c * G.chunkB;
-              const int m = q6_chunk_blocks(nb, c);
-              float acc[4];
+              const uint8_t* st = stage + t0 * G.rowB;
+              float* dst = ps + (rt - sr[s].row0 + t0);
               if (G.type == W_Q4K) {
-                const Q4X xq = q4x_load(X.xq, X.xs, X.xsum, c, nb);
-                if (G.ur == 2) q4k_unit<2>(st, G.rowB, nru, m, xq, acc);
-                else q4k_unit<4>(st, G.rowB, nru, m, xq, acc);
+                const float tot = G.ur == 2 ? q4k_rows<2>(st, G.rowB, nru, nb, X, tr)
+                                            : q4k_rows<4>(st, G.rowB, nru, nb, X, tr);
+                if (lane < nru) dst[lane] = tot;
               } else {
-                Q6L L;
-                q6l_load(X, c, nb, L);
-                if (G.ur == 2) q6k_unit<2>(st, G.rowB, nru, m, L, acc);
-                else q6k_unit<4>(st, G.rowB, nru, m, L, acc);
+                const float tot = q6k_rows(st, G.rowB, nru, nb, X, tr);
+                if ((lane & 7) == 0 && (lane >> 3) < nru) dst[lane >> 3] = tot;
               }
-              const float tot = reduce4(acc);
-              if ((lane & 7) == 0 && (lane >> 3) < nru)
-                ps[(rt - sr[s].row0 + t0 + (lane >> 3)) * G.nch + c] = tot;
             }
             ucount += (unsigned)n_units_full;
             __syncwarp();
@@ -703,9 +703,6 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         if (n_rec) consumers_sync();
       } else {
         consumers_sync();  // the next descriptor is staged; CTAs without items have no other barrier here
-        AttnParams a = D.a;
-        a.n_split = pos / ATTN_CHUNK + 1;
-        if (a.n_split > 1) tick += (unsigned)a.n_split;  // a single split draws no ticket
         AttnLL T;
         T.q = D.x_ll;
         T.k = D.res_ll;
@@ -713,21 +710,17 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         T.out = D.out_ll[0];
         T.in_tag = tag_of(step, D.x_src);
         T.out_tag = tag;
-        T.ticket_target = tick;
         T.err = err;
         T.n_dst = n_ranks<TP>(A);
         T.out_delta = &A.tp_delta[0][XR_LL];
         T.delta_stride = XR_COUNT;
         T.kv_off = A.kv_off;
-        // (kv head, query-head group) units; with tensor parallelism this GPU
-        // runs units rank, rank + world, ... (all splits of a unit stay here)
-        const int n_units = a.n_heads / a.head_group;
-        const int n_loc = (n_units - A.tp_rank + A.tp_world - 1) / A.tp_world;
-        const int items = n_loc * a.n_split;
+        // (query head, dimension slice) units; with tensor parallelism this
+        // GPU runs units rank, rank + world, ...
+        const int n_loc = attn_units_local(attn_units(D.a.n_heads, HD), A.tp_rank, A.tp_world);
         float* sm = reinterpret_cast<float*>(region);
-        for (int it = (int)vcta; it < items; it += grid)
-          bad |= !attn_item<HD, true>(a, A.tp_rank + A.tp_world * (it % n_loc), it / n_loc, pos, sm, t, nt,
-                                      ConsumerSync(), T);
+        for (int it = (int)vcta; it < n_loc; it += grid)
+          bad |= !attn_item<HD, true>(D.a, attn_unit_of(A.tp_rank, A.tp_world, it), pos, sm, t, nt, ConsumerSync(), T);
         // the next phase writes the shared region (activation, epilogue
         // records): every thread must be done with the attention tiles
         consumers_sync();
@@ -787,7 +780,6 @@ void step_ranges(const PhaseDesc* prog, int n_phases, int grid, int cta0, int n_
       for (int s = 0; s < MAX_SEGS; s++) sr[s] = SegRange{0, 0, 1, 0};
       if (prog[ph].kind != PK_GEMV) continue;
       const PhaseParams& p = prog[ph].g;
-      const int nb = p.n_in / QK;
       unsigned goff = 0;
       int pbase = 0;
       for (int s = 0; s < p.n_seg; s++) {
@@ -797,16 +789,17 @@ void step_ranges(const PhaseDesc* prog, int n_phases, int grid, int cta0, int n_
         const int g0 = (int)(idx * G / grid), g1 = (int)((idx + 1) * G / grid);
         sr[s].row0 = 4 * g0;
         sr[s].row1 = std::min(4 * g1, n);
-        sr[s].nch = n_chunks(nb);
+        sr[s].nch = 1;  // one result per row
         sr[s].part_base = pbase;
-        pbase += (sr[s].row1 - sr[s].row0) * sr[s].nch;
+        pbase += sr[s].row1 - sr[s].row0;
         goff += G;
       }
     }
 }
 
 size_t step_smem_bytes(const StepArgs& a) {
-  return SMEM_HEADER + (size_t)a.n_stages * a.slot_bytes + a.region_bytes + (size_t)a.part_floats * 4 + 64 * 4;
+  return SMEM_HEADER + (size_t)a.n_stages * a.slot_bytes + a.region_bytes + (size_t)a.part_floats * 4 + 64 * 4 +
+         WARP_SCRATCH_BYTES;
 }
 
 bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
@@ -815,30 +808,29 @@ bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
   for (int ph = 0; ph < n_phases; ph++) {
     const PhaseDesc& D = prog[ph];
     if (D.kind == PK_ATTN) {
-      if (D.a.n_heads % D.a.n_kv || D.a.n_heads / D.a.n_kv > ATTN_MAXG) return false;
-      if (D.a.head_group <= 0 || (D.a.n_heads / D.a.n_kv) % D.a.head_group || D.a.n_heads / D.a.head_group > 64)
-        return false;
+      if (D.a.n_heads % D.a.n_kv || !D.a.part || D.a.score_stride < 1) return false;
       if (D.a.head_dim != 64 && D.a.head_dim != 128) return false;
       region = std::max(region, attn_smem_bytes(D.a.head_dim));
       continue;
     }
     const PhaseParams& P = D.g;
     if (P.n_in % QK || (P.act != ACT_RMS && P.act != ACT_F32) ||
-        (P.act == ACT_RMS && P.n_in > 8 * RMS_SLOTS * CONSUMER_WARPS * 32))
+        (P.act == ACT_RMS && (P.n_in > 8 * RMS_SLOTS * CONSUMER_WARPS * 32 || !P.rsq)))
       return false;
     const int nb = P.n_in / QK;
-    region = std::max(region, act_bytes(P.n_in, P.need_q8, P.need_q6));
+    region = std::max(region, act_bytes(P.n_in, P.need_q8, P.need_q6 || P.act == ACT_RMS));
     int pf = 0;
     for (int s = 0; s < P.n_seg; s++) {
       max_row = std::max(max_row, dev_row_bytes(P.seg[s].type, nb));
       const int G = (P.seg[s].n_rows + 3) / 4;
-      pf += ((G + grid - 1) / grid) * 4 * n_chunks(nb);
+      pf += ((G + grid - 1) / grid) * 4;
     }
     part = std::max(part, pf);
   }
   a.region_bytes = (int)((region + 127) & ~(size_t)127);
   a.part_floats = (part + 3) & ~3;
-  const long ring = (long)STEP_SMEM_MAX - SMEM_HEADER - a.region_bytes - (long)a.part_floats * 4 - 64 * 4;
+  const long ring =
+      (long)STEP_SMEM_MAX - SMEM_HEADER - a.region_bytes - (long)a.part_floats * 4 - 64 * 4 - WARP_SCRATCH_BYTES;
   if (max_row == 0 || ring < 2L * (long)max_row) return false;
   // slots of at least 4 of the longest rows while that leaves 2 slots;
   // HAKMC_STEP_STAGES overrides the slot count (measurement)
@@ -862,7 +854,7 @@ bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
     if (D.kind != PK_GEMV) continue;
     {
       // per-thread epilogue records past the activation, when they fit
-      const size_t act = (act_bytes(D.g.n_in, D.g.need_q8, D.g.need_q6) + 15) & ~(size_t)15;
+      const size_t act = (act_bytes(D.g.n_in, D.g.need_q8, D.g.need_q6 || D.g.act == ACT_RMS) + 15) & ~(size_t)15;
       const size_t recs = (size_t)CONSUMER_WARPS * 32 * EPI_RECS * sizeof(EpiRec);
       if (act + recs <= (size_t)a.region_bytes) D.epi_rec_off = (int)act;
     }
@@ -873,11 +865,11 @@ bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
       D.st_nch[s] = n_chunks(nb);
       D.st_rn[s] = (65536 + D.st_nch[s] - 1) / D.st_nch[s];
       if (D.st_rows[s] < 1) return false;
-      // a segment that gives each CTA a single 4-row unit (the 3B attn_v
-      // rows) runs as two 2-row units on two warps: half the latency. With
-      // more units per CTA the extra activation loads cost more (measured).
+      // a Q4_K segment that gives each CTA a single 4-row unit runs as two
+      // 2-row units on two warps: half the latency. With more units per CTA
+      // the extra activation loads cost more (measured).
       const int max_groups = ((D.g.seg[s].n_rows + 3) / 4 + grid - 1) / grid;
-      D.st_unit_rows[s] = max_groups * D.st_nch[s] == 1 ? 2 : 4;
+      D.st_unit_rows[s] = (max_groups == 1 && D.g.seg[s].type == W_Q4K) ? 2 : 4;
     }
   }
   return step_smem_bytes(a) <= (size_t)STEP_SMEM_MAX;

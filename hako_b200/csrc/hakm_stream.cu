@@ -15,11 +15,11 @@
 //   warps 1..8  consumers: wait for the previous kernel (griddepcontrol.wait),
 //               rebuild the activation in shared memory (rmsnorm and per-32
 //               int8 quantization, src/nn.c:13-18 and src/quant.c:127-144),
-//               then each takes 4-row units of a stage: Q4_K rows with dp4a
-//               integer sub-block sums (src/quant.c:150-232), Q6_K rows as an
-//               fp32 dot on the fly (src/nn.c:84-95, src/quant.c:94-123).
-//               Per-(row, chunk) partial sums land in shared memory and are
-//               summed in a fixed order, so results are deterministic.
+//               then each takes 4-row units of a stage (whole rows): Q4_K
+//               rows with dp4a integer sub-block sums (src/quant.c:150-232),
+//               Q6_K rows as the fp32 dot on the fly (src/nn.c:84-95,
+//               src/quant.c:94-123), both with the reference's roundings
+//               (hakm_gemv.cuh); one result per row lands in shared memory.
 //   epilogue    bias / residual / NeoX RoPE + K append / V append / SwiGLU /
 //               logits + greedy argmax, and for the lm_head phase the step
 //               finalisation (next token, token log, position + 1).
@@ -32,11 +32,8 @@ namespace hakm {
 
 // ------------------------------------------------------------------ kernel
 
-// KINDS: bit 0 = Q4_K segments, bit 1 = Q6_K segments. CACHE: the lane's
-// activation slices stay in registers for the whole kernel (rows of at most
-// two chunks for Q4_K, one chunk for Q6_K); otherwise they are re-read from
-// shared memory per 4-row unit.
-template <int KINDS, bool CACHE>
+// KINDS: bit 0 = Q4_K segments, bit 1 = Q6_K segments.
+template <int KINDS>
 __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constant__ PhaseParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -45,9 +42,11 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
   uint8_t* ring = smem + SMEM_HEADER;
   const int K = p.n_in, nb = K / QK, nsb = K / 32;
   uint8_t* act = ring + (size_t)S_ * SB;
-  const Act A = carve_act(act, K, p.need_q8, p.need_q6);
-  float* part = reinterpret_cast<float*>(act + act_bytes(K, p.need_q8, p.need_q6));
+  const bool f32 = p.need_q6 || p.act == ACT_RMS;
+  const Act A = carve_act(act, K, p.need_q8, f32);
+  float* part = reinterpret_cast<float*>(act + act_bytes(K, p.need_q8, f32));
   float* red = part + p.part_floats;
+  float* wscr = red + 64;  // per-warp unit scratch
   (void)nsb;
 
   pdl_launch_dependents();
@@ -120,25 +119,14 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
     if (threadIdx.x == 32) TRACE(1);
     const int groups = phase_groups(nb), wpg = CONSUMER_WARPS / groups;
     const int cw = warp - 1, mine = cw / wpg, unit = cw % wpg;
+    float* tr = wscr + cw * WARP_SCRATCH_FLOATS;
     bool first = true;
-    // short rows: the lane's activation slice stays in registers for the kernel
-    const int nch_all = n_chunks(nb);
-    constexpr bool c4 = CACHE && (KINDS & 1);
-    constexpr bool c6 = CACHE && KINDS == 2;
-    Q4X x4c0, x4c1;
-    Q6L x6c;
-    if constexpr (c4) {
-      x4c0 = q4x_load(A.xq, A.xs, A.xsum, 0, nb);
-      x4c1 = nch_all > 1 ? q4x_load(A.xq, A.xs, A.xsum, 1, nb) : x4c0;
-    }
-    if constexpr (c6) q6l_load(A, 0, nb, x6c);
     int i = 0;
     for (int s = 0; s < p.n_seg && !failed; s++) {
       const int type = (KINDS == 1) ? W_Q4K : (KINDS == 2) ? W_Q6K : p.seg[s].type;
       const int rowB = (int)dev_row_bytes(type, nb);
-      const int R = stage_rows(type, nb), nch = sr[s].nch;
-      const int chunkB = type == W_Q4K ? Q4K_CHUNK : Q6K_CHUNK;
-      const int n_units = ((R + 3) / 4) * nch;  // (4-row group, chunk) cells of a stage
+      const int R = stage_rows(type, nb);
+      const int n_units = (R + 3) / 4;  // 4-row units of whole rows
       for (int rt = sr[s].row0; rt < sr[s].row1; rt += R, i++) {
         if (i % groups != mine) continue;
         const int nr = min(R, sr[s].row1 - rt);
@@ -148,32 +136,21 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
         first = false;
         const uint8_t* stage = ring + (size_t)slot * SB;
         for (int u = unit; u < n_units; u += wpg) {
-          const int c = u % nch, t0 = 4 * (u / nch), nru = min(4, nr - t0);
+          const int t0 = 4 * u, nru = min(4, nr - t0);
           if (nru <= 0) continue;
-          const uint8_t* st = stage + (size_t)t0 * rowB + (size_t)c * chunkB;
-          const int m = q6_chunk_blocks(nb, c);
-          float acc[4];
-#pragma unroll
-          for (int r = 0; r < 4; r++) acc[r] = 0.f;
+          const uint8_t* st = stage + (size_t)t0 * rowB;
+          float* dst = part + sr[s].part_base + (rt - sr[s].row0 + t0);
           if (type == W_Q4K) {
             if constexpr (KINDS & 1) {
-              if constexpr (c4) q4k_unit(st, rowB, nru, m, c == 0 ? x4c0 : x4c1, acc);
-              else q4k_unit(st, rowB, nru, m, q4x_load(A.xq, A.xs, A.xsum, c, nb), acc);
+              const float tot = q4k_rows<4>(st, rowB, nru, nb, A, tr);
+              if (lane < nru) dst[lane] = tot;
             }
           } else {
             if constexpr (KINDS & 2) {
-              if constexpr (c6) {
-                q6k_unit(st, rowB, nru, m, x6c, acc);
-              } else {
-                Q6L X;
-                q6l_load(A, c, nb, X);
-                q6k_unit(st, rowB, nru, m, X, acc);
-              }
+              const float tot = q6k_rows(st, rowB, nru, nb, A, tr);
+              if ((lane & 7) == 0 && (lane >> 3) < nru) dst[lane >> 3] = tot;
             }
           }
-          const float tot = reduce4(acc);
-          if ((lane & 7) == 0 && (lane >> 3) < nru)
-            part[sr[s].part_base + (rt - sr[s].row0 + t0 + (lane >> 3)) * nch + c] = tot;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_addr(&empty[slot]));
@@ -234,11 +211,12 @@ static size_t plan(PhaseParams& q, int grid) {
     const size_t sb = (size_t)stage_rows(q.seg[s].type, nb) * dev_row_bytes(q.seg[s].type, nb);
     slot = sb > slot ? sb : slot;
     const int G = (q.seg[s].n_rows + 3) / 4;
-    part += ((G + grid - 1) / grid) * 4 * n_chunks(nb);
+    part += ((G + grid - 1) / grid) * 4;
   }
   q.stage_bytes = (int)slot;
   q.part_floats = (part + 3) & ~3;
-  const size_t fixed = SMEM_HEADER + act_bytes(K, q.need_q8, q.need_q6) + (size_t)q.part_floats * 4 + 64 * 4;
+  const size_t fixed = SMEM_HEADER + act_bytes(K, q.need_q8, q.need_q6 || q.act == ACT_RMS) +
+                       (size_t)q.part_floats * 4 + 64 * 4 + WARP_SCRATCH_BYTES;
   // Stage i lives in slot i % S and is consumed by group i % groups. S must
   // be a multiple of groups: then every slot belongs to one group, which waits
   // on that slot's phases strictly in order — a parity wait can never see a
@@ -258,13 +236,13 @@ size_t phase_smem_bytes(const PhaseParams& p, int grid) {
   return plan(q, grid);
 }
 
-template <int KINDS, bool CACHE>
+template <int KINDS>
 static cudaError_t launch_k(const PhaseParams& p, int grid, size_t smem, cudaStream_t s, bool pdl) {
   static unsigned done = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 32 && !(done & (1u << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(stream_kernel<KINDS, CACHE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(stream_kernel<KINDS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          PHASE_SMEM_MAX);
     if (e != cudaSuccess) return e;
     done |= 1u << dev;
@@ -279,7 +257,7 @@ static cudaError_t launch_k(const PhaseParams& p, int grid, size_t smem, cudaStr
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, stream_kernel<KINDS, CACHE>, p);
+  return cudaLaunchKernelEx(&cfg, stream_kernel<KINDS>, p);
 }
 
 cudaError_t launch_phase(const PhaseParams& p0, int num_sms, cudaStream_t s, bool pdl) {
@@ -288,10 +266,11 @@ cudaError_t launch_phase(const PhaseParams& p0, int num_sms, cudaStream_t s, boo
   const int grid = phase_grid_size(p, num_sms);
   const size_t smem = plan(p, grid);
   if (smem > (size_t)PHASE_SMEM_MAX || p.n_stages > MAX_STAGES) return cudaErrorInvalidValue;
-  const int kinds = phase_kinds(p), nch = n_chunks(p.n_in / QK);
-  if (kinds == 1) return nch <= 2 ? launch_k<1, true>(p, grid, smem, s, pdl) : launch_k<1, false>(p, grid, smem, s, pdl);
-  if (kinds == 2) return nch == 1 ? launch_k<2, true>(p, grid, smem, s, pdl) : launch_k<2, false>(p, grid, smem, s, pdl);
-  return nch <= 2 ? launch_k<3, true>(p, grid, smem, s, pdl) : launch_k<3, false>(p, grid, smem, s, pdl);
+  if (p.act == ACT_RMS && !p.rsq) return cudaErrorInvalidValue;
+  const int kinds = phase_kinds(p);
+  if (kinds == 1) return launch_k<1>(p, grid, smem, s, pdl);
+  if (kinds == 2) return launch_k<2>(p, grid, smem, s, pdl);
+  return launch_k<3>(p, grid, smem, s, pdl);
 }
 
 }  // namespace hakm

@@ -15,9 +15,10 @@ import os
 
 import numpy as np
 
-from ._lib import LIB_DIR
-
+# no import of ._lib here: the workload generator must not map the CUDA library
+LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 SYNTH_LIB_PATH = os.path.join(LIB_DIR, "libhakm_synth.so")
+SYNTH_EXE_PATH = os.path.join(LIB_DIR, "hakm_synth")
 
 
 class _Cfg(C.Structure):
@@ -111,12 +112,26 @@ def lib() -> C.CDLL:
     return _lib
 
 
-def model_size(cfg: ModelConfig) -> int:
+def _exe_args(cfg: ModelConfig) -> list[str]:
+    return [str(v) for v in (cfg.n_layers, cfg.d_model, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn_dim,
+                             cfg.vocab, cfg.ctx, repr(float(cfg.rope_theta)), repr(float(cfg.rms_eps)),
+                             int(cfg.tied), int(cfg.qkv_bias), cfg.seed, repr(float(cfg.wstd)))]
+
+
+def model_size(cfg: ModelConfig, via_exe: bool = False) -> int:
+    if via_exe:
+        import subprocess
+        r = subprocess.run([SYNTH_EXE_PATH, "size", *_exe_args(cfg)], capture_output=True, text=True, check=True)
+        return int(r.stdout.strip())
     c = cfg._c()
     return int(lib().synth_model_size(C.byref(c)))
 
 
-def write_model(path: str, cfg: ModelConfig, threads: int = 0) -> str:
+def write_model(path: str, cfg: ModelConfig, threads: int = 0, via_exe: bool = False) -> str:
+    if via_exe:
+        import subprocess
+        subprocess.run([SYNTH_EXE_PATH, "write", path, *_exe_args(cfg)], check=True)
+        return path
     c = cfg._c()
     rc = lib().synth_write_model(path.encode(), C.byref(c), threads)
     if rc != 0:
@@ -124,22 +139,25 @@ def write_model(path: str, cfg: ModelConfig, threads: int = 0) -> str:
     return path
 
 
-def cached_model(cfg: ModelConfig, directory: str | None = None) -> str:
+def cached_model(cfg: ModelConfig, directory: str | None = None, via_exe: bool = False) -> str:
     """Write the model once per machine (under /dev/shm when it has room) and
-    return its path; the file name carries the full config."""
+    return its path; the file name carries the full config. via_exe: use the
+    stand-alone writer (hakm_synth) so this process maps no library of this
+    package."""
     d = directory or ("/dev/shm" if os.path.isdir("/dev/shm") else "/tmp")
     tag = hashlib.sha1(repr(dataclasses.astuple(cfg)).encode()).hexdigest()[:12]
     path = os.path.join(d, f"hakm_synth_{cfg.name}_{tag}.mlf2")
-    if os.path.exists(path) and os.path.getsize(path) == model_size(cfg):
+    size = model_size(cfg, via_exe)
+    if os.path.exists(path) and os.path.getsize(path) == size:
         return path
     import fcntl
     # one writer per machine: concurrent callers (e.g. the ranks of a
     # multi-GPU job) wait for it instead of writing the same file
     with open(path + ".lock", "w") as lk:
         fcntl.flock(lk, fcntl.LOCK_EX)
-        if not os.path.exists(path) or os.path.getsize(path) != model_size(cfg):
+        if not os.path.exists(path) or os.path.getsize(path) != size:
             tmp = path + f".{os.getpid()}.part"
-            write_model(tmp, cfg)
+            write_model(tmp, cfg, via_exe=via_exe)
             os.replace(tmp, path)
     return path
 

@@ -395,3 +395,30 @@ int synth_write_model(const char *path, const synth_cfg *c, int n_threads) {
 	munmap(m, total);
 	return 0;
 }
+
+#ifdef SYNTH_MAIN
+/* Stand-alone writer (hako_b200/_lib/hakm_synth): lets a process that must
+ * not map this library (the benchmark's reference arm) still produce the
+ * seeded model file.
+ *   hakm_synth size  L D H KVH HD F V CTX THETA EPS TIED BIAS SEED WSTD
+ *   hakm_synth write PATH L D H KVH HD F V CTX THETA EPS TIED BIAS SEED WSTD */
+#include <stdio.h>
+int main(int argc, char **argv) {
+	int write = argc == 17 && strcmp(argv[1], "write") == 0;
+	if (!write && !(argc == 16 && strcmp(argv[1], "size") == 0)) {
+		fprintf(stderr, "usage: %s size|write [PATH] L D H KVH HD F V CTX THETA EPS TIED BIAS SEED WSTD\n", argv[0]);
+		return 2;
+	}
+	char **a = argv + (write ? 3 : 2);
+	synth_cfg c;
+	c.n_layers = atoi(a[0]); c.d_model = atoi(a[1]); c.n_heads = atoi(a[2]); c.n_kv_heads = atoi(a[3]);
+	c.head_dim = atoi(a[4]); c.ffn_dim = atoi(a[5]); c.vocab = atoi(a[6]); c.ctx = atoi(a[7]);
+	c.rope_theta = strtof(a[8], NULL); c.rms_eps = strtof(a[9], NULL); c.tied = atoi(a[10]);
+	c.qkv_bias = atoi(a[11]); c.seed = strtoull(a[12], NULL, 10); c.wstd = strtof(a[13], NULL);
+	if (!write) {
+		printf("%llu\n", (unsigned long long)synth_model_size(&c));
+		return 0;
+	}
+	return synth_write_model(argv[2], &c, 0) == 0 ? 0 : 1;
+}
+#endif

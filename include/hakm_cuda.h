@@ -257,9 +257,11 @@ int hakmc_q4k_subsums(int32_t *iqx, int32_t *ix, const void *w, const int8_t *xq
                       int n_out, int n_in, void *stream);
 
 /* Re-lay n_rows rows of verbatim 210-byte block_q6_K (src/quant.h:19-24)
- * into this library's device layout (same byte count): per row the
- * 208-byte {ql, qh, scales} parts of each block, then one plane of fp16 d.
- * [dev] src and dst must not overlap. */
+ * into this library's device layout (same byte count): per chunk of 8
+ * blocks the 208-byte {ql, qh, scales} parts (the ql/qh bytes regrouped by
+ * the element's index mod 8, the lane of the reference's vectorized dot that
+ * adds it), then the chunk's fp16 d values. [dev] src and dst must not
+ * overlap. */
 int hakmc_q6k_pack(void *dst, const void *src, int n_rows, int n_in, void *stream);
 size_t hakmc_q6k_packed_bytes(int n_rows, int n_in);
 
@@ -280,15 +282,19 @@ int hakmc_lmhead_argmax(float *logits, int *argmax, const void *w_packed,
  * in include/mlf2.h:44-49) to fp32 (src/quant.c:68-123, 234-248). */
 int hakmc_dequant(float *out, const void *w, int type, int n_rows, int n_in, void *stream);
 
-/* y = x / rms(x) * w (src/nn.c:13-18), one vector of n. */
+/* y = x / rms(x) * w (src/nn.c:13-18), one vector of n (a multiple of 8),
+ * with the roundings of the reference's own build (8-lane sum of squares,
+ * rsqrtss plus one Newton step): bit-identical results. */
 int hakmc_rmsnorm(float *y, const float *x, const float *w, int n, float eps, void *stream);
 
 /* GQA decode attention for one layer and one sequence over an fp32 cache in
  * the reference layout [max_seq][n_kv*hd] (src/model.c:124-142, softmax
  * src/nn.c:20-27): out[h] = softmax(q_h . K[0..pos] / sqrt(hd)) V[0..pos]
- * for h < n_heads, kv head h / (n_heads/n_kv). [dev] all buffers.
- * Split over positions in chunks of 256 with an in-kernel combine, using a
- * scratch area the library allocates once per device. */
+ * for h < n_heads, kv head h / (n_heads/n_kv), with the reference build's
+ * roundings (bit-identical results). [dev] all buffers. One CTA per (query
+ * head, 32 dimensions); the score rows, n_heads * (head_dim/32) * (pos+1)
+ * floats, live in a scratch area the library allocates per device (and
+ * regrows). Returns after the kernel has finished. */
 int hakmc_attention(float *out, const float *q, const float *k_cache, const float *v_cache,
                     int pos, int n_heads, int n_kv, int head_dim, void *stream);
 
@@ -296,23 +302,47 @@ int hakmc_attention(float *out, const float *q, const float *k_cache, const floa
  * allocate GPU memory once they are running: a host that has handed the
  * whole device budget to another framework's memory pool, or a latency-bound
  * loop that must not take cudaMalloc's implicit device synchronisation. It
- * launches the same kernel as hakmc_attention, but its scratch (split
- * partials, tickets, the position word) lives in one fixed array of about
- * 1 MiB inside this library, which every GPU that loads the library holds
- * until the process exits. Limit: n_heads * ceil((pos + 1) / 64) *
- * (head_dim + 2) <= 262144 floats (for example 16 heads of 128 up to 8064
- * positions, 28 heads up to 4608); larger calls return HAKMC_ERANGE. The
- * first call on a device looks the array up (cudaGetSymbolAddress), so make
- * it before any stream capture. All calls share the array and it keeps the
+ * launches the same kernel as hakmc_attention, but its scratch (the score
+ * rows and the position word) lives in one fixed array of about 1 MiB
+ * inside this library, which every GPU that loads the library holds until
+ * the process exits. Limit: n_heads * (head_dim / 32) * (pos + 1) <= 262144
+ * floats (for example 16 heads of 128 up to 4096 positions, 28 heads up to
+ * 2340); larger calls return HAKMC_ERANGE. Unlike hakmc_attention it does
+ * not wait: it returns once the kernels are enqueued on `stream`, so q, the
+ * caches and out must stay valid until the stream has reached that point,
+ * and a kernel fault shows at the caller's next synchronisation. The first
+ * call on a device looks the array up (cudaGetSymbolAddress), so make it
+ * before any stream capture. All calls share the array and it keeps the
  * last call's contents: calls that overlap on the GPU (other streams, other
  * threads) race, so serialise them. No counterpart in the reference. */
 int hakmc_attention_noalloc(float *out, const float *q, const float *k_cache, const float *v_cache,
                             int pos, int n_heads, int n_kv, int head_dim, void *stream);
 
 /* NeoX RoPE in place on n_heads heads of head_dim at position pos
- * (src/nn.c:32-42), angles from a table built on the host with the
- * reference's formula. */
+ * (src/nn.c:32-42), (cos, sin) from a table built on the host through the
+ * same glibc vector routines the reference's build calls (bit-identical). */
 int hakmc_rope_neox(float *x, int n_heads, int head_dim, int pos, float theta, void *stream);
+
+/* Host-only planning, for tests and tools (no GPU needed). The rows of a
+ * step-kernel phase that CTA `cta` of a `grid`-CTA group computes (with
+ * tensor parallelism the grid spans every rank's CTAs, rank r owning CTAs
+ * r * n_sms ..): seg_rows[s] rows in each of n_seg (<= 3) segments give
+ * ranges[2s] .. ranges[2s+1] (half open; 4-row groups, so row pairs of the
+ * RoPE and SwiGLU epilogues are never split, and rows are whole, so every
+ * row's q8_32 activation blocks stay on one GPU). The attention units
+ * (query head, 32 dimensions) rank `rank` of `world` runs: returns their
+ * count, the first `cap` written to units. No counterpart in the reference
+ * (it has no multi-GPU path). */
+int hakmc_plan_rows(const int *seg_rows, int n_seg, int grid, int cta, int *ranges);
+int hakmc_plan_attn_units(int n_heads, int head_dim, int rank, int world, int *units, int cap);
+
+/* Test hook: out[i] = the device's restatement of one of the reference
+ * build's exp routines applied to in[i]: variant 0 glibc's scalar expf
+ * (silu_f, the softmax tail), 1 libmvec's 8-wide expf, 2 its 4-wide expf
+ * (the vectorized softmax, src/nn.c:24). [dev] buffers of n floats. No
+ * counterpart in the reference (it pins the device against the host's own
+ * libm / libmvec). */
+int hakmc_test_expf(float *out, const float *in, int n, int variant, void *stream);
 
 #ifdef __cplusplus
 }

@@ -472,6 +472,27 @@ void orc_rope_neox(float *vec, int head_dim, int pos, float theta) {
 	free(cs);
 }
 
+/* GQA decode attention at position pos over caches kc / vc laid out
+ * [pos + 1][KVH * hd] (src/model.c:124-142 as built): scores by the
+ * vectorized dot times the rsqrtss scale, the softmax above, then
+ * out[d] = fma(p_s, v_s[d], out[d]) for s = 0..pos from +0. */
+void orc_attention(float *out, const float *q, const float *kc, const float *vc, int pos, int H, int KVH,
+                   int hd) {
+	int KV = KVH * hd, group = H / KVH;
+	float scale = orc_rsqrt_nr((float)hd);
+	float *sc = malloc(sizeof(float) * (size_t)(pos + 1));
+	for (int h = 0; h < H; h++) {
+		int kh = h / group;
+		for (int s = 0; s <= pos; s++) sc[s] = orc_dot_f32(q + h * hd, kc + (size_t)s * KV + kh * hd, hd) * scale;
+		orc_softmax(sc, pos + 1);
+		float *o = out + h * hd;
+		for (int d = 0; d < hd; d++) o[d] = 0.0f;
+		for (int s = 0; s <= pos; s++)
+			for (int d = 0; d < hd; d++) o[d] = fmaf(sc[s], vc[(size_t)s * KV + kh * hd + d], o[d]);
+	}
+	free(sc);
+}
+
 /* MLF2 tensor types (include/mlf2.h:44-49). */
 enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4K = 12, ORC_Q6K = 14 };
 
@@ -636,8 +657,6 @@ static const float *fp(orc_t t) { return (const float *)t.data; }
 const float *orc_forward(orc_model *m, int token) {
 	int D = m->D, H = m->H, KVH = m->KVH, hd = m->hd, KV = KVH * hd, F = m->F, pos = m->pos;
 	if (pos >= m->max_seq || token < 0 || token >= m->V) return NULL;
-	int group = H / KVH;
-	float scale = orc_rsqrt_nr((float)hd);   /* 1.0f / sqrtf(hd) as built */
 	orc_dequant_row(m->tok_embd.type,
 	                m->tok_embd.data + (size_t)token * orc_row_bytes(m->tok_embd.type, D), m->xb, D);
 	for (int l = 0; l < m->run_layers; l++) {
@@ -651,21 +670,7 @@ const float *orc_forward(orc_model *m, int token) {
 		float *kc = m->kc + ((size_t)l * m->max_seq) * KV, *vc = m->vc + ((size_t)l * m->max_seq) * KV;
 		memcpy(kc + (size_t)pos * KV, m->k, sizeof(float) * KV);
 		memcpy(vc + (size_t)pos * KV, m->v, sizeof(float) * KV);
-		memset(m->att, 0, sizeof(float) * D);
-		for (int h = 0; h < H; h++) {
-			int kh = h / group;
-			const float *qh = m->q + h * hd;
-			for (int s = 0; s <= pos; s++) {
-				const float *ks = kc + (size_t)s * KV + kh * hd;
-				m->scores[s] = orc_dot_f32(qh, ks, hd) * scale;
-			}
-			orc_softmax(m->scores, pos + 1);
-			float *o = m->att + h * hd;
-			for (int s = 0; s <= pos; s++) {
-				const float *vs = vc + (size_t)s * KV + kh * hd;
-				for (int d = 0; d < hd; d++) o[d] = fmaf(m->scores[s], vs[d], o[d]);
-			}
-		}
+		orc_attention(m->att, m->q, kc, vc, pos, H, KVH, hd);
 		orc_matmul(m->xn, m->att, y->wo.type, y->wo.data, NULL, D, D);
 		for (int i = 0; i < D; i++) m->xb[i] += m->xn[i];
 		orc_rmsnorm(m->xn, m->xb, fp(y->ffn_norm), D, m->eps);

@@ -74,6 +74,10 @@ void  orc_softmax(float *x, int n);
 float orc_silu(float x);
 void  orc_rope_neox(float *vec, int head_dim, int pos, float theta);
 
+/* GQA decode attention (src/model.c:124-142) over [pos + 1][KVH * hd] caches. */
+void  orc_attention(float *out, const float *q, const float *kc, const float *vc, int pos, int H, int KVH,
+                    int hd);
+
 /* Row-major out[n_out] = W . x (+bias) for an MLF2 tensor of type `type`
  * (src/nn.c:179-210 and the per-row worker src/nn.c:70-97). */
 int orc_matmul(float *out, const float *x, int type, const void *w,

@@ -70,6 +70,10 @@ class Oracle:
             "orc_forward": (C.POINTER(C.c_float), [_vp, _i]),
             "orc_hidden": (C.POINTER(C.c_float), [_vp]),
             "orc_argmax": (_i, [_vp, _i]),
+            "orc_attention": (None, [_vp, _vp, _vp, _vp, _i, _i, _i, _i]),
+            "orc_expf": (_f, [_f]),
+            "orc_expf_v8": (_f, [_f]),
+            "orc_expf_v4": (_f, [_f]),
         }
         for n, (r, a) in sig.items():
             fn = getattr(L, n)
@@ -119,6 +123,15 @@ class Oracle:
         for h in range(x.size // head_dim):
             self.L.orc_rope_neox(C.c_void_p(x.ctypes.data + 4 * h * head_dim), head_dim, pos, theta)
         return x
+
+    def attention(self, q, kc, vc, pos, H, KVH, hd):
+        """kc / vc: [>= pos + 1][KVH * hd] float32."""
+        out = np.empty(H * hd, np.float32)
+        q = np.ascontiguousarray(q, np.float32)
+        kc = np.ascontiguousarray(kc, np.float32)
+        vc = np.ascontiguousarray(vc, np.float32)
+        self.L.orc_attention(_p(out), _p(q), _p(kc), _p(vc), pos, H, KVH, hd)
+        return out
 
 
 class OracleModel:

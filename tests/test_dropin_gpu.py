@@ -3,22 +3,17 @@ reference CLI (cli/main.c) linked against hako_b200/host/hakm_model_cuda.c in
 place of src/model.c, run as a greedy raw completion (`-t 0 --raw`:
 src/sample.c's argmax over the logits hakm_forward returns).
 
-The ids the drop-in is fed (prompt, then its own picks) are logged; the
-reference's greedy continuation of the same prompt ids must agree with them
-up to the first step where the reference's own top-1/top-2 logit margin is
-inside fp32 rounding noise (the int8 flips explained in test_model_gpu.py).
-Where no such step occurs the two CLIs' outputs are byte-identical."""
+The drop-in's forward pass is bit-identical to the reference's, so the ids it
+is fed (prompt, then its own picks, logged) equal the reference's greedy
+continuation of the same prompt ids, and the two CLIs print the same bytes."""
 import os
 import subprocess
 
 import pytest
 
-from conftest import first_divergence
 from oracle.oracle import DROPIN_CLI, REF_CLI
 
 pytestmark = pytest.mark.gpu
-
-GAP_TOL = 2e-2
 
 
 def _run(cli, path, n, prompt, env_extra=None):
@@ -28,12 +23,6 @@ def _run(cli, path, n, prompt, env_extra=None):
                        capture_output=True, env=env, timeout=600)
     assert r.returncode == 0, r.stderr.decode(errors="replace")[-400:]
     return r.stdout
-
-
-# Logit rel-L2 bound against the reference: int8 rounding flips accumulate
-# with depth (measured on the 36-layer 3B model: 7e-7 with no flip, 4e-3 at 8
-# layers, 3.6e-2 at 36 layers after 10 positions).
-LOGIT_BOUND = {"small": 2e-2, "3b": 5e-2}
 
 
 @pytest.mark.parametrize("preset,n", [("small", 40), ("3b", 24)])
@@ -54,33 +43,9 @@ def test_reference_cli_over_dropin(cuda, tmp_path, preset, n):
     assert ids[:len(prompt_ids)] == prompt_ids
     fed = ids[len(prompt_ids):]  # generate(): each pick is fed back (until eos)
     assert fed
-
-    ref_stream, ref_gaps = ref_greedy(path, prompt_ids, n)
-    i = first_divergence(fed, ref_stream[:len(fed)])
-    if i is None:
-        assert ours == _run(REF_CLI, path, n, prompt)
-        return
-    if ref_gaps[i] < GAP_TOL:
-        return
-    # a wider margin: the flip must be explained by the two engines' measured
-    # logits at that step (same prefix), which stay within the parity bound
-    import numpy as np
-    from conftest import rel_l2
-    from hako_b200 import HakmCtx
-    from oracle.oracle import RefModel
-    prefix = prompt_ids + fed[:i]
-    with HakmCtx(path, max_seq=256) as ctx:
-        for t in prefix:
-            lo, _ = ctx.forward(t)
-    ref = RefModel(path, 256)
-    for t in prefix:
-        lr, _ = ref.forward(t)
-    ref.close()
-    a, b = ref_stream[i], fed[i]
-    assert int(np.argmax(lo)) == b
-    assert rel_l2(lo, lr) < LOGIT_BOUND[preset]
-    d_ours, d_ref = float(lo[a] - lo[b]), float(lr[a] - lr[b])
-    assert d_ref > 0 >= d_ours and d_ref <= abs(d_ours - d_ref), (i, d_ours, d_ref)
+    ref_stream, _ = ref_greedy(path, prompt_ids, n)
+    assert fed == ref_stream[:len(fed)]
+    assert ours == _run(REF_CLI, path, n, prompt)
 
 
 def ref_greedy(path, prompt_ids, n):
