@@ -14,7 +14,7 @@
 namespace hakm {
 
 
-constexpr int CONSUMER_WARPS = 11;  // 12 warps in all: 168 registers a thread, no spills
+constexpr int CONSUMER_WARPS = 11;  // 12 warps in all: at most 168 registers a thread, no spills
 constexpr int THREADS = 32 * (CONSUMER_WARPS + 1);
 constexpr int TILE_ROWS = 16;         // most rows a stage holds
 constexpr int STAGE_TARGET = 40 * 1024;  // bytes a stage aims for
@@ -106,11 +106,15 @@ __device__ __forceinline__ void consumers_sync() {
 
 // ------------------------------------------------------------------ schedule
 
-// The fp32 activation "by lane class": xc[l * cls_pitch(K) + t] = x[8t + l],
-// the element order in which the reference's vectorized Q6_K dot feeds lane
-// l of its accumulator (src/nn.c:92). The pitch is padded by 4 floats so the
-// 8 classes' 16-byte reads of a warp fall in distinct banks.
+// The fp32 activation "by lane class": class l holds x[8t + l], t = 0 ..
+// K/8 - 1, the element order in which the reference's vectorized Q6_K dot
+// feeds lane l of its accumulator (src/nn.c:92). Within each aligned group
+// of four positions the middle two are swapped (t0, t2, t1, t3), so one
+// 16-byte read gives the packed-fp32 operand pairs (t0, t2) and (t1, t3).
+// The pitch is padded by 4 floats so the 8 classes' 16-byte reads of a warp
+// fall in distinct banks.
 __host__ __device__ inline int cls_pitch(int K) { return K / 8 + 4; }
+__host__ __device__ inline int cls_slot(int t) { return (t & ~3) | ((t & 1) << 1) | ((t >> 1) & 1); }
 
 // Shared-memory bytes of the activation for an n_in of K: the int8 codes,
 // scales and code sums of q8_32 (Q4_K rows), and the fp32 activation by lane
@@ -212,8 +216,9 @@ __device__ __forceinline__ Act carve_act(uint8_t* base, int K, bool q8, bool f32
 // block reductions are two shuffles.
 __device__ __forceinline__ void store_slot(const PhaseParams& p, int s, bool live, const float v[8], const Act& A) {
   if (p.need_q6 && live) {
+    const int ts = cls_slot(s);
 #pragma unroll
-    for (int i = 0; i < 8; i++) A.xc[i * A.cp + s] = v[i];
+    for (int i = 0; i < 8; i++) A.xc[i * A.cp + ts] = v[i];
   }
   if (p.need_q8) {
     float amax8 = 0.f;
@@ -250,9 +255,9 @@ __device__ __forceinline__ float rms_scale(const float* sq, int cp, int K, float
   if (lane < 8) {
     const float4* row = reinterpret_cast<const float4*>(sq + l * cp);
     for (int t = 0; t < nt / 4; t++) {
-      const float4 w = row[t];
-      acc = __fadd_rn(acc, w.x); acc = __fadd_rn(acc, w.y);
-      acc = __fadd_rn(acc, w.z); acc = __fadd_rn(acc, w.w);
+      const float4 w = row[t];  // positions (4t, 4t+2, 4t+1, 4t+3)
+      acc = __fadd_rn(acc, w.x); acc = __fadd_rn(acc, w.z);
+      acc = __fadd_rn(acc, w.y); acc = __fadd_rn(acc, w.w);
     }
   }
   const float ss = fold8_lanes(acc);
@@ -290,8 +295,9 @@ static __device__ void build_activation(const PhaseParams& p, const float wpre[R
         const float4 a = __ldcg(x4 + 2 * s), b = __ldcg(x4 + 2 * s + 1);
         v[j][0] = a.x; v[j][1] = a.y; v[j][2] = a.z; v[j][3] = a.w;
         v[j][4] = b.x; v[j][5] = b.y; v[j][6] = b.z; v[j][7] = b.w;
+        const int ts = cls_slot(s);
 #pragma unroll
-        for (int i = 0; i < 8; i++) A.xc[i * A.cp + s] = __fmul_rn(v[j][i], v[j][i]);
+        for (int i = 0; i < 8; i++) A.xc[i * A.cp + ts] = __fmul_rn(v[j][i], v[j][i]);
       } else {
 #pragma unroll
         for (int i = 0; i < 8; i++) v[j][i] = 0.f;
@@ -471,51 +477,88 @@ __device__ __forceinline__ float q4k_rows(const uint8_t* st, int rstride, int nr
 // whole row, reading its class's code bytes (device body layout,
 // hakm_internal.h) and x by class (Act::xc). w = (q - 32) * (d * sc) is
 // exact in fp32 (at most 6 + 18 significant bits), as in dequant_q6_K.
-// ws: the warp's scratch (the rows' (d*sc, d*sc) pairs of the current block).
-// Lanes 8r (r < nrows) return row r's dot product.
+// The products go in pairs (packed fp32) over positions (t0, t2), (t1, t3)
+// of each group of four; the next block's bytes load while this one is
+// worked. Lanes 8r (r < nrows) return row r's dot product.
+struct Q6Blk {
+  uint2 w0, w1, w2;  // the class's 24 code bytes
+  uint4 sc;          // the 16 int8 scales
+  uint32_t dh;       // fp16 d
+};
+__device__ __forceinline__ Q6Blk q6_blk_load(const uint8_t* row, int nb, int b, int l) {
+  const int c = b >> 3, j = b & 7, m = q6_chunk_blocks(nb, c);
+  const uint8_t* chunk = row + (size_t)c * Q6K_CHUNK;
+  const uint8_t* body = chunk + j * Q6K_BODY;
+  const uint2* wp = reinterpret_cast<const uint2*>(body + 24 * l);
+  Q6Blk B;
+  B.w0 = wp[0];
+  B.w1 = wp[1];
+  B.w2 = wp[2];
+  B.sc = *reinterpret_cast<const uint4*>(body + 192);
+  B.dh = *reinterpret_cast<const uint16_t*>(chunk + m * Q6K_BODY + 2 * j);
+  return B;
+}
+// float(v) of byte k of w as a signed int8, without a conversion instruction
+__device__ __forceinline__ float s8_val(uint32_t w, int k) {
+  return __uint_as_float(__byte_perm(w ^ 0x80808080u, 0x4B000000u, 0x7650u | (uint32_t)k)) - 8388736.0f;
+}
+
+// The 16 products of half n of a block, in chain order (positions
+// 16n + 4k + b for k, b = 0..3): w = (q - 32) * (d * sc) exact, times x.
+__device__ __forceinline__ void q6_half_products(const Q6Blk& B, int n, const float* xh, float p[16]) {
+  const float2 bias2 = make_float2(-8388640.0f, -8388640.0f);  // -(2^23 + 32)
+  const float d = half_bits_to_float(B.dh);
+  const float2 dd = make_float2(d, d);
+  const uint32_t W0 = n ? B.w1.y : B.w0.x, W1 = n ? B.w2.x : B.w0.y, WH = n ? B.w2.y : B.w1.x;
+  const uint32_t scw0 = n ? B.sc.z : B.sc.x, scw1 = n ? B.sc.w : B.sc.y;
+#pragma unroll
+  for (int k = 0; k < 4; k++) {
+    uint32_t q;
+    if (k == 0) q = (W0 & 0x0F0F0F0Fu) | ((WH << 4) & 0x30303030u);
+    else if (k == 1) q = (W1 & 0x0F0F0F0Fu) | ((WH << 2) & 0x30303030u);
+    else if (k == 2) q = ((W0 >> 4) & 0x0F0F0F0Fu) | (WH & 0x30303030u);
+    else q = ((W1 >> 4) & 0x0F0F0F0Fu) | ((WH >> 2) & 0x30303030u);
+    // groups g = 8n + 2k (codes b = 0, 1) and g + 1 (b = 2, 3): bytes
+    // 2(k&1), 2(k&1)+1 of scale word 2n + k/2
+    const uint32_t sw = (k >> 1) ? scw1 : scw0;
+    const float2 ds = mul2(make_float2(s8_val(sw, 2 * (k & 1)), s8_val(sw, 2 * (k & 1) + 1)), dd);
+    // x at positions (b0, b2, b1, b3) of this group of four
+    const float4 x4 = *reinterpret_cast<const float4*>(xh + 4 * k);
+    const float2 q02 = add2(make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7650)),
+                                        __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7652))), bias2);
+    const float2 q13 = add2(make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7651)),
+                                        __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7653))), bias2);
+    const float2 p02 = mul2(mul2(q02, ds), make_float2(x4.x, x4.y));
+    const float2 p13 = mul2(mul2(q13, ds), make_float2(x4.z, x4.w));
+    p[4 * k + 0] = p02.x;
+    p[4 * k + 1] = p13.x;
+    p[4 * k + 2] = p02.y;
+    p[4 * k + 3] = p13.y;
+  }
+}
+
+// The chain runs one half-block behind the products, so each half's 16
+// products are formed while the previous half's are being added.
 __device__ __forceinline__ float q6k_rows(const uint8_t* st, int rstride, int nrows, int nb, const Act& A, float* ws) {
+  (void)ws;
   const int lane = threadIdx.x & 31, r = lane >> 3, l = lane & 7;
   const uint8_t* row = st + (size_t)(r < nrows ? r : 0) * rstride;
   const float* xl = A.xc + l * A.cp;
-  float2* dsc = reinterpret_cast<float2*>(ws) + r * 16;
-  const float2 bias2 = make_float2(-8388640.0f, -8388640.0f);  // -(2^23 + 32)
   float acc = 0.f;
+  Q6Blk B = q6_blk_load(row, nb, 0, l);
+  float pv[16];
+  q6_half_products(B, 0, xl, pv);
   for (int b = 0; b < nb; b++) {
-    const int c = b >> 3, j = b & 7, m = q6_chunk_blocks(nb, c);
-    const uint8_t* chunk = row + (size_t)c * Q6K_CHUNK;
-    const uint8_t* body = chunk + j * Q6K_BODY;
-    const float d = half_bits_to_float(*reinterpret_cast<const uint16_t*>(chunk + m * Q6K_BODY + 2 * j));
-    const uint32_t s2 = *reinterpret_cast<const uint16_t*>(body + 192 + 2 * l);
-    const float g0 = __fmul_rn(d, (float)(int8_t)(s2 & 255)), g1 = __fmul_rn(d, (float)(int8_t)(s2 >> 8));
-    const uint2* wp = reinterpret_cast<const uint2*>(body + 24 * l);
-    const uint2 w0 = wp[0], w1 = wp[1], w2 = wp[2];
-    __syncwarp();
-    reinterpret_cast<float4*>(dsc)[l] = make_float4(g0, g0, g1, g1);
-    __syncwarp();
+    float pc[16];
+    q6_half_products(B, 1, xl + 32 * b + 16, pc);
 #pragma unroll
-    for (int n = 0; n < 2; n++) {
-      const uint32_t W0 = n ? w1.y : w0.x, W1 = n ? w2.x : w0.y, WH = n ? w2.y : w1.x;
-#pragma unroll
-      for (int k = 0; k < 4; k++) {
-        uint32_t q;
-        if (k == 0) q = (W0 & 0x0F0F0F0Fu) | ((WH << 4) & 0x30303030u);
-        else if (k == 1) q = (W1 & 0x0F0F0F0Fu) | ((WH << 2) & 0x30303030u);
-        else if (k == 2) q = ((W0 >> 4) & 0x0F0F0F0Fu) | (WH & 0x30303030u);
-        else q = ((W1 >> 4) & 0x0F0F0F0Fu) | ((WH >> 2) & 0x30303030u);
-        const float4 x4 = *reinterpret_cast<const float4*>(xl + 32 * b + 16 * n + 4 * k);
-        const float4 ds = reinterpret_cast<const float4*>(dsc)[4 * n + k];
-        const float2 qa = add2(make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7650)),
-                                           __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7651))), bias2);
-        const float2 qb = add2(make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7652)),
-                                           __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7653))), bias2);
-        const float2 pa = mul2(mul2(qa, make_float2(ds.x, ds.y)), make_float2(x4.x, x4.y));
-        const float2 pb = mul2(mul2(qb, make_float2(ds.z, ds.w)), make_float2(x4.z, x4.w));
-        acc = __fadd_rn(acc, pa.x);
-        acc = __fadd_rn(acc, pa.y);
-        acc = __fadd_rn(acc, pb.x);
-        acc = __fadd_rn(acc, pb.y);
-      }
+    for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pv[i]);
+    if (b + 1 < nb) {
+      B = q6_blk_load(row, nb, b + 1, l);
+      q6_half_products(B, 0, xl + 32 * (b + 1), pv);
     }
+#pragma unroll
+    for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pc[i]);
   }
   return fold8_lanes(acc);
 }

@@ -207,8 +207,9 @@ __device__ bool build_activation_ll(const PhaseParams& p, const uint64_t* x, uin
           for (int i = 0; i < 8; i++) plain[8 * s + i] = v[j][i];
         }
         // squares by lane class for the scale (src/nn.c:15 as built)
+        const int ts = cls_slot(s);
 #pragma unroll
-        for (int i = 0; i < 8; i++) A.xc[i * A.cp + s] = __fmul_rn(v[j][i], v[j][i]);
+        for (int i = 0; i < 8; i++) A.xc[i * A.cp + ts] = __fmul_rn(v[j][i], v[j][i]);
       } else {
 #pragma unroll
         for (int i = 0; i < 8; i++) v[j][i] = 0.f;
