@@ -64,6 +64,8 @@ SIGNATURES = {
     "hakmc_rope_neox": (_i, [_vp, _i, _i, _i, _f, _vp]),
     "hakmc_attention_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "hakmc_test_expf": (_i, [_vp, _vp, _i, _i, _vp]),
+    "hakmc_sample": (_i, [_vp, _i, _f, _f, _i, _vp, _vp, _vp]),
+    "hakmc_sample_last": (_i, [_vp, _f, _f, _i, _vp, _vp]),
     "hakmc_plan_rows": (_i, [_vp, _i, _i, _i, _vp]),
     "hakmc_plan_attn_units": (_i, [_i, _i, _i, _i, _vp, _i]),
 }

@@ -89,3 +89,26 @@ float hakm_host_rsqrt_nr(float v) {
 	float t = fmaf(r, v * r, -3.0f);
 	return (r * -0.5f) * t;
 }
+
+/* The rcpss estimate (the reciprocal gcc's vectorized loop of
+ * `logits[i] /= temp` uses for its 4-wide remainder step, src/sample.c:36,
+ * with one Newton step): a function of the top 11 mantissa bits, the
+ * exponent scaling the result. out[m] = rcpss(1 + m/2048). */
+void hakm_host_rcp_table(uint32_t *out) {
+	for (int m = 0; m < 2048; m++) {
+		float x = bitsf((127u << 23) | ((uint32_t)m << 12));
+		out[m] = fbits(_mm_cvtss_f32(_mm_rcp_ss(_mm_set_ss(x))));
+	}
+}
+
+/* 1 if the table form holds on this host (every 97th mantissa, exponents
+ * -64..64), 0 otherwise. */
+int hakm_host_rcp_table_ok(const uint32_t *tab) {
+	for (int e = -64; e <= 64; e += 8)
+		for (uint32_t m = 0; m < (1u << 23); m += 97) {
+			float x = bitsf(((uint32_t)(127 + e) << 23) | m);
+			uint32_t want = tab[m >> 12] - ((uint32_t)e << 23);
+			if (fbits(_mm_cvtss_f32(_mm_rcp_ss(_mm_set_ss(x)))) != want) return 0;
+		}
+	return 1;
+}

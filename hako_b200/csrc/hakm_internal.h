@@ -217,6 +217,14 @@ cudaError_t attention_noalloc(float* out, const float* q, const float* kc, const
 size_t noalloc_part_floats();
 // Scratch floats of launch_attention for n positions.
 size_t attention_scratch_floats(int n_heads, int head_dim, int n_pos);
+// Sampling for temperature > 0 (hakm_sample.cu): logits[0..n) (n >= 9)
+// become probabilities in place; scratch: sample_scratch_words(n) words;
+// rng_dev / out_dev: the generator state (in/out) and the pick.
+size_t sample_scratch_words(int n);
+cudaError_t launch_sample(float* logits, int n, float temp, float top_p, int top_k, const uint32_t* rcp_tab,
+                          uint32_t* scratch, unsigned long long* rng_dev, int* out_dev, cudaStream_t s);
+// The rcpss table of this host on device `dev` (made on first use).
+const uint32_t* rcp_table_device(int dev);
 // The device's exp restatements on n inputs (variant 0 scalar, 1 8-wide, 2 4-wide).
 cudaError_t launch_exp_probe(float* out, const float* in, int n, int variant, cudaStream_t s);
 // The rsqrtss table of this host on device `dev` (made on first use).

@@ -301,6 +301,36 @@ const uint32_t* rsqrt_table_device(int dev) {
   return g_rsq_dev[dev];
 }
 
+extern "C" void hakm_host_rcp_table(uint32_t* out);
+extern "C" int hakm_host_rcp_table_ok(const uint32_t* tab);
+static uint32_t* g_rcp_dev[64];
+
+const uint32_t* rcp_table_device(int dev) {
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_rsq_mu);
+  if (g_rcp_dev[dev]) return g_rcp_dev[dev];
+  static uint32_t host[2048];
+  static int host_ok = -1;
+  if (host_ok < 0) {
+    hakm_host_rcp_table(host);
+    host_ok = hakm_host_rcp_table_ok(host);
+  }
+  if (!host_ok) return nullptr;
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return nullptr;
+  if (cur != dev && cudaSetDevice(dev) != cudaSuccess) return nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, sizeof host);
+  if (e == cudaSuccess) e = cudaMemcpy(p, host, sizeof host, cudaMemcpyHostToDevice);
+  if (cur != dev) cudaSetDevice(cur);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return nullptr;
+  }
+  g_rcp_dev[dev] = static_cast<uint32_t*>(p);
+  return g_rcp_dev[dev];
+}
+
 // ------------------------------------------------------------ allocation-free attention
 
 // Scratch of hakmc_attention_noalloc: the score rows of the attention units

@@ -1898,6 +1898,68 @@ extern "C" int hakmc_plan_attn_units(int n_heads, int head_dim, int rank, int wo
   return n;
 }
 
+namespace {
+// Per-device scratch of the sampler: the sort keys / indices (4n words) and
+// the generator state and pick.
+struct SampleScratch {
+  uint32_t* words = nullptr;
+  size_t cap = 0;
+  unsigned long long* io = nullptr;  // [0] rng, [1] pick (int)
+};
+std::mutex g_smp_mu;
+std::map<int, SampleScratch> g_smp;
+
+int sample_on(float* logits, int n, float temp, float top_p, int top_k, unsigned long long* rng, int* token,
+              cudaStream_t st) {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (!(temp > 0.0f)) {  // greedy: first index of the maximum (src/sample.c:28-32)
+    DevScratch* s;
+    int r = scratch(&s, 0, 0);
+    if (r) return r;
+    CK(launch_pf_argmax(s->tok, logits, 1, n, st));
+    CK(cudaMemcpyAsync(token, s->tok, 4, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    return 0;
+  }
+  if (n < 9) { set_err("sample: vocabulary below 9 entries"); return HAKMC_EINVAL; }
+  const uint32_t* rcp = rcp_table_device(dev);
+  if (!rcp) { set_err("sample: no rcpss table for this host"); return HAKMC_ECUDA; }
+  std::lock_guard<std::mutex> lk(g_smp_mu);
+  SampleScratch& S = g_smp[dev];
+  if (!S.io) CK(cudaMalloc(&S.io, 64));
+  const size_t need = sample_scratch_words(n);
+  if (need > S.cap) {
+    CK(cudaStreamSynchronize(st));
+    if (S.words) cudaFree(S.words);
+    S.words = nullptr;
+    CK(cudaMalloc(&S.words, need * 4));
+    S.cap = need;
+  }
+  CK(cudaMemcpyAsync(S.io, rng, 8, cudaMemcpyHostToDevice, st));
+  CK(launch_sample(logits, n, temp, top_p, top_k, rcp, S.words, S.io, reinterpret_cast<int*>(S.io + 1), st));
+  unsigned long long back[2];
+  CK(cudaMemcpyAsync(back, S.io, 16, cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  *rng = back[0];
+  *token = (int)(uint32_t)back[1];
+  return 0;
+}
+}  // namespace
+
+extern "C" int hakmc_sample(float* logits, int n, float temp, float top_p, int top_k, unsigned long long* rng,
+                            int* token, void* stream) {
+  if (!logits || n <= 0 || !rng || !token) return HAKMC_EINVAL;
+  return sample_on(logits, n, temp, top_p, top_k, rng, token, (cudaStream_t)stream);
+}
+
+extern "C" int hakmc_sample_last(hakmc_ctx* c, float temp, float top_p, int top_k, unsigned long long* rng,
+                                 int* token) {
+  if (!c || !rng || !token) return HAKMC_EINVAL;
+  CK(cudaSetDevice(c->device));
+  return sample_on(c->logits, c->V, temp, top_p, top_k, rng, token, c->stream);
+}
+
 extern "C" int hakmc_test_expf(float* out, const float* in, int n, int variant, void* stream) {
   if (!out || !in || n < 0 || variant < 0 || variant > 2) return HAKMC_EINVAL;
   CKL(launch_exp_probe(out, in, n, variant, (cudaStream_t)stream));

@@ -323,6 +323,25 @@ int hakmc_attention_noalloc(float *out, const float *q, const float *k_cache, co
  * same glibc vector routines the reference's build calls (bit-identical). */
 int hakmc_rope_neox(float *x, int n_heads, int head_dim, int pos, float theta, void *stream);
 
+/* Sampling for temperature > 0 (src/sample.c:27-58) on the device, with
+ * the reference build's roundings, so token and generator state equal its
+ * own sample_token's bit for bit: logits / temp (as vectorized: one
+ * division, multiplies by 1/temp, one rcpss-Newton group of four, divisions
+ * for the rest), the softmax of src/nn.c:20-27, a stable sort by
+ * probability (glibc's qsort of the candidate list keeps ties in index
+ * order), top_k (0: off), the top_p nucleus (0 or >= 1: off), the
+ * vectorized sum of the kept probabilities, and the xorshift64 draw.
+ * temp <= 0 is the greedy argmax (first index of the maximum); it leaves
+ * logits and *rng alone. [dev] logits (n >= 9 floats) are turned into
+ * probabilities in place, as the reference's are; [host] *rng is the
+ * sampler state (sample.h), advanced by one draw; [host] *token receives
+ * the pick. Synchronous on `stream`; the scratch (4n words) is allocated
+ * once per device and regrown. hakmc_sample_last samples the logits of the
+ * context's last step on the device, so no logits cross to the host. */
+int hakmc_sample(float *logits, int n, float temp, float top_p, int top_k, unsigned long long *rng,
+                 int *token, void *stream);
+int hakmc_sample_last(hakmc_ctx *c, float temp, float top_p, int top_k, unsigned long long *rng, int *token);
+
 /* Host-only planning, for tests and tools (no GPU needed). The rows of a
  * step-kernel phase that CTA `cta` of a `grid`-CTA group computes (with
  * tensor parallelism the grid spans every rank's CTAs, rank r owning CTAs

@@ -187,6 +187,7 @@ class Reference:
             "refd_matmul_raw": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i]),
             "refd_read_kv": (_i, [_vp, _vp, _vp, _i]),
             "refd_set_pos": (None, [_vp, _i]),
+            "refd_write_kv": (_i, [_vp, _vp, _vp, _i]),
             "quantize_row_q8_32": (None, [_vp, _i, _vp, _vp]),
             "q4k_vec_dot": (_f, [_vp, _i, _vp, _vp]),
             "dequant_q4_K": (None, [_vp, _vp, _i]),
@@ -277,6 +278,12 @@ class RefModel:
 
     def set_pos(self, pos: int):
         self.r.L.refd_set_pos(self.h, pos)
+
+    def write_kv(self, k: np.ndarray, v: np.ndarray):
+        """k, v: [n_layers][n_pos][kv_dim] float32; sets pos = n_pos."""
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        assert self.r.L.refd_write_kv(self.h, _p(k), _p(v), k.shape[1]) == 0
 
     def set_layers(self, n):
         self.r.L.refd_set_layers(self.h, n)

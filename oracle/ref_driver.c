@@ -108,3 +108,19 @@ int refd_read_kv(void *cv, float *k, float *v, int n_pos) {
 /* Set the decode position (hakm_ctx.pos, src/model.h:20) over a cache the
  * caller filled. */
 void refd_set_pos(void *cv, int pos) { ((hakm_ctx *)cv)->pos = pos; }
+
+/* Write k / v laid out [layer][n_pos][kv_dim] into the first n_pos
+ * positions of every layer of hakm_ctx.k_cache / v_cache (src/model.h:21-22)
+ * and set pos = n_pos: a pre-filled cache, as a caller of the reference can
+ * make it. */
+int refd_write_kv(void *cv, const float *k, const float *v, int n_pos) {
+	hakm_ctx *c = (hakm_ctx *)cv;
+	if (n_pos > c->max_seq) return -1;
+	size_t row = (size_t)c->kv_dim * n_pos;
+	for (int l = 0; l < c->n_layers; l++) {
+		memcpy(c->k_cache + (size_t)l * c->max_seq * c->kv_dim, k + (size_t)l * row, row * sizeof(float));
+		memcpy(c->v_cache + (size_t)l * c->max_seq * c->kv_dim, v + (size_t)l * row, row * sizeof(float));
+	}
+	c->pos = n_pos;
+	return 0;
+}
