@@ -18,7 +18,8 @@ LIB = os.path.join(HERE, "_lib")
 ROOT = os.path.dirname(HERE)
 
 CUDA_SOURCES = ["csrc/hakm_stream.cu", "csrc/hakm_step.cu", "csrc/hakm_kernels.cu", "csrc/hakm_batch.cu",
-                "csrc/hakm_mma.cu", "csrc/hakm_prefill.cu", "csrc/hakm_sample.cu", "csrc/hakm_runtime.cu"]
+                "csrc/hakm_mma.cu", "csrc/hakm_prefill.cu", "csrc/hakm_rows.cu", "csrc/hakm_sample.cu",
+                "csrc/hakm_runtime.cu"]
 CUDA_HEADERS = ["csrc/hakm_internal.h", "csrc/hakm_device.cuh", "csrc/hakm_exact.cuh", "csrc/hakm_gemv.cuh",
                 "csrc/hakm_attn.cuh", "csrc/hakm_ll.cuh", "csrc/hakm_tmap.h", "../include/hakm_cuda.h"]
 # host tables that carry glibc's vector libm roundings: gcc with AVX2 + FMA

@@ -59,6 +59,50 @@ __host__ __device__ inline size_t attn_smem_bytes(int hd) {
   return (size_t)(hd + 64 + 2 * ATTN_VT * ATTN_SLICE) * 4;
 }
 
+// Softmax of sc[0 .. n) in place (src/nn.c:20-27 as built): the max, the
+// exps by element index (exp_softmax), their sum in the vectorized loop's
+// order (8 lane chains over the first 8*floor(n/8) elements, folded to 4 by
+// adding lanes k and k+4, one 4-lane step when at least 4 remain, the fold
+// of those, then scalar adds), one IEEE reciprocal and a multiply. Run by
+// threads [0, nthr) (a multiple of 32) that sync() synchronises; red: 33
+// floats of shared scratch. Ends with a sync().
+template <class Sync>
+__device__ __forceinline__ void softmax_exact(float* sc, int n, float* red, int tid, int nthr, Sync sync) {
+  const int lane = tid & 31, warp = tid >> 5, nw = nthr >> 5;
+  float mx = -CUDART_INF_F;
+  for (int t = tid; t < n; t += nthr) mx = fmaxf(mx, sc[t]);
+  mx = warp_max(mx);
+  if (lane == 0) red[warp] = mx;
+  sync();
+  mx = red[0];
+  for (int w = 1; w < nw; w++) mx = fmaxf(mx, red[w]);
+  for (int t = tid; t < n; t += nthr) sc[t] = exp_softmax(__fsub_rn(sc[t], mx), t, n);
+  sync();
+  if (warp == 0) {
+    const int n8 = n & ~7, rem = n - n8;
+    float c = 0.f;
+    if (lane < 8)
+      for (int t = lane; t < n8; t += 8) c = __fadd_rn(c, sc[t]);
+    // lanes 0..3: c_k + c_{k+4}, the 4 lanes the remainder step continues
+    const float c4 = __fadd_rn(c, __shfl_xor_sync(0xffffffffu, c, 4));
+    const float u2 = __fadd_rn(c4, __shfl_xor_sync(0xffffffffu, c4, 2));
+    float sum = __fadd_rn(u2, __shfl_xor_sync(0xffffffffu, u2, 1));
+    if (rem >= 4) {
+      const float uk = __fadd_rn(sc[n8 + (lane & 3)], c4);
+      const float a2 = __fadd_rn(uk, __shfl_xor_sync(0xffffffffu, uk, 2));
+      sum = __fadd_rn(a2, __shfl_xor_sync(0xffffffffu, a2, 1));
+    }
+    if (lane == 0) {
+      for (int t = rem >= 4 ? n8 + 4 : n8; t < n; t++) sum = __fadd_rn(sum, sc[t]);
+      red[32] = __fdiv_rn(1.0f, sum);
+    }
+  }
+  sync();
+  const float inv = red[32];
+  for (int t = tid; t < n; t += nthr) sc[t] = __fmul_rn(sc[t], inv);
+  sync();
+}
+
 // tid in [0, nthr), nthr a multiple of 32 and at least 64; sync()
 // synchronises exactly those nthr threads. In tagged mode returns false if a
 // wait for a tagged input gave up.
@@ -116,41 +160,7 @@ __device__ bool attn_item(const AttnParams& a, int unit, int pos, float* sm, int
   }
   sync();
 
-  // softmax: max, exps in place, the sum in the vectorized order, 1/sum
-  float mx = -CUDART_INF_F;
-  for (int t = tid; t < n; t += nthr) mx = fmaxf(mx, sc[t]);
-  mx = warp_max(mx);
-  if (lane == 0) red[warp] = mx;
-  sync();
-  mx = red[0];
-  for (int w = 1; w < nw; w++) mx = fmaxf(mx, red[w]);
-  for (int t = tid; t < n; t += nthr) sc[t] = exp_softmax(__fsub_rn(sc[t], mx), t, n);
-  sync();
-  if (warp == 0) {
-    const int n8 = n & ~7, rem = n - n8;
-    float c = 0.f;
-    if (lane < 8)
-      for (int t = lane; t < n8; t += 8) c = __fadd_rn(c, sc[t]);
-    // lanes 0..3: c_k + c_{k+4}, the 4 lanes the remainder step continues
-    const float c4 = __fadd_rn(c, __shfl_xor_sync(0xffffffffu, c, 4));
-    const float u2 = __fadd_rn(c4, __shfl_xor_sync(0xffffffffu, c4, 2));
-    float sum = __fadd_rn(u2, __shfl_xor_sync(0xffffffffu, u2, 1));
-    if (rem >= 4) {
-      const float uk = __fadd_rn(sc[n8 + (lane & 3)], c4);
-      const float a2 = __fadd_rn(uk, __shfl_xor_sync(0xffffffffu, uk, 2));
-      sum = __fadd_rn(a2, __shfl_xor_sync(0xffffffffu, a2, 1));
-    }
-    if (lane == 0) {
-      for (int t = rem >= 4 ? n8 + 4 : n8; t < n; t++) sum = __fadd_rn(sum, sc[t]);
-      red[32] = __fdiv_rn(1.0f, sum);
-    }
-  }
-  sync();
-  {
-    const float inv = red[32];
-    for (int t = tid; t < n; t += nthr) sc[t] = __fmul_rn(sc[t], inv);
-  }
-  sync();
+  softmax_exact(sc, n, red, tid, nthr, sync);
 
   // weighted V: warp 0 lane d runs out[d] over the staged tiles; the other
   // warps stage tile i + 1 while it works on tile i

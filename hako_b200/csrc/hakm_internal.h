@@ -145,12 +145,10 @@ size_t q4k_batch_ticket_offset(int n_out, int n_in, int n_batch, int num_sms);
 // out[n][r] = sum over c < nch of part[c][n][r] (+ bias[r]), in order.
 cudaError_t launch_chunk_sum(float* out, const float* part, const float* bias, int n_out, int n_batch, int nch,
                              int num_sms, cudaStream_t st);
-// Tensor-core (tcgen05 kind::i8) batched Q4_K x q8_32 matmul (hakm_mma.cu);
-// part: q4k_mma_scratch_bytes (split-K partials), may be null when that is 0.
+// Tensor-core (tcgen05 kind::i8) batched Q4_K x q8_32 matmul (hakm_mma.cu):
+// every output equals the reference's q4k_vec_dot (+ bias) bit for bit.
 cudaError_t launch_q4k_mma(float* out, const uint8_t* w, const int8_t* xq, const float* xs, const float* bias,
-                           int n_out, int n_in, int n_batch, float* part, int* err_flag, int num_sms,
-                           cudaStream_t st);
-size_t q4k_mma_scratch_bytes(int n_out, int n_in, int n_batch, int num_sms);
+                           int n_out, int n_in, int n_batch, int* err_flag, int num_sms, cudaStream_t st);
 cudaError_t launch_q4k_subsums(int32_t* iqx, int32_t* ix, const uint8_t* w, const int8_t* xq,
                                int n_out, int n_in, cudaStream_t s);
 cudaError_t launch_q6k_pack(uint8_t* dst, const uint8_t* src, int n_rows, int n_in, cudaStream_t s);
@@ -162,33 +160,33 @@ cudaError_t launch_embed_q6k(float* xb, const uint8_t* w, const int* token, int 
 cudaError_t launch_rope(float* x, const float* rope_cs, const int* pos_dev, int n_heads, int head_dim,
                         cudaStream_t s);
 
-// ---- batched prompt processing (hakm_prefill.cu): rows of a prompt chunk ----
+// ---- row-wise kernels of the row-batched passes (hakm_prefill.cu) ----
 cudaError_t launch_pf_embed(float* x, const uint8_t* w, const int* tokens, int M, int D, cudaStream_t s);
-cudaError_t launch_pf_norm_quant(const float* x, const float* w, int M, int D, float eps, float* xn, int8_t* xq,
-                                 float* xs, cudaStream_t s);
-// Q6_K x fp32 rows; short batches split K: the partials go to `part`
-// (pf_q6k_part_floats floats; null: no split) and, when accumulating, the
-// sum through `tmp` (M * n_out floats).
-cudaError_t launch_pf_q6k_gemm(float* out, const uint8_t* w, const float* x, const float* bias, int n_out, int K,
-                               int M, bool accumulate, float* part, size_t part_floats, float* tmp, cudaStream_t s);
-size_t pf_q6k_part_floats(int n_out, int K, int M);
 cudaError_t launch_pf_rope_kv(const float* qk, const float* v, float* q, float* kc, float* vc, const float* rope_cs,
                               int M, int pos0, const int* row_pos, size_t slot_stride, int D, int KV, int hd,
                               cudaStream_t s);
 cudaError_t launch_pf_argmax(int* out, const float* logits, int M, int V, cudaStream_t s);
 cudaError_t launch_pf_fill_normal(float* dst, size_t ystride, size_t n, int blocks_y, uint64_t seed, cudaStream_t s);
-cudaError_t launch_pf_attention(float* out, const float* q, const float* kc, const float* vc, int M, int pos0, int H,
-                                int KVH, int hd, float scale, cudaStream_t s);
-// Batched decode rows (row r: sequence r at row_pos[r], its cache slot_stride
-// floats on), positions split over CTAs; part: pf_decode_attention_part_floats.
-cudaError_t launch_pf_decode_attention(float* out, const float* q, const float* kc, const float* vc, int rows,
-                                       const int* row_pos, int max_pos, size_t slot_stride, int H, int KVH, int hd,
-                                       float scale, float* part, size_t part_floats, int sms, cudaStream_t s);
-size_t pf_decode_attention_part_floats(int rows, int H, int KVH, int hd, int max_pos, int sms);
-// its position splits (the return) and tiles per split for max_pos
-int pf_decode_attention_plan(int rows, int KVH, int max_pos, int sms, int* tiles_per);
-cudaError_t launch_pf_swiglu(float* h, const float* gu, int M, int F, cudaStream_t s);
 cudaError_t launch_pf_add(float* x, const float* o, size_t n, cudaStream_t s);
+
+// ---- row-batched kernels with the reference's roundings (hakm_rows.cu) ----
+// Each row's results equal the single-row decode path's bit for bit.
+// rmsnorm of M rows of D (a multiple of 256, at most 8192) into xn and/or
+// their q8_32 codes (xq, xs); either output may be null.
+cudaError_t launch_rx_norm_quant(const float* x, const float* w, int M, int D, float eps, const uint32_t* rsq,
+                                 float* xn, int8_t* xq, float* xs, cudaStream_t s);
+// out[m][n] (+)= Q6_K row n . x[m] (+ bias[n]), m < M.
+cudaError_t launch_rx_q6k_gemm(float* out, const uint8_t* w, const float* x, const float* bias, int n_out, int K,
+                               int M, bool accumulate, cudaStream_t s);
+cudaError_t launch_rx_swiglu(float* h, const float* gu, int M, int F, cudaStream_t s);
+// Attention of `rows` rows: row r at row_pos[r] with its cache slot_stride
+// floats after row r-1's, or (row_pos null) at pos0 + r over one cache;
+// n_max >= every row's position + 1.
+constexpr size_t RX_ATTN_SMEM_MAX = 200 * 1024;
+size_t rx_attention_smem_bytes(int hd, int n_max);
+cudaError_t launch_rx_attention(float* out, const float* q, const float* kc, const float* vc, int rows, int pos0,
+                                const int* row_pos, int n_max, size_t slot_stride, int H, int KVH, int hd,
+                                float scale, cudaStream_t s);
 
 struct AttnParams {
   const float* q;        // [H*hd]

@@ -2,15 +2,19 @@
 // (tcgen05.mma kind::i8), for batches of activations (batched decode,
 // prompt processing).
 //
-// out[n][r] = sum over 32-element sub-blocks j of
-//             xs[n][j] * ((d*s)[r][j] * isum[r][n][j] - (dmin*m)[r][j] * ix[n][j])
-// with isum = sum(q * xq) over the sub-block (q the 4-bit weight codes) and
-// ix = sum(xq): the arithmetic of q4k_vec_dot (src/quant.c:150-232). The
-// per-sub-block integer sums come from the tensor cores, exact (int32
-// accumulators in tensor memory, one fresh accumulator per sub-block: K = 32
-// per MMA); the fp32 combine runs in the epilogue warps. Because the
-// activation scale changes every 32 elements, that epilogue (about five
-// operations per output and sub-block), not the MMA, bounds the kernel.
+// out[n][r] = q4k_vec_dot(row r, xq[n], xs[n]) with the arithmetic of the
+// reference as built (src/quant.c:150-232 under gcc -O3 -ffast-math with
+// FMA): per pair of 32-element sub-blocks (A, B) = (2g, 2g+1) of a
+// super-block with scales d, dmin and 6-bit (s, m) per sub-block,
+//   t  = fma(s, fl(d * isum), -fl(m * fl(dmin * ix)))   for A and B,
+//   acc = acc + fma(tB, xsB, tA * xsA),
+// pairs in order along the row, where isum = sum(q * xq) over the sub-block
+// (q the 4-bit weight codes) and ix = sum(xq). The per-sub-block integer
+// sums come from the tensor cores, exact (int32 accumulators in tensor
+// memory, one fresh accumulator per sub-block: K = 32 per MMA); the fp32
+// steps run in the epilogue warps, about eleven packed (f32x2) operations
+// per two outputs and sub-block pair, and, not the MMA, bound the kernel.
+// The row is never split along K (the sum order is the row's order).
 //
 // CTA tile: 128 weight rows x BN activations, the whole K. Warp roles:
 //   warp 0      producer: per 256-element super-block one 2-D tensor copy of
@@ -23,9 +27,9 @@
 //               sub-block into one of 512/BN accumulator buffers) and
 //               commits them to mbarriers.
 //   warps 2-5   converters (thread = row): unpack the nibbles into int8 A
-//               tiles in the core-matrix layout, the scale products
-//               (d*s, dmin*m) per row and sub-block, and per activation the
-//               code sums ix and the scales transposed to [sub-block][n].
+//               tiles in the core-matrix layout, the row's d, dmin and
+//               (s, m) per sub-block as floats, and per activation the code
+//               sums ix and the scales transposed to [sub-block][n].
 //   warps 6-13  epilogue: warp w reads tensor-memory lanes 32*(w%4).. (its
 //               rows) and half of the columns, accumulates the fp32 result
 //               in registers, and writes out + bias at the end.
@@ -44,7 +48,9 @@ constexpr int MM_CONV = 128;          // converter threads (one row each)
 constexpr int MM_THREADS = 14 * 32;  // producer, MMA, 4 converter and 8 epilogue warps; 128 registers
 constexpr int MM_RAW = MM_ROWS * Q4K_BYTES;  // 18,432
 constexpr int MM_A = MM_ROWS * QK;           // 32,768: 8 sub-blocks x 4 KB
-constexpr int MM_SC = 3 * 8 * MM_ROWS * 4;   // d*s, -1.5*2^23*d*s, dmin*m: [8][128] floats each
+// per row: d, -1.5*2^23*d, dmin, s[8], -m[8] as [19][128] floats
+constexpr int MM_SC_D = 0, MM_SC_DNEG = 1, MM_SC_DMIN = 2, MM_SC_S = 3, MM_SC_NM = 11;
+constexpr int MM_SC = 19 * MM_ROWS * 4;
 constexpr uint32_t MM_BIAS = 0x4B400000u;    // bits of 1.5 * 2^23 (see the epilogue)
 
 template <int BN>
@@ -62,11 +68,12 @@ struct MmaLayout {
   static constexpr int C_A = 0, C_SC = MM_A, C_XT = C_SC + MM_SC, C_STAGE = C_XT + 2 * 8 * XP * 4;
   // rings as deep as fit: converted stages first (the MMAs and the epilogue
   // trail the converters), then copies; two super-blocks of accumulators
-  static constexpr int NT = BN <= 32 ? 3 : 2, NC = 3;
-  static constexpr int NBUF = BN >= 64 ? 512 / BN : 16;  // accumulator buffers in tensor memory
+  static_assert(BN == 16 || BN == 32, "the epilogue takes whole sub-block pairs per tensor-memory round trip");
+  static constexpr int NT = 3, NC = 3;
+  static constexpr int NBUF = 16;                       // accumulator buffers in tensor memory
   static constexpr int TMEM_COLS = NBUF * BN;           // 256 or 512
   static constexpr int HC = BN / 2;                     // columns per epilogue warp
-  static constexpr int LDC = HC < 16 ? HC : 16;         // columns per tensor-memory load
+  static constexpr int LDC = HC;                        // columns per tensor-memory load
   // 1 KB of alignment slack, 1 KB header, the two rings
   static constexpr size_t SMEM = 2048 + (size_t)NT * T_STAGE + (size_t)NC * C_STAGE;
   static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
@@ -74,10 +81,10 @@ struct MmaLayout {
 };
 
 struct MmaArgs {
-  float* out;   // [n_batch][n_out], or the split-K partials [split][n_batch][n_out]
+  float* out;   // [n_batch][n_out]
   const float* bias;
   int* err_flag;
-  int n_out, n_in, n_batch, sb_per_split;
+  int n_out, n_in, n_batch;
 };
 
 __device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
@@ -119,34 +126,6 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
 // Loads without the wait (several in flight, then tmem_wait_ld).
 template <int N>
 __device__ __forceinline__ void tmem_ld_issue(uint32_t taddr, uint32_t* r) {
@@ -164,12 +143,6 @@ __device__ __forceinline__ void tmem_ld_issue(uint32_t taddr, uint32_t* r) {
   }
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-template <int N>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
-  if constexpr (N == 8) tmem_ld8(taddr, r);
-  else tmem_ld16(taddr, r);
-}
 
 // Bounded wait that also gives up once another role has failed; the thread
 // sleeps in the barrier between tests.
@@ -206,8 +179,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
   uint8_t* cring = tring + L::NT * L::T_STAGE;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * MM_ROWS, n0 = blockIdx.y * BN;
-  const int nsb_all = a.n_in / QK;
-  const int sb0 = blockIdx.z * a.sb_per_split, nsb = min(a.sb_per_split, nsb_all - sb0);
+  const int nsb = a.n_in / QK;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < L::NT; i++) {
@@ -248,7 +220,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         if (b >= L::NT && !mm_wait(smem_addr(&t_free[s]), ((b / L::NT) - 1) & 1, abort)) break;
         uint8_t* st = tring + s * L::T_STAGE;
         const uint32_t bar = smem_addr(&t_full[s]);
-        const int g = sb0 + b;
+        const int g = b;
         mbar_expect_tx(bar, L::TX);
         tma_2d(smem_addr(st + L::T_RAW), &wmap, g * (Q4K_BYTES / 8), row0, bar);
         tma_2d(smem_addr(st + L::T_B), &xmap, g * QK, n0, bar);
@@ -333,11 +305,14 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         *reinterpret_cast<uint4*>(A + (2 * g + 1) * 4096) = hi0;
         *reinterpret_cast<uint4*>(A + (2 * g + 1) * 4096 + 2048) = hi1;
       }
-      // scale products per sub-block (get_scale_min_k4, src/quant.c:57-66);
-      // the 12 scale bytes are hd.y, hd.z, hd.w
+      // the row's scales (get_scale_min_k4, src/quant.c:57-66); the 12
+      // scale bytes are hd.y, hd.z, hd.w
       const float d = half_bits_to_float(hd.x), dmin = half_bits_to_float(hd.x >> 16);
       const uint32_t sw[3] = {hd.y, hd.z, hd.w};
       float* ds = reinterpret_cast<float*>(cst + L::C_SC);
+      ds[MM_SC_D * MM_ROWS + t] = d;
+      ds[MM_SC_DNEG * MM_ROWS + t] = -12582912.0f * d;  // exact: d has 11 significant bits
+      ds[MM_SC_DMIN * MM_ROWS + t] = dmin;
 #pragma unroll
       for (int j = 0; j < 8; j++) {
         auto byte = [&](int i) { return (int)((sw[i >> 2] >> (8 * (i & 3))) & 0xFF); };
@@ -349,10 +324,8 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
           sv = (byte(j + 4) & 15) | ((byte(j - 4) >> 6) << 4);
           mv = (byte(j + 4) >> 4) | ((byte(j) >> 6) << 4);
         }
-        const float dsv = d * i22_to_float(sv);
-        ds[j * MM_ROWS + t] = dsv;
-        ds[(8 + j) * MM_ROWS + t] = -12582912.0f * dsv;  // exact: d*s has at most 17 significant bits
-        ds[(16 + j) * MM_ROWS + t] = dmin * i22_to_float(mv);
+        ds[(MM_SC_S + j) * MM_ROWS + t] = (float)sv;
+        ds[(MM_SC_NM + j) * MM_ROWS + t] = -(float)mv;
       }
       // per activation and sub-block: code sum and scale, as [j][n] rows of BN + 4
       const float* xs_in = reinterpret_cast<const float*>(tst + L::T_XS);
@@ -388,19 +361,21 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
   } else {
     // ---------------- epilogue ----------------
     // A result word w is isum (|isum| < 2^22); 1.5*2^23 + isum is exact as
-    // the float with bits 0x4B400000 + w, and fma(that, d*s, -1.5*2^23*d*s)
-    // is the correctly rounded (d*s)*isum. G sub-blocks share one round
-    // trip to tensor memory (G x HC = 32 result words a thread).
-    constexpr int HC = L::HC, LDC = L::LDC, G = 32 / HC > 1 ? 32 / HC : 1;
+    // the float with bits 0x4B400000 + w, and fma(that, d, -1.5*2^23*d) is
+    // the correctly rounded d*isum. G sub-blocks (whole pairs) share one
+    // round trip to tensor memory (G x HC = 32 result words a thread);
+    // columns go two at a time through the packed fp32 operations.
+    constexpr int HC = L::HC, LDC = L::LDC, G = 32 / HC;
+    static_assert(G % 2 == 0, "sub-block pairs");
     const int quad = warp & 3, half = (warp - 6) >> 2;
     const int r = 32 * quad + lane;  // tile row = tensor-memory lane
     const uint32_t lane_base = (uint32_t)(32 * quad) << 16;
     // phase 0 of every d_empty: the buffers start free
     if (lane == 0)
       for (int buf = 0; buf < L::NBUF; buf++) mbar_arrive(smem_addr(&d_empty[buf]));
-    float acc[HC];
+    float2 acc[HC / 2];
 #pragma unroll
-    for (int c = 0; c < HC; c++) acc[c] = 0.f;
+    for (int c = 0; c < HC / 2; c++) acc[c] = make_float2(0.f, 0.f);
     bool ok = true;
     int q = 0;
     for (int b = 0; b < nsb && ok; b++) {
@@ -411,6 +386,9 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
       const float* ix_t = xs_t + 8 * L::XP;
       // the converters' writes for this stage are visible
       if (!mm_wait(smem_addr(&c_full[cs]), (b / L::NC) & 1, abort)) break;
+      const float d = ds[MM_SC_D * MM_ROWS + r], dneg = ds[MM_SC_DNEG * MM_ROWS + r];
+      const float dmin = ds[MM_SC_DMIN * MM_ROWS + r];
+      const float2 d2 = make_float2(d, d), dneg2 = make_float2(dneg, dneg), dmin2 = make_float2(dmin, dmin);
       for (int j0 = 0; j0 < 8; j0 += G, q += G) {
         for (int g = 0; g < G && ok; g++)
           if (!mm_wait(smem_addr(&d_full[(q + g) % L::NBUF]), ((q + g) / L::NBUF) & 1, abort)) ok = false;
@@ -419,32 +397,40 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         uint32_t v[G * HC];
 #pragma unroll
         for (int g = 0; g < G; g++)
-#pragma unroll
-          for (int part = 0; part < HC / LDC; part++)
-            tmem_ld_issue<LDC>(tmem + lane_base + ((q + g) % L::NBUF) * BN + half * HC + LDC * part,
-                               &v[g * HC + LDC * part]);
+          tmem_ld_issue<LDC>(tmem + lane_base + ((q + g) % L::NBUF) * BN + half * HC, &v[g * HC]);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0)
           for (int g = 0; g < G; g++) mbar_arrive(smem_addr(&d_empty[(q + g) % L::NBUF]));
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-          const int j = j0 + g;
-          const float dsv = ds[j * MM_ROWS + r], dsc = ds[(8 + j) * MM_ROWS + r], ndm = -ds[(16 + j) * MM_ROWS + r];
+        for (int g = 0; g < G; g += 2) {
+          const int jA = j0 + g, jB = jA + 1;
+          const float sA = ds[(MM_SC_S + jA) * MM_ROWS + r], nmA = ds[(MM_SC_NM + jA) * MM_ROWS + r];
+          const float sB = ds[(MM_SC_S + jB) * MM_ROWS + r], nmB = ds[(MM_SC_NM + jB) * MM_ROWS + r];
+          const float2 sA2 = make_float2(sA, sA), nmA2 = make_float2(nmA, nmA);
+          const float2 sB2 = make_float2(sB, sB), nmB2 = make_float2(nmB, nmB);
 #pragma unroll
           for (int c4 = 0; c4 < HC / 4; c4++) {
             const int c = half * HC + 4 * c4;
-            const float4 xs4 = *reinterpret_cast<const float4*>(xs_t + j * L::XP + c);
-            const float4 ix4 = *reinterpret_cast<const float4*>(ix_t + j * L::XP + c);
-            const float xsv[4] = {xs4.x, xs4.y, xs4.z, xs4.w}, ixv[4] = {ix4.x, ix4.y, ix4.z, ix4.w};
+            const float4 xA = *reinterpret_cast<const float4*>(xs_t + jA * L::XP + c);
+            const float4 iA = *reinterpret_cast<const float4*>(ix_t + jA * L::XP + c);
+            const float4 xB = *reinterpret_cast<const float4*>(xs_t + jB * L::XP + c);
+            const float4 iB = *reinterpret_cast<const float4*>(ix_t + jB * L::XP + c);
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-              const int k = 4 * c4 + e;
-              const float w = __uint_as_float(MM_BIAS + v[g * HC + k]);
-              const float prod = __fmaf_rn(w, dsv, dsc);  // (d*s)*isum
-              const float tv = __fmaf_rn(ndm, ixv[e], prod);
-              acc[k] = __fmaf_rn(xsv[e], tv, acc[k]);
+            for (int e = 0; e < 2; e++) {
+              const int k = 4 * c4 + 2 * e;
+              const float2 xsA = e ? make_float2(xA.z, xA.w) : make_float2(xA.x, xA.y);
+              const float2 ixA = e ? make_float2(iA.z, iA.w) : make_float2(iA.x, iA.y);
+              const float2 xsB = e ? make_float2(xB.z, xB.w) : make_float2(xB.x, xB.y);
+              const float2 ixB = e ? make_float2(iB.z, iB.w) : make_float2(iB.x, iB.y);
+              const float2 wA = make_float2(__uint_as_float(MM_BIAS + v[g * HC + k]),
+                                            __uint_as_float(MM_BIAS + v[g * HC + k + 1]));
+              const float2 wB = make_float2(__uint_as_float(MM_BIAS + v[(g + 1) * HC + k]),
+                                            __uint_as_float(MM_BIAS + v[(g + 1) * HC + k + 1]));
+              const float2 tA = fma2(sA2, fma2(wA, d2, dneg2), mul2(nmA2, mul2(dmin2, ixA)));
+              const float2 tB = fma2(sB2, fma2(wB, d2, dneg2), mul2(nmB2, mul2(dmin2, ixB)));
+              acc[k / 2] = add2(acc[k / 2], fma2(tB, xsB, mul2(tA, xsA)));
             }
           }
         }
@@ -455,13 +441,12 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
     }
     const int row = row0 + r;
     if (ok && row < a.n_out) {
-      const bool split = gridDim.z > 1;
-      const float bv = (a.bias && !split) ? __ldg(a.bias + row) : 0.f;
-      float* dst = a.out + (split ? (size_t)blockIdx.z * a.n_batch * a.n_out : 0);
+      const float bv = a.bias ? __ldg(a.bias + row) : 0.f;
 #pragma unroll
       for (int c = 0; c < HC; c++) {
         const int n = n0 + half * HC + c;
-        if (n < a.n_batch) dst[(size_t)n * a.n_out + row] = acc[c] + bv;
+        const float y = (c & 1) ? acc[c / 2].y : acc[c / 2].x;
+        if (n < a.n_batch) a.out[(size_t)n * a.n_out + row] = a.bias ? __fadd_rn(y, bv) : y;
       }
     }
   }
@@ -479,24 +464,16 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
 
 namespace {
 
-// Activation tile width for a batch.
-int mma_bn(int n_batch) { return n_batch <= 16 ? 16 : n_batch <= 32 ? 32 : 64; }
-
-// Super-blocks per split so that row tiles x activation tiles x splits
-// covers the SMs (each split at least 4 super-blocks).
-int mma_split(int n_out, int n_in, int n_batch, int num_sms, int* per) {
-  const int bn = mma_bn(n_batch);
-  const int nsb = n_in / QK, tiles = ((n_out + MM_ROWS - 1) / MM_ROWS) * ((n_batch + bn - 1) / bn);
-  // one wave: tiles x split <= SMs (a second, partial wave costs a whole
-  // CTA's time for a few CTAs)
-  int split = std::max(1, std::min(num_sms / tiles, nsb / 4));
-  *per = (nsb + split - 1) / split;
-  return (nsb + *per - 1) / *per;
+// Activation tile width: 32 when the 32-wide tiles already give every SM a
+// CTA, else 16 (twice the CTAs; the weight tile is then read twice, the
+// second time mostly from L2).
+int mma_bn(int n_out, int n_batch, int num_sms) {
+  const int row_tiles = (n_out + MM_ROWS - 1) / MM_ROWS;
+  return n_batch > 16 && row_tiles * ((n_batch + 31) / 32) >= num_sms ? 32 : 16;
 }
 
 template <int BN>
-cudaError_t launch_mma_bn(const uint8_t* w, const int8_t* xq, const float* xs, const MmaArgs& a, int split,
-                          cudaStream_t st) {
+cudaError_t launch_mma_bn(const uint8_t* w, const int8_t* xq, const float* xs, const MmaArgs& a, cudaStream_t st) {
   using L = MmaLayout<BN>;
   CUtensorMap wm, xm, sm;
   const uint64_t rowB = (uint64_t)(a.n_in / QK) * Q4K_BYTES;
@@ -517,8 +494,7 @@ cudaError_t launch_mma_bn(const uint8_t* w, const int8_t* xq, const float* xs, c
     ready.fetch_or(bit);
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((a.n_out + MM_ROWS - 1) / MM_ROWS), (unsigned)((a.n_batch + BN - 1) / BN),
-                     (unsigned)split);
+  cfg.gridDim = dim3((unsigned)((a.n_out + MM_ROWS - 1) / MM_ROWS), (unsigned)((a.n_batch + BN - 1) / BN), 1);
   cfg.blockDim = dim3(MM_THREADS);
   cfg.dynamicSmemBytes = L::SMEM;
   cfg.stream = st;
@@ -532,37 +508,19 @@ cudaError_t launch_mma_bn(const uint8_t* w, const int8_t* xq, const float* xs, c
 
 }  // namespace
 
-size_t q4k_mma_scratch_bytes(int n_out, int n_in, int n_batch, int num_sms) {
-  int per = 0;
-  const int split = mma_split(n_out, n_in, n_batch, num_sms, &per);
-  return split > 1 ? (size_t)split * n_batch * n_out * 4 : 0;
-}
-
-// Tensor-core batched Q4_K matmul; activation tiles of 16, 32 or 64.
-// With a K split, the splits' partials go to `part` and the chunk-sum
-// kernel adds them in split order (deterministic).
+// Tensor-core batched Q4_K matmul; activation tiles of 16 or 32.
 cudaError_t launch_q4k_mma(float* out, const uint8_t* w, const int8_t* xq, const float* xs, const float* bias,
-                           int n_out, int n_in, int n_batch, float* part, int* err_flag, int num_sms,
-                           cudaStream_t st) {
+                           int n_out, int n_in, int n_batch, int* err_flag, int num_sms, cudaStream_t st) {
+  if (n_out <= 0 || n_batch <= 0 || n_in <= 0 || n_in % QK) return cudaErrorInvalidValue;
   MmaArgs a = {};
-  int per = 0;
-  const int split = mma_split(n_out, n_in, n_batch, num_sms, &per);
-  if (split > 1 && !part) return cudaErrorInvalidValue;
-  a.out = split > 1 ? part : out;
+  a.out = out;
   a.bias = bias;
   a.err_flag = err_flag;
   a.n_out = n_out;
   a.n_in = n_in;
   a.n_batch = n_batch;
-  a.sb_per_split = per;
-  cudaError_t e;
-  switch (mma_bn(n_batch)) {
-    case 16: e = launch_mma_bn<16>(w, xq, xs, a, split, st); break;
-    case 32: e = launch_mma_bn<32>(w, xq, xs, a, split, st); break;
-    default: e = launch_mma_bn<64>(w, xq, xs, a, split, st); break;
-  }
-  if (e != cudaSuccess || split == 1) return e;
-  return launch_chunk_sum(out, part, bias, n_out, n_batch, split, num_sms, st);
+  return mma_bn(n_out, n_batch, num_sms) == 32 ? launch_mma_bn<32>(w, xq, xs, a, st)
+                                               : launch_mma_bn<16>(w, xq, xs, a, st);
 }
 
 }  // namespace hakm

@@ -195,26 +195,15 @@ struct hakmc_ctx {
   size_t xr_size[XR_COUNT] = {};
   void* peer_ptr[TP_MAX][XR_COUNT] = {};
   bool peer_ipc[TP_MAX] = {};         // opened through IPC (closed at destroy)
-  // batched prompt processing (hakmc_prefill_batched): buffers for pf_rows
-  // rows of a chunk; pf_part holds pf_part_bytes of tensor-core split partials
+  // row-batched passes (hakmc_prefill_batched, batched decode): buffers for
+  // pf_rows rows
   int pf_rows = 0;
   float *pf_x = nullptr, *pf_xn = nullptr, *pf_qk = nullptr, *pf_v = nullptr, *pf_q = nullptr, *pf_att = nullptr,
-        *pf_gu = nullptr, *pf_h = nullptr, *pf_tmp = nullptr, *pf_xs = nullptr, *pf_part = nullptr;
+        *pf_gu = nullptr, *pf_h = nullptr, *pf_tmp = nullptr, *pf_xs = nullptr;
   int8_t* pf_xq = nullptr;
-  size_t pf_part_bytes = 0;
-  float* pf_part6 = nullptr;  // Q6_K K-split partials, pf_part6_floats
-  size_t pf_part6_floats = 0;
-  // dp4a batched Q4_K (short batches): one zeroed scratch region (partials,
-  // then tickets) per matrix shape, at pf_bscr + offset
-  void* pf_bscr = nullptr;
-  size_t pf_bscr_bytes = 0;
-  int pf_bscr_rows = 0;  // the batch the regions were sized for
-  std::vector<std::array<long long, 3>> pf_bscr_regions;  // {rows, cols, byte offset}
   int* row_io = nullptr;  // batched decode: [max_batch] tokens, positions, picks
-  float* pf_apart = nullptr;  // batched decode: attention split partials, pf_apart_floats
-  size_t pf_apart_floats = 0;
-  // batched decode: one captured graph per (rows, layers, attention splits);
-  // dropped whenever a buffer it names is reallocated
+  // batched decode: one captured graph per (rows, layers, attention score
+  // capacity); dropped whenever a buffer it names is reallocated
   std::map<uint64_t, cudaGraphExec_t> bgraphs;
 };
 
@@ -1002,11 +991,13 @@ extern "C" int hakmc_prefill(hakmc_ctx* c, const int* tokens, int n, float* logi
 
 // ------------------------------------------------------------ batched prefill
 //
-// The rows of a prompt chunk go through every layer together
-// (hakm_prefill.cu): Q4_K matmuls on the tensor cores, Q6_K matmuls as fp32
-// tiles, causal attention over the cache, which the chunk's own K/V rows
-// enter first. Then the last row's final norm, lm_head and argmax run as in
-// a decode step.
+// The rows of a prompt chunk go through every layer together, each weight
+// byte read once per chunk (hakm_rows.cu, hakm_mma.cu, hakm_prefill.cu):
+// Q4_K matmuls on the tensor cores, Q6_K matmuls as fp32 lane chains,
+// attention of each row over the cache, which the chunk's own K/V rows enter
+// first. Every kernel keeps the reference's roundings, so each row equals
+// what hakm_forward gives at its position bit for bit. Then the last row's
+// final norm, lm_head and argmax run as in a decode step.
 
 constexpr int PF_ROWS_DEFAULT = 1024;
 
@@ -1032,117 +1023,61 @@ static int pf_ensure(hakmc_ctx* c, int rows) {
   return 0;
 }
 
-static bool use_tensor_cores(int n_out, int n_in, int n_batch);
-
-// out[M][W.rows] (+)= W x (+ bias) for the chunk's rows: Q4_K on the q8
-// codes (xq, xs) — the dp4a kernel for short batches of small matrices,
-// as hakmc_gemv_q4k_q8_batch routes them, else the tensor cores — and Q6_K
-// on the fp32 rows xn. Accumulating Q4_K products go
-// through pf_tmp, then one add (the reference's order: product, then +=).
+// out[M][W.rows] (+)= W x (+ bias) for M rows: Q4_K on the q8 codes (xq,
+// xs) on the tensor cores, Q6_K on the fp32 rows xn. Accumulating Q4_K
+// products go through pf_tmp, then one add (the reference's order: the
+// product, then +=).
 static cudaError_t pf_matmul(hakmc_ctx* c, float* out, const DevMat& W, const float* xn, const int8_t* xq,
                              const float* xs, const float* bias, int M, bool accumulate) {
-  if (W.type == W_Q6K)
-    return launch_pf_q6k_gemm(out, W.w, xn, bias, W.rows, W.cols, M, accumulate, c->pf_part6, c->pf_part6_floats,
-                              c->pf_tmp, c->stream);
+  if (W.type == W_Q6K) return launch_rx_q6k_gemm(out, W.w, xn, bias, W.rows, W.cols, M, accumulate, c->stream);
   float* dst = accumulate ? c->pf_tmp : out;
-  void* bscr = nullptr;  // this shape's dp4a region (sized for M rows)
-  if (!use_tensor_cores(W.rows, W.cols, M) && c->pf_bscr && c->pf_bscr_rows == M)
-    for (const auto& rg : c->pf_bscr_regions)
-      if (rg[0] == W.rows && rg[1] == W.cols) bscr = (char*)c->pf_bscr + rg[2];
-  cudaError_t e = bscr ? launch_q4k_batch(dst, W.w, xq, xs, bias, W.rows, W.cols, M, bscr, c->err_flag,
-                                          c->num_sms, c->stream)
-                       : launch_q4k_mma(dst, W.w, xq, xs, bias, W.rows, W.cols, M, c->pf_part, c->err_flag,
-                                        c->num_sms, c->stream);
+  cudaError_t e = launch_q4k_mma(dst, W.w, xq, xs, bias, W.rows, W.cols, M, c->err_flag, c->num_sms, c->stream);
   if (e != cudaSuccess || !accumulate) return e;
   return launch_pf_add(out, c->pf_tmp, (size_t)M * W.rows, c->stream);
 }
 
-// Split partials for every matmul of a chunk of M rows: tensor-core (Q4_K)
-// and fp32-tile (Q6_K) ones.
-static int pf_ensure_part(hakmc_ctx* c, int M) {
-  size_t need = 0, need6 = 0;
-  std::vector<std::array<long long, 3>> regions;
-  size_t needb = 0;
-  auto add = [&](const DevMat& W) {
-    if (W.type != W_Q4K) {
-      need6 = std::max(need6, pf_q6k_part_floats(W.rows, W.cols, M));
-    } else if (use_tensor_cores(W.rows, W.cols, M)) {
-      need = std::max(need, q4k_mma_scratch_bytes(W.rows, W.cols, M, c->num_sms));
-    } else {
-      for (const auto& rg : regions)
-        if (rg[0] == W.rows && rg[1] == W.cols) return;
-      regions.push_back({W.rows, W.cols, (long long)needb});
-      needb += (q4k_batch_scratch_bytes(W.rows, W.cols, M, c->num_sms) + 255) & ~(size_t)255;
-    }
-  };
-  for (int l = 0; l < c->run_layers; l++) {
-    const DevLayer& y = c->layers[l];
-    for (const DevMat* W : {&y.wqk, &y.wv, &y.wo, &y.wgu, &y.down}) add(*W);
-  }
-  add(c->lm_head);
-  // the dp4a regions are laid out for this M (a later call with another M
-  // re-lays them; the batched pass sizes them for its row count only)
-  if (needb && (c->pf_bscr_rows != M || needb > c->pf_bscr_bytes)) {
-    if (needb > c->pf_bscr_bytes) {
-      dfree(c, c->pf_bscr);
-      c->pf_bscr = nullptr;
-      c->pf_bscr_bytes = 0;
-      const int r = dalloc(c, &c->pf_bscr, needb);
-      if (r) return r;
-      c->pf_bscr_bytes = needb;
-    } else {
-      drop_bgraphs(c);  // graphs captured for the old layout
-    }
-    CK(cudaMemset(c->pf_bscr, 0, c->pf_bscr_bytes));  // tickets start at zero (each launch leaves them so)
-    c->pf_bscr_rows = M;
-    c->pf_bscr_regions = regions;
-  }
-  if (need6 > c->pf_part6_floats) {
-    dfree(c, c->pf_part6);
-    c->pf_part6 = nullptr;
-    c->pf_part6_floats = 0;
-    const int r = dalloc(c, (void**)&c->pf_part6, need6 * 4);
-    if (r) return r;
-    c->pf_part6_floats = need6;
-  }
-  if (need <= c->pf_part_bytes) return 0;
-  dfree(c, c->pf_part);
-  c->pf_part = nullptr;
-  c->pf_part_bytes = 0;
-  const int r = dalloc(c, (void**)&c->pf_part, need);
-  if (r) return r;
-  c->pf_part_bytes = need;
-  return 0;
-}
-
-// One chunk: rows tokens_dev[0..M) at positions pos0.. of sequence 0 through
-// run_layers layers; leaves the residual rows in pf_x.
-static cudaError_t pf_chunk(hakmc_ctx* c, const int* tokens_dev, int M, int pos0) {
+// The layers for M rows already embedded in pf_x. Row r is at position
+// row_pos[r] with its cache slot_stride floats after row r-1's, or (row_pos
+// null) at pos0 + r of sequence 0; n_max >= every row's position + 1.
+static cudaError_t pf_layers(hakmc_ctx* c, int M, int pos0, const int* row_pos, size_t slot_stride, int n_max) {
   const int D = c->D, KV = c->KV, F = c->F;
   const size_t lstride = (size_t)c->max_seq * KV;
-  const float scale = 1.0f / sqrtf((float)c->hd);
+  const float scale = host_rsqrt_nr((float)c->hd);
   cudaStream_t s = c->stream;
-  cudaError_t e = launch_pf_embed(c->pf_x, c->tok_embd.w, tokens_dev, M, D, s);
+  cudaError_t e = cudaSuccess;
   for (int l = 0; l < c->run_layers && e == cudaSuccess; l++) {
     const DevLayer& y = c->layers[l];
     float* kc = c->k_cache + (size_t)l * lstride;
     float* vc = c->v_cache + (size_t)l * lstride;
     // attention block (src/model.c:102-146)
-    if ((e = launch_pf_norm_quant(c->pf_x, y.attn_norm, M, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
+    if ((e = launch_rx_norm_quant(c->pf_x, y.attn_norm, M, D, c->eps, c->rsq, c->pf_xn, c->pf_xq, c->pf_xs, s)))
+      break;
     if ((e = pf_matmul(c, c->pf_qk, y.wqk, c->pf_xn, c->pf_xq, c->pf_xs, y.bqk, M, false))) break;
     if ((e = pf_matmul(c, c->pf_v, y.wv, c->pf_xn, c->pf_xq, c->pf_xs, y.bv, M, false))) break;
-    if ((e = launch_pf_rope_kv(c->pf_qk, c->pf_v, c->pf_q, kc, vc, c->rope_cs, M, pos0, nullptr, 0, D, KV, c->hd, s))) break;
-    if ((e = launch_pf_attention(c->pf_att, c->pf_q, kc, vc, M, pos0, c->H, c->KVH, c->hd, scale, s))) break;
+    if ((e = launch_pf_rope_kv(c->pf_qk, c->pf_v, c->pf_q, kc, vc, c->rope_cs, M, pos0, row_pos, slot_stride, D, KV,
+                               c->hd, s)))
+      break;
+    if ((e = launch_rx_attention(c->pf_att, c->pf_q, kc, vc, M, pos0, row_pos, n_max, slot_stride, c->H, c->KVH,
+                                 c->hd, scale, s)))
+      break;
     if (y.wo.type == W_Q4K && (e = launch_quantize_q8(c->pf_att, M * D, c->pf_xq, c->pf_xs, s))) break;
     if ((e = pf_matmul(c, c->pf_x, y.wo, c->pf_att, c->pf_xq, c->pf_xs, nullptr, M, true))) break;
     // feed-forward block (src/model.c:148-156)
-    if ((e = launch_pf_norm_quant(c->pf_x, y.ffn_norm, M, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
+    if ((e = launch_rx_norm_quant(c->pf_x, y.ffn_norm, M, D, c->eps, c->rsq, c->pf_xn, c->pf_xq, c->pf_xs, s)))
+      break;
     if ((e = pf_matmul(c, c->pf_gu, y.wgu, c->pf_xn, c->pf_xq, c->pf_xs, nullptr, M, false))) break;
-    if ((e = launch_pf_swiglu(c->pf_h, c->pf_gu, M, F, s))) break;
+    if ((e = launch_rx_swiglu(c->pf_h, c->pf_gu, M, F, s))) break;
     if (y.down.type == W_Q4K && (e = launch_quantize_q8(c->pf_h, M * F, c->pf_xq, c->pf_xs, s))) break;
     e = pf_matmul(c, c->pf_x, y.down, c->pf_h, c->pf_xq, c->pf_xs, nullptr, M, true);
   }
   return e;
+}
+
+// One chunk: rows tokens_dev[0..M) at positions pos0.. of sequence 0 through
+// run_layers layers; leaves the residual rows in pf_x.
+static cudaError_t pf_chunk(hakmc_ctx* c, const int* tokens_dev, int M, int pos0) {
+  const cudaError_t e = launch_pf_embed(c->pf_x, c->tok_embd.w, tokens_dev, M, c->D, c->stream);
+  return e != cudaSuccess ? e : pf_layers(c, M, pos0, nullptr, 0, pos0 + M);
 }
 
 extern "C" int hakmc_prefill_batched(hakmc_ctx* c, const int* tokens, int n, int chunk_rows, float* logits,
@@ -1152,12 +1087,11 @@ extern "C" int hakmc_prefill_batched(hakmc_ctx* c, const int* tokens, int n, int
   if (c->pos + n > c->max_seq) { set_err("prefill: sequence exceeds max_seq"); return HAKMC_ERANGE; }
   for (int i = 0; i < n; i++)
     if (tokens[i] < 0 || tokens[i] >= c->V) { set_err("prefill: token %d out of range", tokens[i]); return HAKMC_EINVAL; }
-  if (c->H / c->KVH > 32) { set_err("prefill: more than 32 query heads per kv head"); return HAKMC_EINVAL; }
+  // the batched attention keeps a row's scores in shared memory
+  if (rx_attention_smem_bytes(c->hd, c->pos + n) > RX_ATTN_SMEM_MAX) return hakmc_prefill(c, tokens, n, logits, argmax);
   CK(cudaSetDevice(c->device));
   const int rows = std::min(n, chunk_rows > 0 ? chunk_rows : PF_ROWS_DEFAULT);
   int r = pf_ensure(c, rows);
-  if (!r) r = pf_ensure_part(c, rows);
-  if (!r && n % rows) r = pf_ensure_part(c, n % rows);
   if (r) return r;
   if (n > c->prompt_cap) {
     void* p = nullptr;
@@ -1384,10 +1318,9 @@ extern "C" int hakmc_trace_step(hakmc_ctx* c, unsigned long long* stamps, int ma
 // in logits[0..n).
 static int batch_decode(hakmc_ctx* c, const int* tokens, const int* pos, int n, float* logits, int* argmax) {
   int r = pf_ensure(c, n);
-  if (!r) r = pf_ensure_part(c, n);
   if (!r && !c->row_io) r = dalloc(c, (void**)&c->row_io, (size_t)3 * c->max_batch * 4);
   if (r) return r;
-  const int D = c->D, KV = c->KV, F = c->F, B = c->max_batch;
+  const int D = c->D, B = c->max_batch;
   int* tok_dev = c->row_io;
   int* pos_dev = c->row_io + B;
   int* pick_dev = c->row_io + 2 * B;
@@ -1396,46 +1329,21 @@ static int batch_decode(hakmc_ctx* c, const int* tokens, const int* pos, int n, 
   CK(cudaMemcpyAsync(pos_dev, pos, (size_t)n * 4, cudaMemcpyHostToDevice, s));
   int max_pos = 0;
   for (int i = 0; i < n; i++) max_pos = std::max(max_pos, pos[i]);
-  const size_t lstride = (size_t)c->max_seq * KV, slot = (size_t)c->L * lstride;
-  const float scale = 1.0f / sqrtf((float)c->hd);
-  const size_t apart = pf_decode_attention_part_floats(n, c->H, c->KVH, c->hd, max_pos, c->num_sms);
-  if (apart > c->pf_apart_floats) {
-    dfree(c, c->pf_apart);
-    c->pf_apart = nullptr;
-    c->pf_apart_floats = 0;
-    if ((r = dalloc(c, (void**)&c->pf_apart, apart * 4))) return r;
-    c->pf_apart_floats = apart;
-  }
-  // the kernels of the step, captured once per (rows, layers, attention
-  // splits) into a graph: ~370 launches of short kernels per step
-  int tiles_per = 0;
-  const int n_split = pf_decode_attention_plan(n, c->KVH, max_pos, c->num_sms, &tiles_per);
-  const uint64_t key = ((uint64_t)n << 48) | ((uint64_t)c->run_layers << 40) | ((uint64_t)n_split << 24) |
-                       (uint64_t)tiles_per;
+  const size_t slot = (size_t)c->L * c->max_seq * c->KV;
+  // score capacity of the attention launch: a power of two from 1024, so a
+  // captured graph serves every step until the positions pass it
+  int n_cap = 1024;
+  while (n_cap < max_pos + 1) n_cap *= 2;
+  n_cap = std::min(n_cap, c->max_seq);
+  // the kernels of the step, captured once per (rows, layers, score
+  // capacity) into a graph: ~15 launches per layer
+  const uint64_t key = ((uint64_t)n << 48) | ((uint64_t)c->run_layers << 32) | (uint64_t)n_cap;
   auto enqueue = [&]() -> cudaError_t {
     cudaError_t e = launch_pf_embed(c->pf_x, c->tok_embd.w, tok_dev, n, D, s);
-    for (int l = 0; l < c->run_layers && e == cudaSuccess; l++) {
-      const DevLayer& y = c->layers[l];
-      float* kc = c->k_cache + (size_t)l * lstride;
-      float* vc = c->v_cache + (size_t)l * lstride;
-      if ((e = launch_pf_norm_quant(c->pf_x, y.attn_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
-      if ((e = pf_matmul(c, c->pf_qk, y.wqk, c->pf_xn, c->pf_xq, c->pf_xs, y.bqk, n, false))) break;
-      if ((e = pf_matmul(c, c->pf_v, y.wv, c->pf_xn, c->pf_xq, c->pf_xs, y.bv, n, false))) break;
-      if ((e = launch_pf_rope_kv(c->pf_qk, c->pf_v, c->pf_q, kc, vc, c->rope_cs, n, 0, pos_dev, slot, D, KV, c->hd, s)))
-        break;
-      if ((e = launch_pf_decode_attention(c->pf_att, c->pf_q, kc, vc, n, pos_dev, max_pos, slot, c->H, c->KVH, c->hd,
-                                          scale, c->pf_apart, c->pf_apart_floats, c->num_sms, s)))
-        break;
-      if (y.wo.type == W_Q4K && (e = launch_quantize_q8(c->pf_att, n * D, c->pf_xq, c->pf_xs, s))) break;
-      if ((e = pf_matmul(c, c->pf_x, y.wo, c->pf_att, c->pf_xq, c->pf_xs, nullptr, n, true))) break;
-      if ((e = launch_pf_norm_quant(c->pf_x, y.ffn_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s))) break;
-      if ((e = pf_matmul(c, c->pf_gu, y.wgu, c->pf_xn, c->pf_xq, c->pf_xs, nullptr, n, false))) break;
-      if ((e = launch_pf_swiglu(c->pf_h, c->pf_gu, n, F, s))) break;
-      if (y.down.type == W_Q4K && (e = launch_quantize_q8(c->pf_h, n * F, c->pf_xq, c->pf_xs, s))) break;
-      e = pf_matmul(c, c->pf_x, y.down, c->pf_h, c->pf_xq, c->pf_xs, nullptr, n, true);
-    }
+    if (e == cudaSuccess) e = pf_layers(c, n, 0, pos_dev, slot, n_cap);
     // final norm, lm_head, greedy pick per row (src/model.c:159-164, src/sample.c:28-32)
-    if (e == cudaSuccess) e = launch_pf_norm_quant(c->pf_x, c->out_norm, n, D, c->eps, c->pf_xn, c->pf_xq, c->pf_xs, s);
+    if (e == cudaSuccess)
+      e = launch_rx_norm_quant(c->pf_x, c->out_norm, n, D, c->eps, c->rsq, c->pf_xn, c->pf_xq, c->pf_xs, s);
     if (e == cudaSuccess) e = pf_matmul(c, c->logits, c->lm_head, c->pf_xn, c->pf_xq, c->pf_xs, nullptr, n, false);
     if (e == cudaSuccess) e = launch_pf_argmax(pick_dev, c->logits, n, c->V, s);
     return e;
@@ -1482,11 +1390,9 @@ extern "C" int hakmc_forward_batch(hakmc_ctx* c, const int* tokens, const int* p
   }
   CK(cudaSetDevice(c->device));
   // BATCH_ROWS_MIN or more sequences on one GPU: one batched pass (weights
-  // read once). Fewer run the step kernel per sequence: the batched pass
-  // costs ~8 ms on the 3B shapes whatever the batch up to 16 (about 470
-  // launches of short kernels), the step kernel 1.4 ms per sequence.
-  // (its attention takes up to 8 query heads per kv head)
-  if (n_seq >= BATCH_ROWS_MIN && c->tp_world == 1 && c->H / c->KVH <= 8)
+  // read once), while a row's attention scores fit in shared memory. Fewer
+  // run the step kernel per sequence. Both give the same bits.
+  if (n_seq >= BATCH_ROWS_MIN && c->tp_world == 1 && rx_attention_smem_bytes(c->hd, c->max_seq) <= RX_ATTN_SMEM_MAX)
     return batch_decode(c, tokens, pos, n_seq, logits, argmax);
   if (!c->use_step) { set_err("forward_batch runs on the step kernel (HAKMC_STEP=0 is set)"); return HAKMC_EINVAL; }
   // sequence 0 is also the single-sequence API's: its position and last pick
@@ -1693,9 +1599,8 @@ static bool use_tensor_cores(int n_out, int n_in, int n_batch) {
 extern "C" size_t hakmc_gemv_q4k_q8_batch_scratch(int n_out, int n_in, int n_batch) {
   if (n_out <= 0 || n_in <= 0 || n_in % QK || n_batch <= 0) return 0;
   const int sms = device_sms();
-  // the dp4a kernel's partials and tickets, then the tensor-core partials
-  const size_t dp = (q4k_batch_scratch_bytes(n_out, n_in, n_batch, sms) + 255) & ~(size_t)255;
-  return dp + (use_tensor_cores(n_out, n_in, n_batch) ? q4k_mma_scratch_bytes(n_out, n_in, n_batch, sms) : (size_t)0);
+  // the dp4a kernel's partials and tickets (the tensor-core kernel needs none)
+  return (q4k_batch_scratch_bytes(n_out, n_in, n_batch, sms) + 255) & ~(size_t)255;
 }
 
 extern "C" int hakmc_gemv_q4k_q8_batch(float* out, const void* w, const int8_t* xq, const float* xs,
@@ -1714,14 +1619,7 @@ extern "C" int hakmc_gemv_q4k_q8_batch(float* out, const void* w, const int8_t* 
   }
   const cudaStream_t st = (cudaStream_t)stream;
   if (use_tensor_cores(n_out, n_in, n_batch) && aligned16(xs)) {
-    // the tensor-core path uses only its K-split partials, after the dp4a part
-    const size_t tb = q4k_mma_scratch_bytes(n_out, n_in, n_batch, sms);
-    void* s = scratch ? (char*)scratch + (bytes - tb) : nullptr;
-    if (!scratch && tb) CKL(cudaMallocAsync(&s, tb, st));
-    const cudaError_t e = launch_q4k_mma(out, (const uint8_t*)w, xq, xs, bias, n_out, n_in, n_batch, (float*)s,
-                                         nullptr, sms, st);
-    if (!scratch && tb) CKL(cudaFreeAsync(s, st));
-    CKL(e);
+    CKL(launch_q4k_mma(out, (const uint8_t*)w, xq, xs, bias, n_out, n_in, n_batch, nullptr, sms, st));
     return 0;
   }
   void* s = scratch;
@@ -1739,13 +1637,14 @@ extern "C" int hakmc_gemv_q4k_q8_batch(float* out, const void* w, const int8_t* 
 }
 
 extern "C" size_t hakmc_gemm_q4k_q8_scratch(int n_out, int n_in, int n_batch) {
-  if (n_out <= 0 || n_in <= 0 || n_in % QK || n_batch <= 0) return 0;
-  return q4k_mma_scratch_bytes(n_out, n_in, n_batch, device_sms());
+  (void)n_out, (void)n_in, (void)n_batch;
+  return 0;  // the kernel never splits K, so it needs no scratch
 }
 
 extern "C" int hakmc_gemm_q4k_q8(float* out, const void* w, const int8_t* xq, const float* xs, const float* bias,
                                  int n_out, int n_in, int n_batch, void* scratch, size_t scratch_bytes,
                                  void* stream) {
+  (void)scratch, (void)scratch_bytes;
   if (!out || !w || !xq || !xs || n_out <= 0 || n_in <= 0 || n_in % QK || n_batch <= 0) {
     set_err("gemm: n_in must be a positive multiple of 256, n_batch >= 1");
     return HAKMC_EINVAL;
@@ -1754,19 +1653,8 @@ extern "C" int hakmc_gemm_q4k_q8(float* out, const void* w, const int8_t* xq, co
     set_err("gemm: w, xq and xs must be 16-byte aligned");
     return HAKMC_EINVAL;
   }
-  const int sms = device_sms();
-  const size_t bytes = q4k_mma_scratch_bytes(n_out, n_in, n_batch, sms);
-  if (scratch && bytes && (scratch_bytes < bytes || !aligned16(scratch))) {
-    set_err("gemm: scratch needs %zu bytes, 16-byte aligned", bytes);
-    return HAKMC_EINVAL;
-  }
-  const cudaStream_t st = (cudaStream_t)stream;
-  void* s = scratch;
-  if (!s && bytes) CKL(cudaMallocAsync(&s, bytes, st));  // stream-ordered scratch for callers that pass none
-  const cudaError_t e = launch_q4k_mma(out, (const uint8_t*)w, xq, xs, bias, n_out, n_in, n_batch, (float*)s,
-                                       nullptr, sms, st);
-  if (!scratch && bytes) CKL(cudaFreeAsync(s, st));
-  CKL(e);
+  CKL(launch_q4k_mma(out, (const uint8_t*)w, xq, xs, bias, n_out, n_in, n_batch, nullptr, device_sms(),
+                     (cudaStream_t)stream));
   return 0;
 }
 

@@ -80,17 +80,18 @@ int hakmc_generate(hakmc_ctx *c, const int *prompt, int n_prompt, int n_gen,
 int hakmc_prefill(hakmc_ctx *c, const int *tokens, int n, float *logits, int *argmax);
 
 /* Prompt processing with the positions batched: the same state and outputs
- * as hakmc_prefill, but the n [host] ids go through each layer together in
- * chunks of chunk_rows positions (<= 0: 1024), so every weight byte read
- * serves a whole chunk: Q4_K matmuls on the tensor cores over each row's
- * q8_32 codes, Q6_K matmuls as fp32 products of dequantized tiles, causal
- * attention over the cache (which each chunk's own K/V rows enter first).
- * Each position's arithmetic is the per-position arithmetic of
- * hakm_forward (src/model.c:93-165); summation orders differ, so results
- * agree with hakmc_prefill to fp32 rounding (and the int8 rounding flips
- * it can move), not bit for bit. No counterpart in the reference, whose
- * feed loop calls hakm_forward per id (cli/main.c:56-60). Under tensor
- * parallelism this runs hakmc_prefill. 0 or a negative code. */
+ * as hakmc_prefill, bit for bit, but the n [host] ids go through each layer
+ * together in chunks of chunk_rows positions (<= 0: 1024), so every weight
+ * byte read serves a whole chunk: Q4_K matmuls on the tensor cores over each
+ * row's q8_32 codes, Q6_K matmuls as fp32 lane chains over dequantized
+ * tiles, each row's attention over the cache (which each chunk's own K/V
+ * rows enter first). Every kernel keeps the per-position arithmetic of
+ * hakm_forward (src/model.c:93-165) with the reference build's roundings
+ * and summation orders. No counterpart in the reference, whose feed loop
+ * calls hakm_forward per id (cli/main.c:56-60). Under tensor parallelism,
+ * or when a row's attention scores would not fit in shared memory
+ * (positions beyond about 51,000), this runs hakmc_prefill. 0 or a
+ * negative code. */
 int hakmc_prefill_batched(hakmc_ctx *c, const int *tokens, int n, int chunk_rows, float *logits,
                           int *argmax);
 
@@ -109,10 +110,10 @@ int hakmc_decode(hakmc_ctx *c, int n_steps, int *out_tokens);
  * a context holding that sequence's cache. Eight or more sequences on one GPU
  * go through each layer together as the rows of one pass (the kernels of
  * hakmc_prefill_batched; attention reads each row's own cache slot up to its
- * position), so each weight byte is read once per call: rows agree with
- * single-sequence runs to fp32 rounding plus the int8 flips it can move.
- * Fewer sequences (or tensor parallelism) run the step kernel per sequence,
- * bit for bit. argmax [host] gets n_seq ids;
+ * position), so each weight byte is read once per call. Fewer sequences
+ * (or tensor parallelism, or max_seq beyond about 51,000) run the step
+ * kernel per sequence. Either way every row equals hakm_forward's logits
+ * and pick bit for bit. argmax [host] gets n_seq ids;
  * logits [host] (may be NULL) n_seq*vocab floats. 0, HAKMC_ERANGE for a
  * position beyond max_seq, or another negative code. */
 int hakmc_forward_batch(hakmc_ctx *c, const int *tokens, const int *pos,
@@ -215,9 +216,11 @@ int hakmc_gemv_q4k_q8(float *out, const void *w, const int8_t *xq, const float *
  * Q4_K matmul (src/nn.c:76-82, src/quant.c:150-232) applied to n_batch
  * activations; the reference has no batched call (it runs one vector per
  * hakm_forward). Small batches: dp4a, each weight byte read once per 16
- * activations; batches above 16 (above 8 for matrices of 16M weights or
- * more) run on the tensor cores as hakmc_gemm_q4k_q8 does (when xs is
- * 16-byte aligned; else dp4a in launches of 16). [dev]
+ * activations, per-chunk partials summed in a fixed order (fp32-close to
+ * the reference, rel-L2 <= 1e-5, deterministic); batches above 16 (above 8
+ * for matrices of 16M weights or more) run on the tensor cores as
+ * hakmc_gemm_q4k_q8 does, bit for bit (when xs is 16-byte aligned; else
+ * dp4a in launches of 16). [dev]
  * buffers; w and xq 16-byte aligned; n_in % 256 == 0.
  * scratch: [dev] hakmc_gemv_q4k_q8_batch_scratch(n_out, n_in, n_batch)
  * bytes, 16-byte aligned, zeroed before its first use (a call leaves it
@@ -231,16 +234,16 @@ int hakmc_gemv_q4k_q8_batch(float *out, const void *w, const int8_t *xq, const f
                             const float *bias, int n_out, int n_in, int n_batch,
                             void *scratch, size_t scratch_bytes, void *stream);
 
-/* The same product on the tensor cores (tcgen05 kind::i8): the per-32
- * integer sums q*xq are exact int32 MMA results, combined in fp32 as
- * q4k_vec_dot does (src/quant.c:224-227). For batches (batched decode,
- * prompt processing); any n_batch >= 1, tiles of 16, 32 or 64 activations;
- * shapes with few row tiles split K over several CTAs and add the splits
- * in order in a second kernel. [dev] w, xq and xs 16-byte aligned;
- * n_in % 256 == 0. scratch: [dev] hakmc_gemm_q4k_q8_scratch(n_out, n_in,
- * n_batch) bytes (0 when no split is needed), any contents; NULL takes it
- * from the stream-ordered allocator. Launched as a programmatic dependent
- * of the preceding kernel (it waits for that kernel before reading). */
+/* The same product on the tensor cores (tcgen05 kind::i8), bit-identical
+ * to q4k_vec_dot as built: the per-32 integer sums q*xq are exact int32 MMA
+ * results, combined in fp32 with the reference's steps and order
+ * (src/quant.c:224-227 under -O3 -ffast-math with FMA). For batches
+ * (batched decode, prompt processing); any n_batch >= 1, tiles of 16 or 32
+ * activations; a row is never split along K. [dev] w, xq and xs 16-byte
+ * aligned; n_in % 256 == 0. scratch: unused (hakmc_gemm_q4k_q8_scratch
+ * returns 0; kept for callers written against a splitting kernel).
+ * Launched as a programmatic dependent of the preceding kernel (it waits
+ * for that kernel before reading). */
 size_t hakmc_gemm_q4k_q8_scratch(int n_out, int n_in, int n_batch);
 int hakmc_gemm_q4k_q8(float *out, const void *w, const int8_t *xq, const float *xs,
                       const float *bias, int n_out, int n_in, int n_batch,

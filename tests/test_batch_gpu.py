@@ -1,11 +1,14 @@
-"""Batched Q4_K x q8_32 matmul (hakmc_gemv_q4k_q8_batch) against the
-reference's own Q4_K matmul (src/nn.c:76-82 -> q4k_vec_dot,
-src/quant.c:150-232), applied to each activation of the batch.
+"""Batched Q4_K x q8_32 matmuls against the reference's own Q4_K matmul
+(src/nn.c:76-82 -> q4k_vec_dot, src/quant.c:150-232), applied to each
+activation of the batch.
 
-Bars: rel-L2 <= 1e-5 per activation (the q8 codes and the per-32 integer
-sums are exact; only the fp32 summation order differs); bit-identical
-results across repeated calls (the chunk partials are summed in a fixed
-order whatever the grid)."""
+Bars: the tensor-core kernel (hakmc_gemm_q4k_q8, and hakmc_gemv_q4k_q8_batch
+where it routes there) restates the reference's fp32 steps and order, so it
+is bit-identical. The dp4a kernel behind hakmc_gemv_q4k_q8_batch's short
+batches sums per-chunk partials: rel-L2 <= 1e-5 per activation (the q8 codes
+and the per-32 integer sums are exact; only the fp32 summation order
+differs), and bit-identical results across repeated calls (the partials are
+summed in a fixed order whatever the grid)."""
 import ctypes as C
 
 import numpy as np
@@ -17,6 +20,11 @@ from hako_b200 import check, lib, synth
 pytestmark = pytest.mark.gpu
 
 TOL = 1e-5
+
+
+def same(a, b):
+    return np.array_equal(np.ascontiguousarray(a, np.float32).view(np.uint32),
+                          np.ascontiguousarray(b, np.float32).view(np.uint32))
 
 
 def P(t):
@@ -58,9 +66,15 @@ def test_gemv_q4k_batch_matches_reference(cuda, reference, rows, k, n):
     xs = np.stack([b for _, b in q])
     bias = synth.normal(rows, 79) if n % 2 else None
     out = run_batch(cuda, w, xq, xs, bias, rows, k, n, scratch=(rows % 2 == 0))
+    # the routing of hakmc_gemv_q4k_q8_batch: above 16 activations (above 8
+    # for 16M weights or more) the tensor cores
+    exact = n > 16 or (n > 8 and rows * k >= 16 << 20)
     for i in range(n):
         ref = reference.matmul(w, 12, xs_f[i], rows, k, bias=bias)
-        assert rel_l2(out[i], ref) < TOL, i
+        if exact:
+            assert same(out[i], ref), (i, rel_l2(out[i], ref))
+        else:
+            assert rel_l2(out[i], ref) < TOL, i
 
 
 @pytest.mark.parametrize("rows,k,n", [(2048, 11008, 16), (3584, 18944, 4)])
@@ -99,9 +113,9 @@ def run_tc(cuda, w, xq, xs, bias, rows, k, n):
     return out.cpu().numpy()
 
 
-# tensor-core path: activation tiles of 16, 32, 64 or 128; ragged rows (not
-# a multiple of the 128-row tile), ragged batches, one super-block, K split
-# over several CTAs (few row tiles)
+# tensor-core path: activation tiles of 16 or 32; ragged rows (not a
+# multiple of the 128-row tile), ragged batches, one super-block, long rows
+# with few row tiles
 TC_CASES = [(256, 2048, 16), (2048, 2048, 64), (11008, 2048, 64), (2048, 11008, 64), (3584, 18944, 16),
             (300, 512, 100), (5, 256, 1), (130, 2304, 130), (512, 3584, 256), (1000, 1024, 30), (18944, 3584, 4)]
 
@@ -117,7 +131,7 @@ def test_gemm_q4k_tensor_cores_match_reference(cuda, reference, rows, k, n):
     out = run_tc(cuda, w, xq, xs, bias, rows, k, n)
     for i in range(n):
         ref = reference.matmul(w, 12, xs_f[i], rows, k, bias=bias)
-        assert rel_l2(out[i], ref) < TOL, i
+        assert same(out[i], ref), (i, rel_l2(out[i], ref))
 
 
 def test_gemm_q4k_tensor_cores_deterministic(cuda, reference):
