@@ -3,22 +3,28 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--model 3b|7b]
 
-Workload (config 0 of the benchmark spec): random-init Qwen2 3B-shaped model
-in MLF2 (Q4_K + Q6_K, seed 0), 16 seeded prompt ids, then greedy decode. One
-step = one decoded token at batch 1. The prompt and W warm-up tokens run
-untimed; exactly K decode steps are timed with CUDA events, bracketed by a
-barrier and a device synchronize. Weights (2.03 GB) exceed the 126 MB L2, so
-every step streams them from HBM.
+Workload at N = 1 (config 0 of the benchmark spec): random-init Qwen2
+3B-shaped model in MLF2 (Q4_K + Q6_K, seed 0), 16 seeded prompt ids, then
+greedy decode (default 64 steps). At N > 1 (config 3): the 7B-shaped model,
+32 seeded prompt ids, greedy decode (default 128 steps). One step = one
+decoded token at batch 1. The prompt and W warm-up tokens run untimed;
+exactly K decode steps are timed with CUDA events, bracketed by a barrier
+and a device synchronize. Weights (2.03 GB / 5.07 GB) exceed the 126 MB L2,
+so every step streams them from HBM.
 
 - value: K / device time of one hakmc_decode call, which runs all K steps
   in one launch of the persistent step kernel (CUDA events on its stream).
 - e2e: the same K steps through the reference-facing per-token call
   (hakmc_forward: host token in, host argmax out, synchronous), wall clock.
+- stream_match: the W + K ids decoded against the reference engine's own
+  greedy stream for the same prompt (tests/golden/3b.json, 7b.json).
 - roofline: that step-kernel launch (the only kernel of the decode path):
   algorithmic bytes = every step's weights + its K/V reads at that
   position, over the launch's device time.
 - cpu_baseline: the reference engine's own compiled decode (oracle/_ref) on
   this host's cores, on a bounded sample of the same workload.
+- config3_7b_1gpu (N = 1): config 3 on the one GPU, the N = 1 point of the
+  7B series the N > 1 runs measure.
 - prefill / batched_decode (one GPU; --no-next-rows skips them): short samples
   of configs 4a and 4b on the 7B shapes, whose full lines come from
   --workload prefill and --workload batch.
@@ -372,6 +378,90 @@ def step_profile(model):
     return 0
 
 
+def golden_stream(model: str):
+    """The reference's greedy stream for the bench prompt (tests/golden/,
+    made by the reference engine itself: tests/golden/make_golden.py)."""
+    p = os.path.join(ROOT, "tests", "golden", f"{model}.json")
+    try:
+        with open(p) as f:
+            g = json.load(f)
+    except OSError:
+        return None
+    return g["tokens"] if g.get("prompt") == prompt_ids(model) else None
+
+
+def measure_decode(model: str, steps: int, warmup: int, world: int, local: int, pg, device):
+    """Batch-1 greedy decode of `model` after its seeded prompt: the prompt
+    and `warmup` steps untimed, then `steps` steps in one hakmc_decode call
+    (device time, max over ranks), the same steps again through the
+    per-token hakmc_forward (wall clock), and the stream's agreement with
+    the reference's golden stream."""
+    import ctypes as C
+    from hako_b200 import HakmCtx, lib, synth
+    cfg = synth.PRESETS[model]
+    prompt = prompt_ids(model)
+    max_seq = len(prompt) + 2 * (warmup + steps) + 16
+    ctx = HakmCtx(synth.cached_model(cfg), max_seq=max_seq, device=local)
+    if world > 1:
+        from hako_b200 import tp
+        tp.connect(ctx)
+    for t in prompt:
+        ctx.forward(t, want_logits=False)
+    toks = np.zeros(warmup, np.int32)
+    lib.hakmc_decode(ctx._h, warmup, C.c_void_p(toks.ctypes.data))
+    pos0 = ctx.pos
+    barrier(pg, device)
+    with ClockSampler(local) as clk:
+        barrier(pg, device)
+        t0 = time.perf_counter()
+        out = np.zeros(steps, np.int32)
+        rc = lib.hakmc_decode(ctx._h, steps, C.c_void_p(out.ctypes.data))
+        barrier(pg, device)
+        wall = time.perf_counter() - t0
+    if rc != 0:
+        raise RuntimeError(f"hakmc_decode failed: {rc}")
+    dev_ms = float(ctx.last_device_ms)
+    max_ms = reduce_max(pg, dev_ms, device)
+    # e2e: the same steps through the per-token host call
+    ctx.set_pos(pos0)
+    am = int(out[0])
+    barrier(pg, device)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        _, am = ctx.forward(am, want_logits=False)
+    e2e_s = reduce_max(pg, time.perf_counter() - t0, device)
+    ctx.close()
+    stream = toks.tolist() + out.tolist()
+    gold = golden_stream(model)
+    if gold is None:
+        match = {"golden": None}
+    else:
+        n = min(len(gold), len(stream))
+        first_bad = next((i for i in range(n) if stream[i] != gold[i]), None)
+        match = {"golden": f"tests/golden/{model}.json", "compared": n,
+                 "matched": n if first_bad is None else first_bad, "identical": first_bad is None}
+    # roofline: the step-kernel launch of the timed region; per GPU, with
+    # tensor parallelism each GPU streams 1/world of the weights
+    pk, pk_kind = peaks()
+    alg_bytes = sum(cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(pos0 + i) for i in range(steps)) / world
+    achieved = alg_bytes / (max_ms / 1e3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            per_tok = json.load(f).get(f"step_kernel_{model}_bytes_per_token")
+        if per_tok:
+            traffic = per_tok * steps / world  # per GPU, like bytes_per_launch
+    tok_bytes = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(pos0 + steps // 2)
+    roof = {"bound": "hbm", "kernel": "step_kernel (whole decode steps, one launch)",
+            "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": achieved / pk["hbm_gbs"], "peak_source": pk_kind, "traffic": traffic,
+            "bytes_per_launch": alg_bytes, "launch_ms": dev_ms,
+            "roofline_tok_s": world * pk["hbm_gbs"] * 1e9 / tok_bytes}
+    return {"value": steps / (max_ms / 1e3), "max_ms": max_ms, "e2e": steps / e2e_s, "wall": wall,
+            "roofline": roof, "stream_match": match, "clocks": clk.summary()}
+
+
 def config_block(args, world):
     from hako_b200 import synth
     cfg = synth.PRESETS[args.model]
@@ -381,7 +471,7 @@ def config_block(args, world):
             "heads": f"{cfg.n_heads}/{cfg.n_kv_heads}", "ffn": cfg.ffn_dim, "vocab": cfg.vocab,
             "prompt_len": len(prompt_ids(args.model)), "global_batch": 1, "seq_len": None,
             "parallelism": f"tp{world} (rows of every phase over all GPUs, peer-store all-gather)" if world > 1 else "single",
-            "l2": "weights stream from HBM every step (2.03 GB > 126 MB L2)"}
+            "l2": f"weights stream from HBM every step ({cfg.weight_bytes_per_token() / 1e9:.2f} GB > 126 MB L2)"}
 
 
 def run_prefill(args, emit: bool = True):
@@ -502,11 +592,13 @@ def batch_summary(steps: int, warmup: int, model: str = "7b"):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="default: 64 (3B decode), 128 (7B decode), 32 (batch), 8 (prefill)")
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default=None, choices=["3b", "7b"],
-                    help="default: 3b for decode, 7b for the prefill and batch workloads")
+                    help="default: 3b for decode on one GPU (config 0), 7b for decode on several GPUs "
+                         "(config 3) and for the prefill and batch workloads (config 4)")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "batch"],
                     help="decode: batch-1 greedy decode (the headline); prefill: config 4a; batch: config 4b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -522,7 +614,10 @@ def main():
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.model is None:
-        args.model = "3b" if args.workload == "decode" else "7b"
+        # decode: config 0 (3B) on one GPU, config 3 (7B) across several
+        args.model = "3b" if args.workload == "decode" and args.gpus == 1 else "7b"
+    if args.steps is None:
+        args.steps = {"prefill": 8, "batch": 32}.get(args.workload, 64 if args.model == "3b" else 128)
     if args.impl == "ours" and args.workload == "prefill":
         return run_prefill(args)
     if args.impl == "ours" and args.workload == "batch":
@@ -538,85 +633,35 @@ def main():
     world, rank, local, pg = dist_setup(args.gpus)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    from hako_b200 import HakmCtx, lib, synth
+    from hako_b200 import synth
     cfg = synth.PRESETS[args.model]
     path = synth.cached_model(cfg)
     prompt = prompt_ids(args.model)
-    max_seq = len(prompt) + 2 * (args.warmup + args.steps) + 16
-    ctx = HakmCtx(path, max_seq=max_seq, device=local)
-    if world > 1:
-        from hako_b200 import tp
-        tp.connect(ctx)
-
-    # prompt + warm-up (untimed)
-    for t in prompt:
-        ctx.forward(t, want_logits=False)
-    toks = np.zeros(args.warmup, np.int32)
-    import ctypes as C
-    lib.hakmc_decode(ctx._h, args.warmup, C.c_void_p(toks.ctypes.data))
-
-    # timed: K device-resident decode steps
-    pos0 = ctx.pos
-    barrier(pg, device)
-    with ClockSampler(local) as clk:
-        barrier(pg, device)
-        t0 = time.perf_counter()
-        out = np.zeros(args.steps, np.int32)
-        rc = lib.hakmc_decode(ctx._h, args.steps, C.c_void_p(out.ctypes.data))
-        barrier(pg, device)
-        wall = time.perf_counter() - t0
-    if rc != 0:
-        raise RuntimeError(f"hakmc_decode failed: {rc}")
-    dev_ms = float(ctx.last_device_ms)
-    max_ms = reduce_max(pg, dev_ms, device)
-    value = args.steps / (max_ms / 1e3)  # one sequence, whatever the GPU count
-
-    # e2e: the same number of steps through the per-token host call
-    ctx.set_pos(pos0)
-    am = int(out[0])
-    barrier(pg, device)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        _, am = ctx.forward(am, want_logits=False)
-    e2e_s = reduce_max(pg, time.perf_counter() - t0, device)
-    e2e = args.steps / e2e_s
-
-    # roofline: the step-kernel launch of the timed region
-    pk, pk_kind = peaks()
-    # per GPU: with tensor parallelism each GPU streams 1/world of the weights
-    alg_bytes = sum(cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(pos0 + i) for i in range(args.steps)) / world
-    achieved = alg_bytes / (max_ms / 1e3) / 1e9
-    traffic = None
-    tpath = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tpath):
-        with open(tpath) as f:
-            per_tok = json.load(f).get(f"step_kernel_{args.model}_bytes_per_token")
-        if per_tok:
-            traffic = per_tok * args.steps / world  # per GPU, like bytes_per_launch
-    tok_bytes = cfg.weight_bytes_per_token() + cfg.kv_bytes_per_token(pos0 + args.steps // 2)
-
-    line = {"metric": "decode tok/s (batch 1)", "value": value, "unit": "tok/s", "n_gpus": world,
+    d = measure_decode(args.model, args.steps, args.warmup, world, local, pg, device)
+    max_ms = d["max_ms"]
+    line = {"metric": "decode tok/s (batch 1)", "value": d["value"], "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": max_ms / args.steps,
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
             "dtype": "int8 x int4/int6 dot, fp32 accumulate", "data": "synthetic (seeded random-init weights, seeded prompt ids)",
             "config": config_block(args, world),
-            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-            "gpu_launches": 1,
-            "roofline": {"bound": "hbm", "kernel": "step_kernel (whole decode steps, one launch)",
-                         "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / pk["hbm_gbs"], "peak_source": pk_kind, "traffic": traffic,
-                         "bytes_per_launch": alg_bytes, "launch_ms": dev_ms,
-                         "roofline_tok_s": world * pk["hbm_gbs"] * 1e9 / tok_bytes},
-            "clocks": clk.summary(), "wall_s": wall}
+            "e2e": {"value": d["e2e"], "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+            "gpu_launches": 1, "roofline": d["roofline"], "stream_match": d["stream_match"],
+            "clocks": d["clocks"], "wall_s": d["wall"]}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         n_cpu = 96 if args.model == "3b" else 48
         v, cores = cpu_reference_decode(path, args.model, n_cpu, len(prompt) + n_cpu + 8)
         line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
                                 "sample": f"{n_cpu} greedy decode steps after the {len(prompt)}-id prompt "
                                           "(reference hakm_forward, oracle/_ref)"}
-    ctx.close()
+    if rank == 0 and world == 1 and args.model == "3b" and not args.no_next_rows:
+        # config 3 (7B, 32-id prompt, 128 tokens) on this one GPU: the N = 1
+        # point of the 7B series that --gpus N > 1 measures
+        d7 = measure_decode("7b", 128, args.warmup, 1, local, None, device)
+        line["config3_7b_1gpu"] = {"value": d7["value"], "unit": "tok/s", "steps": 128,
+                                   "ms_per_step": d7["max_ms"] / 128, "e2e_tok_s": d7["e2e"],
+                                   "roofline_frac": d7["roofline"]["frac"], "stream_match": d7["stream_match"]}
     if rank == 0 and world == 1 and not args.no_gemv_sweep:
-        line["gemv_sweep"] = gemv_sweep(device, pk["hbm_gbs"])
+        line["gemv_sweep"] = gemv_sweep(device, peaks()[0]["hbm_gbs"])
     if rank == 0 and world == 1 and not args.no_next_rows:
         # the survey's next rows, short samples (their own lines: --workload prefill / batch)
         line["prefill"] = prefill_summary(steps=2, warmup=2)

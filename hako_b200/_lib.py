@@ -63,6 +63,8 @@ SIGNATURES = {
     "hakmc_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "hakmc_rope_neox": (_i, [_vp, _i, _i, _i, _f, _vp]),
     "hakmc_attention_noalloc": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
+    "hakmc_attention_rows": (_i, [_vp, _vp, _vp, _vp, _i, _i, _vp, _i, _sz, _i, _i, _i, _vp]),
+    "hakmc_gemm_q6k": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp]),
     "hakmc_test_expf": (_i, [_vp, _vp, _i, _i, _vp]),
     "hakmc_sample": (_i, [_vp, _i, _f, _f, _i, _vp, _vp, _vp]),
     "hakmc_sample_last": (_i, [_vp, _f, _f, _i, _vp, _vp]),

@@ -1658,6 +1658,35 @@ extern "C" int hakmc_gemm_q4k_q8(float* out, const void* w, const int8_t* xq, co
   return 0;
 }
 
+extern "C" int hakmc_attention_rows(float* out, const float* q, const float* k_cache, const float* v_cache,
+                                    int rows, int pos0, const int* row_pos, int max_pos, size_t slot_stride,
+                                    int n_heads, int n_kv, int head_dim, void* stream) {
+  if (!out || !q || !k_cache || !v_cache || rows <= 0 || max_pos < 0 || n_heads <= 0 || n_kv <= 0 ||
+      n_heads % n_kv || (head_dim != 64 && head_dim != 128) || (!row_pos && (pos0 < 0 || pos0 + rows - 1 > max_pos))) {
+    set_err("attention_rows: bad arguments");
+    return HAKMC_EINVAL;
+  }
+  if (rx_attention_smem_bytes(head_dim, max_pos + 1) > RX_ATTN_SMEM_MAX) {
+    set_err("attention_rows: %d positions exceed the shared-memory score row", max_pos + 1);
+    return HAKMC_ERANGE;
+  }
+  CKL(launch_rx_attention(out, q, k_cache, v_cache, rows, pos0, row_pos, max_pos + 1, slot_stride, n_heads, n_kv,
+                          head_dim, host_rsqrt_nr((float)head_dim), (cudaStream_t)stream));
+  return 0;
+}
+
+extern "C" int hakmc_gemm_q6k(float* out, const void* w, const float* x, const float* bias, int n_out, int n_in,
+                              int n_batch, int accumulate, void* stream) {
+  if (!out || !w || !x || n_out <= 0 || n_in <= 0 || n_in % QK || n_batch <= 0) {
+    set_err("gemm_q6k: n_in must be a positive multiple of 256, n_batch >= 1");
+    return HAKMC_EINVAL;
+  }
+  if (!aligned16(w)) { set_err("gemm_q6k: w must be 16-byte aligned"); return HAKMC_EINVAL; }
+  CKL(launch_rx_q6k_gemm(out, (const uint8_t*)w, x, bias, n_out, n_in, n_batch, accumulate != 0,
+                         (cudaStream_t)stream));
+  return 0;
+}
+
 extern "C" int hakmc_gemv_q4k(float* out, const void* w, const float* x, const float* bias, int n_out, int n_in,
                               void* stream) {
   if (!x) return HAKMC_EINVAL;

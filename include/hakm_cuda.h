@@ -321,6 +321,31 @@ int hakmc_attention(float *out, const float *q, const float *k_cache, const floa
 int hakmc_attention_noalloc(float *out, const float *q, const float *k_cache, const float *v_cache,
                             int pos, int n_heads, int n_kv, int head_dim, void *stream);
 
+/* Attention of many rows at once (prompt chunks, batched decode), each row
+ * bit-identical to hakmc_attention at its position: row r attends over
+ * positions 0 .. row_pos[r] of its own cache, k_cache + r * slot_stride
+ * (decode rows: one sequence per row), or, when row_pos is NULL, over
+ * positions 0 .. pos0 + r of one cache (the rows of a prompt chunk, whose
+ * own K/V rows are already in it). q, out: [dev] rows x n_heads*head_dim;
+ * row_pos: [dev] int[rows] or NULL; max_pos >= every row's position (it
+ * sizes the shared-memory score row: (max_pos + 1) * 4 bytes plus
+ * (head_dim + 64) * 4 must stay within 200 KB, else HAKMC_ERANGE). The
+ * reference has no batched call; its per-row arithmetic is
+ * src/model.c:124-142. Asynchronous on `stream`. */
+int hakmc_attention_rows(float *out, const float *q, const float *k_cache, const float *v_cache,
+                         int rows, int pos0, const int *row_pos, int max_pos, size_t slot_stride,
+                         int n_heads, int n_kv, int head_dim, void *stream);
+
+/* Q6_K matmul of many fp32 activation rows: out[n*n_out + r] (+)=
+ * dot(dequant(w row r), x + n*n_in) (+ bias[r]) for n < n_batch, each
+ * output bit-identical to the reference's generic matmul (src/nn.c:84-95
+ * as built: 8 lane chains of rounded products, folded), accumulate != 0
+ * adding it to out as the residual add does (src/model.c:146,156). [dev]
+ * w in the packed layout of hakmc_q6k_pack; n_in % 256 == 0. Asynchronous
+ * on `stream`. */
+int hakmc_gemm_q6k(float *out, const void *w, const float *x, const float *bias, int n_out, int n_in,
+                   int n_batch, int accumulate, void *stream);
+
 /* NeoX RoPE in place on n_heads heads of head_dim at position pos
  * (src/nn.c:32-42), (cos, sin) from a table built on the host through the
  * same glibc vector routines the reference's build calls (bit-identical). */

@@ -6,7 +6,8 @@ exp), so the bar is bit identity with the reference's compiled functions
 (or, for attention, which the reference has no function for, with the
 oracle's restatement that the whole-forward tests pin): the int8 quantizer,
 Q4_K integer sub-block sums, dequantization, Q4_K and Q6_K matmuls with
-bias, the fused lm_head + first-index greedy pick, rmsnorm, RoPE, attention,
+bias (one vector, and many rows at once), the fused lm_head + first-index
+greedy pick, rmsnorm, RoPE, attention (one vector, and prompt / decode rows),
 and the device's exp routines against the host's libm / libmvec."""
 import ctypes as C
 
@@ -285,6 +286,79 @@ def test_attention(cuda, oracle, H, KVH, hd, pos):
     check(lib.hakmc_attention(P(out), P(dev(q, cuda)), P(dev(kc, cuda)), P(dev(vc, cuda)), pos, H, KVH, hd, None))
     sync()
     assert same(out.cpu().numpy(), oracle.attention(q, kc, vc, pos, H, KVH, hd))
+
+
+@pytest.mark.parametrize("H,KVH,hd,pos0,rows", [(16, 2, 128, 0, 40), (28, 4, 128, 300, 17), (8, 2, 64, 5, 3),
+                                                (4, 2, 64, 0, 1)])
+def test_attention_rows_prompt(cuda, oracle, H, KVH, hd, pos0, rows):
+    """hakmc_attention_rows over a prompt chunk (row r at position pos0 + r
+    of one cache): every row equals the oracle's attention at its position."""
+    import torch
+    rng = np.random.default_rng(pos0 + rows)
+    n = pos0 + rows
+    q = rng.standard_normal((rows, H * hd)).astype(np.float32)
+    kc = rng.standard_normal((n, KVH * hd)).astype(np.float32)
+    vc = rng.standard_normal((n, KVH * hd)).astype(np.float32)
+    out = empty((rows, H * hd), torch.float32, cuda)
+    check(lib.hakmc_attention_rows(P(out), P(dev(q, cuda)), P(dev(kc, cuda)), P(dev(vc, cuda)), rows, pos0, None,
+                                   n - 1, 0, H, KVH, hd, None))
+    sync()
+    got = out.cpu().numpy()
+    for r in range(rows):
+        assert same(got[r], oracle.attention(q[r], kc, vc, pos0 + r, H, KVH, hd)), r
+
+
+def test_attention_rows_decode(cuda, oracle):
+    """Decode rows: row r reads its own cache slot up to its own position
+    (ragged positions, around multiples of 8 and of the 8-wide exp split)."""
+    import torch
+    H, KVH, hd, cap = 28, 4, 128, 1100
+    pos = [0, 3, 7, 8, 12, 255, 256, 1000, 1027, 1099]
+    rows = len(pos)
+    rng = np.random.default_rng(11)
+    q = rng.standard_normal((rows, H * hd)).astype(np.float32)
+    kc = rng.standard_normal((rows, cap, KVH * hd)).astype(np.float32)
+    vc = rng.standard_normal((rows, cap, KVH * hd)).astype(np.float32)
+    out = empty((rows, H * hd), torch.float32, cuda)
+    rp = dev(np.array(pos, np.int32), cuda)
+    check(lib.hakmc_attention_rows(P(out), P(dev(q, cuda)), P(dev(kc, cuda)), P(dev(vc, cuda)), rows, 0, P(rp),
+                                   max(pos), cap * KVH * hd, H, KVH, hd, None))
+    sync()
+    got = out.cpu().numpy()
+    for r in range(rows):
+        assert same(got[r], oracle.attention(q[r], kc[r], vc[r], pos[r], H, KVH, hd)), r
+
+
+def test_attention_rows_rejects_long_rows(cuda):
+    import torch
+    buf = empty(1 << 10, torch.float32, cuda)
+    assert lib.hakmc_attention_rows(P(buf), P(buf), P(buf), P(buf), 1, 0, None, 60000, 0, 16, 2, 128, None) < 0
+    assert lib.hakmc_attention_rows(P(buf), P(buf), P(buf), P(buf), 1, 0, None, 10, 0, 16, 3, 128, None) < 0
+
+
+@pytest.mark.parametrize("rows,k,n", [(256, 2048, 9), (2048, 11008, 64), (3584, 18944, 17), (512, 3584, 1),
+                                      (151936, 2048, 4), (5, 256, 33), (100, 2304, 40)])
+def test_gemm_q6k_matches_reference(cuda, reference, rows, k, n):
+    """hakmc_gemm_q6k: every output row of every activation equals the
+    reference's Q6_K matmul (src/nn.c:84-95 as built) bit for bit; with
+    accumulate, out + that value (one IEEE add)."""
+    import torch
+    w = synth.random_q6k(rows, k, 3 * rows + k + n)
+    packed = packed_q6k(w, rows, k, cuda)
+    x = np.stack([synth.normal(k, 300 + i) for i in range(n)])
+    b = synth.normal(rows, 79) if n % 2 else None
+    base = np.random.default_rng(n).standard_normal((n, rows)).astype(np.float32)
+    out = dev(base, cuda)
+    acc = n % 3 == 0
+    check(lib.hakmc_gemm_q6k(P(out), P(packed), P(dev(x, cuda)), P(dev(b, cuda)) if b is not None else None, rows, k,
+                             n, int(acc), None))
+    sync()
+    got = out.cpu().numpy()
+    for i in range(n):
+        want = reference.matmul(w, 14, x[i], rows, k, bias=b)
+        if acc:
+            want = (base[i] + want).astype(np.float32)
+        assert same(got[i], want), i
 
 
 def test_device_exp_matches_host_libm(cuda, oracle):
