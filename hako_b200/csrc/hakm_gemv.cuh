@@ -537,30 +537,62 @@ __device__ __forceinline__ void q6_half_products(const Q6Blk& B, int n, const fl
   }
 }
 
-// The chain runs one half-block behind the products, so each half's 16
-// products are formed while the previous half's are being added.
-__device__ __forceinline__ float q6k_rows(const uint8_t* st, int rstride, int nrows, int nb, const Act& A, float* ws) {
-  (void)ws;
+// NRL = 1: the chain runs one half-block behind the products, so each
+// half's 16 products are formed while the previous half's are being added.
+// NRL = 2: a lane runs the chains of two rows (r and r + 4 of an 8-row
+// unit), their adds interleaved so one chain's add latency hides behind the
+// other's (no half-block lag: it would not fit the registers); for phases
+// with many rows per CTA (the lm_head). out[i] of lanes 8r is row
+// (r + 4i)'s dot product.
+template <int NRL>
+__device__ __forceinline__ void q6k_rows(const uint8_t* st, int rstride, int nrows, int nb, const Act& A,
+                                         float out[NRL]) {
   const int lane = threadIdx.x & 31, r = lane >> 3, l = lane & 7;
-  const uint8_t* row = st + (size_t)(r < nrows ? r : 0) * rstride;
   const float* xl = A.xc + l * A.cp;
-  float acc = 0.f;
-  Q6Blk B = q6_blk_load(row, nb, 0, l);
-  float pv[16];
-  q6_half_products(B, 0, xl, pv);
-  for (int b = 0; b < nb; b++) {
-    float pc[16];
-    q6_half_products(B, 1, xl + 32 * b + 16, pc);
+  if constexpr (NRL == 1) {
+    const uint8_t* row = st + (size_t)(r < nrows ? r : 0) * rstride;
+    float acc = 0.f;
+    Q6Blk B = q6_blk_load(row, nb, 0, l);
+    float pv[16];
+    q6_half_products(B, 0, xl, pv);
+    for (int b = 0; b < nb; b++) {
+      float pc[16];
+      q6_half_products(B, 1, xl + 32 * b + 16, pc);
 #pragma unroll
-    for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pv[i]);
-    if (b + 1 < nb) {
-      B = q6_blk_load(row, nb, b + 1, l);
-      q6_half_products(B, 0, xl + 32 * (b + 1), pv);
+      for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pv[i]);
+      if (b + 1 < nb) {
+        B = q6_blk_load(row, nb, b + 1, l);
+        q6_half_products(B, 0, xl + 32 * (b + 1), pv);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pc[i]);
     }
+    out[0] = fold8_lanes(acc);
+  } else {
+    const uint8_t* row0 = st + (size_t)(r < nrows ? r : 0) * rstride;
+    const uint8_t* row1 = st + (size_t)(r + 4 < nrows ? r + 4 : 0) * rstride;
+    float a0 = 0.f, a1 = 0.f;
+    Q6Blk B0 = q6_blk_load(row0, nb, 0, l), B1 = q6_blk_load(row1, nb, 0, l);
+    for (int b = 0; b < nb; b++) {
 #pragma unroll
-    for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pc[i]);
+      for (int n = 0; n < 2; n++) {
+        float p0[16], p1[16];
+        q6_half_products(B0, n, xl + 32 * b + 16 * n, p0);
+        q6_half_products(B1, n, xl + 32 * b + 16 * n, p1);
+        if (n == 1 && b + 1 < nb) {
+          B0 = q6_blk_load(row0, nb, b + 1, l);
+          B1 = q6_blk_load(row1, nb, b + 1, l);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          a0 = __fadd_rn(a0, p0[i]);
+          a1 = __fadd_rn(a1, p1[i]);
+        }
+      }
+    }
+    out[0] = fold8_lanes(a0);
+    out[1] = fold8_lanes(a1);
   }
-  return fold8_lanes(acc);
 }
 
 // ------------------------------------------------------------------ epilogue

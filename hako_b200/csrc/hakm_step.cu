@@ -682,9 +682,15 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
                 const float tot = G.ur == 2 ? q4k_rows<2>(st, G.rowB, nru, nb, X, tr)
                                             : q4k_rows<4>(st, G.rowB, nru, nb, X, tr);
                 if (lane < nru) dst[lane] = tot;
+              } else if (G.ur == 8) {
+                float tot[2];
+                q6k_rows<2>(st, G.rowB, nru, nb, X, tot);
+                if ((lane & 7) == 0 && (lane >> 3) < nru) dst[lane >> 3] = tot[0];
+                if ((lane & 7) == 0 && (lane >> 3) + 4 < nru) dst[(lane >> 3) + 4] = tot[1];
               } else {
-                const float tot = q6k_rows(st, G.rowB, nru, nb, X, tr);
-                if ((lane & 7) == 0 && (lane >> 3) < nru) dst[lane >> 3] = tot;
+                float tot[1];
+                q6k_rows<1>(st, G.rowB, nru, nb, X, tot);
+                if ((lane & 7) == 0 && (lane >> 3) < nru) dst[lane >> 3] = tot[0];
               }
             }
             ucount += (unsigned)n_units_full;
@@ -871,6 +877,9 @@ bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
       // the extra activation loads cost more (measured).
       const int max_groups = ((D.g.seg[s].n_rows + 3) / 4 + grid - 1) / grid;
       D.st_unit_rows[s] = (max_groups == 1 && D.g.seg[s].type == W_Q4K) ? 2 : 4;
+      // Q6_K rows by the hundred per CTA (the lm_head): two rows a lane
+      if (D.g.seg[s].type == W_Q6K && 4 * max_groups >= 8 * CONSUMER_WARPS && D.st_rows[s] >= 8)
+        D.st_unit_rows[s] = 8;
     }
   }
   return step_smem_bytes(a) <= (size_t)STEP_SMEM_MAX;

@@ -117,26 +117,29 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
     pdl_wait();
     build_activation(p, wpre, A, red);
     if (threadIdx.x == 32) TRACE(1);
-    const int groups = phase_groups(nb), wpg = CONSUMER_WARPS / groups;
-    const int cw = warp - 1, mine = cw / wpg, unit = cw % wpg;
+    const int cw = warp - 1;
     float* tr = wscr + cw * WARP_SCRATCH_FLOATS;
     bool first = true;
     int i = 0;
+    unsigned ucount = 0;  // units seen: rotates the units over the warps
     for (int s = 0; s < p.n_seg && !failed; s++) {
       const int type = (KINDS == 1) ? W_Q4K : (KINDS == 2) ? W_Q6K : p.seg[s].type;
       const int rowB = (int)dev_row_bytes(type, nb);
       const int R = stage_rows(type, nb);
-      const int n_units = (R + 3) / 4;  // 4-row units of whole rows
+      // units of whole rows: 4, or 8 (two a lane) for Q6_K rows by the
+      // hundred per CTA (the lm_head)
+      const int ur = (type == W_Q6K && R >= 8 && sr[s].row1 - sr[s].row0 >= 8 * CONSUMER_WARPS) ? 8 : 4;
+      const int n_units = (R + ur - 1) / ur;
       for (int rt = sr[s].row0; rt < sr[s].row1; rt += R, i++) {
-        if (i % groups != mine) continue;
         const int nr = min(R, sr[s].row1 - rt);
         const int slot = i % S_;
         if (!mbar_wait(smem_addr(&full[slot]), (i / S_) & 1)) { failed = true; break; }
         if (first && threadIdx.x == 32) TRACE(2);
         first = false;
         const uint8_t* stage = ring + (size_t)slot * SB;
-        for (int u = unit; u < n_units; u += wpg) {
-          const int t0 = 4 * u, nru = min(4, nr - t0);
+        const int u0 = (int)((unsigned)(cw + CONSUMER_WARPS) - ucount % CONSUMER_WARPS) % CONSUMER_WARPS;
+        for (int u = u0; u < n_units; u += CONSUMER_WARPS) {
+          const int t0 = ur * u, nru = min(ur, nr - t0);
           if (nru <= 0) continue;
           const uint8_t* st = stage + (size_t)t0 * rowB;
           float* dst = part + sr[s].part_base + (rt - sr[s].row0 + t0);
@@ -147,11 +150,20 @@ __global__ void __launch_bounds__(THREADS, 1) stream_kernel(const __grid_constan
             }
           } else {
             if constexpr (KINDS & 2) {
-              const float tot = q6k_rows(st, rowB, nru, nb, A, tr);
-              if ((lane & 7) == 0 && (lane >> 3) < nru) dst[lane >> 3] = tot;
+              if (ur == 8) {
+                float tot[2];
+                q6k_rows<2>(st, rowB, nru, nb, A, tot);
+                if ((lane & 7) == 0 && (lane >> 3) < nru) dst[lane >> 3] = tot[0];
+                if ((lane & 7) == 0 && (lane >> 3) + 4 < nru) dst[(lane >> 3) + 4] = tot[1];
+              } else {
+                float tot[1];
+                q6k_rows<1>(st, rowB, nru, nb, A, tot);
+                if ((lane & 7) == 0 && (lane >> 3) < nru) dst[lane >> 3] = tot[0];
+              }
             }
           }
         }
+        ucount += (unsigned)n_units;
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_addr(&empty[slot]));
       }
