@@ -1,36 +1,68 @@
 /* hakm_model_cuda.c — drop-in replacement for the reference engine's
  * src/model.c on a B200: the same four entry points of src/model.h
- * (hakm_ctx_new, hakm_ctx_free, hakm_forward, hakm_reset) over libhakm_cuda.
+ * (hakm_ctx_new, hakm_ctx_free, hakm_forward, hakm_reset) over libhakm_cuda,
+ * plus sample_token (src/sample.h) so that the pick is made on the device.
  *
- * Link this file instead of src/model.c. The callers keep working unchanged:
- * cli/main.c, src/hakm_api.c and src/sample.c only read c->model (tokenizer,
- * tensor directory), c->logits, c->vocab, c->pos, c->max_seq and the shape
- * fields, all of which are maintained here. C11, no CUDA headers: the device
- * side is reached only through include/hakm_cuda.h.
+ * Link this file instead of src/model.c, and compile the reference's
+ * src/sample.c with -Dsample_token=hakm_ref_sample_token (its own sampler
+ * stays available under that name for logits that are not a context's).
+ * The callers keep working unchanged: cli/main.c, src/hakm_api.c read
+ * c->model (tokenizer, tensor directory), c->pos, c->max_seq, c->vocab and
+ * the shape fields, all maintained here, and they read the logits only
+ * through sample_token(sp, c->logits, c->vocab).
+ *
+ * Deferred feed. hakm_forward records the id and returns at once; the ids
+ * run on the GPU when their logits are first needed, that is when
+ * sample_token is called on c->logits. A prompt fed id by id therefore runs
+ * as one batched pass (hakmc_prefill_batched: every position through each
+ * layer together, each weight read once per chunk) or, for a few ids, one
+ * step-kernel launch (hakmc_prefill); a generated id runs as one decode
+ * step. The pick is then made on the device (hakmc_sample_last: greedy or
+ * temperature / top-k / top-p, bit-identical to the reference's
+ * sample_token), so the logits never cross to the host. Results are the
+ * reference's, bit for bit, whichever way the ids are grouped.
  *
  * Differences a caller can see:
  *   - k_cache / v_cache and the scratch pointers are NULL: the KV cache and
  *     the activations live in device memory.
- *   - hakm_forward copies the logits of the step into c->logits (the
- *     reference returns its own scratch buffer; the pointer is equally valid
- *     until the next call).
+ *   - c->logits holds the step's logits only with HAKMC_EAGER=1 (every
+ *     hakm_forward then runs at once and copies its logits, as the
+ *     reference's returns its scratch buffer). Without it, code that reads
+ *     c->logits other than through sample_token sees stale values.
+ *   - sample_token on c->logits does not turn the array into probabilities
+ *     (the reference's does, in place); no caller reads them afterwards.
  *   - HAKMC_DEVICE (environment) picks the GPU, default 0.
  *   - HAKMC_TOKEN_LOG (environment), if set, names a file that receives
  *     every id hakm_forward is given, one per line (stream comparisons).
  */
+#include <pthread.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
 #include "hakm_cuda.h"
 #include "model.h"
+#include "sample.h"
+
+/* the reference's own sampler (src/sample.c compiled with
+ * -Dsample_token=hakm_ref_sample_token) */
+int hakm_ref_sample_token(sampler *s, float *logits, int n);
+
+enum { BATCHED_MIN = 16 };  /* pending ids from which the batched prompt pass runs */
 
 /* hakm_ctx first, so the pointer callers hold is also the wrapper's */
-typedef struct {
-	hakm_ctx   c;
-	hakmc_ctx *dev;
-	FILE      *token_log;
+typedef struct cuda_ctx {
+	hakm_ctx         c;
+	hakmc_ctx       *dev;
+	FILE            *token_log;
+	int              eager;
+	int             *pending;     /* ids recorded, not yet run */
+	int              n_pending, cap_pending;
+	struct cuda_ctx *next;        /* live contexts (sample_token finds c->logits) */
 } cuda_ctx;
+
+static cuda_ctx *live;
+static pthread_mutex_t live_mu = PTHREAD_MUTEX_INITIALIZER;
 
 static cuda_ctx *wrapper(hakm_ctx *c) { return (cuda_ctx *)c; }
 
@@ -60,19 +92,28 @@ hakm_ctx *hakm_ctx_new(const char *mlf2_path, int max_seq)
 	                                                  : mlf2_find(&c->model, "output.weight");
 
 	c->logits = malloc((size_t)c->vocab * sizeof(float));
+	w->cap_pending = max_seq > 0 ? max_seq : 1;
+	w->pending = malloc((size_t)w->cap_pending * sizeof(int));
 	const char *dev_env = getenv("HAKMC_DEVICE");
 	const int dev = dev_env ? atoi(dev_env) : 0;
-	if (c->logits)
+	if (c->logits && w->pending)
 		w->dev = hakmc_create(c->model.map, c->model.map_size, max_seq, 1, dev);
 	if (!w->dev) {
-		fprintf(stderr, "hakm: %s\n", c->logits ? hakmc_last_error() : "out of memory");
+		fprintf(stderr, "hakm: %s\n", c->logits && w->pending ? hakmc_last_error() : "out of memory");
+		free(w->pending);
 		free(c->logits);
 		mlf2_close(&c->model);
 		free(w);
 		return NULL;
 	}
+	const char *eager = getenv("HAKMC_EAGER");
+	w->eager = eager && eager[0] && strcmp(eager, "0") != 0;
 	const char *log_path = getenv("HAKMC_TOKEN_LOG");
 	if (log_path && log_path[0]) w->token_log = fopen(log_path, "w");
+	pthread_mutex_lock(&live_mu);
+	w->next = live;
+	live = w;
+	pthread_mutex_unlock(&live_mu);
 	return c;
 }
 
@@ -80,20 +121,54 @@ void hakm_ctx_free(hakm_ctx *c)
 {
 	if (!c) return;
 	cuda_ctx *w = wrapper(c);
+	pthread_mutex_lock(&live_mu);
+	for (cuda_ctx **p = &live; *p; p = &(*p)->next)
+		if (*p == w) { *p = w->next; break; }
+	pthread_mutex_unlock(&live_mu);
 	if (w->token_log) fclose(w->token_log);
 	hakmc_destroy(w->dev);
+	free(w->pending);
 	free(c->logits);
 	mlf2_close(&c->model);
 	free(w);
+}
+
+/* Run the recorded ids; their last position's logits stay on the device.
+ * 0, or -1 after reporting on stderr. */
+static int flush(cuda_ctx *w)
+{
+	const int n = w->n_pending;
+	if (n == 0) return 0;
+	w->n_pending = 0;
+	int rc;
+	if (n >= BATCHED_MIN)
+		rc = hakmc_prefill_batched(w->dev, w->pending, n, 0, NULL, NULL);
+	else if (n > 1)
+		rc = hakmc_prefill(w->dev, w->pending, n, NULL, NULL);
+	else
+		rc = hakmc_forward(w->dev, w->pending[0], NULL, NULL);
+	if (rc != 0) {
+		fprintf(stderr, "hakm: forward of %d id(s): %s\n", n, hakmc_last_error());
+		return -1;
+	}
+	return 0;
 }
 
 const float *hakm_forward(hakm_ctx *c, int token)
 {
 	cuda_ctx *w = wrapper(c);
 	if (w->token_log) fprintf(w->token_log, "%d\n", token);
-	if (hakmc_forward(w->dev, token, c->logits, NULL) != 0) {
-		fprintf(stderr, "hakm: forward at position %d: %s\n", c->pos, hakmc_last_error());
+	if (c->pos >= c->max_seq || token < 0 || token >= c->vocab) {
+		fprintf(stderr, "hakm: forward of id %d at position %d: out of range\n", token, c->pos);
 		return c->logits;
+	}
+	if (w->eager) {
+		if (hakmc_forward(w->dev, token, c->logits, NULL) != 0) {
+			fprintf(stderr, "hakm: forward at position %d: %s\n", c->pos, hakmc_last_error());
+			return c->logits;
+		}
+	} else {
+		w->pending[w->n_pending++] = token;
 	}
 	c->pos++;
 	return c->logits;
@@ -101,6 +176,27 @@ const float *hakm_forward(hakm_ctx *c, int token)
 
 void hakm_reset(hakm_ctx *c)
 {
-	hakmc_reset(wrapper(c)->dev);
+	cuda_ctx *w = wrapper(c);
+	w->n_pending = 0;
+	hakmc_reset(w->dev);
 	c->pos = 0;
+}
+
+int sample_token(sampler *s, float *logits, int n)
+{
+	cuda_ctx *w = NULL;
+	pthread_mutex_lock(&live_mu);
+	for (cuda_ctx *p = live; p; p = p->next)
+		if (p->c.logits == logits && p->c.vocab == n) { w = p; break; }
+	pthread_mutex_unlock(&live_mu);
+	if (!w) return hakm_ref_sample_token(s, logits, n);
+	if (flush(w) != 0) return 0;
+	unsigned long long rng = s->rng;
+	int tok = 0;
+	if (hakmc_sample_last(w->dev, s->temp, s->top_p, s->top_k, &rng, &tok) != 0) {
+		fprintf(stderr, "hakm: sample: %s\n", hakmc_last_error());
+		return hakm_ref_sample_token(s, logits, n);
+	}
+	s->rng = rng;
+	return tok;
 }

@@ -1,11 +1,15 @@
 """The drop-in boundary exercised by the reference's own caller: the
 reference CLI (cli/main.c) linked against hako_b200/host/hakm_model_cuda.c in
-place of src/model.c, run as a greedy raw completion (`-t 0 --raw`:
-src/sample.c's argmax over the logits hakm_forward returns).
+place of src/model.c (and src/sample.c's sample_token renamed, so the pick is
+made on the device), run as a raw completion.
 
-The drop-in's forward pass is bit-identical to the reference's, so the ids it
-is fed (prompt, then its own picks, logged) equal the reference's greedy
-continuation of the same prompt ids, and the two CLIs print the same bytes."""
+The drop-in defers the fed ids until sample_token needs their logits (the
+prompt then runs as one batched pass), and its forward pass and sampler are
+bit-identical to the reference's: the ids it is fed (prompt, then its own
+picks, logged) equal the reference's greedy continuation of the same prompt
+ids, and the two CLIs print the same bytes, greedy (`-t 0`), with
+temperature / top-k / top-p sampling from a fixed seed, and with the
+deferred feed switched off (HAKMC_EAGER=1)."""
 import os
 import subprocess
 
@@ -16,10 +20,10 @@ from oracle.oracle import DROPIN_CLI, REF_CLI
 pytestmark = pytest.mark.gpu
 
 
-def _run(cli, path, n, prompt, env_extra=None):
+def _run(cli, path, n, prompt, env_extra=None, sampling=("-t", "0")):
     env = dict(os.environ, HAKM_THREADS=str(min(os.cpu_count() or 1, 16)))
     env.update(env_extra or {})
-    r = subprocess.run([cli, path, "-t", "0", "--raw", "--ctx", "256", "-n", str(n), prompt],
+    r = subprocess.run([cli, path, *sampling, "--raw", "--ctx", "256", "-n", str(n), prompt],
                        capture_output=True, env=env, timeout=600)
     assert r.returncode == 0, r.stderr.decode(errors="replace")[-400:]
     return r.stdout
@@ -46,6 +50,33 @@ def test_reference_cli_over_dropin(cuda, tmp_path, preset, n):
     ref_stream, _ = ref_greedy(path, prompt_ids, n)
     assert fed == ref_stream[:len(fed)]
     assert ours == _run(REF_CLI, path, n, prompt)
+
+
+@pytest.mark.parametrize("sampling", [("-t", "0.8", "-k", "40", "-p", "0.9", "-s", "1234"),
+                                      ("-t", "1.1", "-k", "0", "-p", "0.95", "-s", "77"),
+                                      ("-t", "0.6", "-k", "5", "-p", "0", "-s", "9")])
+def test_reference_cli_sampling_over_dropin(cuda, sampling):
+    """Temperature / top-k / top-p sampling from a fixed seed: the drop-in's
+    device sampler draws the reference's ids, so both CLIs print the same
+    bytes (and the generator state advances alike, step after step)."""
+    from hako_b200 import synth
+    if not (os.path.exists(REF_CLI) and os.path.exists(DROPIN_CLI)):
+        pytest.skip("oracle/_ref CLIs not built (make -C oracle ref dropin)")
+    path = synth.cached_model(synth.PRESETS["small"])
+    prompt = "once upon a time there was a"
+    ours = _run(DROPIN_CLI, path, 48, prompt, sampling=sampling)
+    assert ours == _run(REF_CLI, path, 48, prompt, sampling=sampling)
+
+
+def test_reference_cli_over_dropin_eager(cuda):
+    """HAKMC_EAGER=1: every hakm_forward runs at once and copies its logits
+    (the reference's contract for c->logits); same bytes."""
+    from hako_b200 import synth
+    if not (os.path.exists(REF_CLI) and os.path.exists(DROPIN_CLI)):
+        pytest.skip("oracle/_ref CLIs not built (make -C oracle ref dropin)")
+    path = synth.cached_model(synth.PRESETS["small"])
+    prompt = "the quick brown fox jumps over"
+    assert _run(DROPIN_CLI, path, 32, prompt, {"HAKMC_EAGER": "1"}) == _run(REF_CLI, path, 32, prompt)
 
 
 def ref_greedy(path, prompt_ids, n):
