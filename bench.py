@@ -474,6 +474,140 @@ def config_block(args, world):
             "l2": f"weights stream from HBM every step ({cfg.weight_bytes_per_token() / 1e9:.2f} GB > 126 MB L2)"}
 
 
+INT8_TOPS_NOMINAL = 4500.0  # dense int8 tensor peak of a B200 (NVIDIA's figure; no measured one on this pool)
+FP32_TFLOPS_NOMINAL = 148 * 128 * 2 * 1.965  # fp32 FMA issue peak of 148 SMs at the max clock
+
+
+def _event_us(torch, fn, reps=5):
+    """Mean device time of `reps` launches of fn (after two warm-up calls)."""
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps * 1e3
+
+
+def row_kernel_times(cfg, M: int, attn_rows: int, attn_pos0: int, attn_row_pos: int):
+    """CUDA-event times of the row-batched pass's kernels on its own shapes
+    (seeded data; weights > L2 for the large matrices): the tensor-core Q4_K
+    matmuls and the Q6_K row matmuls at M activation rows, and the attention
+    of attn_rows rows (prompt rows at attn_pos0.., or decode rows at
+    attn_row_pos each with its own cache). Per launch, with the work each
+    launch does, so each kernel's roofline fraction follows."""
+    import ctypes as C
+    import torch
+    from hako_b200 import check, lib, synth
+    P = lambda t: C.c_void_p(t.data_ptr())
+    dev = torch.device("cuda:0")
+    D, F, KV, H, KVH = cfg.d_model, cfg.ffn_dim, cfg.kv_dim, cfg.n_heads, cfg.n_kv_heads
+    hd = D // H
+    g = torch.Generator(device="cpu").manual_seed(M)
+    xq = torch.randint(-127, 128, (M, max(D, F)), dtype=torch.int8, generator=g).to(dev)
+    xs = (torch.rand((M, max(D, F) // 32), generator=g) * 0.01).to(dev)
+    x = torch.randn((M, max(D, F)), generator=g).to(dev)
+    res = {}
+    for name, rows, k in (("wqk", D + KV, D), ("wo", D, D), ("wgu", 2 * F, D)):
+        w = torch.from_numpy(synth.random_q4k(rows, k, rows + k)).to(dev)
+        out = torch.empty((M, rows), device=dev)
+        us = _event_us(torch, lambda: check(lib.hakmc_gemm_q4k_q8(P(out), P(w), P(xq), P(xs), None, rows, k, M,
+                                                                   None, 0, None)))
+        res[f"q4k_{name}"] = {"us": us, "ops": 2 * rows * k * M}
+        del w
+    for name, rows, k in (("wv", KV, D), ("down", D, F)):
+        src = torch.from_numpy(synth.random_q6k(rows, k, rows + k)).to(dev)
+        w = torch.empty(lib.hakmc_q6k_packed_bytes(rows, k), dtype=torch.uint8, device=dev)
+        check(lib.hakmc_q6k_pack(P(w), P(src), rows, k, None))
+        del src
+        out = torch.empty((M, rows), device=dev)
+        us = _event_us(torch, lambda: check(lib.hakmc_gemm_q6k(P(out), P(w), P(x), None, rows, k, M, 0, None)))
+        res[f"q6k_{name}"] = {"us": us, "ops": 2 * rows * k * M}
+        del w
+    if attn_row_pos is None:
+        n = attn_pos0 + attn_rows
+        kc = torch.randn((n, KV), generator=g).to(dev)
+        vc = torch.randn((n, KV), generator=g).to(dev)
+        q = torch.randn((attn_rows, D), generator=g).to(dev)
+        out = torch.empty((attn_rows, D), device=dev)
+        us = _event_us(torch, lambda: check(lib.hakmc_attention_rows(P(out), P(q), P(kc), P(vc), attn_rows, attn_pos0,
+                                                                      None, n - 1, 0, H, KVH, hd, None)))
+        kv_bytes = 2 * n * KV * 4
+    else:
+        cap = attn_row_pos + 1
+        kc = torch.randn((attn_rows, cap, KV), generator=g).to(dev)
+        vc = torch.randn((attn_rows, cap, KV), generator=g).to(dev)
+        q = torch.randn((attn_rows, D), generator=g).to(dev)
+        out = torch.empty((attn_rows, D), device=dev)
+        rp = torch.full((attn_rows,), attn_row_pos, dtype=torch.int32, device=dev)
+        us = _event_us(torch, lambda: check(lib.hakmc_attention_rows(P(out), P(q), P(kc), P(vc), attn_rows, 0, P(rp),
+                                                                      attn_row_pos, cap * KV, H, KVH, hd, None)))
+        kv_bytes = attn_rows * 2 * cap * KV * 4
+    res["attention"] = {"us": us, "kv_bytes": kv_bytes}
+    return res
+
+
+def cpu_reference_rows(model: str, n_prompt: int, n_decode: int, cache_pos: int):
+    """The reference's own hakm_forward (oracle/_ref) on the host cores: a
+    bounded sample of the row-batched workloads, which the reference runs
+    one position (or one sequence) at a time. n_prompt prompt positions
+    (prefill rate) or, after writing cache_pos seeded cache positions,
+    n_decode decode steps of one sequence (decode rate at that context)."""
+    cores = min(os.cpu_count() or 1, 16)
+    os.environ["HAKM_THREADS"] = str(cores)
+    from hako_b200 import synth
+    from oracle.oracle import RefModel
+    cfg = synth.PRESETS[model]
+    path = synth.cached_model(cfg)
+    if n_prompt:
+        m = RefModel(path, n_prompt + 8)
+        ids = np.random.default_rng(41).integers(0, 151643, n_prompt).tolist()
+        t0 = time.perf_counter()
+        for i, t in enumerate(ids):
+            m.forward(t, want_logits=i == n_prompt - 1)
+        dt = time.perf_counter() - t0
+        m.close()
+        return n_prompt / dt, cores
+    m = RefModel(path, cache_pos + n_decode + 8)
+    rng = np.random.default_rng(7)
+    m.write_kv(rng.standard_normal((cfg.n_layers, cache_pos, cfg.kv_dim), dtype=np.float32),
+               rng.standard_normal((cfg.n_layers, cache_pos, cfg.kv_dim), dtype=np.float32))
+    am = 11
+    t0 = time.perf_counter()
+    for _ in range(n_decode):
+        _, am = m.forward(am, want_logits=False)
+    dt = time.perf_counter() - t0
+    m.close()
+    return n_decode / dt, cores
+
+
+def rows_rooflines(times, pk):
+    """Roofline objects for the row kernels: the tensor-core Q4_K matmul
+    (int8 tensor pipe), the Q6_K row matmul (fp32 issue) and the attention
+    (HBM: K/V bytes)."""
+    q4 = max((v for k, v in times.items() if k.startswith("q4k_")), key=lambda v: v["us"])
+    q6 = max((v for k, v in times.items() if k.startswith("q6k_")), key=lambda v: v["us"])
+    at = times["attention"]
+    a4 = q4["ops"] / q4["us"] / 1e6
+    a6 = q6["ops"] / q6["us"] / 1e6
+    aa = at["kv_bytes"] / at["us"] / 1e3
+    return {
+        "tensor": {"bound": "tensor", "kernel": "q4k_mma_kernel (largest Q4_K matmul)", "achieved": a4,
+                   "peak": INT8_TOPS_NOMINAL, "unit": "TOP/s", "frac": a4 / INT8_TOPS_NOMINAL,
+                   "peak_source": "nominal dense int8 (no measured int8 peak on this pool)", "traffic": None,
+                   "launch_us": q4["us"]},
+        "fp32": {"bound": "fp32", "kernel": "rx_q6k_gemm_kernel (largest Q6_K matmul)", "achieved": a6,
+                 "peak": FP32_TFLOPS_NOMINAL, "unit": "TFLOP/s", "frac": a6 / FP32_TFLOPS_NOMINAL,
+                 "peak_source": "nominal fp32 FMA issue rate (the exact chains use a rounded product and a "
+                                "separate add: at most half of it)", "traffic": None, "launch_us": q6["us"]},
+        "hbm": {"bound": "hbm", "kernel": "rx_attention kernels (K/V bytes)", "achieved": aa, "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "frac": aa / pk["hbm_gbs"], "peak_source": "measured", "traffic": None,
+                "launch_us": at["us"]}}
+
+
 def run_prefill(args, emit: bool = True):
     """Config 4a: a seeded 2048-id prompt through hakmc_prefill_batched (each
     call restarts the sequence, so every step is the whole prompt)."""
@@ -509,6 +643,18 @@ def run_prefill(args, emit: bool = True):
             "e2e": {"value": args.steps * n / wall, "unit": "tok/s", "h2d_bytes_per_step": 4 * n,
                     "d2h_bytes_per_step": 4 * cfg.vocab},
             "per_position_prefill_tok_s": per_pos, "clocks": clk.summary()}
+    if emit:
+        # the dominant kernels timed alone on this workload's shapes
+        # (1024-row chunks; attention of the second chunk's rows)
+        times = row_kernel_times(cfg, 1024, 1024, 1024, None)
+        roofs = rows_rooflines(times, peaks()[0])
+        line["roofline"] = roofs["fp32"]
+        line["roofline_tensor"] = roofs["tensor"]
+        line["roofline_attention"] = roofs["hbm"]
+        line["kernel_us"] = {k: v["us"] for k, v in times.items()}
+        v, cores = cpu_reference_rows(args.model, 16, 0, 0)
+        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
+                                "sample": "the reference's hakm_forward feed of the first 16 prompt ids (oracle/_ref)"}
     if not emit:
         return line
     print(json.dumps(line), flush=True)
@@ -564,6 +710,18 @@ def run_batch(args, emit: bool = True):
             "e2e": {"value": world * n_seq * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8 * n_seq,
                     "d2h_bytes_per_step": 4 * n_seq},
             "clocks": clk.summary()}
+    if emit and rank == 0:
+        times = row_kernel_times(cfg, n_seq, n_seq, 0, ctx_len)
+        roofs = rows_rooflines(times, peaks()[0])
+        line["roofline"] = roofs["hbm"]
+        line["roofline_fp32"] = roofs["fp32"]
+        line["roofline_tensor"] = roofs["tensor"]
+        line["kernel_us"] = {k: v["us"] for k, v in times.items()}
+        if world == 1:
+            v, cores = cpu_reference_rows(args.model, 0, 4, ctx_len)
+            line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
+                                    "sample": f"4 decode steps of one sequence after {ctx_len} seeded cache positions "
+                                              "(the reference decodes its sequences one at a time; oracle/_ref)"}
     if not emit:
         return line
     if rank == 0:

@@ -1330,11 +1330,9 @@ static int batch_decode(hakmc_ctx* c, const int* tokens, const int* pos, int n, 
   int max_pos = 0;
   for (int i = 0; i < n; i++) max_pos = std::max(max_pos, pos[i]);
   const size_t slot = (size_t)c->L * c->max_seq * c->KV;
-  // score capacity of the attention launch: a power of two from 1024, so a
-  // captured graph serves every step until the positions pass it
-  int n_cap = 1024;
-  while (n_cap < max_pos + 1) n_cap *= 2;
-  n_cap = std::min(n_cap, c->max_seq);
+  // score capacity of the attention launch: a multiple of 1024, so a
+  // captured graph serves the next steps until the positions pass it
+  const int n_cap = std::min((max_pos + 1 + 1023) / 1024 * 1024, c->max_seq);
   // the kernels of the step, captured once per (rows, layers, score
   // capacity) into a graph: ~15 launches per layer
   const uint64_t key = ((uint64_t)n << 48) | ((uint64_t)c->run_layers << 32) | (uint64_t)n_cap;

@@ -308,12 +308,14 @@ def test_attention_rows_prompt(cuda, oracle, H, KVH, hd, pos0, rows):
         assert same(got[r], oracle.attention(q[r], kc, vc, pos0 + r, H, KVH, hd)), r
 
 
-def test_attention_rows_decode(cuda, oracle):
+@pytest.mark.parametrize("H,KVH,hd,cap", [(28, 4, 128, 1100), (16, 2, 128, 9000), (8, 2, 64, 300)])
+def test_attention_rows_decode(cuda, oracle, H, KVH, hd, cap):
     """Decode rows: row r reads its own cache slot up to its own position
-    (ragged positions, around multiples of 8 and of the 8-wide exp split)."""
+    (ragged positions, around multiples of 8 and of the 8-wide exp split).
+    Up to ~6,000 positions a CTA serves all query heads of a kv head; the
+    9,000-position case takes the one-head-per-CTA kernel."""
     import torch
-    H, KVH, hd, cap = 28, 4, 128, 1100
-    pos = [0, 3, 7, 8, 12, 255, 256, 1000, 1027, 1099]
+    pos = sorted({min(p, cap - 1) for p in (0, 3, 7, 8, 12, 255, 256, 1000, 1027, cap - 1)})
     rows = len(pos)
     rng = np.random.default_rng(11)
     q = rng.standard_normal((rows, H * hd)).astype(np.float32)
