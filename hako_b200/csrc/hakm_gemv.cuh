@@ -550,20 +550,29 @@ __device__ __forceinline__ void q6k_rows(const uint8_t* st, int rstride, int nro
   const int lane = threadIdx.x & 31, r = lane >> 3, l = lane & 7;
   const float* xl = A.xc + l * A.cp;
   if constexpr (NRL == 1) {
+    // the loop body has no branch, so the scheduler can interleave each
+    // half's adds with the next half's products (the last block is peeled)
     const uint8_t* row = st + (size_t)(r < nrows ? r : 0) * rstride;
     float acc = 0.f;
     Q6Blk B = q6_blk_load(row, nb, 0, l);
     float pv[16];
     q6_half_products(B, 0, xl, pv);
-    for (int b = 0; b < nb; b++) {
+    int b = 0;
+    for (; b + 1 < nb; b++) {
+      float pc[16];
+      q6_half_products(B, 1, xl + 32 * b + 16, pc);
+      B = q6_blk_load(row, nb, b + 1, l);
+#pragma unroll
+      for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pv[i]);
+      q6_half_products(B, 0, xl + 32 * (b + 1), pv);
+#pragma unroll
+      for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pc[i]);
+    }
+    {
       float pc[16];
       q6_half_products(B, 1, xl + 32 * b + 16, pc);
 #pragma unroll
       for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pv[i]);
-      if (b + 1 < nb) {
-        B = q6_blk_load(row, nb, b + 1, l);
-        q6_half_products(B, 0, xl + 32 * (b + 1), pv);
-      }
 #pragma unroll
       for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pc[i]);
     }
