@@ -475,7 +475,7 @@ def config_block(args, world):
 
 
 INT8_TOPS_NOMINAL = 4500.0  # dense int8 tensor peak of a B200 (NVIDIA's figure; no measured one on this pool)
-FP32_TFLOPS_NOMINAL = 148 * 128 * 2 * 1.965  # fp32 FMA issue peak of 148 SMs at the max clock
+FP32_TFLOPS_NOMINAL = 148 * 128 * 2 * 1.965e9 / 1e12  # fp32 FMA issue peak of 148 SMs at the max clock, TFLOP/s
 
 
 def _event_us(torch, fn, reps=5):
@@ -528,6 +528,8 @@ def row_kernel_times(cfg, M: int, attn_rows: int, attn_pos0: int, attn_row_pos: 
         res[f"q6k_{name}"] = {"us": us, "ops": 2 * rows * k * M}
         del w
     if attn_row_pos is None:
+        # prompt rows: row r reads positions 0 .. attn_pos0 + r (from L2
+        # after the first rows: the bound is the score arithmetic)
         n = attn_pos0 + attn_rows
         kc = torch.randn((n, KV), generator=g).to(dev)
         vc = torch.randn((n, KV), generator=g).to(dev)
@@ -535,7 +537,7 @@ def row_kernel_times(cfg, M: int, attn_rows: int, attn_pos0: int, attn_row_pos: 
         out = torch.empty((attn_rows, D), device=dev)
         us = _event_us(torch, lambda: check(lib.hakmc_attention_rows(P(out), P(q), P(kc), P(vc), attn_rows, attn_pos0,
                                                                       None, n - 1, 0, H, KVH, hd, None)))
-        kv_bytes = 2 * n * KV * 4
+        kv_bytes = sum(2 * (attn_pos0 + r + 1) * KV * 4 for r in range(attn_rows))
     else:
         cap = attn_row_pos + 1
         kc = torch.randn((attn_rows, cap, KV), generator=g).to(dev)
@@ -603,7 +605,8 @@ def rows_rooflines(times, pk):
                  "peak": FP32_TFLOPS_NOMINAL, "unit": "TFLOP/s", "frac": a6 / FP32_TFLOPS_NOMINAL,
                  "peak_source": "nominal fp32 FMA issue rate (the exact chains use a rounded product and a "
                                 "separate add: at most half of it)", "traffic": None, "launch_us": q6["us"]},
-        "hbm": {"bound": "hbm", "kernel": "rx_attention kernels (K/V bytes)", "achieved": aa, "peak": pk["hbm_gbs"],
+        "hbm": {"bound": "hbm", "kernel": "rx_attention_gqa_kernel (K/V bytes every row reads)", "achieved": aa,
+                "peak": pk["hbm_gbs"],
                 "unit": "GB/s", "frac": aa / pk["hbm_gbs"], "peak_source": "measured", "traffic": None,
                 "launch_us": at["us"]}}
 
@@ -652,9 +655,11 @@ def run_prefill(args, emit: bool = True):
         line["roofline_tensor"] = roofs["tensor"]
         line["roofline_attention"] = roofs["hbm"]
         line["kernel_us"] = {k: v["us"] for k, v in times.items()}
-        v, cores = cpu_reference_rows(args.model, 16, 0, 0)
-        line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
-                                "sample": "the reference's hakm_forward feed of the first 16 prompt ids (oracle/_ref)"}
+        if not getattr(args, "no_cpu_baseline", False):
+            v, cores = cpu_reference_rows(args.model, 16, 0, 0)
+            line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
+                                    "sample": "the reference's hakm_forward feed of the first 16 prompt ids "
+                                              "(oracle/_ref)"}
     if not emit:
         return line
     print(json.dumps(line), flush=True)
@@ -717,7 +722,7 @@ def run_batch(args, emit: bool = True):
         line["roofline_fp32"] = roofs["fp32"]
         line["roofline_tensor"] = roofs["tensor"]
         line["kernel_us"] = {k: v["us"] for k, v in times.items()}
-        if world == 1:
+        if world == 1 and not getattr(args, "no_cpu_baseline", False):
             v, cores = cpu_reference_rows(args.model, 0, 4, ctx_len)
             line["cpu_baseline"] = {"value": v, "unit": "tok/s", "cores": cores, "kind": "reference",
                                     "sample": f"4 decode steps of one sequence after {ctx_len} seeded cache positions "

@@ -1588,10 +1588,13 @@ static int device_sms() {
 // Which batches go to the tensor cores (hakm_mma.cu): their MMAs take the
 // integer work that bounds the dp4a kernel as the batch grows. Measured on
 // the config-1 shapes: above 16 activations always; from 9 (where the dp4a
-// kernel runs its 16-wide instance) once the matrix has 16M weights or more;
-// small matrices stay on dp4a, whose launch is lighter.
+// kernel runs its 16-wide instance) once the matrix has 16M weights or more
+// in at least 64 row tiles of 128 (the tensor-core kernel never splits a
+// row along K, so a long-K matrix of few rows runs on few SMs); the rest
+// stay on dp4a, whose launch is lighter.
 static bool use_tensor_cores(int n_out, int n_in, int n_batch) {
-  return n_batch > 16 || (n_batch > 8 && (long long)n_out * n_in >= (16ll << 20));
+  if (n_batch > 16) return true;
+  return n_batch > 8 && (long long)n_out * n_in >= (16ll << 20) && (n_out + 127) / 128 >= 64;
 }
 
 extern "C" size_t hakmc_gemv_q4k_q8_batch_scratch(int n_out, int n_in, int n_batch) {

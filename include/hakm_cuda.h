@@ -218,9 +218,9 @@ int hakmc_gemv_q4k_q8(float *out, const void *w, const int8_t *xq, const float *
  * hakm_forward). Small batches: dp4a, each weight byte read once per 16
  * activations, per-chunk partials summed in a fixed order (fp32-close to
  * the reference, rel-L2 <= 1e-5, deterministic); batches above 16 (above 8
- * for matrices of 16M weights or more) run on the tensor cores as
- * hakmc_gemm_q4k_q8 does, bit for bit (when xs is 16-byte aligned; else
- * dp4a in launches of 16). [dev]
+ * for matrices of 16M weights or more in at least 64 row tiles of 128) run
+ * on the tensor cores as hakmc_gemm_q4k_q8 does, bit for bit (when xs is
+ * 16-byte aligned; else dp4a in launches of 16). [dev]
  * buffers; w and xq 16-byte aligned; n_in % 256 == 0.
  * scratch: [dev] hakmc_gemv_q4k_q8_batch_scratch(n_out, n_in, n_batch)
  * bytes, 16-byte aligned, zeroed before its first use (a call leaves it

@@ -67,8 +67,8 @@ def test_gemv_q4k_batch_matches_reference(cuda, reference, rows, k, n):
     bias = synth.normal(rows, 79) if n % 2 else None
     out = run_batch(cuda, w, xq, xs, bias, rows, k, n, scratch=(rows % 2 == 0))
     # the routing of hakmc_gemv_q4k_q8_batch: above 16 activations (above 8
-    # for 16M weights or more) the tensor cores
-    exact = n > 16 or (n > 8 and rows * k >= 16 << 20)
+    # for 16M weights or more in 64 or more row tiles) the tensor cores
+    exact = n > 16 or (n > 8 and rows * k >= 16 << 20 and (rows + 127) // 128 >= 64)
     for i in range(n):
         ref = reference.matmul(w, 12, xs_f[i], rows, k, bias=bias)
         if exact:
