@@ -78,6 +78,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 // Weight rows are read once per token: the copy carries an L2 evict-first
 // policy so the stream does not push the small hot data (exchanged vectors,
 // K/V rows, norm weights, descriptors) out of L2.
+// 2-D tiled tensor copy (no multicast) of the box at (x, y) into shared memory.
+__device__ __forceinline__ void tma_2d(uint32_t dst, const void* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
@@ -485,9 +494,8 @@ struct Q6Blk {
   uint4 sc;          // the 16 int8 scales
   uint32_t dh;       // fp16 d
 };
-__device__ __forceinline__ Q6Blk q6_blk_load(const uint8_t* row, int nb, int b, int l) {
-  const int c = b >> 3, j = b & 7, m = q6_chunk_blocks(nb, c);
-  const uint8_t* chunk = row + (size_t)c * Q6K_CHUNK;
+// Block j of a chunk of m blocks, class l's code bytes.
+__device__ __forceinline__ Q6Blk q6_blk_load_chunk(const uint8_t* chunk, int m, int j, int l) {
   const uint8_t* body = chunk + j * Q6K_BODY;
   const uint2* wp = reinterpret_cast<const uint2*>(body + 24 * l);
   Q6Blk B;
@@ -497,6 +505,10 @@ __device__ __forceinline__ Q6Blk q6_blk_load(const uint8_t* row, int nb, int b, 
   B.sc = *reinterpret_cast<const uint4*>(body + 192);
   B.dh = *reinterpret_cast<const uint16_t*>(chunk + m * Q6K_BODY + 2 * j);
   return B;
+}
+__device__ __forceinline__ Q6Blk q6_blk_load(const uint8_t* row, int nb, int b, int l) {
+  const int c = b >> 3;
+  return q6_blk_load_chunk(row + (size_t)c * Q6K_CHUNK, q6_chunk_blocks(nb, c), b & 7, l);
 }
 // float(v) of byte k of w as a signed int8, without a conversion instruction
 __device__ __forceinline__ float s8_val(uint32_t w, int k) {
@@ -602,6 +614,39 @@ __device__ __forceinline__ void q6k_rows(const uint8_t* st, int rstride, int nro
     out[0] = fold8_lanes(a0);
     out[1] = fold8_lanes(a1);
   }
+}
+
+// Chunk c of the unit's rows (rows rstride bytes apart, each holding only
+// that chunk: a chunk-streamed stage) continues the lane's chain `acc`, in
+// the order and with the roundings of q6k_rows<1>; the caller folds the
+// lanes after the last chunk.
+__device__ __forceinline__ float q6k_rows_chunk(const uint8_t* st, int rstride, int nrows, int nb, int c,
+                                                const Act& A, float acc) {
+  const int lane = threadIdx.x & 31, r = lane >> 3, l = lane & 7;
+  const uint8_t* chunk = st + (size_t)(r < nrows ? r : 0) * rstride;
+  const int m = q6_chunk_blocks(nb, c);
+  const float* xl = A.xc + l * A.cp + 32 * CHUNK_BLOCKS * c;
+  Q6Blk B = q6_blk_load_chunk(chunk, m, 0, l);
+  float pv[16];
+  q6_half_products(B, 0, xl, pv);
+  int j = 0;
+  for (; j + 1 < m; j++) {
+    float pc[16];
+    q6_half_products(B, 1, xl + 32 * j + 16, pc);
+    B = q6_blk_load_chunk(chunk, m, j + 1, l);
+#pragma unroll
+    for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pv[i]);
+    q6_half_products(B, 0, xl + 32 * (j + 1), pv);
+#pragma unroll
+    for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pc[i]);
+  }
+  float pc[16];
+  q6_half_products(B, 1, xl + 32 * j + 16, pc);
+#pragma unroll
+  for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pv[i]);
+#pragma unroll
+  for (int i = 0; i < 16; i++) acc = __fadd_rn(acc, pc[i]);
+  return acc;
 }
 
 // ------------------------------------------------------------------ epilogue

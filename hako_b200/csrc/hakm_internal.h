@@ -265,6 +265,13 @@ struct alignas(16) PhaseDesc {  // copied to shared memory as 16-byte words
   // bytes, chunks per row, and ceil(2^16 / chunks) for unit -> (group, chunk)
   int st_rows[MAX_SEGS], st_row_bytes[MAX_SEGS], st_nch[MAX_SEGS], st_rn[MAX_SEGS];
   int st_unit_rows[MAX_SEGS];  // rows per unit: 4, or 2 where a CTA holds few rows (shorter latency)
+  // Q6_K segments whose CTAs hold a few long rows stream chunk by chunk: a
+  // stage is st_chunk_rows[s] rows x one 8-block chunk, one 2-D tensor copy
+  // through st_map[s] (two CUtensorMaps in device memory: boxes of
+  // st_chunk_rows and st_chunk_rows - 4 rows, the second for CTAs with
+  // fewer rows), so every row's chains run at once. 0: stages of whole rows.
+  int st_chunk_rows[MAX_SEGS];
+  const void* st_map[MAX_SEGS];
   // byte offset, within the shared activation region, of the per-thread
   // epilogue records (past this phase's activation); -1: no room, no records
   int epi_rec_off;
@@ -311,8 +318,11 @@ struct StepArgs {
   int trace_k;
 };
 
-// Fills the shared-memory plan of `a` for this program; false if it cannot fit.
-bool plan_step(PhaseDesc* prog_host, int n_phases, int grid, StepArgs& a);
+// Fills the shared-memory plan of `a` for this program (grid: the CTAs of all
+// GPUs the rows split over); false if it cannot fit. With `chunked`, Q6_K
+// segments of few long rows per CTA stream chunk by chunk (their
+// st_chunk_rows set; the caller then supplies their tensor maps).
+bool plan_step(PhaseDesc* prog_host, int n_phases, int grid, StepArgs& a, bool chunked = true);
 // The row table of StepArgs::ranges for this program: the rows of CTAs
 // cta0 .. cta0 + n_ctas - 1 of a grid of `grid` CTAs (all GPUs' CTAs).
 void step_ranges(const PhaseDesc* prog_host, int n_phases, int grid, int cta0, int n_ctas, SegRange* out);

@@ -87,13 +87,6 @@ struct MmaArgs {
   int n_out, n_in, n_batch;
 };
 
-__device__ __forceinline__ void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
-}
 
 // Shared-memory matrix descriptor, K-major. No swizzle (layout 0): core
 // matrices of 8 rows x 16 bytes (rows 16 B apart); lbo = bytes between the

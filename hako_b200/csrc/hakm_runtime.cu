@@ -14,6 +14,7 @@
 // then lm_head (rmsnorm; Q6_K logits + argmax + step finalisation).
 #include "../../include/hakm_cuda.h"
 #include "hakm_internal.h"
+#include "hakm_tmap.h"
 
 #include <algorithm>
 #include <array>
@@ -174,6 +175,8 @@ struct hakmc_ctx {
   bool use_step = true;        // HAKMC_STEP=0 selects the per-phase graphs
   PhaseDesc* prog_dev = nullptr;
   int prog_cap = 0, prog_layers = -1;
+  CUtensorMap* tmaps_dev = nullptr;  // the program's chunk-stream tensor maps
+  size_t tmaps_cap = 0;
   SegRange* ranges_dev = nullptr;  // [phase][cta][segment] rows of the step program
   size_t ranges_cap = 0;
   StepArgs step = {};
@@ -528,9 +531,47 @@ static int ensure_program(hakmc_ctx* c) {
   std::vector<PhaseDesc> prog;
   build_program(c, 0, prog);
   StepArgs a = {};
-  if (!plan_step(prog.data(), (int)prog.size(), c->num_sms, a)) {
+  if (!plan_step(prog.data(), (int)prog.size(), c->num_sms * c->tp_world, a)) {
     set_err("step kernel: shapes do not fit its shared-memory plan");
     return HAKMC_EINVAL;
+  }
+  {
+    // tensor maps of the chunk-streamed segments: two per segment, boxes of
+    // st_chunk_rows and st_chunk_rows - 4 rows x one chunk
+    std::vector<CUtensorMap> maps;
+    std::vector<std::pair<int, int>> where;
+    for (size_t ph = 0; ph < prog.size(); ph++) {
+      const PhaseDesc& D = prog[ph];
+      if (D.kind != PK_GEMV) continue;
+      for (int s = 0; s < D.g.n_seg; s++) {
+        const int cr = D.st_chunk_rows[s];
+        if (!cr) continue;
+        const Seg& S = D.g.seg[s];
+        const uint64_t rowB = dev_row_bytes(W_Q6K, D.g.n_in / QK);
+        CUtensorMap m[2];
+        for (int k = 0; k < 2; k++)
+          if (!encode_tmap_2d(&m[k], CU_TENSOR_MAP_DATA_TYPE_UINT64, S.w, rowB / 8, (uint64_t)S.n_rows, rowB,
+                              Q6K_CHUNK / 8, (uint32_t)std::max(4, cr - 4 * k))) {
+            set_err("step kernel: tensor map of a %d x %d Q6_K matrix rejected", S.n_rows, D.g.n_in);
+            return HAKMC_EINVAL;
+          }
+        maps.push_back(m[0]);
+        maps.push_back(m[1]);
+        where.push_back({(int)ph, s});
+      }
+    }
+    if (maps.size() > c->tmaps_cap) {
+      dfree(c, c->tmaps_dev);
+      c->tmaps_dev = nullptr;
+      c->tmaps_cap = 0;
+      const int r = dalloc(c, (void**)&c->tmaps_dev, maps.size() * sizeof(CUtensorMap));
+      if (r) return r;
+      c->tmaps_cap = maps.size();
+    }
+    if (!maps.empty())
+      CK(cudaMemcpy(c->tmaps_dev, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice));
+    for (size_t i = 0; i < where.size(); i++)
+      prog[where[i].first].st_map[where[i].second] = c->tmaps_dev + 2 * i;
   }
   if ((int)prog.size() > c->prog_cap) {
     void* p = nullptr;

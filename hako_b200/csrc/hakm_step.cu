@@ -162,6 +162,8 @@ struct EpiPre {
 // rows per stage (one bulk copy), units of ur (4, or 2) whole rows.
 struct SegGeo {
   int type, rowB, R, nch, chunkB, rn, ur;
+  int cr;           // chunk-stream rows (0: whole-row stages)
+  const void* map;  // its two tensor maps
 };
 // Read from the descriptor (computed by plan_step on the host).
 __device__ __forceinline__ SegGeo seg_geo(const PhaseDesc& D, int s) {
@@ -173,6 +175,8 @@ __device__ __forceinline__ SegGeo seg_geo(const PhaseDesc& D, int s) {
   g.chunkB = g.type == W_Q4K ? Q4K_CHUNK : Q6K_CHUNK;
   g.rn = D.st_rn[s];
   g.ur = D.st_unit_rows[s];
+  g.cr = D.st_chunk_rows[s];
+  g.map = D.st_map[s];
   return g;
 }
 
@@ -490,6 +494,29 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
           const SegGeo G = seg_geo(D, s);
           const uint8_t* w = D.g.seg[s].w;
           const int4 rr = __ldg(reinterpret_cast<const int4*>(rtab + s));
+          if (G.cr > 0) {
+            // chunk stages: the CTA's rows x chunk c, one tensor copy each
+            if (rr.x >= rr.y) continue;
+            const bool fewer = rr.y - rr.x <= G.cr - 4;
+            const void* map = reinterpret_cast<const uint8_t*>(G.map) + (fewer ? 128 : 0);
+            const uint32_t bytes = (uint32_t)((fewer ? G.cr - 4 : G.cr) * Q6K_CHUNK);
+            for (int c = 0; c < G.nch && ok; c++) {
+              if (rp.lapped) {
+                bool wok = true;
+                if (lane == 0) wok = mbar_wait_or_abort(smem_addr(&empty[rp.slot]), rp.par ^ 1u, A.err_flag);
+                if (!__shfl_sync(0xffffffffu, wok, 0)) { ok = false; break; }
+              }
+              if (lane == 0) {
+                mbar_expect_tx(smem_addr(&full[rp.slot]), bytes);
+                tma_2d(smem_addr(ring + (size_t)rp.slot * SB), map, c * (Q6K_CHUNK / 8), rr.x,
+                       smem_addr(&full[rp.slot]));
+              }
+              __syncwarp();
+              rp.advance(S_);
+              issued++;
+            }
+            continue;
+          }
           for (int rt = rr.x; rt < rr.y; rt += G.R) {
             const int nr = min(G.R, rr.y - rt);
             if (rp.lapped) {
@@ -659,10 +686,36 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         bool failed = false;
         for (int s = 0; s < P.n_seg && !failed; s++) {
           const SegGeo G = seg_geo(D, s);
+          float* ps = part + sr[s].part_base;
+          if (G.cr > 0) {
+            // chunk stages: warp cw runs rows 4cw.. of the CTA's range, its
+            // lane chains carried from chunk to chunk
+            const int nr = sr[s].row1 - sr[s].row0;
+            if (nr <= 0) continue;
+            const bool mine = 4 * cw < nr;
+            const int nru = min(4, nr - 4 * cw);
+            float acc = 0.f;
+            for (int c = 0; c < G.nch; c++) {
+              const bool got = mbar_wait_or_abort(smem_addr(&full[rc.slot]), rc.par, err);
+              if (!__all_sync(0xffffffffu, got)) {  // the warp leaves together
+                failed = true;
+                break;
+              }
+              const uint8_t* stage = ring + (size_t)rc.slot * SB;
+              if (mine) acc = q6k_rows_chunk(stage + (size_t)4 * cw * Q6K_CHUNK, Q6K_CHUNK, nru, nb, c, X, acc);
+              __syncwarp();
+              if (lane == 0) mbar_arrive(smem_addr(&empty[rc.slot]));
+              rc.advance(S_);
+            }
+            if (mine && !failed) {
+              const float tot = fold8_lanes(acc);
+              if ((lane & 7) == 0 && (lane >> 3) < nru) ps[4 * cw + (lane >> 3)] = tot;
+            }
+            continue;
+          }
           // units of ur whole rows (every chunk, in order: the row sums are
           // sequential over the row, as the reference's are)
           const int n_units_full = (G.R + G.ur - 1) / G.ur;
-          float* ps = part + sr[s].part_base;
           float* tr = wscr + cw * WARP_SCRATCH_FLOATS;
           for (int rt = sr[s].row0; rt < sr[s].row1; rt += G.R) {
             if (!mbar_wait_or_abort(smem_addr(&full[rc.slot]), rc.par, err)) {
@@ -809,8 +862,16 @@ size_t step_smem_bytes(const StepArgs& a) {
          WARP_SCRATCH_BYTES;
 }
 
-bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
-  size_t region = 0, max_row = 0;
+// Q6_K segments that stream chunk by chunk (see PhaseDesc::st_chunk_rows):
+// more than one chunk per row and at most one 4-row group per consumer warp.
+static int chunk_rows_of(const PhaseDesc& D, int s, int grid) {
+  const Seg& S = D.g.seg[s];
+  const int nb = D.g.n_in / QK, max_groups = ((S.n_rows + 3) / 4 + grid - 1) / grid;
+  return (S.type == W_Q6K && nb > CHUNK_BLOCKS && max_groups <= CONSUMER_WARPS) ? 4 * max_groups : 0;
+}
+
+bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a, bool chunked) {
+  size_t region = 0, max_row = 0, chunk_stage = 0;
   int part = 0;
   for (int ph = 0; ph < n_phases; ph++) {
     const PhaseDesc& D = prog[ph];
@@ -828,20 +889,24 @@ bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
     region = std::max(region, act_bytes(P.n_in, P.need_q8, P.need_q6 || P.act == ACT_RMS));
     int pf = 0;
     for (int s = 0; s < P.n_seg; s++) {
-      max_row = std::max(max_row, dev_row_bytes(P.seg[s].type, nb));
+      const int cr = chunked ? chunk_rows_of(D, s, grid) : 0;
+      if (cr) chunk_stage = std::max(chunk_stage, (size_t)cr * Q6K_CHUNK);
+      else max_row = std::max(max_row, dev_row_bytes(P.seg[s].type, nb));
       const int G = (P.seg[s].n_rows + 3) / 4;
       pf += ((G + grid - 1) / grid) * 4;
     }
     part = std::max(part, pf);
   }
+  if (max_row == 0) max_row = Q6K_CHUNK;
   a.region_bytes = (int)((region + 127) & ~(size_t)127);
   a.part_floats = (part + 3) & ~3;
   const long ring =
       (long)STEP_SMEM_MAX - SMEM_HEADER - a.region_bytes - (long)a.part_floats * 4 - 64 * 4 - WARP_SCRATCH_BYTES;
-  if (max_row == 0 || ring < 2L * (long)max_row) return false;
-  // slots of at least 4 of the longest rows while that leaves 2 slots;
-  // HAKMC_STEP_STAGES overrides the slot count (measurement)
-  int S = (int)(ring / (4L * (long)max_row));
+  if (ring < 2L * (long)max_row) return false;
+  // slots of at least 4 of the longest rows (and a whole chunk stage) while
+  // that leaves 2 slots; HAKMC_STEP_STAGES overrides the slot count
+  // (measurement)
+  int S = (int)(ring / std::max(4L * (long)max_row, (long)chunk_stage));
   S = std::max(2, std::min(S, 8));
   if (const char* e = getenv("HAKMC_STEP_STAGES")) {
     const int v = atoi(e);
@@ -853,6 +918,7 @@ bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
     if (S < 2) return false;
     slot = (ring / S) & ~127L;
   }
+  if (slot < (long)chunk_stage) return plan_step(prog, n_phases, grid, a, false);
   a.n_stages = S;
   a.slot_bytes = (int)slot;
   for (int ph = 0; ph < n_phases; ph++) {
@@ -867,7 +933,8 @@ bool plan_step(PhaseDesc* prog, int n_phases, int grid, StepArgs& a) {
     }
     const int nb = D.g.n_in / QK;
     for (int s = 0; s < D.g.n_seg; s++) {
-      D.st_rows[s] = stage_rows_for(D.g.seg[s].type, nb, a.slot_bytes);
+      D.st_chunk_rows[s] = chunked ? chunk_rows_of(D, s, grid) : 0;
+      D.st_rows[s] = D.st_chunk_rows[s] ? D.st_chunk_rows[s] : stage_rows_for(D.g.seg[s].type, nb, a.slot_bytes);
       D.st_row_bytes[s] = (int)dev_row_bytes(D.g.seg[s].type, nb);
       D.st_nch[s] = n_chunks(nb);
       D.st_rn[s] = (65536 + D.st_nch[s] - 1) / D.st_nch[s];
