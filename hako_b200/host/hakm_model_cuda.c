@@ -32,6 +32,11 @@
  *   - sample_token on c->logits does not turn the array into probabilities
  *     (the reference's does, in place); no caller reads them afterwards.
  *   - HAKMC_DEVICE (environment) picks the GPU, default 0.
+ *   - HAKMC_GPUS=N (environment, 2..8) runs the context tensor parallel over
+ *     GPUs HAKMC_DEVICE .. HAKMC_DEVICE+N-1 (hakmc_tp_*: every phase's rows
+ *     split over all GPUs, outputs all-gathered by peer stores), one thread
+ *     per GPU making the same calls; the results are the one-GPU results,
+ *     bit for bit.
  *   - HAKMC_TOKEN_LOG (environment), if set, names a file that receives
  *     every id hakm_forward is given, one per line (stream comparisons).
  */
@@ -49,11 +54,14 @@
 int hakm_ref_sample_token(sampler *s, float *logits, int n);
 
 enum { BATCHED_MIN = 16 };  /* pending ids from which the batched prompt pass runs */
+enum { MAX_GPUS = 8 };
 
 /* hakm_ctx first, so the pointer callers hold is also the wrapper's */
 typedef struct cuda_ctx {
 	hakm_ctx         c;
-	hakmc_ctx       *dev;
+	hakmc_ctx       *dev;         /* rank 0 (the pick and the logits are read here) */
+	hakmc_ctx       *devs[MAX_GPUS];
+	int              n_dev;
 	FILE            *token_log;
 	int              eager;
 	int             *pending;     /* ids recorded, not yet run */
@@ -65,6 +73,78 @@ static cuda_ctx *live;
 static pthread_mutex_t live_mu = PTHREAD_MUTEX_INITIALIZER;
 
 static cuda_ctx *wrapper(hakm_ctx *c) { return (cuda_ctx *)c; }
+
+/* One call made on every GPU of the context at once (tensor parallelism
+ * needs all ranks in the same call): rank 0 in the calling thread, the
+ * others on threads of their own. */
+enum { OP_FORWARD, OP_PREFILL, OP_PREFILL_BATCHED, OP_RESET };
+typedef struct {
+	hakmc_ctx *h;
+	int        op, n, rc;
+	const int *ids;
+	float     *logits;   /* rank 0 of OP_FORWARD only (may be NULL) */
+} job;
+
+static void *job_run(void *p)
+{
+	job *j = p;
+	switch (j->op) {
+	case OP_FORWARD:         j->rc = hakmc_forward(j->h, j->ids[0], j->logits, NULL); break;
+	case OP_PREFILL:         j->rc = hakmc_prefill(j->h, j->ids, j->n, NULL, NULL); break;
+	case OP_PREFILL_BATCHED: j->rc = hakmc_prefill_batched(j->h, j->ids, j->n, 0, NULL, NULL); break;
+	default:                 hakmc_reset(j->h); j->rc = 0; break;
+	}
+	return NULL;
+}
+
+static int run_all(struct cuda_ctx *w, int op, const int *ids, int n, float *logits)
+{
+	job jobs[MAX_GPUS];
+	pthread_t th[MAX_GPUS];
+	int started[MAX_GPUS] = {0};
+	for (int r = 0; r < w->n_dev; r++)
+		jobs[r] = (job){ w->devs[r], op, n, 0, ids, r == 0 ? logits : NULL };
+	for (int r = 1; r < w->n_dev; r++)
+		started[r] = pthread_create(&th[r], NULL, job_run, &jobs[r]) == 0;
+	job_run(&jobs[0]);
+	int rc = jobs[0].rc;
+	for (int r = 1; r < w->n_dev; r++) {
+		if (!started[r]) { rc = rc ? rc : -1; continue; }
+		pthread_join(th[r], NULL);
+		if (!rc) rc = jobs[r].rc;
+	}
+	return rc;
+}
+
+/* The device contexts: one, or n tensor-parallel ranks joined in this
+ * process. 0, or -1 after reporting on stderr (every context created is
+ * destroyed again). */
+static int open_devices(struct cuda_ctx *w, int max_seq, int dev0, int n)
+{
+	const hakm_model *m = &w->c.model;
+	for (int r = 0; r < n; r++) {
+		w->devs[r] = hakmc_create(m->map, m->map_size, max_seq, 1, dev0 + r);
+		if (!w->devs[r]) goto fail;
+		w->n_dev = r + 1;
+	}
+	if (n > 1) {
+		const size_t hb = hakmc_tp_handle_bytes();
+		unsigned char *handles = calloc((size_t)n, hb);
+		if (!handles) goto fail;
+		int rc = 0;
+		for (int r = 0; r < n && !rc; r++) rc = hakmc_tp_export(w->devs[r], handles + (size_t)r * hb);
+		for (int r = 0; r < n && !rc; r++) rc = hakmc_tp_connect(w->devs[r], r, n, handles);
+		free(handles);
+		if (rc) goto fail;
+	}
+	w->dev = w->devs[0];
+	return 0;
+fail:
+	fprintf(stderr, "hakm: %s\n", hakmc_last_error());
+	for (int r = 0; r < w->n_dev; r++) hakmc_destroy(w->devs[r]);
+	w->n_dev = 0;
+	return -1;
+}
 
 hakm_ctx *hakm_ctx_new(const char *mlf2_path, int max_seq)
 {
@@ -94,12 +174,13 @@ hakm_ctx *hakm_ctx_new(const char *mlf2_path, int max_seq)
 	c->logits = malloc((size_t)c->vocab * sizeof(float));
 	w->cap_pending = max_seq > 0 ? max_seq : 1;
 	w->pending = malloc((size_t)w->cap_pending * sizeof(int));
-	const char *dev_env = getenv("HAKMC_DEVICE");
+	const char *dev_env = getenv("HAKMC_DEVICE"), *gpus_env = getenv("HAKMC_GPUS");
 	const int dev = dev_env ? atoi(dev_env) : 0;
-	if (c->logits && w->pending)
-		w->dev = hakmc_create(c->model.map, c->model.map_size, max_seq, 1, dev);
-	if (!w->dev) {
-		fprintf(stderr, "hakm: %s\n", c->logits && w->pending ? hakmc_last_error() : "out of memory");
+	int n_gpus = gpus_env ? atoi(gpus_env) : 1;
+	if (n_gpus < 1) n_gpus = 1;
+	if (n_gpus > MAX_GPUS) n_gpus = MAX_GPUS;
+	if (!c->logits || !w->pending) fprintf(stderr, "hakm: out of memory\n");
+	if (!c->logits || !w->pending || open_devices(w, max_seq, dev, n_gpus) != 0) {
 		free(w->pending);
 		free(c->logits);
 		mlf2_close(&c->model);
@@ -126,7 +207,7 @@ void hakm_ctx_free(hakm_ctx *c)
 		if (*p == w) { *p = w->next; break; }
 	pthread_mutex_unlock(&live_mu);
 	if (w->token_log) fclose(w->token_log);
-	hakmc_destroy(w->dev);
+	for (int r = 0; r < w->n_dev; r++) hakmc_destroy(w->devs[r]);
 	free(w->pending);
 	free(c->logits);
 	mlf2_close(&c->model);
@@ -140,13 +221,8 @@ static int flush(cuda_ctx *w)
 	const int n = w->n_pending;
 	if (n == 0) return 0;
 	w->n_pending = 0;
-	int rc;
-	if (n >= BATCHED_MIN)
-		rc = hakmc_prefill_batched(w->dev, w->pending, n, 0, NULL, NULL);
-	else if (n > 1)
-		rc = hakmc_prefill(w->dev, w->pending, n, NULL, NULL);
-	else
-		rc = hakmc_forward(w->dev, w->pending[0], NULL, NULL);
+	const int op = n >= BATCHED_MIN ? OP_PREFILL_BATCHED : n > 1 ? OP_PREFILL : OP_FORWARD;
+	const int rc = run_all(w, op, w->pending, n, NULL);
 	if (rc != 0) {
 		fprintf(stderr, "hakm: forward of %d id(s): %s\n", n, hakmc_last_error());
 		return -1;
@@ -163,7 +239,7 @@ const float *hakm_forward(hakm_ctx *c, int token)
 		return c->logits;
 	}
 	if (w->eager) {
-		if (hakmc_forward(w->dev, token, c->logits, NULL) != 0) {
+		if (run_all(w, OP_FORWARD, &token, 1, c->logits) != 0) {
 			fprintf(stderr, "hakm: forward at position %d: %s\n", c->pos, hakmc_last_error());
 			return c->logits;
 		}
@@ -178,7 +254,7 @@ void hakm_reset(hakm_ctx *c)
 {
 	cuda_ctx *w = wrapper(c);
 	w->n_pending = 0;
-	hakmc_reset(w->dev);
+	run_all(w, OP_RESET, NULL, 0, NULL);
 	c->pos = 0;
 }
 

@@ -64,3 +64,23 @@ def test_tp2_bit_identical_to_one_gpu(cuda, preset):
         assert res[r]["tp"] == res[0]["single"], r
         assert np.array_equal(res[r]["logits"], res[0]["single_logits"]), r
         assert res[r]["pos"] == len(PROMPT) + n_gen
+
+
+@pytest.mark.parametrize("sampling", [("-t", "0"), ("-t", "0.8", "-k", "40", "-p", "0.9", "-s", "1234")])
+def test_dropin_cli_tensor_parallel(cuda, sampling):
+    """The reference CLI over the drop-in with HAKMC_GPUS=2: one context
+    tensor parallel over two GPUs (two threads making the same calls), the
+    deferred prompt and the device pick as on one GPU; the printed bytes
+    equal the unmodified reference CLI's."""
+    import torch
+    from oracle.oracle import DROPIN_CLI, REF_CLI
+    from test_dropin_gpu import _run
+    from hako_b200 import synth
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    if not (os.path.exists(REF_CLI) and os.path.exists(DROPIN_CLI)):
+        pytest.skip("oracle/_ref CLIs not built (make -C oracle ref dropin)")
+    path = synth.cached_model(synth.PRESETS["small"])
+    prompt = "once upon a time there was a"
+    ours = _run(DROPIN_CLI, path, 40, prompt, {"HAKMC_GPUS": "2"}, sampling=sampling)
+    assert ours == _run(REF_CLI, path, 40, prompt, sampling=sampling)
