@@ -143,6 +143,8 @@ struct DevLayer {
   DevMat wqk, wv, wo, wgu, down;
 };
 
+struct UpStage;
+
 struct hakmc_ctx {
   int device = 0, num_sms = 148;
   int L, D, H, KVH, hd, KV, F, V, max_seq, max_batch;
@@ -175,6 +177,7 @@ struct hakmc_ctx {
   bool use_step = true;        // HAKMC_STEP=0 selects the per-phase graphs
   PhaseDesc* prog_dev = nullptr;
   int prog_cap = 0, prog_layers = -1;
+  UpStage* up = nullptr;             // weight-upload staging, while loading
   CUtensorMap* tmaps_dev = nullptr;  // the program's chunk-stream tensor maps
   size_t tmaps_cap = 0;
   SegRange* ranges_dev = nullptr;  // [phase][cta][segment] rows of the step program
@@ -237,9 +240,39 @@ static void dfree(hakmc_ctx* c, void* p) {
     }
 }
 
+// Pinned staging of the weight upload: two host buffers and two device
+// buffers used in turn, so the host copy of one slice of rows (from the
+// mapped file, in device row order) overlaps the transfer and the device
+// repack of the previous one. Held only while a context loads.
+struct UpStage {
+  static constexpr size_t BYTES = 32u << 20;
+  uint8_t* host[2] = {nullptr, nullptr};
+  uint8_t* dev[2] = {nullptr, nullptr};
+  cudaEvent_t done[2] = {nullptr, nullptr};
+  bool used[2] = {false, false};
+  int k = 0;
+  cudaError_t open() {
+    for (int b = 0; b < 2; b++) {
+      cudaError_t e = cudaHostAlloc((void**)&host[b], BYTES, cudaHostAllocDefault);
+      if (e == cudaSuccess) e = cudaMalloc((void**)&dev[b], BYTES);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done[b], cudaEventDisableTiming);
+      if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+  }
+  ~UpStage() {
+    for (int b = 0; b < 2; b++) {
+      if (done[b]) { cudaEventSynchronize(done[b]); cudaEventDestroy(done[b]); }
+      if (dev[b]) cudaFree(dev[b]);
+      if (host[b]) cudaFreeHost(host[b]);
+    }
+  }
+};
+
 // Upload rows of a Q4_K / Q6_K matrix. `order[i]` is the source row of device
 // row i (identity when empty). Q6_K rows are split into 208-byte bodies (bytes
-// reordered by lane class) and an fp16 d plane (hakmc_q6k_pack layout).
+// reordered by lane class) and an fp16 d plane (hakmc_q6k_pack layout): the
+// verbatim rows go to the device and the repack kernel lays them out there.
 static int upload_mat(hakmc_ctx* c, DevMat& dm, const MTensor& t, int exp_cols, int exp_rows,
                       const std::vector<int>& order, const MTensor* t2 = nullptr) {
   if (t.type != W_Q4K && t.type != W_Q6K) {
@@ -271,25 +304,25 @@ static int upload_mat(hakmc_ctx* c, DevMat& dm, const MTensor& t, int exp_cols, 
     return t.data + (size_t)s * rb;
   };
   const size_t drb = dev_row_bytes((int)t.type, nb);
-  std::vector<uint8_t> host((size_t)rows * drb, 0);
-  if (t.type == W_Q4K) {
-    for (int i = 0; i < rows; i++) memcpy(host.data() + (size_t)i * drb, src_row(i), rb);
-  } else {
-    // chunks of 8 blocks: the 208-byte bodies, then the 8 fp16 d values
-    for (int i = 0; i < rows; i++) {
-      const uint8_t* s = src_row(i);
-      uint8_t* d = host.data() + (size_t)i * drb;
-      for (int b = 0; b < nb; b++) {
-        const int c = b / CHUNK_BLOCKS, j = b % CHUNK_BLOCKS, m = q6_chunk_blocks(nb, c);
-        uint8_t* chunk = d + (size_t)c * Q6K_CHUNK;
-        for (int i = 0; i < Q6K_BODY; i++) chunk[j * Q6K_BODY + q6k_body_pos(i)] = s[(size_t)b * Q6K_BYTES + i];
-        memcpy(chunk + m * Q6K_BODY + 2 * j, s + (size_t)b * Q6K_BYTES + Q6K_BODY, 2);
-      }
-    }
-  }
-  int e = dalloc(c, (void**)&dm.w, host.size());
+  int e = dalloc(c, (void**)&dm.w, (size_t)rows * drb);
   if (e) return e;
-  CK(cudaMemcpy(dm.w, host.data(), host.size(), cudaMemcpyHostToDevice));
+  UpStage& U = *c->up;
+  const int per = (int)std::max<size_t>(1, UpStage::BYTES / rb);  // rows per slice
+  if ((size_t)per * rb > UpStage::BYTES) { set_err("tensor %s: rows too long to stage", t.name.c_str()); return HAKMC_EFORMAT; }
+  for (int r0 = 0; r0 < rows; r0 += per) {
+    const int n = std::min(per, rows - r0), b = U.k++ & 1;
+    if (U.used[b]) CK(cudaEventSynchronize(U.done[b]));  // the slice before last has left this buffer
+    for (int i = 0; i < n; i++) memcpy(U.host[b] + (size_t)i * rb, src_row(r0 + i), rb);
+    uint8_t* dst = dm.w + (size_t)r0 * drb;
+    if (t.type == W_Q4K) {  // the device row is the verbatim row
+      CK(cudaMemcpyAsync(dst, U.host[b], (size_t)n * rb, cudaMemcpyHostToDevice, c->stream));
+    } else {
+      CK(cudaMemcpyAsync(U.dev[b], U.host[b], (size_t)n * rb, cudaMemcpyHostToDevice, c->stream));
+      CK(launch_q6k_pack(dst, U.dev[b], n, exp_cols, c->stream));
+    }
+    CK(cudaEventRecord(U.done[b], c->stream));
+    U.used[b] = true;
+  }
   return 0;
 }
 
@@ -729,6 +762,14 @@ static int create_impl(hakmc_ctx* c, const uint8_t* img, size_t size) {
   c->pdl = !(pe && pe[0] == '0');
   const char* se = getenv("HAKMC_STEP");
   c->use_step = !(se && se[0] == '0');
+  // weight staging for the uploads below; released when this returns
+  UpStage stage;
+  struct Unset {
+    hakmc_ctx* c;
+    ~Unset() { c->up = nullptr; }
+  } unset{c};
+  CK(stage.open());
+  c->up = &stage;
 
   const MTensor *te = need("token_embd.weight"), *on = need("output_norm.weight");
   if (!te || !on) return HAKMC_EFORMAT;
