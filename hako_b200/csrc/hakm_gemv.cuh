@@ -167,7 +167,7 @@ __host__ __device__ inline int stage_rows_for(int type, int nb, int slot_bytes) 
 // This CTA's rows of segment s: the segment's 4-row groups split evenly over
 // the grid, each segment's split rotated by the groups before it so the
 // remainders of consecutive segments land on different CTAs. One result per
-// row (nch = 1): a unit runs whole rows, every chunk, in order.
+// row: a unit runs whole rows, every chunk, in order.
 // 32-bit arithmetic throughout (groups * grid < 2^31): this runs in every
 // CTA at the start of every phase, on the critical path.
 __device__ __forceinline__ void cta_ranges(const PhaseParams& p, SegRange* sr) {
@@ -181,7 +181,7 @@ __device__ __forceinline__ void cta_ranges(const PhaseParams& p, SegRange* sr) {
     const int g0 = (int)(idx * G / grid), g1 = (int)((idx + 1) * G / grid);
     sr[s].row0 = 4 * g0;
     sr[s].row1 = min(4 * g1, n);
-    sr[s].nch = 1;
+    sr[s].wdelta = 0;
     sr[s].part_base = pbase;
     pbase += sr[s].row1 - sr[s].row0;
     goff += G;

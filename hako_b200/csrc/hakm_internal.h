@@ -92,6 +92,10 @@ struct Seg {
   int n_rows;
   int epi;
   int split;             // EPI_ROPE_QK: first k row (= q rows)
+  // tensor parallelism: w holds only this GPU's rows, w_rows of them,
+  // cyclically from row w_row0 (rows w_row0 .. n_rows-1, then 0 ..);
+  // w_rows 0: all rows
+  int w_row0, w_rows;
 };
 
 struct PhaseParams {
@@ -233,7 +237,9 @@ float host_rsqrt_nr(float v);
 // Rows of one segment that one CTA computes, and where its per-(row, chunk)
 // partial sums start in shared memory.
 struct SegRange {
-  int row0, row1, nch, part_base;
+  int row0, row1;
+  int wdelta;  // device row rt of the segment is row rt - wdelta of its weights (0 unless they are a shard)
+  int part_base;
 };
 
 // ---- persistent decode-step kernel (hakm_step.cu) ----
@@ -330,6 +336,6 @@ size_t step_smem_bytes(const StepArgs& a);
 cudaError_t launch_step(const StepArgs& a, int grid, cudaStream_t s);
 // Unpacks n tagged words into floats (debug reads of the exchange buffers).
 cudaError_t launch_ll_unpack(float* out, const uint64_t* in, int n, cudaStream_t s);
-constexpr int STEP_SMEM_MAX = 225 * 1024;  // dynamic; the opt-in limit (227 KB) also covers static smem
+constexpr int STEP_SMEM_MAX = 224 * 1024;  // dynamic; the opt-in limit (227 KB) also covers the ~2.2 KB static
 
 }  // namespace hakm

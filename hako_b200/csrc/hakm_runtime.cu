@@ -136,6 +136,8 @@ constexpr int BATCH_ROWS_MIN = 8;
 struct DevMat {         // one weight matrix on the device (layout: hakm_internal.h)
   int type = 0, rows = 0, cols = 0;
   uint8_t* w = nullptr;
+  // tensor parallelism: w holds only this GPU's rows (Seg::w_row0 / w_rows)
+  int shard_row0 = 0, shard_rows = 0;
 };
 
 struct DevLayer {
@@ -356,6 +358,8 @@ static std::vector<int> rope_pair_order(int n_heads, int hd) {
 static Seg make_seg(const DevMat& m, int epi, float* out) {
   Seg s = {};
   s.w = m.w;
+  s.w_row0 = m.shard_row0;
+  s.w_rows = m.shard_rows;
   s.type = m.type;
   s.n_rows = m.rows;
   s.epi = epi;
@@ -583,7 +587,8 @@ static int ensure_program(hakmc_ctx* c) {
         const uint64_t rowB = dev_row_bytes(W_Q6K, D.g.n_in / QK);
         CUtensorMap m[2];
         for (int k = 0; k < 2; k++)
-          if (!encode_tmap_2d(&m[k], CU_TENSOR_MAP_DATA_TYPE_UINT64, S.w, rowB / 8, (uint64_t)S.n_rows, rowB,
+          if (!encode_tmap_2d(&m[k], CU_TENSOR_MAP_DATA_TYPE_UINT64, S.w, rowB / 8,
+                              (uint64_t)(S.w_rows ? S.w_rows : S.n_rows), rowB,
                               Q6K_CHUNK / 8, (uint32_t)std::max(4, cr - 4 * k))) {
             set_err("step kernel: tensor map of a %d x %d Q6_K matrix rejected", S.n_rows, D.g.n_in);
             return HAKMC_EINVAL;
@@ -1253,6 +1258,7 @@ extern "C" int hakmc_decode(hakmc_ctx* c, int n_steps, int* out) {
 
 extern "C" int hakmc_time_phase(hakmc_ctx* c, int phase, int iters, float* avg_ms) {
   if (!c || phase < 0 || phase > PH_LMHEAD || iters <= 0 || !avg_ms) return HAKMC_EINVAL;
+  if (c->tp_world > 1) { set_err("time_phase: one GPU only (tensor-parallel weights are shards)"); return HAKMC_EINVAL; }
   CK(cudaSetDevice(c->device));
   const int ns = n_split_for(c, c->pos < c->max_seq ? c->pos : c->max_seq - 1);
   for (int i = 0; i < 3; i++) CK(enqueue_phase(c, i % c->L, phase, ns, true));  // warm-up
@@ -1267,6 +1273,7 @@ extern "C" int hakmc_time_phase(hakmc_ctx* c, int phase, int iters, float* avg_m
 }
 
 extern "C" int hakmc_trace_phase(hakmc_ctx* c, int phase, int layer, unsigned long long* stamps, int max_ctas) {
+  if (c && c->tp_world > 1) { set_err("trace_phase: one GPU only (tensor-parallel weights are shards)"); return HAKMC_EINVAL; }
   if (!c || phase < 0 || phase > PH_LMHEAD || phase == PH_ATTN || !stamps || layer < 0 || layer >= c->L)
     return HAKMC_EINVAL;
   CK(cudaSetDevice(c->device));
@@ -1314,6 +1321,60 @@ extern "C" int hakmc_tp_export(hakmc_ctx* c, void* handle) {
     CK(cudaIpcGetMemHandle(&h.ipc[x], c->xr_ptr[x]));
   }
   memcpy(handle, &h, sizeof h);
+  return 0;
+}
+
+// Tensor parallelism: keep only this GPU's rows of every matrix the step
+// program splits (the lm_head too unless it is the embedding, which every
+// token needs whole). A GPU's rows of a segment are the ranges of its CTAs,
+// which run on cyclically (the split of each segment is rotated), so they
+// are kept from the first CTA's first row on, wrapping past the last row.
+static int shard_weights(hakmc_ctx* c) {
+  const int keep = c->run_layers;
+  c->run_layers = c->L;
+  std::vector<PhaseDesc> prog;
+  build_program(c, 0, prog);
+  c->run_layers = keep;
+  const int ns = c->num_sms;
+  std::vector<SegRange> tab(prog.size() * (size_t)ns * MAX_SEGS);
+  step_ranges(prog.data(), (int)prog.size(), ns * c->tp_world, c->tp_rank * ns, ns, tab.data());
+  std::vector<DevMat*> mats;
+  for (int l = 0; l < c->L; l++) {
+    DevLayer& y = c->layers[l];
+    for (DevMat* m : {&y.wqk, &y.wv, &y.wo, &y.wgu, &y.down}) mats.push_back(m);
+  }
+  if (!c->tied) mats.push_back(&c->lm_head);
+  for (DevMat* m : mats) {
+    int ph = -1, sg = -1;
+    for (size_t i = 0; i < prog.size() && ph < 0; i++)
+      if (prog[i].kind == PK_GEMV)
+        for (int s = 0; s < prog[i].g.n_seg; s++)
+          if (prog[i].g.seg[s].w == m->w) { ph = (int)i; sg = s; break; }
+    if (ph < 0) continue;
+    const int n = m->rows;
+    int lo = -1, owned = 0, next = -1;
+    for (int lc = 0; lc < ns; lc++) {
+      const SegRange& r = tab[((size_t)ph * ns + lc) * MAX_SEGS + sg];
+      if (r.row1 <= r.row0) continue;
+      if (lo < 0) lo = r.row0;
+      else if (r.row0 != next % n) { set_err("tp_connect: rows of a matrix are not contiguous"); return HAKMC_EINVAL; }
+      owned += r.row1 - r.row0;
+      next = r.row1;
+    }
+    if (lo < 0 || owned >= n) continue;
+    const size_t rowB = dev_row_bytes(m->type, m->cols / QK);
+    uint8_t* w = nullptr;
+    int e = dalloc(c, (void**)&w, (size_t)owned * rowB);
+    if (e) return e;
+    const int first = std::min(owned, n - lo);
+    CK(cudaMemcpy(w, m->w + (size_t)lo * rowB, (size_t)first * rowB, cudaMemcpyDeviceToDevice));
+    if (owned > first) CK(cudaMemcpy(w + (size_t)first * rowB, m->w, (size_t)(owned - first) * rowB,
+                                     cudaMemcpyDeviceToDevice));
+    dfree(c, m->w);
+    m->w = w;
+    m->shard_row0 = lo;
+    m->shard_rows = owned;
+  }
   return 0;
 }
 
@@ -1366,7 +1427,7 @@ extern "C" int hakmc_tp_connect(hakmc_ctx* c, int rank, int world, const void* h
   c->tp_rank = rank;
   c->tp_world = world;
   c->prog_layers = -1;  // rebuild the program: rows over all GPUs' CTAs
-  return 0;
+  return world > 1 ? shard_weights(c) : 0;
 }
 
 extern "C" int hakmc_tp_rank(const hakmc_ctx* c) { return c ? c->tp_rank : -1; }

@@ -287,9 +287,9 @@ __device__ __forceinline__ EpiRec epi_prepare(const PhaseDesc& D, const SegRange
   if (S.epi == EPI_ROPE_QK || S.epi == EPI_SWIGLU) {
     if (2 * t + 1 >= r.row1 - r.row0) return e;
     const int dr = r.row0 + 2 * t;
-    e.pidx = r.part_base + 2 * t * r.nch;
+    e.pidx = r.part_base + 2 * t;
     if (S.epi == EPI_SWIGLU) {
-      e.kind = EPI_SWIGLU | (r.nch << 8);
+      e.kind = EPI_SWIGLU | (1 << 8);
       e.o0 = dr >> 1;
       return e;
     }
@@ -297,7 +297,7 @@ __device__ __forceinline__ EpiRec epi_prepare(const PhaseDesc& D, const SegRange
     const int lr = is_k ? dr - S.split : dr;
     const int hd = p.head_dim, half = hd >> 1;
     const int head = lr / hd, pi = (lr % hd) >> 1;
-    e.kind = (is_k ? EPI_ROPE_K : EPI_ROPE_QK) | (r.nch << 8);
+    e.kind = (is_k ? EPI_ROPE_K : EPI_ROPE_QK) | (1 << 8);
     e.o0 = head * hd + pi;
     e.o1 = e.o0 + half;
     if (S.bias) { e.f0 = __ldg(S.bias + dr); e.f1 = __ldg(S.bias + dr + 1); }
@@ -308,8 +308,8 @@ __device__ __forceinline__ EpiRec epi_prepare(const PhaseDesc& D, const SegRange
   }
   const int row = r.row0 + t;
   if (row >= r.row1 || S.epi == EPI_ARGMAX) return e;
-  e.kind = S.epi | (r.nch << 8);
-  e.pidx = r.part_base + t * r.nch;
+  e.kind = S.epi | (1 << 8);
+  e.pidx = r.part_base + t;
   e.o0 = row;
   if (S.epi == EPI_RESID) ok &= ll_get1(D.res_ll + row, res_tag, e.f0, err);
   else if (S.bias) e.f0 = __ldg(S.bias + row);
@@ -508,7 +508,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
               }
               if (lane == 0) {
                 mbar_expect_tx(smem_addr(&full[rp.slot]), bytes);
-                tma_2d(smem_addr(ring + (size_t)rp.slot * SB), map, c * (Q6K_CHUNK / 8), rr.x,
+                tma_2d(smem_addr(ring + (size_t)rp.slot * SB), map, c * (Q6K_CHUNK / 8), rr.x - rr.z,
                        smem_addr(&full[rp.slot]));
               }
               __syncwarp();
@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
             if (lane == 0) {
               const uint32_t bytes = (uint32_t)(nr * G.rowB);
               mbar_expect_tx(smem_addr(&full[rp.slot]), bytes);
-              bulk_g2s(smem_addr(ring + (size_t)rp.slot * SB), w + (size_t)rt * G.rowB, bytes,
+              bulk_g2s(smem_addr(ring + (size_t)rp.slot * SB), w + (size_t)(rt - rr.z) * G.rowB, bytes,
                        smem_addr(&full[rp.slot]));
             }
             __syncwarp();
@@ -849,7 +849,8 @@ void step_ranges(const PhaseDesc* prog, int n_phases, int grid, int cta0, int n_
         const int g0 = (int)(idx * G / grid), g1 = (int)((idx + 1) * G / grid);
         sr[s].row0 = 4 * g0;
         sr[s].row1 = std::min(4 * g1, n);
-        sr[s].nch = 1;  // one result per row
+        const Seg& S = p.seg[s];
+        sr[s].wdelta = (S.w_rows > 0 && S.w_rows < n) ? (sr[s].row0 >= S.w_row0 ? S.w_row0 : S.w_row0 - n) : 0;
         sr[s].part_base = pbase;
         pbase += sr[s].row1 - sr[s].row0;
         goff += G;

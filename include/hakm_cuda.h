@@ -131,7 +131,10 @@ int hakmc_forward_batch(hakmc_ctx *c, const int *tokens, const int *pos,
  * All ranks must then make the same calls (forward / prefill / generate /
  * decode / reset with the same arguments) concurrently; every rank gets the
  * same tokens and logits. Ranks may be threads of one process or separate
- * processes (CUDA IPC). 0 or a negative code. */
+ * processes (CUDA IPC). On connecting, every rank keeps only its own rows
+ * of each split matrix (about 1/world of the weights; the embedding, and a
+ * tied lm_head, stay whole), so the per-phase entry points (hakmc_time_phase,
+ * hakmc_trace_phase) refuse a connected context. 0 or a negative code. */
 size_t hakmc_tp_handle_bytes(void);
 int hakmc_tp_export(hakmc_ctx *c, void *handle);
 int hakmc_tp_connect(hakmc_ctx *c, int rank, int world, const void *handles);

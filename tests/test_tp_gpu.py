@@ -1,7 +1,8 @@
 """Tensor parallelism on 2 GPUs, one process per GPU (CUDA IPC): the step
 kernel splits every phase's rows over both GPUs' CTAs and all-gathers each
 output by peer stores. Row sharding leaves every float sum as on one GPU,
-so tokens and logits must be bit-identical to a single-GPU context's.
+so tokens and logits must be bit-identical to a single-GPU context's; and
+each rank keeps only its own rows of the split matrices.
 Skipped on a box with fewer than 2 GPUs."""
 import os
 
@@ -23,10 +24,13 @@ def _rank(rank, world, preset, n_gen, conn):
         with HakmCtx(path, max_seq=128, device=0) as one:
             out["single_logits"], _ = one.prefill(PROMPT)
             out["single"] = one.generate([int(np.argmax(out["single_logits"]))], n_gen)
+    import torch
     ctx = HakmCtx(path, max_seq=128, device=rank)
     conn.send(ctx.tp_export())
     handles = conn.recv()
+    free0 = torch.cuda.mem_get_info(rank)[0]
     ctx.tp_connect(rank, handles)
+    out["freed"] = torch.cuda.mem_get_info(rank)[0] - free0  # the rows of other ranks, dropped
     out["logits"], am = ctx.prefill(PROMPT)
     out["tp"] = ctx.generate([am], n_gen)
     out["pos"] = ctx.pos
@@ -60,10 +64,16 @@ def test_tp2_bit_identical_to_one_gpu(cuda, preset):
             p.join(timeout=60)
             if p.is_alive():
                 p.kill()
+    cfg = synth.PRESETS[preset]
+    # the bytes of the matrices the step program splits: a decode step's
+    # weights less the tied lm_head (the embedding, which stays whole)
+    split = cfg.weight_bytes_per_token() - cfg.vocab * cfg.d_model // 256 * 210
     for r in range(world):
         assert res[r]["tp"] == res[0]["single"], r
         assert np.array_equal(res[r]["logits"], res[0]["single_logits"]), r
         assert res[r]["pos"] == len(PROMPT) + n_gen
+        if preset == "3b":  # each rank keeps about half of the split weights
+            assert res[r]["freed"] > 0.4 * split, (r, res[r]["freed"], split)
 
 
 @pytest.mark.parametrize("sampling", [("-t", "0"), ("-t", "0.8", "-k", "40", "-p", "0.9", "-s", "1234")])
