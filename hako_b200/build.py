@@ -1,10 +1,12 @@
 """Build recipe for the native parts of hako_b200 (run in-tree).
 
-    python -m hako_b200.build          # libhakm_cuda.so + libhakm_synth.so
+    python -m hako_b200.build          # libhakm_cuda.so, libhakm_tok.so, libhakm_synth.so
 
 libhakm_cuda.so is compiled by nvcc for sm_100a only (no PTX fallback, no
 other architectures) with the CUDA runtime linked statically, so the library
-is self-contained next to the package. Outputs land in hako_b200/_lib/.
+is self-contained next to the package. libhakm_tok.so (the Qwen2 tokenizer,
+include/hakm_tok.h) is plain C compiled by gcc. Outputs land in
+hako_b200/_lib/.
 """
 from __future__ import annotations
 
@@ -78,8 +80,23 @@ def build_synth(force: bool = False) -> str:
     return out
 
 
+TOK_SOURCES = ["host/hakm_bpe.c", "host/hakm_pretok.c"]
+TOK_HEADERS = ["host/hakm_unicode_tables.h", "../include/hakm_tok.h"]
+
+
+def build_tok(force: bool = False) -> str:
+    out = os.path.join(LIB, "libhakm_tok.so")
+    deps = [os.path.join(HERE, s) for s in TOK_SOURCES + TOK_HEADERS]
+    if force or _stale(out, deps):
+        os.makedirs(LIB, exist_ok=True)
+        _run(["gcc", "-O2", "-std=c11", "-Wall", "-Wextra", "-fPIC", "-shared", "-I", os.path.join(ROOT, "include"),
+              "-o", out, *TOK_SOURCES])
+    return out
+
+
 def build_all(force: bool = False) -> None:
     build_synth(force)
+    build_tok(force)
     build_cuda(force)
 
 

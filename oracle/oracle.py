@@ -28,12 +28,14 @@ _vp, _i, _f = C.c_void_p, C.c_int, C.c_float
 
 def build(ref: bool = True) -> None:
     """Compile the restatement, and the reference too when its sources exist
-    (with the reference CLI relinked over the CUDA drop-in once
-    libhakm_cuda is built)."""
+    (its tokenizer on its own, and the reference CLI relinked over the CUDA
+    drop-in and the Qwen2 tokenizer once libhakm_cuda and libhakm_tok are
+    built)."""
     targets = ["all"]
     if ref and os.path.isdir(os.path.join(REF_SRC, "src")):
-        targets.append("ref")
-        if os.path.exists(os.path.join(os.path.dirname(HERE), "hako_b200", "_lib", "libhakm_cuda.so")):
+        targets += ["ref", "reftok"]
+        lib = os.path.join(os.path.dirname(HERE), "hako_b200", "_lib")
+        if all(os.path.exists(os.path.join(lib, f)) for f in ("libhakm_cuda.so", "libhakm_tok.so")):
             targets.append("dropin")
     subprocess.run(["make", "-s", "-C", HERE, *targets, f"REF={REF_SRC}"], check=True)
 

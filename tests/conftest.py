@@ -22,6 +22,7 @@ def pytest_configure(config):
     # build once per session (no-ops when the outputs are newer than the sources)
     from hako_b200 import build as hb
     hb.build_synth()
+    hb.build_tok()
     hb.build_cuda()
     from oracle import oracle as orc
     orc.build(ref=True)

@@ -1,7 +1,8 @@
 """The drop-in boundary exercised by the reference's own caller: the
 reference CLI (cli/main.c) linked against hako_b200/host/hakm_model_cuda.c in
 place of src/model.c (and src/sample.c's sample_token renamed, so the pick is
-made on the device), run as a raw completion.
+made on the device) and hakm_tok_dropin.c (libhakm_tok, the Qwen2 tokenizer)
+in place of src/bpe.c, run as a raw completion.
 
 The drop-in defers the fed ids until sample_token needs their logits (the
 prompt then runs as one batched pass), and its forward pass and sampler are
@@ -66,6 +67,31 @@ def test_reference_cli_sampling_over_dropin(cuda, sampling):
     prompt = "once upon a time there was a"
     ours = _run(DROPIN_CLI, path, 48, prompt, sampling=sampling)
     assert ours == _run(REF_CLI, path, 48, prompt, sampling=sampling)
+
+
+def test_reference_cli_over_dropin_qwen2_tokenizer(cuda, tmp_path):
+    """The prompt reaches the model as the Qwen2 tokenizer's ids
+    (hako_b200.tokenizer over the model file's tokenizer blob): digit,
+    punctuation and whitespace runs and contractions included; the
+    continuation of those ids is the reference model's."""
+    from hako_b200 import synth
+    from hako_b200.tokenizer import Tokenizer
+    if not os.path.exists(DROPIN_CLI):
+        pytest.skip("oracle/_ref/hakm_cuda not built (make -C oracle dropin)")
+    path = synth.cached_model(synth.PRESETS["small"])
+    prompt = "It's 2024!!!  Numbers: 12345,\n\nand don't   stop... the end"
+    want = Tokenizer.from_mlf2(path).encode(prompt)
+    log = tmp_path / "ids.txt"
+    _run(DROPIN_CLI, path, 0, prompt, {"HAKMC_TOKEN_LOG": str(log)})
+    assert [int(x) for x in log.read_text().split()] == want
+    out = _run(DROPIN_CLI, path, 24, prompt, {"HAKMC_TOKEN_LOG": str(log)})
+    assert out.startswith(prompt.encode())
+    ids = [int(x) for x in log.read_text().split()]
+    assert ids[:len(want)] == want
+    fed = ids[len(want):]
+    assert fed
+    ref_stream, _ = ref_greedy(path, want, 24)
+    assert fed == ref_stream[:len(fed)]
 
 
 def test_reference_cli_over_dropin_eager(cuda):
