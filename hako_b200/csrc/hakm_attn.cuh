@@ -19,8 +19,10 @@
 // V chain, which is sequential in t) and runs the V chains of its slice,
 // one dimension per lane of warp 0, while the other warps stage the next
 // tile of V rows in shared memory. Scores live in a global scratch row per
-// unit (score_stride floats). Inputs are read with L2-coherent loads:
-// other SMs may have written them earlier in the same kernel.
+// unit (score_stride floats), or in shared memory past the V tiles when the
+// caller has room for them (tagged-word mode, AttnLL::sc_cap). Inputs are
+// read with L2-coherent loads: other SMs may have written them earlier in
+// the same kernel.
 #pragma once
 #include "hakm_device.cuh"
 #include "hakm_exact.cuh"
@@ -46,6 +48,10 @@ struct AttnLL {
   const long long* out_delta;
   int delta_stride;
   long long kv_off;  // elements from the cache pointers to this sequence's cache (0: the first)
+  // shared floats past the attention tiles (attn_smem_bytes): rows of at
+  // most this many positions keep their scores there instead of in the
+  // global scratch row
+  int sc_cap = 0;
 };
 
 // Tagged output word to every destination GPU.
@@ -118,10 +124,44 @@ __device__ bool attn_item(const AttnParams& a, int unit, int pos, float* sm, int
   float* red = qs + HD;    // [64]
   float* vt = red + 64;    // [2][ATTN_VT][ATTN_SLICE]
   float* sc = a.part + (size_t)unit * a.score_stride;
+  if (LL && n <= T.sc_cap) sc = vt + 2 * ATTN_VT * ATTN_SLICE;
   const long long kv_off = LL ? T.kv_off : 0;
   const float* kb = a.k_cache + kv_off + kvh * HD;
   const float* vb = a.v_cache + kv_off + kvh * HD + sl * ATTN_SLICE;
   bool ok = true;
+  const int l = lane & 7;
+
+  // V rows of the first tile into buffer 0; in tagged-word mode the row of
+  // this position comes from a tagged word of the qkv phase and waits for
+  // the softmax (fill_pos_row), the others are cache rows of earlier steps
+  // and load at once
+  auto stage = [&](int tile, int buf, int t_lo, int t_n, bool skip_pos) {
+    float* dst = vt + buf * ATTN_VT * ATTN_SLICE;
+    const int t0 = tile * ATTN_VT, cnt = min(ATTN_VT, n - t0);
+    for (int i = t_lo; i < cnt * (ATTN_SLICE / 4); i += t_n) {
+      const int r = i / (ATTN_SLICE / 4), c4 = i % (ATTN_SLICE / 4), t = t0 + r;
+      float4 v;
+      if (LL && t == pos) {
+        if (skip_pos) continue;
+        float w[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+          ok &= ll_get1(T.v + kvh * HD + sl * ATTN_SLICE + 4 * c4 + k, T.in_tag, w[k], T.err);
+        v = make_float4(w[0], w[1], w[2], w[3]);
+      } else {
+        v = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)t * kv_dim) + c4);
+      }
+      reinterpret_cast<float4*>(dst)[i] = v;
+    }
+  };
+  if constexpr (LL) {
+    // the K rows this thread will score into L2 (no registers held across
+    // the wait for q): lanes 0..HD/32-1 of each position one 128-byte line
+    if (l < HD / 32)
+      for (int t = 4 * warp + (lane >> 3); t < n; t += 4 * nw)
+        if (t != pos) asm volatile("prefetch.global.L2 [%0];" ::"l"(kb + (size_t)t * kv_dim + 32 * l));
+    stage(0, 0, tid, nthr, true);
+  }
 
   for (int i = tid; i < HD; i += nthr) {
     float v;
@@ -134,7 +174,6 @@ __device__ bool attn_item(const AttnParams& a, int unit, int pos, float* sm, int
   // scores: lane (p, l) = (lane / 8, lane % 8) runs chain l of position
   // 4 * (iteration) + p; the 8 chains of a position fold over its lanes
   {
-    const int l = lane & 7;
     float qv[HD / 8];
 #pragma unroll
     for (int j = 0; j < HD / 8; j++) qv[j] = qs[8 * j + l];
@@ -165,25 +204,17 @@ __device__ bool attn_item(const AttnParams& a, int unit, int pos, float* sm, int
   // weighted V: warp 0 lane d runs out[d] over the staged tiles; the other
   // warps stage tile i + 1 while it works on tile i
   const int n_tiles = (n + ATTN_VT - 1) / ATTN_VT;
-  auto stage = [&](int tile, int buf, int t_lo, int t_n) {
-    float* dst = vt + buf * ATTN_VT * ATTN_SLICE;
-    const int t0 = tile * ATTN_VT, cnt = min(ATTN_VT, n - t0);
-    for (int i = t_lo; i < cnt * (ATTN_SLICE / 4); i += t_n) {
-      const int r = i / (ATTN_SLICE / 4), c4 = i % (ATTN_SLICE / 4), t = t0 + r;
-      float4 v;
-      if (LL && t == pos) {
-        float w[4];
+  if constexpr (LL) {
+    // tile 0 was staged before q but for this position's row
+    if (pos < ATTN_VT && tid < ATTN_SLICE / 4) {
+      float w[4];
 #pragma unroll
-        for (int k = 0; k < 4; k++)
-          ok &= ll_get1(T.v + kvh * HD + sl * ATTN_SLICE + 4 * c4 + k, T.in_tag, w[k], T.err);
-        v = make_float4(w[0], w[1], w[2], w[3]);
-      } else {
-        v = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)t * kv_dim) + c4);
-      }
-      reinterpret_cast<float4*>(dst)[i] = v;
+      for (int k = 0; k < 4; k++) ok &= ll_get1(T.v + kvh * HD + sl * ATTN_SLICE + 4 * tid + k, T.in_tag, w[k], T.err);
+      reinterpret_cast<float4*>(vt)[pos * (ATTN_SLICE / 4) + tid] = make_float4(w[0], w[1], w[2], w[3]);
     }
-  };
-  stage(0, 0, tid, nthr);
+  } else {
+    stage(0, 0, tid, nthr, false);
+  }
   sync();
   float acc = 0.f;
   for (int tile = 0; tile < n_tiles; tile++) {
@@ -192,7 +223,7 @@ __device__ bool attn_item(const AttnParams& a, int unit, int pos, float* sm, int
       const int t0 = tile * ATTN_VT, cnt = min(ATTN_VT, n - t0);
       for (int r = 0; r < cnt; r++) acc = __fmaf_rn(sc[t0 + r], src[r * ATTN_SLICE], acc);
     } else if (tile + 1 < n_tiles) {
-      stage(tile + 1, (tile + 1) & 1, tid - 32, nthr - 32);
+      stage(tile + 1, (tile + 1) & 1, tid - 32, nthr - 32, false);
     }
     sync();
   }

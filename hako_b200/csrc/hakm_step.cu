@@ -775,6 +775,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
         T.out_delta = &A.tp_delta[0][XR_LL];
         T.delta_stride = XR_COUNT;
         T.kv_off = A.kv_off;
+        T.sc_cap = A.region_bytes / 4 - (int)(attn_smem_bytes(HD) / 4);
         // (query head, dimension slice) units; with tensor parallelism this
         // GPU runs units rank, rank + world, ...
         const int n_loc = attn_units_local(attn_units(D.a.n_heads, HD), A.tp_rank, A.tp_world);
