@@ -144,9 +144,7 @@ __device__ bool attn_item(const AttnParams& a, int unit, int pos, float* sm, int
       if (LL && t == pos) {
         if (skip_pos) continue;
         float w[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++)
-          ok &= ll_get1(T.v + kvh * HD + sl * ATTN_SLICE + 4 * c4 + k, T.in_tag, w[k], T.err);
+        ok &= ll_get<4>(T.v + kvh * HD + sl * ATTN_SLICE + 4 * c4, T.in_tag, w, T.err);
         v = make_float4(w[0], w[1], w[2], w[3]);
       } else {
         v = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)t * kv_dim) + c4);
@@ -183,8 +181,7 @@ __device__ bool attn_item(const AttnParams& a, int unit, int pos, float* sm, int
       if (t < n) {
         float kv[HD / 8];
         if (LL && t == pos) {
-#pragma unroll
-          for (int j = 0; j < HD / 8; j++) ok &= ll_get1(T.k + kvh * HD + 8 * j + l, T.in_tag, kv[j], T.err);
+          ok &= ll_get_strided<HD / 8>(T.k + kvh * HD + l, 8, T.in_tag, kv, T.err);
         } else {
           const float* kr = kb + (size_t)t * kv_dim + l;
 #pragma unroll
@@ -208,8 +205,7 @@ __device__ bool attn_item(const AttnParams& a, int unit, int pos, float* sm, int
     // tile 0 was staged before q but for this position's row
     if (pos < ATTN_VT && tid < ATTN_SLICE / 4) {
       float w[4];
-#pragma unroll
-      for (int k = 0; k < 4; k++) ok &= ll_get1(T.v + kvh * HD + sl * ATTN_SLICE + 4 * tid + k, T.in_tag, w[k], T.err);
+      ok &= ll_get<4>(T.v + kvh * HD + sl * ATTN_SLICE + 4 * tid, T.in_tag, w, T.err);
       reinterpret_cast<float4*>(vt)[pos * (ATTN_SLICE / 4) + tid] = make_float4(w[0], w[1], w[2], w[3]);
     }
   } else {

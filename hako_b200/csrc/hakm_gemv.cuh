@@ -75,15 +75,25 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     if (clock64() - t0 > WAIT_LIMIT) return false;
   return true;
 }
-// Weight rows are read once per token: the copy carries an L2 evict-first
-// policy so the stream does not push the small hot data (exchanged vectors,
-// K/V rows, norm weights, descriptors) out of L2.
 // 2-D tiled tensor copy (no multicast) of the box at (x, y) into shared memory.
 __device__ __forceinline__ void tma_2d(uint32_t dst, const void* map, int x, int y, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+// Weight rows are read once per token: these copies carry an L2
+// evict-first policy, so that the stream does not push what is reused out
+// of L2 (the kernel's own code, exchanged vectors, K/V rows, norm weights,
+// activations that other CTAs read). tma_2d_stream is tma_2d with it.
+__device__ __forceinline__ void tma_2d_stream(uint32_t dst, const void* map, int x, int y, uint32_t bar) {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(pol)
       : "memory");
 }
 

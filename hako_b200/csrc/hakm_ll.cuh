@@ -104,6 +104,50 @@ __device__ __forceinline__ bool ll_finish8(const uint64_t* p, uint32_t tag, uint
   return true;
 }
 
+// N tagged floats p[0], p[stride], ..., p[(N-1)*stride]: all N loads in
+// flight before the first tag check (a loop of ll_get1 would wait for each
+// load's answer before it issues the next), then only the words still
+// lacking the tag are read again, a short sleep between rounds. Gives up as
+// ll_get does.
+template <int N>
+__device__ __forceinline__ bool ll_get_strided(const uint64_t* p, int stride, uint32_t tag, float* out,
+                                               const int* err) {
+  uint64_t w[N];
+#pragma unroll
+  for (int i = 0; i < N; i++)
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[i]) : "l"(p + (size_t)i * stride) : "memory");
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < N; i++) ok = ok && ll_has(w[i], tag);
+  if (!ok) {
+    const long long t0 = clock64();
+    long long next = t0 + 4096;
+    for (;;) {
+      __nanosleep(64);
+#pragma unroll
+      for (int i = 0; i < N; i++)
+        if (!ll_has(w[i], tag))
+          asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w[i]) : "l"(p + (size_t)i * stride) : "memory");
+      ok = true;
+#pragma unroll
+      for (int i = 0; i < N; i++) ok = ok && ll_has(w[i], tag);
+      if (ok) break;
+      const long long now = clock64();
+      if (now > next) {
+        if (ll_aborted(err) || now - t0 > LL_WAIT_LIMIT) {
+#pragma unroll
+          for (int i = 0; i < N; i++) out[i] = 0.f;
+          return false;
+        }
+        next = now + 4096;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < N; i++) out[i] = ll_value(w[i]);
+  return true;
+}
+
 // One tagged float (p 8-byte aligned).
 __device__ __forceinline__ bool ll_get1(const uint64_t* p, uint32_t tag, float& out, const int* err) {
   uint64_t w;

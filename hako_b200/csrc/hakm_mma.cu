@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(MM_THREADS, 1)
         const uint32_t bar = smem_addr(&t_full[s]);
         const int g = b;
         mbar_expect_tx(bar, L::TX);
-        tma_2d(smem_addr(st + L::T_RAW), &wmap, g * (Q4K_BYTES / 8), row0, bar);
+        tma_2d_stream(smem_addr(st + L::T_RAW), &wmap, g * (Q4K_BYTES / 8), row0, bar);
         tma_2d(smem_addr(st + L::T_B), &xmap, g * QK, n0, bar);
         tma_2d(smem_addr(st + L::T_B + BN * 128), &xmap, g * QK + 128, n0, bar);
         tma_2d(smem_addr(st + L::T_XS), &smap, g * 8, n0, bar);

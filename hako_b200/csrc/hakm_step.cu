@@ -508,7 +508,7 @@ __global__ void __launch_bounds__(THREADS, 1) step_kernel(const __grid_constant_
               }
               if (lane == 0) {
                 mbar_expect_tx(smem_addr(&full[rp.slot]), bytes);
-                tma_2d(smem_addr(ring + (size_t)rp.slot * SB), map, c * (Q6K_CHUNK / 8), rr.x - rr.z,
+                tma_2d_stream(smem_addr(ring + (size_t)rp.slot * SB), map, c * (Q6K_CHUNK / 8), rr.x - rr.z,
                        smem_addr(&full[rp.slot]));
               }
               __syncwarp();
