@@ -272,12 +272,33 @@ __device__ __forceinline__ float rms_scale(const float* sq, int cp, int K, float
   const int lane = threadIdx.x & 31, l = lane & 7, nt = K / 8;
   float acc = 0.f;
   if (lane < 8) {
+    // float4 w holds positions (4t, 4t+2, 4t+1, 4t+3). The chain is 4 adds a
+    // float4; groups of RG float4 are loaded one group ahead, so the shared
+    // loads' latency hides behind the previous group's adds
+    constexpr int RG = 4;
     const float4* row = reinterpret_cast<const float4*>(sq + l * cp);
-    for (int t = 0; t < nt / 4; t++) {
-      const float4 w = row[t];  // positions (4t, 4t+2, 4t+1, 4t+3)
+    const int n4 = nt / 4, ng = n4 / RG;
+    auto add4 = [&](const float4& w) {
       acc = __fadd_rn(acc, w.x); acc = __fadd_rn(acc, w.z);
       acc = __fadd_rn(acc, w.y); acc = __fadd_rn(acc, w.w);
+    };
+    if (ng > 0) {
+      float4 cur[RG];
+#pragma unroll
+      for (int i = 0; i < RG; i++) cur[i] = row[i];
+      for (int g = 1; g < ng; g++) {
+        float4 nxt[RG];
+#pragma unroll
+        for (int i = 0; i < RG; i++) nxt[i] = row[RG * g + i];
+#pragma unroll
+        for (int i = 0; i < RG; i++) add4(cur[i]);
+#pragma unroll
+        for (int i = 0; i < RG; i++) cur[i] = nxt[i];
+      }
+#pragma unroll
+      for (int i = 0; i < RG; i++) add4(cur[i]);
     }
+    for (int t = RG * ng; t < n4; t++) add4(row[t]);
   }
   const float ss = fold8_lanes(acc);
   return rsqrt_nr(__fadd_rn(__fdiv_rn(ss, (float)K), eps), rsq);
@@ -407,6 +428,14 @@ __device__ __forceinline__ Q4X q4x_load(const int8_t* xq, const float* xs, const
 //   v  = fma(tB, xsB, tA*xsA)
 // which the row's running sum then takes with one rounded add (q4k_chain).
 // The integer sums are exact dp4a results.
+// Sum of the four products of unsigned bytes of a with signed bytes of b,
+// plus c (PTX dp4a.u32.s32).
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
 template <int NR = 4>
 __device__ __forceinline__ void q4k_pairs(const uint8_t* st, int rstride, int nrows, int m, const Q4X& X,
                                           float v[4]) {
@@ -428,12 +457,18 @@ __device__ __forceinline__ void q4k_pairs(const uint8_t* st, int rstride, int nr
 #pragma unroll
   for (int r = 0; r < NR; r++) {
     const uint32_t qw[8] = {q0[r].x, q0[r].y, q0[r].z, q0[r].w, q1[r].x, q1[r].y, q1[r].z, q1[r].w};
-    int ia = 0, ib = 0;
+    // exact integer sums, in two independent chains each (shorter
+    // dependency chains); the high nibbles stay in place (16 * q) through
+    // an unsigned x signed dp4a and the sum is divided by 16 at the end
+    int ia0 = 0, ia1 = 0, ib0 = 0, ib1 = 0;
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-      ia = __dp4a((int)(qw[i] & 0x0F0F0F0Fu), X.a[i], ia);
-      ib = __dp4a((int)((qw[i] >> 4) & 0x0F0F0F0Fu), X.b[i], ib);
+    for (int i = 0; i < 4; i++) {
+      ia0 = __dp4a((int)(qw[i] & 0x0F0F0F0Fu), X.a[i], ia0);
+      ia1 = __dp4a((int)(qw[i + 4] & 0x0F0F0F0Fu), X.a[i + 4], ia1);
+      ib0 = dp4a_us(qw[i] & 0xF0F0F0F0u, X.b[i], ib0);
+      ib1 = dp4a_us(qw[i + 4] & 0xF0F0F0F0u, X.b[i + 4], ib1);
     }
+    const int ia = ia0 + ia1, ib = (ib0 + ib1) >> 4;
     const float d = half_bits_to_float(hd[r].x), dmin = half_bits_to_float(hd[r].x >> 16);
     // get_scale_min_k4 (src/quant.c:57-66) for j = 2g, 2g+1, branch-free:
     // scales[0..3] in hd.y, [4..7] in hd.z, [8..11] in hd.w
